@@ -1,0 +1,236 @@
+/*
+ * wx_api.h — C ABI of libwx, the B200 (sm_100a) implementation of the
+ * MiniMax-H3 video-DiT denoising step of HuaChayu/wuxianhuabu.
+ *
+ * The reference is Swift over MLX; every entry point below names the Swift
+ * interface it replaces (file:line within the reference project). Callers pass
+ * device pointers they own; tensors are row-major, bf16 values are raw 16-bit
+ * patterns. Calls are ordered on the context's stream and never abort the
+ * process: each returns WX_OK or a negative wx_status, and wx_last_error()
+ * gives the message. A context is not thread-safe; use one per thread/GPU.
+ */
+#ifndef WX_API_H
+#define WX_API_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct wx_ctx wx_ctx;
+
+enum wx_status {
+  WX_OK = 0,
+  WX_ERR_INVALID = -1,     /* bad shape, pointer, alignment or option */
+  WX_ERR_CUDA = -2,        /* a CUDA runtime/driver call failed */
+  WX_ERR_NOMEM = -3,       /* workspace allocation failed */
+  WX_ERR_DEVICE = -4,      /* a kernel reported a device-side error (bounded wait expired) */
+  WX_ERR_UNSUPPORTED = -5, /* geometry not supported by this build */
+};
+
+/* fused GEMM epilogues (applied to t = bf16(bf16(acc) + bias)) */
+enum wx_epilogue {
+  WX_EPI_NONE = 0,       /* y = t */
+  WX_EPI_GELU = 1,       /* y = bf16(gelu_tanh(t)) */
+  WX_EPI_GATE_RESID = 2, /* y = bf16(resid + t * gate[rowmap[m]]); y_raw = t (optional) */
+  WX_EPI_SWIGLU = 3,     /* fc1 emits [gate | up]: y[:, j] = bf16(silu(t[:, j]) * t[:, F + j]) */
+};
+
+enum wx_sparse_mode {
+  WX_SPARSE_DENSE = 0, /* SDPA over every key */
+  WX_SPARSE_SOL = 1,   /* SOL tau routing + tail pooled term */
+  WX_SPARSE_TOPK = 2,  /* diagonal + top-k fraction of key blocks */
+};
+
+enum wx_mlp_kind { WX_MLP_GELU = 0, WX_MLP_SWIGLU = 1 };
+
+/* 6-bit (2..8-bit) MLX-affine group-quantized weight of a linear layer:
+ * wq [n, k*bits/32] uint32, scales/biases [n, k/group] bf16, bias [n] bf16 or NULL.
+ * Mirrors MfLinear's quantized fields (model/minimax h3/H3Common.swift:283-338). */
+typedef struct wx_qweight {
+  const uint32_t* wq;
+  const void* scales;
+  const void* biases;
+  const void* bias;
+  int64_t n;
+  int64_t k;
+  int32_t group;
+  int32_t bits;
+} wx_qweight;
+
+/* H3SolAttnConfig + SparseSpec (网络算子-稀疏注意力-SOL通用.swift:79-98;
+ * model/minimax h3/H3Layout.swift:909-920). */
+typedef struct wx_sparse_spec {
+  int32_t mode;       /* wx_sparse_mode */
+  int32_t block;      /* key/query block rows: 64 (SOL) or 128 (top-k) */
+  int64_t g;          /* strip rows [0, g) = SparseSpec.videoStart */
+  float tau;          /* SOL threshold multiplier (default 1.3) */
+  float density;      /* top-k kept fraction of off-diagonal blocks (0.25) */
+  int32_t sink_start; /* always-exact video blocks [sink_start, sink_end) */
+  int32_t sink_end;
+  int32_t tail;       /* 1: unselected blocks add the pooled tail term */
+  int32_t reserved;
+} wx_sparse_spec;
+
+/* one DiT block's weights (H3BlockW / H3AttnW / H3MlpW, H3Transformer.swift:405-660) */
+typedef struct wx_block_weights {
+  wx_qweight qkv; /* hidden -> 3*inner */
+  wx_qweight out; /* inner -> hidden */
+  wx_qweight fc1; /* hidden -> ffn (GELU) or 2*ffn (SwiGLU) */
+  wx_qweight fc2; /* ffn -> hidden */
+  const void* q_norm; /* [head_dim] bf16 */
+  const void* k_norm;
+  const void* norm1; /* [hidden] bf16 */
+  const void* norm2;
+} wx_block_weights;
+
+/* model geometry (H3Config, H3Common.swift:78-139) */
+typedef struct wx_dit_config {
+  int64_t hidden;
+  int32_t heads;
+  int32_t head_dim;
+  int64_t ffn;
+  int32_t mlp_kind; /* wx_mlp_kind */
+  int32_t rot;      /* rotated dims (rotHalf*2); dims [rot, head_dim) pass through */
+  float eps;        /* RMSNorm epsilon */
+  int32_t reserved;
+} wx_dit_config;
+
+/* AdaLN modulation tables of one block, each [num_mod_rows, hidden] bf16:
+ * shift/scale/gate for attention (MSA) and MLP (H3Transformer.swift:1083-1107) */
+typedef struct wx_block_mods {
+  const void* shift_msa;
+  const void* scale_msa;
+  const void* gate_msa;
+  const void* shift_mlp;
+  const void* scale_mlp;
+  const void* gate_mlp;
+} wx_block_mods;
+
+/* ModRun (H3Layout.swift:744-753) */
+typedef struct wx_mod_run {
+  uint32_t start;
+  uint32_t end;
+  uint32_t mod_row;
+} wx_mod_run;
+
+/* ------------------------------------------------------------- context */
+int wx_ctx_create(int device, wx_ctx** out);
+int wx_ctx_destroy(wx_ctx* ctx);
+/* stream: a cudaStream_t (NULL = legacy default stream) */
+int wx_ctx_set_stream(wx_ctx* ctx, void* stream);
+const char* wx_last_error(wx_ctx* ctx);
+/* synchronises the stream and returns WX_ERR_DEVICE if a kernel set the
+ * device error word since the last call (the word is cleared) */
+int wx_ctx_check_device(wx_ctx* ctx);
+/* bytes currently held by the context workspace arena */
+size_t wx_ctx_workspace_bytes(wx_ctx* ctx);
+int wx_version(void);
+
+/* ---------------------------------------------------- quantized linear */
+/* Affine group quantization of fp32 w [n, k] (the offline step of
+ * model/minimax h3/tools/quantize_h3_g64.py:92-99, done on the GPU). */
+int wx_quantize_affine(wx_ctx* ctx, const float* w, int64_t n, int64_t k, int group, int bits,
+                       uint32_t* wq, void* scales, void* biases);
+/* MfLinear.dequantizedWeight (H3Common.swift:379-401): w_out[n][k] =
+ * bf16(q*scale + bias) computed in fp32. */
+int wx_dequantize_affine(wx_ctx* ctx, const wx_qweight* w, void* w_out);
+/* MfLinear.forward quantized branch (H3Common.swift:341-377; quantizedMM
+ * :358-359, +bias :366-368) with a fused epilogue (wx_epilogue).
+ * x [m, k] row pitch lda; y [m, n] (SWIGLU: [m, n/2]) row pitch ldy;
+ * gate [num_mod_rows, n] and resid [m, n] (pitch ldy) for WX_EPI_GATE_RESID. */
+int wx_qlinear(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+               int epilogue, const void* gate, const void* resid, const uint32_t* rowmap,
+               void* y, int64_t ldy, void* y_raw);
+
+/* ------------------------------------------------------ fused row ops */
+/* H3FusedKernels.fusedRmsnormRope (网络算子-融合-RMSNormRoPE-通用.swift:111-129):
+ * rows (s, h) of head_dim at x[s*x_stride + h*head_dim]; cos/sin [S, rot/2] bf16;
+ * out may alias x. */
+int wx_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, int64_t S, int H, int head_dim,
+                    const void* w, const void* cos_t, const void* sin_t, int rot, float eps,
+                    void* out, int64_t out_stride);
+/* q and k of a packed qkv buffer [S, 3*H*head_dim] normalised + rotated in place
+ * in one launch (the two fusedRmsnormRope calls of H3AttnW.forward, H3Transformer.swift:454-475) */
+int wx_qk_norm_rope_qkv(wx_ctx* ctx, void* qkv, int64_t S, int H, int head_dim, const void* q_w,
+                        const void* k_w, const void* cos_t, const void* sin_t, int rot, float eps);
+/* H3FusedKernels.fusedNormModscale (fused:262-283); rowmap NULL = fusedNormModscaleRow (:295-315) */
+int wx_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w,
+                     const void* shift, const void* scale, const uint32_t* rowmap, float eps,
+                     void* out);
+/* H3FusedKernels.fusedModGate (fused:324-343): out = bf16(x + other*gate[map[r]]) */
+int wx_mod_gate(wx_ctx* ctx, const void* x, const void* other, const void* gate,
+                const uint32_t* rowmap, int64_t S, int64_t hidden, void* out);
+/* H3FusedKernels.buildRowModMap (fused:238-250), host memory in and out */
+int wx_build_row_mod_map(const wx_mod_run* runs, int nruns, int64_t count, uint32_t* map_out);
+
+/* ----------------------------------------------------------- attention */
+/* Routing tables of H3SolAttn.forward (SOL:455-497), for inspection/tests.
+ * q/k/v rows at base + s*row_stride + h*head_dim; nb = ceil((S-g)/block).
+ * sel [H,nb,nb] u8, thr [H,nb] f32, cm [H,nb,nb] bf16, vsum [H,nb,hd] bf16, lens [nb] f32 */
+int wx_sol_route(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t row_stride,
+                 int64_t S, int H, int head_dim, const wx_sparse_spec* spec, float scale,
+                 uint8_t* sel, float* thr, void* cm, void* vsum, float* lens);
+/* top-k router (benchmark mode); scores [H,nb,nb] f32, other outputs as above */
+int wx_topk_route(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t row_stride,
+                  int64_t S, int H, int head_dim, const wx_sparse_spec* spec, float scale,
+                  uint8_t* sel, float* scores, void* cm, void* vsum, float* lens);
+/* H3SolAttn.forward (SOL:388-532) / scaledDotProductAttention for dense layers:
+ * routing + tcgen05 flash attention; out rows at out + s*out_stride + h*head_dim.
+ * head_dim must be 128; q/k/v rows 16-byte aligned. */
+int wx_sparse_attention(wx_ctx* ctx, const void* q, const void* k, const void* v,
+                        int64_t row_stride, int64_t S, int H, int head_dim,
+                        const wx_sparse_spec* spec, float scale, void* out, int64_t out_stride);
+/* the flash kernel alone with a caller-provided selection sel [H,nb,nb] (device);
+ * cm/vsum/lens are needed only when spec->tail is set */
+int wx_attention_from_sel(wx_ctx* ctx, const void* q, const void* k, const void* v,
+                          int64_t row_stride, int64_t S, int H, int head_dim,
+                          const wx_sparse_spec* spec, float scale, const uint8_t* sel,
+                          const void* cm, const void* vsum, const float* lens, void* out,
+                          int64_t out_stride);
+
+/* --------------------------------------------------- PAB + schedules (host) */
+/* attnBroadcastRefresh (网络算子-注意力跨步缓存-通用.swift:73-79) */
+int wx_pab_refresh(int i, uint32_t steps, uint32_t k);
+/* attnBroadcastMustRefresh (:85-87) */
+int wx_pab_must_refresh(double cached_sigma, double sigma, double max_stale);
+/* attnBroadcastPlan (:92-105): out[nfe] = 1 refresh / 0 reuse; returns nfe */
+int wx_pab_plan(const double* sigmas, int nsigmas, uint32_t k, double max_stale, uint8_t* out);
+/* sigmaSchedule (model/minimax h3/H3Layout.swift:175-182): out[steps+1] */
+int wx_sigma_schedule(uint32_t steps, double shift, double* out);
+/* sparseModeForLayer (H3Layout.swift:896-906); policy 0 off, 1 mix, 2 spatial, 3 temporal;
+ * returns 0 dense, 1 spatial, 2 temporal */
+int wx_sparse_mode_for_layer(int layer, int nlayers, int policy);
+
+/* ------------------------------------------------------------ DiT block */
+/* Byte size of the scratch buffer wx_dit_block_forward needs for S rows. */
+int64_t wx_dit_block_scratch_bytes(const wx_dit_config* cfg, int64_t S);
+/* One iteration of the block loop of H3DiT.forward (H3Transformer.swift:1078-1159):
+ *   refresh (or pab_slot == NULL): m1 = norm_modscale(h); at = attn(m1) [-> pab_slot]
+ *   reuse: at = pab_slot
+ *   hAttn = h + at*gateMSA; m2 = norm_modscale(hAttn); h = hAttn + mlp(m2)*gateMLP
+ * h [S, hidden] bf16 is updated in place. cos/sin [S, rot/2] bf16.
+ * scratch: wx_dit_block_scratch_bytes(cfg, S) bytes of device memory. */
+int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_weights* w,
+                         const wx_block_mods* mods, const uint32_t* rowmap, void* h, int64_t S,
+                         const void* cos_t, const void* sin_t, const wx_sparse_spec* spec,
+                         void* pab_slot, int refresh, void* scratch);
+
+/* fp32 dense linear y = x*w + b (H3TensorOps.denseLinear: patch embed and final
+ * head islands, H3Transformer.swift:1036-1039, 1192-1203); w [k, n] fp32. */
+int wx_dense_f32(wx_ctx* ctx, const float* x, int64_t m, int64_t k, const float* w, int64_t n,
+                 const float* b, float* y);
+/* bf16 -> fp32 copy of rows (the .asType(.float32) before the final head) */
+int wx_bf16_to_f32(wx_ctx* ctx, const void* x, int64_t n, float* y);
+/* fp32 -> bf16 (embedding cast) */
+int wx_f32_to_bf16(wx_ctx* ctx, const float* x, int64_t n, void* y);
+/* Euler update of the sampler loop (H3Pipeline.swift:1436-1443) with the
+ * negated velocity of H3DiT.forward (:1188): x[i] += (-v[i]) * dsigma */
+int wx_euler_update(wx_ctx* ctx, float* x, const float* v, int64_t n, float dsigma);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* WX_API_H */

@@ -1,0 +1,257 @@
+"""numpy front end of the C oracle (oracle/wx_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+CPU-baseline / reference legs of bench.py, never by the product package.
+bf16 arrays are numpy uint16 bit patterns. Parity status: see wx_oracle.h.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "_build" / "libwxoracle.so"
+
+EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SWIGLU = 0, 1, 2, 3
+
+_vp, _i64, _i32, _f32, _u64 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_uint64
+_SIGS = {
+    "wxo_f32_to_bf16": (None, [_vp, _vp, _i64]),
+    "wxo_bf16_to_f32": (None, [_vp, _vp, _i64]),
+    "wxo_fill_normal_f32": (None, [_vp, _i64, _u64, _u64, _f32, _f32]),
+    "wxo_fill_normal_bf16": (None, [_vp, _i64, _u64, _u64, _f32, _f32]),
+    "wxo_quantize_affine": (_i32, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
+    "wxo_dequantize_affine": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _vp]),
+    "wxo_qlinear": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "wxo_qk_norm_rope": (_i32, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _i32, _f32, _vp, _i64]),
+    "wxo_norm_modscale": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp, _vp, _f32, _vp]),
+    "wxo_mod_gate": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "wxo_sol_route": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i64, _i32, _f32, _f32, _i32, _i32,
+                             _vp, _vp, _vp, _vp, _vp]),
+    "wxo_topk_route": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i64, _i32, _f32, _f32,
+                              _vp, _vp, _vp, _vp, _vp]),
+    "wxo_sparse_attention": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i64, _i32, _f32, _vp, _vp, _vp, _vp,
+                                    _i32, _vp, _i64]),
+    "wxo_dense_f32": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "wxo_num_threads": (_i32, []),
+}
+
+_lib = None
+
+
+def build() -> Path:
+    src, hdr = HERE / "wx_oracle.c", HERE / "wx_oracle.h"
+    LIB.parent.mkdir(exist_ok=True)
+    if not LIB.exists() or LIB.stat().st_mtime < max(src.stat().st_mtime, hdr.stat().st_mtime):
+        subprocess.check_call(["gcc", "-O3", "-march=x86-64-v2", "-fopenmp", "-ffp-contract=off", "-fPIC",
+                               "-shared", "-o", str(LIB), str(src), "-lm"])
+    return LIB
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build()
+        l = C.CDLL(str(LIB))
+        for n, (r, a) in _SIGS.items():
+            f = getattr(l, n)
+            f.restype = r
+            f.argtypes = a
+        _lib = l
+    return _lib
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data
+
+
+def _chk(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"oracle {what} failed ({rc})")
+
+
+# ------------------------------------------------------------------------- bf16 / RNG
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    lib().wxo_f32_to_bf16(_ptr(x), _ptr(out), x.size)
+    return out
+
+
+def bf16_to_f32(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    out = np.empty(x.shape, dtype=np.float32)
+    lib().wxo_bf16_to_f32(_ptr(x), _ptr(out), x.size)
+    return out
+
+
+def normal_f32(shape, seed: int, stream: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(shape, dtype=np.float32)
+    lib().wxo_fill_normal_f32(_ptr(out), out.size, seed, stream, mean, std)
+    return out
+
+
+def normal_bf16(shape, seed: int, stream: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    out = np.empty(shape, dtype=np.uint16)
+    lib().wxo_fill_normal_bf16(_ptr(out), out.size, seed, stream, mean, std)
+    return out
+
+
+# ------------------------------------------------------------------------ quantization
+def quantize(w: np.ndarray, bits: int = 6, group: int = 64):
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    wq = np.empty((n, k * bits // 32), dtype=np.uint32)
+    sc = np.empty((n, k // group), dtype=np.uint16)
+    bi = np.empty((n, k // group), dtype=np.uint16)
+    _chk(lib().wxo_quantize_affine(_ptr(w), n, k, group, bits, _ptr(wq), _ptr(sc), _ptr(bi)), "quantize")
+    return wq, sc, bi
+
+
+def dequantize(wq, sc, bi, k: int, bits: int = 6, group: int = 64) -> np.ndarray:
+    n = wq.shape[0]
+    out = np.empty((n, k), dtype=np.uint16)
+    _chk(lib().wxo_dequantize_affine(_ptr(np.ascontiguousarray(wq)), _ptr(np.ascontiguousarray(sc)),
+                                     _ptr(np.ascontiguousarray(bi)), n, k, group, bits, _ptr(out)), "dequantize")
+    return out
+
+
+def qlinear(x, wq, sc, bi, bits=6, group=64, bias=None, epilogue=EPI_NONE, gate=None, resid=None, rowmap=None,
+            want_raw=False):
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    m, k = x.shape
+    n = wq.shape[0]
+    ncols = n // 2 if epilogue == EPI_SWIGLU else n
+    y = np.empty((m, ncols), dtype=np.uint16)
+    raw = np.empty((m, n), dtype=np.uint16) if want_raw else None
+    _chk(lib().wxo_qlinear(_ptr(x), m, k, _ptr(np.ascontiguousarray(wq)), _ptr(np.ascontiguousarray(sc)),
+                           _ptr(np.ascontiguousarray(bi)), n, group, bits, _ptr(bias), epilogue, _ptr(gate),
+                           _ptr(resid), _ptr(rowmap), _ptr(y), _ptr(raw)), "qlinear")
+    return (y, raw) if want_raw else y
+
+
+# --------------------------------------------------------------------------- row ops
+def qk_norm_rope(x: np.ndarray, w, cos, sin, rot: int, eps: float) -> np.ndarray:
+    """x [S, H, hd] uint16 (contiguous)."""
+    x = np.ascontiguousarray(x)
+    S, H, hd = x.shape
+    out = np.empty_like(x)
+    _chk(lib().wxo_qk_norm_rope(_ptr(x), H * hd, S, H, hd, _ptr(w), _ptr(cos), _ptr(sin), rot, eps, _ptr(out),
+                                H * hd), "qk_norm_rope")
+    return out
+
+
+def norm_modscale(x, w, shift, scale, rowmap, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    S, hidden = x.shape
+    out = np.empty_like(x)
+    _chk(lib().wxo_norm_modscale(_ptr(x), S, hidden, _ptr(w), _ptr(shift), _ptr(scale), _ptr(rowmap), eps,
+                                 _ptr(out)), "norm_modscale")
+    return out
+
+
+def mod_gate(x, other, gate, rowmap) -> np.ndarray:
+    x = np.ascontiguousarray(x)
+    S, hidden = x.shape
+    out = np.empty_like(x)
+    _chk(lib().wxo_mod_gate(_ptr(x), _ptr(np.ascontiguousarray(other)), _ptr(gate), _ptr(rowmap), S, hidden,
+                            _ptr(out)), "mod_gate")
+    return out
+
+
+# ------------------------------------------------------------------------- attention
+def sol_route(q, k, v, g: int, scale: float, tau: float, block: int = 64, sink=(0, 0)):
+    """q/k/v [S, H, hd] uint16 contiguous. Returns dict(sel, thr, cm, vsum, lens)."""
+    S, H, hd = q.shape
+    nb = (S - g + block - 1) // block
+    sel = np.empty((H, nb, nb), dtype=np.uint8)
+    thr = np.empty((H, nb), dtype=np.float32)
+    cm = np.empty((H, nb, nb), dtype=np.uint16)
+    vsum = np.empty((H, nb, hd), dtype=np.uint16)
+    lens = np.empty((nb,), dtype=np.float32)
+    _chk(lib().wxo_sol_route(_ptr(q), _ptr(k), _ptr(v), H * hd, S, H, hd, g, block, scale, tau, sink[0], sink[1],
+                             _ptr(sel), _ptr(thr), _ptr(cm), _ptr(vsum), _ptr(lens)), "sol_route")
+    return dict(sel=sel, thr=thr, cm=cm, vsum=vsum, lens=lens)
+
+
+def topk_route(q, k, v, g: int, scale: float, density: float, block: int = 128):
+    S, H, hd = q.shape
+    nb = (S - g + block - 1) // block
+    sel = np.empty((H, nb, nb), dtype=np.uint8)
+    scores = np.empty((H, nb, nb), dtype=np.float32)
+    cm = np.empty((H, nb, nb), dtype=np.uint16)
+    vsum = np.empty((H, nb, hd), dtype=np.uint16)
+    lens = np.empty((nb,), dtype=np.float32)
+    _chk(lib().wxo_topk_route(_ptr(q), _ptr(k), _ptr(v), H * hd, S, H, hd, g, block, scale, density, _ptr(sel),
+                              _ptr(scores), _ptr(cm), _ptr(vsum), _ptr(lens)), "topk_route")
+    return dict(sel=sel, scores=scores, cm=cm, vsum=vsum, lens=lens)
+
+
+def sparse_attention(q, k, v, g: int, scale: float, block: int = 64, route=None, tail: bool = True):
+    """route None: dense attention for every row; else SOL semantics with route's tables."""
+    S, H, hd = q.shape
+    out = np.empty((S, H, hd), dtype=np.uint16)
+    if route is None:
+        _chk(lib().wxo_sparse_attention(_ptr(q), _ptr(k), _ptr(v), H * hd, S, H, hd, 0, block, scale, None, None,
+                                        None, None, 0, _ptr(out), H * hd), "attention")
+    else:
+        _chk(lib().wxo_sparse_attention(_ptr(q), _ptr(k), _ptr(v), H * hd, S, H, hd, g, block, scale,
+                                        _ptr(route["sel"]), _ptr(route["cm"]), _ptr(route["vsum"]),
+                                        _ptr(route["lens"]), int(tail), _ptr(out), H * hd), "attention")
+    return out
+
+
+def dense_f32(x, w, b=None):
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    m, k = x.shape
+    n = w.shape[1]
+    y = np.empty((m, n), dtype=np.float32)
+    _chk(lib().wxo_dense_f32(_ptr(x), m, k, _ptr(w), n, _ptr(b), _ptr(y)), "dense_f32")
+    return y
+
+
+def num_threads() -> int:
+    return lib().wxo_num_threads()
+
+
+# ---------------------------------------------------------------- block composition
+def block_forward(h, w, mods, rowmap, cos, sin, cfg, route_fn=None, at_cached=None, refresh=True):
+    """One H3 DiT block (H3Transformer.swift:1078-1159) composed from the oracle ops.
+
+    w: dict of quantized triples qkv/out/fc1/fc2 (wq, sc, bi, bias) and norms; mods: 6 tables;
+    route_fn(q, k, v) -> route dict or None for dense. Returns (h_new, at)."""
+    S, hidden = h.shape
+    H, hd = cfg["heads"], cfg["head_dim"]
+    inner = H * hd
+    eps = cfg["eps"]
+    if refresh or at_cached is None:
+        m1 = norm_modscale(h, w["norm1"], mods[0], mods[1], rowmap, eps)
+        qkv = qlinear(m1, *w["qkv"][:3], bias=w["qkv"][3])
+        q = qkv[:, :inner].reshape(S, H, hd)
+        k = qkv[:, inner:2 * inner].reshape(S, H, hd)
+        v = np.ascontiguousarray(qkv[:, 2 * inner:].reshape(S, H, hd))
+        q = qk_norm_rope(q, w["q_norm"], cos, sin, cfg["rot"], eps)
+        k = qk_norm_rope(k, w["k_norm"], cos, sin, cfg["rot"], eps)
+        scale = 1.0 / np.sqrt(np.float32(hd))
+        route = route_fn(q, k, v) if route_fn else None
+        if route is None:
+            att = sparse_attention(q, k, v, 0, float(scale))
+        else:
+            att = sparse_attention(q, k, v, route["g"], float(scale), block=route["block"], route=route,
+                                   tail=route["tail"])
+        ha, at = qlinear(att.reshape(S, inner), *w["out"][:3], bias=w["out"][3], epilogue=EPI_GATE_RESID,
+                         gate=mods[2], resid=h, rowmap=rowmap, want_raw=True)
+    else:
+        at = at_cached
+        ha = mod_gate(h, at, mods[2], rowmap)
+    m2 = norm_modscale(ha, w["norm2"], mods[3], mods[4], rowmap, eps)
+    act = EPI_SWIGLU if cfg.get("mlp_kind", 0) == 1 else EPI_GELU
+    f1 = qlinear(m2, *w["fc1"][:3], bias=w["fc1"][3], epilogue=act)
+    hn = qlinear(f1, *w["fc2"][:3], bias=w["fc2"][3], epilogue=EPI_GATE_RESID, gate=mods[5], resid=ha,
+                 rowmap=rowmap)
+    return hn, at

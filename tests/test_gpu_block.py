@@ -1,0 +1,126 @@
+"""GPU parity of one DiT block (H3Transformer.swift:1078-1159) through
+wx_dit_block_forward against the oracle composition, in dense, SOL and top-k
+attention modes, GELU and SwiGLU MLPs, and the PAB refresh/reuse paths."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from tests._util import assert_close, f32, to_np_bf16, to_torch_bf16
+
+pytestmark = pytest.mark.gpu
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def make_block(seed, hidden, heads, ffn, mlp_kind, S, rot=96):
+    hd = 128
+    inner = heads * hd
+    fc1_n = 2 * ffn if mlp_kind == 1 else ffn
+    w = {}
+    for i, (name, n, k) in enumerate([("qkv", 3 * inner, hidden), ("out", hidden, inner), ("fc1", fc1_n, hidden),
+                                      ("fc2", hidden, ffn)]):
+        wq, sc, bi = O.quantize(O.normal_f32((n, k), seed, 10 + i, std=0.02))
+        w[name] = (wq, sc, bi, O.normal_bf16((n,), seed, 20 + i, std=0.02))
+    w["q_norm"] = O.normal_bf16((hd,), seed, 30, mean=1.0, std=0.02)
+    w["k_norm"] = O.normal_bf16((hd,), seed, 31, mean=1.0, std=0.02)
+    w["norm1"] = O.normal_bf16((hidden,), seed, 32, mean=1.0, std=0.02)
+    w["norm2"] = O.normal_bf16((hidden,), seed, 33, mean=1.0, std=0.02)
+    mods = [O.normal_bf16((6, hidden), seed, 40 + j, std=0.1) for j in range(6)]
+    h = O.normal_bf16((S, hidden), seed, 50)
+    cos = O.normal_bf16((S, rot // 2), seed, 51)
+    sin = O.normal_bf16((S, rot // 2), seed, 52)
+    g = json.load(open(GOLD / "modrun.json"))
+    rowmap = np.array((g["map"] * (S // 16 + 1))[:S], dtype=np.uint32)
+    return w, mods, h, cos, sin, rowmap
+
+
+def gpu_block(w, hidden, heads, ffn, mlp_kind, rot, eps):
+    import torch
+    from wuxianhuabu_b200 import h3
+
+    def lin(t, k):
+        wq, sc, bi, b = t
+        return h3.MfLinear(torch.from_numpy(wq.view(np.int32)).cuda(), to_torch_bf16(sc), to_torch_bf16(bi), k,
+                           to_torch_bf16(b))
+    inner = heads * 128
+    bw = h3.H3BlockWeights(lin(w["qkv"], hidden), lin(w["out"], inner), lin(w["fc1"], hidden), lin(w["fc2"], ffn),
+                           to_torch_bf16(w["q_norm"]), to_torch_bf16(w["k_norm"]), to_torch_bf16(w["norm1"]),
+                           to_torch_bf16(w["norm2"]))
+    cfg = h3.H3DiTConfig(hidden=hidden, heads=heads, head_dim=128, ffn=ffn, mlp_kind=mlp_kind, rot=rot, eps=eps,
+                         layers=1)
+    return h3.H3DiTBlocks(cfg, [bw])
+
+
+CASES = [
+    ("dense", 0, None),
+    ("sol_all", 0, dict(tau=-100.0)),
+    ("sol", 0, dict(tau=0.4)),
+    ("topk", 0, dict(block=128, topk_ratio=0.25, tail=False)),
+    ("dense_swiglu", 1, None),
+]
+
+
+@pytest.mark.parametrize("name,mlp_kind,sparse", CASES)
+def test_block_vs_oracle(name, mlp_kind, sparse):
+    import torch
+    from wuxianhuabu_b200 import h3
+    hidden, heads, ffn, rot, eps = 256, 2, 512, 96, 1e-6
+    g, L = 44, 300
+    S = g + L
+    w, mods, h, cos, sin, rowmap = make_block(7, hidden, heads, ffn, mlp_kind, S, rot)
+    cfgd = dict(heads=heads, head_dim=128, eps=eps, rot=rot, mlp_kind=mlp_kind)
+    scale = float(1 / np.sqrt(np.float32(128)))
+
+    def route_fn(q, k, v):
+        if sparse is None:
+            return None
+        if sparse.get("topk_ratio"):
+            r = O.topk_route(q, k, v, g, scale, sparse["topk_ratio"])
+            r.update(g=g, block=128, tail=False)
+        else:
+            r = O.sol_route(q, k, v, g, scale, sparse["tau"])
+            r.update(g=g, block=64, tail=True)
+        return r
+
+    ref, ref_at = O.block_forward(h, w, mods, rowmap, cos, sin, cfgd, route_fn=route_fn)
+    blk = gpu_block(w, hidden, heads, ffn, mlp_kind, rot, eps)
+    ht = to_torch_bf16(h)
+    spec = None if sparse is None else h3.H3SolAttnConfig(**sparse).spec(g)
+    slot = torch.empty((S, hidden), dtype=torch.bfloat16, device="cuda")
+    blk.block_forward(0, ht, [to_torch_bf16(m) for m in mods], torch.from_numpy(rowmap.view(np.int32)).cuda(),
+                      to_torch_bf16(cos), to_torch_bf16(sin), spec, pab_slot=slot, refresh=True)
+    h3.context().check_device()
+    # routing decisions can flip at bf16 ties for tau=0.4: require the cosine bound there
+    rel = 2e-2 if name != "sol" else 5e-2
+    assert_close(f32(to_np_bf16(slot)), f32(ref_at), rel=rel, cos=0.999, what=f"{name} at")
+    assert_close(f32(to_np_bf16(ht)), f32(ref), rel=rel, cos=0.999, what=f"{name} h")
+
+
+def test_pab_reuse_equals_refresh_with_same_inputs():
+    """A reuse step with the slot written by a refresh step on the same h and mods
+    gives bit-identical output (PAB skips only the attention branch)."""
+    import torch
+    from wuxianhuabu_b200 import h3
+    hidden, heads, ffn, rot, eps = 256, 2, 512, 96, 1e-6
+    S = 300
+    w, mods, h, cos, sin, rowmap = make_block(8, hidden, heads, ffn, 0, S, rot)
+    blk = gpu_block(w, hidden, heads, ffn, 0, rot, eps)
+    md = [to_torch_bf16(m) for m in mods]
+    rm = torch.from_numpy(rowmap.view(np.int32)).cuda()
+    c, s = to_torch_bf16(cos), to_torch_bf16(sin)
+    slot = torch.empty((S, hidden), dtype=torch.bfloat16, device="cuda")
+    h1 = to_torch_bf16(h)
+    blk.block_forward(0, h1, md, rm, c, s, None, pab_slot=slot, refresh=True)
+    h2 = to_torch_bf16(h)
+    blk.block_forward(0, h2, md, rm, c, s, None, pab_slot=slot, refresh=False)
+    torch.cuda.synchronize()
+    assert torch.equal(h1, h2)
+    # reuse with a different gate uses the current step's gate (PAB:19-21)
+    md2 = list(md)
+    md2[2] = md[2] * 2
+    h3_ = to_torch_bf16(h)
+    blk.block_forward(0, h3_, md2, rm, c, s, None, pab_slot=slot, refresh=False)
+    assert not torch.equal(h1, h3_)
+    h3.context().check_device()

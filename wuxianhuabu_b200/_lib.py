@@ -1,0 +1,134 @@
+"""ctypes binding of libwx.so (the C ABI declared in include/wx_api.h).
+
+The shared library is loaded from the package directory only; there is no
+fallback implementation. Every call is checked: a non-zero wx_status raises
+``WxError`` carrying ``wx_last_error``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = _PKG / "libwx.so"
+
+WX_OK = 0
+WX_ERR_INVALID = -1
+WX_ERR_CUDA = -2
+WX_ERR_NOMEM = -3
+WX_ERR_DEVICE = -4
+WX_ERR_UNSUPPORTED = -5
+
+EPI_NONE, EPI_GELU, EPI_GATE_RESID, EPI_SWIGLU = 0, 1, 2, 3
+SPARSE_DENSE, SPARSE_SOL, SPARSE_TOPK = 0, 1, 2
+MLP_GELU, MLP_SWIGLU = 0, 1
+
+
+class WxError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"wx status {status}: {msg}")
+        self.status = status
+
+
+class QWeight(C.Structure):
+    _fields_ = [("wq", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p), ("bias", C.c_void_p),
+                ("n", C.c_int64), ("k", C.c_int64), ("group", C.c_int32), ("bits", C.c_int32)]
+
+
+class SparseSpec(C.Structure):
+    _fields_ = [("mode", C.c_int32), ("block", C.c_int32), ("g", C.c_int64), ("tau", C.c_float),
+                ("density", C.c_float), ("sink_start", C.c_int32), ("sink_end", C.c_int32),
+                ("tail", C.c_int32), ("reserved", C.c_int32)]
+
+
+class BlockWeights(C.Structure):
+    _fields_ = [("qkv", QWeight), ("out", QWeight), ("fc1", QWeight), ("fc2", QWeight),
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("norm1", C.c_void_p), ("norm2", C.c_void_p)]
+
+
+class DitConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int64), ("heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int64),
+                ("mlp_kind", C.c_int32), ("rot", C.c_int32), ("eps", C.c_float), ("reserved", C.c_int32)]
+
+
+class BlockMods(C.Structure):
+    _fields_ = [("shift_msa", C.c_void_p), ("scale_msa", C.c_void_p), ("gate_msa", C.c_void_p),
+                ("shift_mlp", C.c_void_p), ("scale_mlp", C.c_void_p), ("gate_mlp", C.c_void_p)]
+
+
+class ModRun(C.Structure):
+    _fields_ = [("start", C.c_uint32), ("end", C.c_uint32), ("mod_row", C.c_uint32)]
+
+
+_vp, _i64, _i32, _f32, _f64, _u32 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_double, C.c_uint32
+
+# name -> (restype, argtypes)
+_SIGS = {
+    "wx_version": (_i32, []),
+    "wx_ctx_create": (_i32, [_i32, C.POINTER(_vp)]),
+    "wx_ctx_destroy": (_i32, [_vp]),
+    "wx_ctx_set_stream": (_i32, [_vp, _vp]),
+    "wx_last_error": (C.c_char_p, [_vp]),
+    "wx_ctx_check_device": (_i32, [_vp]),
+    "wx_ctx_workspace_bytes": (C.c_size_t, [_vp]),
+    "wx_quantize_affine": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
+    "wx_dequantize_affine": (_i32, [_vp, C.POINTER(QWeight), _vp]),
+    "wx_qlinear": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "wx_qk_norm_rope": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _i32, _f32, _vp, _i64]),
+    "wx_qk_norm_rope_qkv": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _f32]),
+    "wx_norm_modscale": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _f32, _vp]),
+    "wx_mod_gate": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "wx_build_row_mod_map": (_i32, [C.POINTER(ModRun), _i32, _i64, _vp]),
+    "wx_sol_route": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, C.POINTER(SparseSpec), _f32,
+                            _vp, _vp, _vp, _vp, _vp]),
+    "wx_topk_route": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, C.POINTER(SparseSpec), _f32,
+                             _vp, _vp, _vp, _vp, _vp]),
+    "wx_sparse_attention": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, C.POINTER(SparseSpec), _f32,
+                                   _vp, _i64]),
+    "wx_attention_from_sel": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, C.POINTER(SparseSpec), _f32,
+                                     _vp, _vp, _vp, _vp, _vp, _i64]),
+    "wx_pab_refresh": (_i32, [_i32, _u32, _u32]),
+    "wx_pab_must_refresh": (_i32, [_f64, _f64, _f64]),
+    "wx_pab_plan": (_i32, [_vp, _i32, _u32, _f64, _vp]),
+    "wx_sigma_schedule": (_i32, [_u32, _f64, _vp]),
+    "wx_sparse_mode_for_layer": (_i32, [_i32, _i32, _i32]),
+    "wx_dit_block_scratch_bytes": (_i64, [C.POINTER(DitConfig), _i64]),
+    "wx_dit_block_forward": (_i32, [_vp, C.POINTER(DitConfig), C.POINTER(BlockWeights), C.POINTER(BlockMods), _vp,
+                                    _vp, _i64, _vp, _vp, C.POINTER(SparseSpec), _vp, _i32, _vp]),
+    "wx_dense_f32": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
+    "wx_bf16_to_f32": (_i32, [_vp, _vp, _i64, _vp]),
+    "wx_f32_to_bf16": (_i32, [_vp, _vp, _i64, _vp]),
+    "wx_euler_update": (_i32, [_vp, _vp, _vp, _i64, _f32]),
+}
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Load libwx.so (raises if it has not been built: there is no fallback)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: run __graft_entry__.build() (no CPU fallback exists)")
+    lib = C.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def check(status: int, ctx=None) -> None:
+    if status != WX_OK:
+        msg = ""
+        if ctx is not None:
+            raw = load().wx_last_error(ctx)
+            msg = raw.decode() if raw else ""
+        raise WxError(status, msg)

@@ -1,0 +1,921 @@
+// wx_attn.cu — SOL block-sparse self-attention (H3SolAttn.forward,
+// 网络算子-稀疏注意力-SOL通用.swift:388-532) and dense SDPA on sm_100a.
+//
+// Pipeline per layer:
+//   1. block statistics of the video segment (q/k centroids, v sums, lengths)
+//   2. router: SOL tau (centred centroid scores vs a per-(head, q-block)
+//      threshold, diagonal +-1 and sink forced) or top-k (diagonal + the
+//      ceil(density*nb) best other blocks)
+//   3. tail pooling: the unselected blocks of each (head, q-block) folded into
+//      one (max score C, weight sum L, value vector T) triple
+//   4. kept-list builder: per (head, 128-row q tile) a list of 128-key tiles,
+//      each made of two 64-key halves with per-(q-half, key-half) masks
+//   5. flash kernel (tcgen05): one CTA per (head, q tile); S = Q K^T and
+//      O += P V on the tensor cores with S double-buffered and O resident in
+//      TMEM; online softmax in registers with lazy rescaling; tail term and
+//      normalisation in the epilogue.
+// The routing arithmetic uses a fixed fp32 operation order (explicit _rn
+// intrinsics) so that its decisions are bit-identical to the CPU oracle.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <algorithm>
+
+#include "wx_internal.h"
+#include "wx_ptx.cuh"
+
+namespace wx {
+
+struct WorkItem {
+  int q_start, q_rows, tail0, tail1;
+  int list_begin, list_len, n_implicit, implicit_end;
+  int head, pad0, pad1, pad2;
+};
+
+// ------------------------------------------------------------ 1. statistics
+// grid (nb, H), block hd: sequential sums over the block's real rows.
+__global__ void block_stats_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                                   const __nv_bfloat16* __restrict__ v, int64_t row_stride, int64_t S, int hd,
+                                   int64_t g, int block, int nb, float* __restrict__ qc, float* __restrict__ kc,
+                                   __nv_bfloat16* __restrict__ vsum, float* __restrict__ lens) {
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int64_t r0 = g + (int64_t)b * block;
+  const int64_t r1 = min(r0 + block, S);
+  const float len = (float)(r1 - r0);
+  float aq = 0.f, ak = 0.f, av = 0.f;
+  for (int64_t s = r0; s < r1; ++s) {
+    const int64_t o = s * row_stride + (int64_t)h * hd + d;
+    aq = __fadd_rn(aq, __bfloat162float(q[o]));
+    ak = __fadd_rn(ak, __bfloat162float(k[o]));
+    av = __fadd_rn(av, __bfloat162float(v[o]));
+  }
+  const int64_t idx = ((int64_t)h * nb + b) * hd + d;
+  if (qc) qc[idx] = __fdiv_rn(aq, len);
+  kc[idx] = __fdiv_rn(ak, len);
+  vsum[idx] = __float2bfloat16_rn(av);
+  if (h == 0 && d == 0) lens[b] = len;
+}
+
+// grid H, block hd: kMean over blocks, centre in place, kcVar = mean(kcc^2)
+__global__ void kcenter_kernel(float* __restrict__ kc, int nb, int hd, float* __restrict__ kvar) {
+  const int h = blockIdx.x, d = threadIdx.x;
+  float* base = kc + (int64_t)h * nb * hd + d;
+  float acc = 0.f;
+  for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, base[(int64_t)b * hd]);
+  const float mean = __fdiv_rn(acc, (float)nb);
+  float vacc = 0.f;
+  for (int b = 0; b < nb; ++b) {
+    const float c = __fsub_rn(base[(int64_t)b * hd], mean);
+    base[(int64_t)b * hd] = c;
+    vacc = __fadd_rn(vacc, __fmul_rn(c, c));
+  }
+  kvar[(int64_t)h * hd + d] = __fdiv_rn(vacc, (float)nb);
+}
+
+// thread per (h, qb): thr = tau * sqrt(sum_d((qc*qc)*kvar) * scale^2 + 1e-6)
+__global__ void thr_kernel(const float* __restrict__ qc, const float* __restrict__ kvar, int H, int nb, int hd,
+                           float scale, float tau, float* __restrict__ thr) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (i >= (int64_t)H * nb) return;
+  const int h = (int)(i / nb);
+  const float* qr = qc + i * hd;
+  const float* kv = kvar + (int64_t)h * hd;
+  float var = 0.f;
+  for (int d = 0; d < hd; ++d) var = __fadd_rn(var, __fmul_rn(__fmul_rn(qr[d], qr[d]), kv[d]));
+  thr[i] = __fmul_rn(tau, __fsqrt_rn(__fadd_rn(__fmul_rn(var, __fmul_rn(scale, scale)), 1e-6f)));
+}
+
+// grid (ceil(nb/32), ceil(nb/8), H), block 256 = 32 key blocks x 8 query blocks.
+// cm = bf16(fma-chain(qc, kc) * scale); mode 1: SOL selection, mode 2: f32 scores.
+__global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc, const float* __restrict__ kc,
+                                                    int nb, int hd, float scale, int mode,
+                                                    const float* __restrict__ thr, int sink_start, int sink_end,
+                                                    __nv_bfloat16* __restrict__ cm, uint8_t* __restrict__ sel,
+                                                    float* __restrict__ scores) {
+  __shared__ float ks[32][129];
+  __shared__ float qs[8][128];
+  const int h = blockIdx.z;
+  const int kb0 = blockIdx.x * 32, qb0 = blockIdx.y * 8;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 32 * hd; i += 256) {
+    const int r = i / hd, d = i % hd;
+    ks[r][d] = (kb0 + r < nb) ? kc[((int64_t)h * nb + kb0 + r) * hd + d] : 0.f;
+  }
+  for (int i = threadIdx.x; i < 8 * hd; i += 256) {
+    const int r = i / hd, d = i % hd;
+    qs[r][d] = (qb0 + r < nb) ? qc[((int64_t)h * nb + qb0 + r) * hd + d] : 0.f;
+  }
+  __syncthreads();
+  const int qb = qb0 + ty, kb = kb0 + tx;
+  if (qb >= nb || kb >= nb) return;
+  float acc = 0.f;
+  for (int d = 0; d < hd; ++d) acc = __fmaf_rn(qs[ty][d], ks[tx][d], acc);
+  const float sc = __fmul_rn(acc, scale);
+  const __nv_bfloat16 c = __float2bfloat16_rn(sc);
+  const int64_t idx = ((int64_t)h * nb + qb) * nb + kb;
+  cm[idx] = c;
+  if (mode == WX_SPARSE_SOL) {
+    bool s = __bfloat162float(c) > thr[(int64_t)h * nb + qb];
+    if (abs(qb - kb) <= 1) s = true;
+    if (kb >= sink_start && kb < sink_end) s = true;
+    sel[idx] = (uint8_t)s;
+  } else {
+    scores[idx] = sc;
+  }
+}
+
+// grid (nb, H), block 512: bitonic sort of (valid desc, score desc, index asc)
+__global__ void __launch_bounds__(512) topk_select_kernel(const float* __restrict__ scores, int nb, int P, int keep,
+                                                          uint8_t* __restrict__ sel) {
+  extern __shared__ uint8_t tsm[];
+  float* key = reinterpret_cast<float*>(tsm);
+  int* idx = reinterpret_cast<int*>(tsm + (size_t)P * 4);
+  const int qb = blockIdx.x, h = blockIdx.y;
+  const float* row = scores + ((int64_t)h * nb + qb) * nb;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    const bool valid = i < nb && i != qb;
+    key[i] = valid ? row[i] : 0.f;
+    idx[i] = valid ? i : (0x40000000 | i);  // invalid entries sort last
+  }
+  __syncthreads();
+  // "a before b" ordering
+  auto before = [](float ka, int ia, float kb_, int ib) {
+    const bool va = ia < 0x40000000, vb = ib < 0x40000000;
+    if (va != vb) return va;
+    if (ka != kb_) return ka > kb_;
+    return ia < ib;
+  };
+  for (int size = 2; size <= P; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < P; i += blockDim.x) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const bool up = (i & size) == 0;
+          const bool ij = before(key[i], idx[i], key[j], idx[j]);
+          if (up ? !ij : ij) {
+            float tk = key[i]; key[i] = key[j]; key[j] = tk;
+            int ti = idx[i]; idx[i] = idx[j]; idx[j] = ti;
+          }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  uint8_t* srow = sel + ((int64_t)h * nb + qb) * nb;
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) srow[i] = (i == qb) ? 1 : 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < keep; i += blockDim.x) {
+    const int id = idx[i];
+    if (id < 0x40000000) srow[id] = 1;
+  }
+}
+
+// ------------------------------------------------------------- 3. tail pool
+// grid (nb, H), block hd: C = max over unselected bf16(cm); T = sum p*vsum; L = sum p*len
+__global__ void tail_kernel(const uint8_t* __restrict__ sel, const __nv_bfloat16* __restrict__ cm,
+                            const __nv_bfloat16* __restrict__ vsum, const float* __restrict__ lens, int nb, int hd,
+                            float* __restrict__ tT, float* __restrict__ tL, float* __restrict__ tC) {
+  const int qb = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int64_t rb = ((int64_t)h * nb + qb) * nb;
+  float cmax = -INFINITY;
+  for (int j = 0; j < nb; ++j)
+    if (!sel[rb + j]) cmax = fmaxf(cmax, __bfloat162float(cm[rb + j]));
+  float t = 0.f, l = 0.f;
+  if (cmax > -INFINITY) {
+    for (int j = 0; j < nb; ++j) {
+      if (sel[rb + j]) continue;
+      const float p = expf(__bfloat162float(cm[rb + j]) - cmax);
+      t += p * __bfloat162float(vsum[((int64_t)h * nb + j) * hd + d]);
+      l += p * lens[j];
+    }
+  }
+  const int64_t o = (int64_t)h * nb + qb;
+  tT[o * hd + d] = t;
+  if (d == 0) {
+    tL[o] = l;
+    tC[o] = cmax;
+  }
+}
+
+// ------------------------------------------------------------ 4. kept lists
+// warp per (h, t): number of list entries of video q tile t
+__global__ void list_count_kernel(const uint8_t* __restrict__ sel, int H, int nb, int nvt, int qpb,
+                                  int* __restrict__ counts) {
+  const int64_t wid = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (int64_t)H * nvt) return;
+  const int h = (int)(wid / nvt), t = (int)(wid % nvt);
+  int cnt = 0;
+  for (int kb0 = 0; kb0 < nb; kb0 += 32) {
+    const int kb = kb0 + lane;
+    bool u = false;
+    if (kb < nb)
+      for (int e = 0; e < qpb; ++e) {
+        const int qb = t * qpb + e;
+        if (qb < nb && sel[((int64_t)h * nb + qb) * nb + kb]) u = true;
+      }
+    cnt += __popc(__ballot_sync(0xffffffffu, u));
+  }
+  if (lane == 0) counts[wid] = (cnt + (qpb - 1)) / qpb;  // qpb == kpt: 2 halves per entry for 64-blocks
+}
+
+// single block: exclusive scan of counts[n] into offsets[n+1]
+__global__ void scan_kernel(const int* __restrict__ counts, int n, int* __restrict__ offsets) {
+  __shared__ int part[1024];
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int chunk = (n + nt - 1) / nt;
+  const int b = tid * chunk, e = min(n, b + chunk);
+  int s = 0;
+  for (int i = b; i < e; ++i) s += counts[i];
+  part[tid] = s;
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int i = 0; i < nt; ++i) {
+      int v = part[i];
+      part[i] = run;
+      run += v;
+    }
+    offsets[n] = run;
+  }
+  __syncthreads();
+  int run = part[tid];
+  for (int i = b; i < e; ++i) {
+    offsets[i] = run;
+    run += counts[i];
+  }
+}
+
+// warp per (h, t): write the entries {start0, start1, len0|qmask0<<8, len1|qmask1<<8}
+__global__ void list_fill_kernel(const uint8_t* __restrict__ sel, int H, int nb, int nvt, int qpb, int block,
+                                 int64_t g, int64_t S, const int* __restrict__ offsets, int4* __restrict__ entries) {
+  const int64_t wid = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (int64_t)H * nvt) return;
+  const int h = (int)(wid / nvt), t = (int)(wid % nvt);
+  int* base = reinterpret_cast<int*>(entries + offsets[wid]);
+  int pos0 = 0;
+  int total = 0;
+  // total union count (for the odd-tail padding)
+  for (int kb0 = 0; kb0 < nb; kb0 += 32) {
+    const int kb = kb0 + lane;
+    bool u = false;
+    if (kb < nb)
+      for (int e = 0; e < qpb; ++e) {
+        const int qb = t * qpb + e;
+        if (qb < nb && sel[((int64_t)h * nb + qb) * nb + kb]) u = true;
+      }
+    total += __popc(__ballot_sync(0xffffffffu, u));
+  }
+  for (int kb0 = 0; kb0 < nb; kb0 += 32) {
+    const int kb = kb0 + lane;
+    uint32_t qm = 0;
+    if (kb < nb)
+      for (int e = 0; e < qpb; ++e) {
+        const int qb = t * qpb + e;
+        if (qb < nb && sel[((int64_t)h * nb + qb) * nb + kb]) qm |= 1u << e;
+      }
+    const uint32_t bal = __ballot_sync(0xffffffffu, qm != 0);
+    if (qm) {
+      const int pos = pos0 + __popc(bal & ((1u << lane) - 1u));
+      const int64_t start = g + (int64_t)kb * block;
+      if (block == 64) {
+        const int len = (int)min64(64, S - start);
+        const int slot = pos & 1;
+        int* ent = base + (pos >> 1) * 4;
+        ent[slot] = (int)start;
+        ent[2 + slot] = len | (int)(qm << 8);
+        if (slot == 0 && pos == total - 1) {  // odd count: empty second half
+          ent[1] = (int)start;
+          ent[3] = 0;
+        }
+      } else {  // 128-row blocks: both q halves share the decision
+        const int len0 = (int)max64(0, min64(64, S - start));
+        const int len1 = (int)max64(0, min64(64, S - start - 64));
+        int* ent = base + pos * 4;
+        ent[0] = (int)start;
+        ent[1] = (int)(start + 64);
+        ent[2] = len0 | (3 << 8);
+        ent[3] = len1 | (3 << 8);
+      }
+    }
+    pos0 += __popc(bal);
+  }
+}
+
+// thread per item: strip/dense items first (all heads), then video tiles
+__global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int dense_all, int qpb, int nb,
+                             const int* __restrict__ offsets, WorkItem* __restrict__ items) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t n_strip = (int64_t)H * nst;
+  const int64_t n_items = n_strip + (int64_t)H * nvt;
+  if (i >= n_items) return;
+  WorkItem it;
+  it.pad0 = it.pad1 = it.pad2 = 0;
+  const int kt_all = (int)((S + 127) / 128);
+  if (i < n_strip) {
+    const int t = (int)(i / H);
+    it.head = (int)(i % H);
+    it.q_start = t * 128;
+    const int64_t lim = dense_all ? S : g;
+    it.q_rows = (int)min64(128, lim - (int64_t)t * 128);
+    it.tail0 = it.tail1 = -1;
+    it.list_begin = 0;
+    it.list_len = 0;
+    it.n_implicit = kt_all;
+    it.implicit_end = (int)S;
+  } else {
+    const int64_t j = i - n_strip;
+    const int t = (int)(j / H);
+    const int h = (int)(j % H);
+    it.head = h;
+    it.q_start = (int)(g + (int64_t)t * 128);
+    it.q_rows = (int)min64(128, S - it.q_start);
+    it.tail0 = t * qpb;
+    it.tail1 = (t * qpb + qpb - 1 < nb) ? t * qpb + qpb - 1 : -1;
+    const int64_t w = (int64_t)h * nvt + t;
+    it.list_begin = offsets[w];
+    it.list_len = offsets[w + 1] - offsets[w];
+    it.n_implicit = (int)((g + 127) / 128);
+    it.implicit_end = (int)g;
+  }
+  items[i] = it;
+}
+
+// ------------------------------------------------------------ 5. flash kernel
+constexpr int kAttnThreads = 192;
+constexpr int kTileBytes = 128 * 128 * 2;  // one 128x128 bf16 operand tile
+constexpr int kAttnSmem = 6 * kTileBytes + 256 + 1024;
+
+struct AttnParams {
+  const WorkItem* items;
+  const int4* entries;
+  const float* tailT;
+  const float* tailL;
+  const float* tailC;
+  int nqb;
+  int H;
+  float sl2;  // softmax scale * log2(e)
+  __nv_bfloat16* out;
+  int64_t out_stride;
+  int* err;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void kv_entry(const WorkItem& it, const int4* entries, int j, int& s0, int& s1,
+                                         int& w0, int& w1) {
+  if (j < it.n_implicit) {
+    s0 = j * 128;
+    s1 = s0 + 64;
+    w0 = max(0, min(64, it.implicit_end - s0)) | (3 << 8);
+    w1 = max(0, min(64, it.implicit_end - s1)) | (3 << 8);
+  } else {
+    const int4 e = entries[it.list_begin + (j - it.n_implicit)];
+    s0 = e.x;
+    s1 = e.y;
+    w0 = e.z;
+    w1 = e.w;
+  }
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK[2] = {smem + kTileBytes, smem + 3 * kTileBytes};
+  uint8_t* sV[2] = {smem + 2 * kTileBytes, smem + 4 * kTileBytes};
+  uint8_t* sP = smem + 5 * kTileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
+  // q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_done
+  const uint32_t q_full = smem_u32(bars + 0);
+  const uint32_t kv_full[2] = {smem_u32(bars + 1), smem_u32(bars + 2)};
+  const uint32_t kv_empty[2] = {smem_u32(bars + 3), smem_u32(bars + 4)};
+  const uint32_t s_full[2] = {smem_u32(bars + 5), smem_u32(bars + 6)};
+  const uint32_t p_full = smem_u32(bars + 7);
+  const uint32_t o_done = smem_u32(bars + 8);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const WorkItem it = p.items[blockIdx.x];
+  const int n_kv = it.n_implicit + it.list_len;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(kv_full[i], 1);
+      mbar_init(kv_empty[i], 1);
+      mbar_init(s_full[i], 1);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // S0: cols [0,128), S1: [128,256), O: [256,384)
+  const int hcol = it.head * 128;
+
+  if (warp == 0) {
+    if (lane == 0 && n_kv > 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, kTileBytes);
+      for (int ch = 0; ch < 2; ++ch)
+        for (int rh = 0; rh < 2; ++rh)
+          tma_load_2d(smem_u32(sQ + ch * 16384 + rh * 8192), &tmQ, q_full, hcol + ch * 64, it.q_start + rh * 64);
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
+        int s0, s1, w0, w1;
+        kv_entry(it, p.entries, j, s0, s1, w0, w1);
+        mbar_arrive_expect_tx(kv_full[st], 2 * kTileBytes);
+        for (int ch = 0; ch < 2; ++ch) {
+          const uint32_t ko = smem_u32(sK[st] + ch * 16384), vo = smem_u32(sV[st] + ch * 16384);
+          tma_load_2d(ko, &tmK, kv_full[st], hcol + ch * 64, s0);
+          tma_load_2d(ko + 8192, &tmK, kv_full[st], hcol + ch * 64, s1);
+          tma_load_2d(vo, &tmV, kv_full[st], hcol + ch * 64, s0);
+          tma_load_2d(vo + 8192, &tmV, kv_full[st], hcol + ch * 64, s1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && n_kv > 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);  // B = V, MN-major
+      const uint32_t qa = smem_u32(sQ), pa = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutFull, abort_flag);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(kv_full[st], (j >> 1) & 1, p.err, kDevTimeoutFull, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sK[st]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+          umma_bf16(tmem + st * 128, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + off, 16, 1024),
+                    idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        if (!mbar_wait(p_full, j & 1, p.err, kDevTimeoutSoftmax, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t va = smem_u32(sV[j & 1]);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = smem_desc_sw128(pa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(va + kk * 2048, 16384, 1024);
+          umma_bf16(tmem + 256, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(o_done);
+        umma_commit(kv_empty[j & 1]);
+      }
+    }
+  } else {
+    // softmax / correction / epilogue warps: thread owns TMEM lane (= q row) r
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qh = r >> 6;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv && ok; ++j) {
+      int s0, s1, w0, w1;
+      kv_entry(it, p.entries, j, s0, s1, w0, w1);
+      const int b = j & 1;
+      if (!mbar_wait(s_full[b], (j >> 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float sv[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float t[32];
+        tmem_ld32(tmem + lane_addr + b * 128 + c * 32, t);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = t[i];
+      }
+      tmem_wait_ld();
+      const int len0 = w0 & 0xFF, len1 = w1 & 0xFF;
+      const bool on0 = (w0 >> (8 + qh)) & 1, on1 = (w1 >> (8 + qh)) & 1;
+      const int lim0 = on0 ? len0 : 0, lim1 = on1 ? len1 : 0;
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const bool valid = (c < 64) ? (c < lim0) : ((c - 64) < lim1);
+        sv[c] = valid ? sv[c] * p.sl2 : -INFINITY;
+        rmax = fmaxf(rmax, sv[c]);
+      }
+      const float m_new = fmaxf(m, rmax);
+      if (j > 0) {
+        if (!mbar_wait(o_done, (j - 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      bool need = false;
+      if (j == 0) {
+        m = m_new;
+      } else {
+        need = m_new > m + 8.0f;
+      }
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = need ? ex2(m - m_new) : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float t[32];
+          tmem_ld32(tmem + lane_addr + 256 + c * 32, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) t[i] *= alpha;
+          tmem_st32(tmem + lane_addr + 256 + c * 32, t);
+        }
+        tmem_wait_st();
+        l *= alpha;
+        if (need) m = m_new;
+      }
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      float rs = 0.f;
+      uint8_t* prow = sP + r * 128;
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = ex2(sv[cc * 8 + e] - mu);
+          rs += pv[e];
+        }
+        const uint4 pk = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]),
+                                    pack_bf16x2(pv[4], pv[5]), pack_bf16x2(pv[6], pv[7]));
+        const int atom = cc >> 3, c8 = cc & 7;
+        *reinterpret_cast<uint4*>(prow + atom * 16384 + ((c8 ^ (r & 7)) << 4)) = pk;
+      }
+      l += rs;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_kv > 0) ok = mbar_wait(o_done, (n_kv - 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag);
+    tc_fence_after();
+    // epilogue: tail term, normalisation, bf16 store
+    const int ti = qh == 0 ? it.tail0 : it.tail1;
+    float a1 = 1.f, a2 = 0.f, lt = l;
+    const float* T = nullptr;
+    if (p.tailT && ti >= 0) {
+      const int64_t o = (int64_t)it.head * p.nqb + ti;
+      const float C2 = p.tailC[o] * 1.4426950408889634f;
+      if (C2 > -INFINITY) {
+        const float M2 = fmaxf(m, C2);
+        a1 = (m == -INFINITY) ? 0.f : ex2(m - M2);
+        a2 = ex2(C2 - M2);
+        lt = l * a1 + p.tailL[o] * a2;
+        T = p.tailT + o * 128;
+      }
+    }
+    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+    const bool row_ok = ok && r < it.q_rows;
+    __nv_bfloat16* orow = p.out + (int64_t)(it.q_start + r) * p.out_stride + hcol;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float t[32];
+      tmem_ld32(tmem + lane_addr + 256 + c * 32, t);
+      tmem_wait_ld();
+      if (n_kv == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = 0.f;
+      }
+      if (T) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) t[i] = t[i] * a1 + T[c * 32 + i] * a2;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8)
+          *reinterpret_cast<uint4*>(orow + c * 32 + i) =
+              make_uint4(pack_bf16x2(t[i] * inv, t[i + 1] * inv), pack_bf16x2(t[i + 2] * inv, t[i + 3] * inv),
+                         pack_bf16x2(t[i + 4] * inv, t[i + 5] * inv), pack_bf16x2(t[i + 6] * inv, t[i + 7] * inv));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------- host driver
+struct AttnGeom {
+  int64_t S, g;
+  int H, hd, block, nb, nvt, nst, qpb;
+  bool dense;
+};
+
+static size_t route_bytes(const AttnGeom& a, int mode) {
+  Carve c;
+  const size_t hnb = (size_t)a.H * a.nb;
+  c.take(hnb * a.hd * 4);           // qc
+  c.take(hnb * a.hd * 4);           // kc
+  c.take((size_t)a.H * a.hd * 4);   // kvar
+  c.take(hnb * 4);                  // thr
+  c.take(hnb * a.nb * 2);           // cm
+  c.take(hnb * a.nb);               // sel
+  if (mode == WX_SPARSE_TOPK) c.take(hnb * a.nb * 4);  // scores
+  c.take(hnb * a.hd * 2);           // vsum
+  c.take((size_t)a.nb * 4);         // lens
+  return c.off;
+}
+
+static size_t list_bytes(const AttnGeom& a) {
+  Carve c;
+  const size_t hnb = (size_t)a.H * a.nb;
+  c.take(hnb * a.hd * 4);  // tailT
+  c.take(hnb * 4);         // tailL
+  c.take(hnb * 4);         // tailC
+  c.take((size_t)a.H * a.nvt * 4);            // counts
+  c.take(((size_t)a.H * a.nvt + 1) * 4);      // offsets
+  c.take((size_t)a.H * a.nvt * (size_t)((a.nb + a.qpb - 1) / a.qpb + 1) * 16);  // entries (worst case)
+  c.take((size_t)a.H * (a.nst + a.nvt) * sizeof(WorkItem));
+  return c.off;
+}
+
+static int geom_from(wx_ctx* ctx, int64_t S, int H, int hd, const wx_sparse_spec* spec, AttnGeom& a) {
+  a.S = S;
+  a.H = H;
+  a.hd = hd;
+  a.dense = !spec || spec->mode == WX_SPARSE_DENSE;
+  if (a.dense) {
+    a.g = 0;
+    a.block = 128;
+    a.nb = 0;
+    a.nvt = 0;
+    a.qpb = 1;
+    a.nst = (int)((S + 127) / 128);
+    return WX_OK;
+  }
+  a.g = spec->g;
+  a.block = spec->block;
+  if (a.block != 64 && a.block != 128)
+    return set_error(ctx, WX_ERR_UNSUPPORTED, "sparse block must be 64 or 128 (got %d)", a.block);
+  if (a.g < 0 || a.g >= S) return set_error(ctx, WX_ERR_INVALID, "strip rows g=%lld must be in [0, S)", (long long)a.g);
+  a.nb = (int)((S - a.g + a.block - 1) / a.block);
+  a.qpb = 128 / a.block;
+  a.nvt = (a.nb + a.qpb - 1) / a.qpb;
+  a.nst = (int)((a.g + 127) / 128);
+  return WX_OK;
+}
+
+static int run_routing(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, const AttnGeom& a,
+                       const wx_sparse_spec* spec, float scale, uint8_t* base, uint8_t** sel_out,
+                       __nv_bfloat16** cm_out, __nv_bfloat16** vsum_out, float** lens_out, float** thr_out,
+                       float** scores_out) {
+  Carve c;
+  const size_t hnb = (size_t)a.H * a.nb;
+  float* qc = reinterpret_cast<float*>(base + c.take(hnb * a.hd * 4));
+  float* kc = reinterpret_cast<float*>(base + c.take(hnb * a.hd * 4));
+  float* kvar = reinterpret_cast<float*>(base + c.take((size_t)a.H * a.hd * 4));
+  float* thr = reinterpret_cast<float*>(base + c.take(hnb * 4));
+  __nv_bfloat16* cm = reinterpret_cast<__nv_bfloat16*>(base + c.take(hnb * a.nb * 2));
+  uint8_t* sel = base + c.take(hnb * a.nb);
+  float* scores = nullptr;
+  if (spec->mode == WX_SPARSE_TOPK) scores = reinterpret_cast<float*>(base + c.take(hnb * a.nb * 4));
+  __nv_bfloat16* vsum = reinterpret_cast<__nv_bfloat16*>(base + c.take(hnb * a.hd * 2));
+  float* lens = reinterpret_cast<float*>(base + c.take((size_t)a.nb * 4));
+  auto Q = static_cast<const __nv_bfloat16*>(q);
+  auto K = static_cast<const __nv_bfloat16*>(k);
+  auto V = static_cast<const __nv_bfloat16*>(v);
+  block_stats_kernel<<<dim3(a.nb, a.H), a.hd, 0, ctx->stream>>>(Q, K, V, rs, a.S, a.hd, a.g, a.block, a.nb, qc, kc,
+                                                                  vsum, lens);
+  int st = launch_status(ctx, "block_stats");
+  if (st) return st;
+  if (spec->mode == WX_SPARSE_SOL) {
+    kcenter_kernel<<<a.H, a.hd, 0, ctx->stream>>>(kc, a.nb, a.hd, kvar);
+    thr_kernel<<<(unsigned)((hnb + 127) / 128), 128, 0, ctx->stream>>>(qc, kvar, a.H, a.nb, a.hd, scale,
+                                                                        spec->tau, thr);
+  }
+  dim3 sg((a.nb + 31) / 32, (a.nb + 7) / 8, a.H);
+  score_kernel<<<sg, 256, 0, ctx->stream>>>(qc, kc, a.nb, a.hd, scale, spec->mode, thr, spec->sink_start,
+                                           spec->sink_end, cm, sel, scores);
+  st = launch_status(ctx, "score");
+  if (st) return st;
+  if (spec->mode == WX_SPARSE_TOPK) {
+    int P = 1;
+    while (P < a.nb) P <<= 1;
+    if (P > 8192) return set_error(ctx, WX_ERR_UNSUPPORTED, "top-k router supports at most 8192 blocks");
+    double want = ceil((double)spec->density * (double)a.nb);
+    int keep = (int)std::min<double>(want, a.nb - 1);
+    if (keep < 0) keep = 0;
+    const size_t smem = (size_t)P * 8;
+    if (smem > 48 * 1024) {
+      cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
+    topk_select_kernel<<<dim3(a.nb, a.H), 512, smem, ctx->stream>>>(scores, a.nb, P, keep, sel);
+    st = launch_status(ctx, "topk_select");
+    if (st) return st;
+  }
+  *sel_out = sel;
+  *cm_out = cm;
+  *vsum_out = vsum;
+  *lens_out = lens;
+  if (thr_out) *thr_out = thr;
+  if (scores_out) *scores_out = scores;
+  return WX_OK;
+}
+
+static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, const AttnGeom& a,
+                     const wx_sparse_spec* spec, float scale, const uint8_t* sel, const __nv_bfloat16* cm,
+                     const __nv_bfloat16* vsum, const float* lens, uint8_t* base, void* out, int64_t os) {
+  Carve c;
+  const size_t hnb = (size_t)a.H * a.nb;
+  float* tT = reinterpret_cast<float*>(base + c.take(hnb * a.hd * 4));
+  float* tL = reinterpret_cast<float*>(base + c.take(hnb * 4));
+  float* tC = reinterpret_cast<float*>(base + c.take(hnb * 4));
+  int* counts = reinterpret_cast<int*>(base + c.take((size_t)a.H * a.nvt * 4));
+  int* offsets = reinterpret_cast<int*>(base + c.take(((size_t)a.H * a.nvt + 1) * 4));
+  int4* entries = reinterpret_cast<int4*>(
+      base + c.take((size_t)a.H * a.nvt * (size_t)((a.nb + a.qpb - 1) / a.qpb + 1) * 16));
+  WorkItem* items = reinterpret_cast<WorkItem*>(base + c.take((size_t)a.H * (a.nst + a.nvt) * sizeof(WorkItem)));
+  const bool tail = !a.dense && spec->tail && cm && vsum && lens;
+  int st;
+  if (!a.dense) {
+    if (tail) {
+      tail_kernel<<<dim3(a.nb, a.H), a.hd, 0, ctx->stream>>>(sel, cm, vsum, lens, a.nb, a.hd, tT, tL, tC);
+      if ((st = launch_status(ctx, "tail"))) return st;
+    }
+    const int64_t warps = (int64_t)a.H * a.nvt;
+    const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
+    list_count_kernel<<<blocks, 256, 0, ctx->stream>>>(sel, a.H, a.nb, a.nvt, a.qpb, counts);
+    scan_kernel<<<1, 1024, 0, ctx->stream>>>(counts, a.H * a.nvt, offsets);
+    list_fill_kernel<<<blocks, 256, 0, ctx->stream>>>(sel, a.H, a.nb, a.nvt, a.qpb, a.block, a.g, a.S, offsets,
+                                                      entries);
+    if ((st = launch_status(ctx, "list build"))) return st;
+  }
+  const int64_t n_items = (int64_t)a.H * (a.nst + a.nvt);
+  items_kernel<<<(unsigned)((n_items + 127) / 128), 128, 0, ctx->stream>>>(a.H, a.nst, a.nvt, a.S, a.g, a.dense,
+                                                                             a.qpb, a.nb, offsets, items);
+  if ((st = launch_status(ctx, "items"))) return st;
+
+  const int64_t cols = (int64_t)a.H * a.hd;
+  CUtensorMap tq, tk, tv;
+  if ((st = make_tmap_bf16_2d(ctx, &tq, q, (uint64_t)a.S, (uint64_t)cols, (uint64_t)rs, 64, 64))) return st;
+  if ((st = make_tmap_bf16_2d(ctx, &tk, k, (uint64_t)a.S, (uint64_t)cols, (uint64_t)rs, 64, 64))) return st;
+  if ((st = make_tmap_bf16_2d(ctx, &tv, v, (uint64_t)a.S, (uint64_t)cols, (uint64_t)rs, 64, 64))) return st;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(flash_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
+    attr = true;
+  }
+  AttnParams p;
+  p.items = items;
+  p.entries = entries;
+  p.tailT = tail ? tT : nullptr;
+  p.tailL = tL;
+  p.tailC = tC;
+  p.nqb = a.nb;
+  p.H = a.H;
+  p.sl2 = scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out_stride = os;
+  p.err = ctx->dev_err;
+  if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
+  flash_attn_kernel<<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
+  return launch_status(ctx, "flash_attn");
+}
+
+static int check_attn_args(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
+                           int hd, const void* out, int64_t os) {
+  WX_CHECK_ARG(ctx, ctx && q && k && v && out && S > 0 && H > 0);
+  if (hd != 128) return set_error(ctx, WX_ERR_UNSUPPORTED, "attention head_dim must be 128 (got %d)", hd);
+  WX_CHECK_ARG(ctx, rs >= (int64_t)H * hd && os >= (int64_t)H * hd && rs % 8 == 0 && os % 8 == 0);
+  WX_CHECK_ARG(ctx, aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out));
+  WX_CHECK_ARG(ctx, S < (int64_t)1 << 30);
+  return WX_OK;
+}
+
+size_t attention_scratch_bytes(int64_t S, int H, int hd, const wx_sparse_spec* spec) {
+  AttnGeom a;
+  if (geom_from(nullptr, S, H, hd, spec, a)) return 0;
+  return (a.dense ? 0 : route_bytes(a, spec->mode)) + list_bytes(a) + (size_t(64) << 10);
+}
+
+// routing + flash with caller scratch (used by the block forward)
+int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
+                           int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os, void* scratch) {
+  AttnGeom a;
+  int st = geom_from(ctx, S, H, hd, spec, a);
+  if (st) return st;
+  uint8_t* base = static_cast<uint8_t*>(scratch);
+  uint8_t* sel = nullptr;
+  __nv_bfloat16 *cm = nullptr, *vsum = nullptr;
+  float* lens = nullptr;
+  size_t off = 0;
+  if (!a.dense) {
+    st = run_routing(ctx, q, k, v, rs, a, spec, scale, base, &sel, &cm, &vsum, &lens, nullptr, nullptr);
+    if (st) return st;
+    off = (route_bytes(a, spec->mode) + 255) & ~size_t(255);
+  }
+  return run_flash(ctx, q, k, v, rs, a, spec, scale, sel, cm, vsum, lens, base + off, out, os);
+}
+
+}  // namespace wx
+
+using namespace wx;
+
+extern "C" {
+
+int wx_sparse_attention(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t row_stride, int64_t S,
+                        int H, int head_dim, const wx_sparse_spec* spec, float scale, void* out,
+                        int64_t out_stride) {
+  int st = check_attn_args(ctx, q, k, v, row_stride, S, H, head_dim, out, out_stride);
+  if (st) return st;
+  AttnGeom a;
+  if ((st = geom_from(ctx, S, H, head_dim, spec, a))) return st;
+  void* ws = workspace(ctx, attention_scratch_bytes(S, H, head_dim, spec), &st);
+  if (!ws) return st;
+  return attention_with_scratch(ctx, q, k, v, row_stride, S, H, head_dim, spec, scale, out, out_stride, ws);
+}
+
+static int route_api(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H, int hd,
+                     const wx_sparse_spec* spec, float scale, int want_mode, uint8_t* sel, float* thr_or_scores,
+                     void* cm, void* vsum, float* lens) {
+  WX_CHECK_ARG(ctx, ctx && q && k && v && spec && sel && cm && vsum && lens && S > 0 && H > 0);
+  WX_CHECK_ARG(ctx, spec->mode == want_mode);
+  if (hd != 128) return set_error(ctx, WX_ERR_UNSUPPORTED, "routing head_dim must be 128");
+  AttnGeom a;
+  int st = geom_from(ctx, S, H, hd, spec, a);
+  if (st) return st;
+  void* ws = workspace(ctx, route_bytes(a, spec->mode), &st);
+  if (!ws) return st;
+  uint8_t* dsel;
+  __nv_bfloat16 *dcm, *dvs;
+  float *dl, *dthr, *dsc;
+  st = run_routing(ctx, q, k, v, rs, a, spec, scale, static_cast<uint8_t*>(ws), &dsel, &dcm, &dvs, &dl, &dthr, &dsc);
+  if (st) return st;
+  const size_t hnb = (size_t)a.H * a.nb;
+  cudaStream_t s = ctx->stream;
+  WX_CUDA_TRY(ctx, cudaMemcpyAsync(sel, dsel, hnb * a.nb, cudaMemcpyDeviceToDevice, s));
+  WX_CUDA_TRY(ctx, cudaMemcpyAsync(cm, dcm, hnb * a.nb * 2, cudaMemcpyDeviceToDevice, s));
+  WX_CUDA_TRY(ctx, cudaMemcpyAsync(vsum, dvs, hnb * a.hd * 2, cudaMemcpyDeviceToDevice, s));
+  WX_CUDA_TRY(ctx, cudaMemcpyAsync(lens, dl, (size_t)a.nb * 4, cudaMemcpyDeviceToDevice, s));
+  if (thr_or_scores) {
+    const float* src = want_mode == WX_SPARSE_SOL ? dthr : dsc;
+    const size_t n = want_mode == WX_SPARSE_SOL ? hnb : hnb * a.nb;
+    WX_CUDA_TRY(ctx, cudaMemcpyAsync(thr_or_scores, src, n * 4, cudaMemcpyDeviceToDevice, s));
+  }
+  return WX_OK;
+}
+
+int wx_sol_route(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t row_stride, int64_t S, int H,
+                 int head_dim, const wx_sparse_spec* spec, float scale, uint8_t* sel, float* thr, void* cm,
+                 void* vsum, float* lens) {
+  return route_api(ctx, q, k, v, row_stride, S, H, head_dim, spec, scale, WX_SPARSE_SOL, sel, thr, cm, vsum, lens);
+}
+
+int wx_topk_route(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t row_stride, int64_t S, int H,
+                  int head_dim, const wx_sparse_spec* spec, float scale, uint8_t* sel, float* scores, void* cm,
+                  void* vsum, float* lens) {
+  return route_api(ctx, q, k, v, row_stride, S, H, head_dim, spec, scale, WX_SPARSE_TOPK, sel, scores, cm, vsum,
+                   lens);
+}
+
+int wx_attention_from_sel(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t row_stride, int64_t S,
+                          int H, int head_dim, const wx_sparse_spec* spec, float scale, const uint8_t* sel,
+                          const void* cm, const void* vsum, const float* lens, void* out, int64_t out_stride) {
+  int st = check_attn_args(ctx, q, k, v, row_stride, S, H, head_dim, out, out_stride);
+  if (st) return st;
+  WX_CHECK_ARG(ctx, spec && spec->mode != WX_SPARSE_DENSE && sel);
+  WX_CHECK_ARG(ctx, !spec->tail || (cm && vsum && lens));
+  AttnGeom a;
+  if ((st = geom_from(ctx, S, H, head_dim, spec, a))) return st;
+  void* ws = workspace(ctx, list_bytes(a) + 1024, &st);
+  if (!ws) return st;
+  return run_flash(ctx, q, k, v, row_stride, a, spec, scale, sel, static_cast<const __nv_bfloat16*>(cm),
+                   static_cast<const __nv_bfloat16*>(vsum), lens, static_cast<uint8_t*>(ws), out, out_stride);
+}
+
+}  // extern "C"

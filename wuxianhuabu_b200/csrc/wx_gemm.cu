@@ -1,0 +1,355 @@
+// wx_gemm.cu — the quantized linear layer (MfLinear.forward, H3Common.swift:341-377)
+// on sm_100a tensor cores.
+//
+// Y[M,N] = X[M,K] · deq(Wq)[N,K]^T with fused epilogues. The 6-bit weight is
+// expanded to bf16 by the dequant kernel into context scratch, then this
+// persistent warp-specialised kernel streams 128xBK A tiles and BNxBK B tiles
+// with TMA (128-byte swizzle) through a 4-stage mbarrier ring, issues
+// tcgen05.mma (kind::f16, M=128, N=BN, K=16) from one thread into a
+// double-buffered TMEM accumulator, and 4 epilogue warps drain TMEM with
+// tcgen05.ld, apply bias / GELU / gate+residual and store bf16.
+//
+// Warp roles (192 threads): warp 0 TMA producer, warp 1 MMA issuer + TMEM
+// owner, warps 2-5 epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "wx_internal.h"
+#include "wx_ptx.cuh"
+
+namespace wx {
+
+int launch_dequant(wx_ctx* ctx, const wx_qweight* w, void* out);
+int launch_swiglu(wx_ctx* ctx, const void* t, int64_t m, int64_t F, int64_t ldt, void* y, int64_t ldy);
+bool qweight_ok(const wx_qweight* w);
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr int kGroupM = 16;
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles;
+  __nv_bfloat16* y;
+  int64_t ldy;
+  const __nv_bfloat16* bias;
+  int epi;
+  const __nv_bfloat16* gate;
+  const __nv_bfloat16* resid;
+  const uint32_t* rowmap;
+  __nv_bfloat16* y_raw;
+  int* err;
+};
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = kGemmStages * kStageBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
+  const int per_group = kGroupM * tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * kGroupM;
+  const int gsize = min(tiles_m - first_m, kGroupM);
+  const int in_group = tile % per_group;
+  mb = first_m + in_group % gsize;
+  nb = in_group / gsize;
+}
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float c = 0.7978845608028654f;
+  return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        GemmParams p) {
+  using L = GemmSmem<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  // bars: full[4] empty[4] acc_full[2] acc_empty[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kGemmStages + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };
+  auto empty_bar = [&](int s) { return smem_u32(bars + kGemmStages + s); };
+  auto accf_bar = [&](int a) { return smem_u32(bars + 2 * kGemmStages + a); };
+  auto acce_bar = [&](int a) { return smem_u32(bars + 2 * kGemmStages + 2 + a); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf_bar(a), 1);
+      mbar_init(acce_bar(a), 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int kblocks = p.K / kGemmBK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, p.tiles_m, p.tiles_n, mb, nb);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
+          const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+          tma_load_2d(sa, &tmA, full_bar(stage), kb * kGemmBK, mb * kGemmBM);
+          tma_load_2d(sa + L::kABytes, &tmB, full_bar(stage), kb * kGemmBK, nb * BN);
+          if (++stage == kGemmStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kGemmBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(acce_bar(acc), acc_phase ^ 1u, p.err, kDevTimeoutAcc, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, p.err, kDevTimeoutFull, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t sb = sa + L::kABytes;
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk) {
+            const uint64_t ad = smem_desc_sw128(sa + kk * 32, 16, 1024);
+            const uint64_t bd = smem_desc_sw128(sb + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(stage));
+          if (++stage == kGemmStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(accf_bar(acc));
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(accf_bar(acc), acc_phase, p.err, kDevTimeoutAcc, abort_flag)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(tile, p.tiles_m, p.tiles_n, mb, nb);
+      const int64_t m = (int64_t)mb * kGemmBM + row_in_tile;
+      const bool row_ok = m < p.M;
+      const int64_t mr = (p.epi == WX_EPI_GATE_RESID && row_ok && p.rowmap) ? (int64_t)p.rowmap[m] : 0;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + c * 32, v);
+        tmem_wait_ld();
+        if (!row_ok) continue;
+        const int64_t n0 = (int64_t)nb * BN + c * 32;
+        // t = bf16(acc) (+ bias, rounded again)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = round_bf16(v[i]);
+        if (p.bias) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 bv = *reinterpret_cast<const uint4*>(p.bias + n0 + i);
+            const uint32_t bu[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              v[i + 2 * q] = round_bf16(v[i + 2 * q] + bf16_lo(bu[q]));
+              v[i + 2 * q + 1] = round_bf16(v[i + 2 * q + 1] + bf16_hi(bu[q]));
+            }
+          }
+        }
+        __nv_bfloat16* yrow = p.y + m * p.ldy + n0;
+        if (p.epi == WX_EPI_GATE_RESID) {
+          const __nv_bfloat16* rrow = p.resid + m * p.ldy + n0;
+          const __nv_bfloat16* grow = p.gate + mr * (int64_t)p.N + n0;
+          if (p.y_raw) {
+            __nv_bfloat16* raw = p.y_raw + m * p.ldy + n0;
+#pragma unroll
+            for (int i = 0; i < 32; i += 8)
+              *reinterpret_cast<uint4*>(raw + i) =
+                  make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                             pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 rv = *reinterpret_cast<const uint4*>(rrow + i);
+            uint4 gv = *reinterpret_cast<const uint4*>(grow + i);
+            const uint32_t ru[4] = {rv.x, rv.y, rv.z, rv.w}, gu[4] = {gv.x, gv.y, gv.z, gv.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              o[q] = pack_bf16x2(bf16_lo(ru[q]) + v[i + 2 * q] * bf16_lo(gu[q]),
+                                 bf16_hi(ru[q]) + v[i + 2 * q + 1] * bf16_hi(gu[q]));
+            *reinterpret_cast<uint4*>(yrow + i) = make_uint4(o[0], o[1], o[2], o[3]);
+          }
+        } else {
+          if (p.epi == WX_EPI_GELU) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 8)
+            *reinterpret_cast<uint4*>(yrow + i) =
+                make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                           pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce_bar(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+template <int BN>
+static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p) {
+  using L = GemmSmem<BN>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::kBytes);
+    if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
+    attr_done = true;
+  }
+  p.tiles_m = (p.M + kGemmBM - 1) / kGemmBM;
+  p.tiles_n = p.N / BN;
+  p.num_tiles = p.tiles_m * p.tiles_n;
+  const int grid = std::min(p.num_tiles, ctx->num_sms);
+  gemm_bf16_tc_kernel<BN><<<grid, kGemmThreads, L::kBytes, ctx->stream>>>(ta, tb, p);
+  return launch_status(ctx, "gemm_bf16_tc");
+}
+
+// bf16 GEMM core: Y = X · Wd^T with X [M,K] (pitch lda), Wd [N,K] (pitch K)
+int gemm_bf16(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd, int64_t N, int64_t K,
+              const void* bias, int epi, const void* gate, const void* resid, const uint32_t* rowmap, void* y,
+              int64_t ldy, void* y_raw) {
+  if (M == 0) return WX_OK;
+  if (K % kGemmBK != 0 || N % 64 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return set_error(ctx, WX_ERR_UNSUPPORTED, "gemm needs K %% 64 == 0 and N %% 64 == 0 (M=%lld N=%lld K=%lld)",
+                     (long long)M, (long long)N, (long long)K);
+  if (!aligned16(y) || ldy % 8 != 0 || (bias && !aligned16(bias)) ||
+      (epi == WX_EPI_GATE_RESID && (!aligned16(gate) || !aligned16(resid) || (y_raw && !aligned16(y_raw)))))
+    return set_error(ctx, WX_ERR_INVALID, "gemm outputs/epilogue operands need 16-byte alignment");
+  const int BN = (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64);
+  CUtensorMap ta, tb;
+  int st = make_tmap_bf16_2d(ctx, &ta, x, (uint64_t)M, (uint64_t)K, (uint64_t)lda, kGemmBK, kGemmBM);
+  if (st) return st;
+  st = make_tmap_bf16_2d(ctx, &tb, wd, (uint64_t)N, (uint64_t)K, (uint64_t)K, kGemmBK, BN);
+  if (st) return st;
+  GemmParams p{};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.epi = epi;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.resid = static_cast<const __nv_bfloat16*>(resid);
+  p.rowmap = rowmap;
+  p.y_raw = static_cast<__nv_bfloat16*>(y_raw);
+  p.err = ctx->dev_err;
+  if (BN == 256) return launch_gemm_bn<256>(ctx, ta, tb, p);
+  if (BN == 128) return launch_gemm_bn<128>(ctx, ta, tb, p);
+  return launch_gemm_bn<64>(ctx, ta, tb, p);
+}
+
+// Full quantized linear: dequant into scratch `wd` (N*K bf16), then GEMM.
+int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,
+                         const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
+                         void* y_raw, void* wd, void* swiglu_tmp) {
+  int st = launch_dequant(ctx, w, wd);
+  if (st) return st;
+  if (epilogue == WX_EPI_SWIGLU) {
+    st = gemm_bf16(ctx, x, m, lda, wd, w->n, w->k, w->bias, WX_EPI_NONE, nullptr, nullptr, nullptr, swiglu_tmp,
+                   w->n, nullptr);
+    if (st) return st;
+    return launch_swiglu(ctx, swiglu_tmp, m, w->n / 2, w->n, y, ldy);
+  }
+  return gemm_bf16(ctx, x, m, lda, wd, w->n, w->k, w->bias, epilogue, gate, resid, rowmap, y, ldy, y_raw);
+}
+
+size_t qlinear_scratch_bytes(const wx_qweight* w, int64_t m, int epilogue) {
+  size_t b = ((size_t)w->n * w->k * 2 + 255) & ~size_t(255);
+  if (epilogue == WX_EPI_SWIGLU) b += ((size_t)m * w->n * 2 + 255) & ~size_t(255);
+  return b;
+}
+
+}  // namespace wx
+
+using namespace wx;
+
+extern "C" int wx_qlinear(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,
+                          const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
+                          void* y_raw) {
+  WX_CHECK_ARG(ctx, ctx && x && y && qweight_ok(w) && m >= 0 && lda >= w->k);
+  WX_CHECK_ARG(ctx, epilogue >= WX_EPI_NONE && epilogue <= WX_EPI_SWIGLU);
+  WX_CHECK_ARG(ctx, epilogue != WX_EPI_GATE_RESID || (gate && resid));
+  WX_CHECK_ARG(ctx, epilogue != WX_EPI_SWIGLU || w->n % 2 == 0);
+  WX_CHECK_ARG(ctx, ldy >= (epilogue == WX_EPI_SWIGLU ? w->n / 2 : w->n));
+  int st = WX_OK;
+  void* ws = workspace(ctx, qlinear_scratch_bytes(w, m, epilogue), &st);
+  if (!ws) return st;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  void* wd = base;
+  void* tmp = base + (((size_t)w->n * w->k * 2 + 255) & ~size_t(255));
+  return qlinear_with_scratch(ctx, x, m, lda, w, epilogue, gate, resid, rowmap, y, ldy, y_raw, wd, tmp);
+}

@@ -1,0 +1,62 @@
+// wx_internal.h — host-side context, status plumbing and TMA map encoding
+// shared by the translation units of libwx.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/wx_api.h"
+
+struct wx_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  int* dev_err = nullptr;         // device error word (wx::DevErr)
+  void* ws = nullptr;             // workspace arena
+  size_t ws_bytes = 0;
+  std::string last_error;
+};
+
+namespace wx {
+
+int set_error(wx_ctx* ctx, int status, const char* fmt, ...);
+
+#define WX_CUDA_TRY(ctx, expr)                                                              \
+  do {                                                                                      \
+    cudaError_t e__ = (expr);                                                               \
+    if (e__ != cudaSuccess)                                                                 \
+      return ::wx::set_error((ctx), WX_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,            \
+                             cudaGetErrorString(e__), __FILE__, __LINE__);                  \
+  } while (0)
+
+#define WX_CHECK_ARG(ctx, cond)                                                             \
+  do {                                                                                      \
+    if (!(cond)) return ::wx::set_error((ctx), WX_ERR_INVALID, "invalid argument: %s", #cond); \
+  } while (0)
+
+// Returns a device buffer of at least `bytes` from the context arena (grown on
+// demand; contents undefined; valid until the next call that grows it).
+void* workspace(wx_ctx* ctx, size_t bytes, int* status);
+
+// Carves 256-byte-aligned sub-buffers out of one arena request.
+struct Carve {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  }
+};
+
+// 2-D bf16 tensor map: `rows` x `cols` elements, row pitch `ld` elements,
+// box `box_cols` x `box_rows`, 128-byte swizzle, zero fill out of bounds.
+int make_tmap_bf16_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t rows,
+                      uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows);
+
+int launch_status(wx_ctx* ctx, const char* what);
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace wx

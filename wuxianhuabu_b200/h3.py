@@ -1,0 +1,431 @@
+"""Host-side mirror of the reference's H3 hot-path interface over libwx.
+
+Names follow the Swift API of HuaChayu/wuxianhuabu so that a caller (and the
+parity tests) read like the reference:
+
+* ``MfLinear``              — model/minimax h3/H3Common.swift:283-404
+* ``H3FusedKernels``        — model/2网络算子/网络算子-融合-RMSNormRoPE-通用.swift:28-345
+* ``H3SolAttnConfig`` / ``H3SolAttn`` — 网络算子-稀疏注意力-SOL通用.swift:79-678
+* ``H3AttnBroadcast`` + ``attn_broadcast_*`` — 网络算子-注意力跨步缓存-通用.swift:36-112
+* ``sigma_schedule`` / ``sparse_mode_for_layer`` — model/minimax h3/H3Layout.swift:175-182, 896-906
+* ``H3DiTBlocks``           — the block loop of H3DiT.forward, H3Transformer.swift:1078-1159
+
+Tensors are torch CUDA tensors used purely as device buffers; all compute is
+in libwx (sm_100a). q/k/v use the reference's pre-transpose layout [S, H, hd].
+Errors raise ``WxError``; nothing falls back to a CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass, field
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import (EPI_GATE_RESID, EPI_GELU, EPI_NONE, EPI_SWIGLU, MLP_GELU, MLP_SWIGLU, SPARSE_DENSE, SPARSE_SOL,
+                   SPARSE_TOPK, BlockMods, BlockWeights, DitConfig, ModRun, QWeight, SparseSpec, WxError, check)
+
+__all__ = [
+    "Context", "context", "MfLinear", "H3FusedKernels", "H3SolAttnConfig", "H3SolAttn", "H3AttnBroadcast",
+    "attn_broadcast_refresh", "attn_broadcast_must_refresh", "attn_broadcast_plan",
+    "attn_broadcast_default_max_stale", "sigma_schedule", "sparse_mode_for_layer", "SparsePolicy",
+    "H3DiTConfig", "H3BlockWeights", "H3DiTBlocks", "ModRun", "WxError",
+    "EPI_NONE", "EPI_GELU", "EPI_GATE_RESID", "EPI_SWIGLU",
+]
+
+
+def _p(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+class Context:
+    """One libwx context per CUDA device; calls are ordered on torch's current stream."""
+
+    def __init__(self, device: int = 0):
+        self.lib = _lib.load()
+        if not torch.cuda.is_available():
+            raise RuntimeError("libwx needs a CUDA device (sm_100a); no CPU fallback exists")
+        self.device = device
+        h = C.c_void_p()
+        st = self.lib.wx_ctx_create(device, C.byref(h))
+        if st != 0:
+            raise WxError(st, f"wx_ctx_create(device={device}) failed")
+        self.h = h
+
+    def sync_stream(self) -> None:
+        s = torch.cuda.current_stream(self.device).cuda_stream
+        check(self.lib.wx_ctx_set_stream(self.h, C.c_void_p(s)), self.h)
+
+    def check_device(self) -> None:
+        check(self.lib.wx_ctx_check_device(self.h), self.h)
+
+    def call(self, name: str, *args) -> None:
+        self.sync_stream()
+        check(getattr(self.lib, name)(self.h, *args), self.h)
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.wx_ctx_destroy(self.h)
+            self.h = None
+
+
+_contexts: dict[int, Context] = {}
+
+
+def context(device: Optional[int] = None) -> Context:
+    dev = torch.cuda.current_device() if device is None else device
+    if dev not in _contexts:
+        _contexts[dev] = Context(dev)
+    return _contexts[dev]
+
+
+def _need_bf16_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda or t.dtype != torch.bfloat16:
+            raise WxError(_lib.WX_ERR_INVALID, f"expected a CUDA bf16 tensor, got {t.dtype} on {t.device}")
+
+
+# --------------------------------------------------------------------------- MfLinear
+class MfLinear:
+    """6-bit (2..8-bit) MLX-affine group-quantized linear layer (H3Common.swift:283-404).
+
+    ``w`` packed uint32 [out, in*bits/32] (stored as int32), ``scales``/``biases`` bf16
+    [out, in/group], optional ``bias`` bf16 [out]. bits and group are derived as in
+    MfLinear.load (:321-323)."""
+
+    def __init__(self, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, in_dim: int,
+                 bias: Optional[torch.Tensor] = None):
+        if w.dtype not in (torch.int32, torch.uint32):
+            raise WxError(_lib.WX_ERR_INVALID, "packed weight must be 32-bit words")
+        self.w, self.scales, self.biases, self.bias = w.contiguous(), scales.contiguous(), biases.contiguous(), bias
+        self.in_dim = in_dim
+        self.out_dim = w.shape[0]
+        self.bits = 32 * w.shape[1] // in_dim
+        self.group_size = in_dim // scales.shape[1]
+
+    @classmethod
+    def quantize(cls, w_f32: torch.Tensor, bits: int = 6, group: int = 64,
+                 bias: Optional[torch.Tensor] = None) -> "MfLinear":
+        """Quantize an fp32 [out, in] weight on the GPU (offline step of tools/quantize_h3_g64.py)."""
+        n, k = w_f32.shape
+        dev = w_f32.device
+        wq = torch.empty((n, k * bits // 32), dtype=torch.int32, device=dev)
+        sc = torch.empty((n, k // group), dtype=torch.bfloat16, device=dev)
+        bi = torch.empty_like(sc)
+        ctx = context(dev.index)
+        ctx.call("wx_quantize_affine", _p(w_f32.contiguous()), n, k, group, bits, _p(wq), _p(sc), _p(bi))
+        return cls(wq, sc, bi, k, bias)
+
+    def qweight(self) -> QWeight:
+        return QWeight(_p(self.w), _p(self.scales), _p(self.biases), _p(self.bias), self.out_dim, self.in_dim,
+                       self.group_size, self.bits)
+
+    def dequantized_weight(self) -> torch.Tensor:
+        """MfLinear.dequantizedWeight (:379-401): [out, in] bf16."""
+        out = torch.empty((self.out_dim, self.in_dim), dtype=torch.bfloat16, device=self.w.device)
+        qw = self.qweight()
+        context(self.w.device.index).call("wx_dequantize_affine", C.byref(qw), _p(out))
+        return out
+
+    def forward(self, x: torch.Tensor, epilogue: int = EPI_NONE, gate: Optional[torch.Tensor] = None,
+                resid: Optional[torch.Tensor] = None, rowmap: Optional[torch.Tensor] = None,
+                y_raw: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """x[..., in] -> [..., out] (quantizedMM + bias, :341-377) with a fused epilogue."""
+        _need_bf16_cuda(x, gate, resid, y_raw)
+        x2 = x.reshape(-1, self.in_dim)
+        if x2.stride(1) != 1:
+            x2 = x2.contiguous()
+        m = x2.shape[0]
+        n_out = self.out_dim // 2 if epilogue == EPI_SWIGLU else self.out_dim
+        y = out if out is not None else torch.empty((m, n_out), dtype=torch.bfloat16, device=x.device)
+        qw = self.qweight()
+        context(x.device.index).call("wx_qlinear", _p(x2), m, x2.stride(0), C.byref(qw), epilogue, _p(gate),
+                                     _p(resid), _p(rowmap), _p(y), y.stride(0), _p(y_raw))
+        return y.reshape(*x.shape[:-1], n_out)
+
+    __call__ = forward
+
+
+# ------------------------------------------------------------------- fused row kernels
+class H3FusedKernels:
+    """h3_fused_rmsnorm_rope / h3_fused_norm_modscale / h3_fused_mod_gate (fused:28-345)."""
+
+    @staticmethod
+    def build_row_mod_map(count: int, runs: Sequence[ModRun]) -> np.ndarray:
+        """buildRowModMap (fused:238-250): [count] uint32 row -> modRow."""
+        lib = _lib.load()
+        arr = (ModRun * max(1, len(runs)))(*runs)
+        out = np.zeros(count, dtype=np.uint32)
+        check(lib.wx_build_row_mod_map(arr, len(runs), count, out.ctypes.data))
+        return out
+
+    @staticmethod
+    def fused_rmsnorm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                           rot: int, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """fusedRmsnormRope (fused:111-129). x [S, H, hd] (row stride may exceed H*hd)."""
+        _need_bf16_cuda(x, weight, cos, sin)
+        S, H, hd = x.shape
+        if x.stride(2) != 1 or x.stride(1) != hd:
+            raise WxError(_lib.WX_ERR_INVALID, "x must have contiguous heads")
+        o = out if out is not None else torch.empty((S, H, hd), dtype=torch.bfloat16, device=x.device)
+        context(x.device.index).call("wx_qk_norm_rope", _p(x), x.stride(0), S, H, hd, _p(weight), _p(cos), _p(sin),
+                                     rot, float(eps), _p(o), o.stride(0))
+        return o
+
+    @staticmethod
+    def fused_norm_modscale(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+                            rowmap: Optional[torch.Tensor], eps: float,
+                            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """fusedNormModscale (fused:262-283); rowmap [S] int32/uint32 on the device."""
+        _need_bf16_cuda(x, weight, shift, scale)
+        S, hidden = x.shape
+        o = out if out is not None else torch.empty_like(x)
+        context(x.device.index).call("wx_norm_modscale", _p(x), S, hidden, _p(weight), _p(shift), _p(scale),
+                                     _p(rowmap), float(eps), _p(o))
+        return o
+
+    @staticmethod
+    def fused_norm_modscale_row(x: torch.Tensor, weight: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor,
+                                eps: float) -> torch.Tensor:
+        """fusedNormModscaleRow (fused:295-315): one shift/scale row for every row."""
+        return H3FusedKernels.fused_norm_modscale(x, weight, shift, scale, None, eps)
+
+    @staticmethod
+    def fused_mod_gate(x: torch.Tensor, gate: torch.Tensor, other: torch.Tensor,
+                       rowmap: Optional[torch.Tensor], out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """fusedModGate (fused:324-343): x + other * gate[map[r]]."""
+        _need_bf16_cuda(x, gate, other)
+        S, hidden = x.shape
+        o = out if out is not None else torch.empty_like(x)
+        context(x.device.index).call("wx_mod_gate", _p(x), _p(other), _p(gate), _p(rowmap), S, hidden, _p(o))
+        return o
+
+
+# --------------------------------------------------------------------- SOL attention
+@dataclass
+class H3SolAttnConfig:
+    """H3SolAttnConfig (SOL:79-98). ``topk_ratio`` selects the top-k router (benchmark mode)."""
+    tau: float = 1.3
+    sink_blocks: Optional[range] = None
+    tail: bool = True
+    block: int = 64
+    topk_ratio: Optional[float] = None
+
+    def spec(self, g: int) -> SparseSpec:
+        mode = SPARSE_TOPK if self.topk_ratio is not None else SPARSE_SOL
+        sink = self.sink_blocks or range(0, 0)
+        return SparseSpec(mode, self.block, g, float(self.tau), float(self.topk_ratio or 0.0), sink.start,
+                          sink.stop, int(self.tail), 0)
+
+
+def dense_spec() -> SparseSpec:
+    return SparseSpec(SPARSE_DENSE, 128, 0, 0.0, 0.0, 0, 0, 0, 0)
+
+
+class H3SolAttn:
+    """H3SolAttn (SOL:383-678) over q/k/v in [S, H, 128] (rows may be strided, e.g. a packed qkv)."""
+
+    @staticmethod
+    def _geom(q: torch.Tensor):
+        S, H, hd = q.shape
+        if q.stride(2) != 1 or q.stride(1) != hd:
+            raise WxError(_lib.WX_ERR_INVALID, "q/k/v must have contiguous heads")
+        return S, H, hd, q.stride(0)
+
+    @staticmethod
+    def forward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: int, scale: float,
+                cfg: Optional[H3SolAttnConfig] = H3SolAttnConfig(),
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """SOL attention (cfg) or dense SDPA (cfg None). Returns [S, H, hd] bf16."""
+        _need_bf16_cuda(q, k, v)
+        S, H, hd, rs = H3SolAttn._geom(q)
+        if k.stride(0) != rs or v.stride(0) != rs:
+            raise WxError(_lib.WX_ERR_INVALID, "q, k and v must share one row stride")
+        o = out if out is not None else torch.empty((S, H, hd), dtype=torch.bfloat16, device=q.device)
+        spec = dense_spec() if cfg is None else cfg.spec(g)
+        context(q.device.index).call("wx_sparse_attention", _p(q), _p(k), _p(v), rs, S, H, hd, C.byref(spec),
+                                     float(scale), _p(o), o.stride(0))
+        return o
+
+    @staticmethod
+    def route(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: int, scale: float, cfg: H3SolAttnConfig):
+        """Routing tables: dict(sel, thr|scores, cm, vsum, lens) as device tensors."""
+        _need_bf16_cuda(q, k, v)
+        S, H, hd, rs = H3SolAttn._geom(q)
+        nb = (S - g + cfg.block - 1) // cfg.block
+        dev = q.device
+        sel = torch.empty((H, nb, nb), dtype=torch.uint8, device=dev)
+        cm = torch.empty((H, nb, nb), dtype=torch.bfloat16, device=dev)
+        vsum = torch.empty((H, nb, hd), dtype=torch.bfloat16, device=dev)
+        lens = torch.empty((nb,), dtype=torch.float32, device=dev)
+        spec = cfg.spec(g)
+        if spec.mode == SPARSE_SOL:
+            thr = torch.empty((H, nb), dtype=torch.float32, device=dev)
+            context(dev.index).call("wx_sol_route", _p(q), _p(k), _p(v), rs, S, H, hd, C.byref(spec), float(scale),
+                                    _p(sel), _p(thr), _p(cm), _p(vsum), _p(lens))
+            return dict(sel=sel, thr=thr, cm=cm, vsum=vsum, lens=lens)
+        scores = torch.empty((H, nb, nb), dtype=torch.float32, device=dev)
+        context(dev.index).call("wx_topk_route", _p(q), _p(k), _p(v), rs, S, H, hd, C.byref(spec), float(scale),
+                                _p(sel), _p(scores), _p(cm), _p(vsum), _p(lens))
+        return dict(sel=sel, scores=scores, cm=cm, vsum=vsum, lens=lens)
+
+    @staticmethod
+    def attend_with_selection(q, k, v, g: int, scale: float, cfg: H3SolAttnConfig, sel: torch.Tensor,
+                              cm=None, vsum=None, lens=None) -> torch.Tensor:
+        """The flash kernel alone over a given block selection [H, nb, nb]."""
+        _need_bf16_cuda(q, k, v)
+        S, H, hd, rs = H3SolAttn._geom(q)
+        o = torch.empty((S, H, hd), dtype=torch.bfloat16, device=q.device)
+        spec = cfg.spec(g)
+        context(q.device.index).call("wx_attention_from_sel", _p(q), _p(k), _p(v), rs, S, H, hd, C.byref(spec),
+                                     float(scale), _p(sel), _p(cm), _p(vsum), _p(lens), _p(o), o.stride(0))
+        return o
+
+
+# ----------------------------------------------------------------- PAB + schedules
+def attn_broadcast_refresh(i: int, steps: int, k: int) -> bool:
+    """attnBroadcastRefresh (PAB:73-79)."""
+    return bool(_lib.load().wx_pab_refresh(i, steps, k))
+
+
+def attn_broadcast_must_refresh(cached_sigma: float, sigma: float, max_stale: float) -> bool:
+    """attnBroadcastMustRefresh (PAB:85-87)."""
+    return bool(_lib.load().wx_pab_must_refresh(cached_sigma, sigma, max_stale))
+
+
+def attn_broadcast_plan(sigmas: Sequence[float], k: int, max_stale: float) -> list[bool]:
+    """attnBroadcastPlan (PAB:92-105): per-step refresh flags."""
+    arr = np.asarray(sigmas, dtype=np.float64)
+    out = np.zeros(max(0, len(arr) - 1), dtype=np.uint8)
+    _lib.load().wx_pab_plan(arr.ctypes.data, len(arr), k, max_stale, out.ctypes.data if len(out) else None)
+    return [bool(x) for x in out]
+
+
+def attn_broadcast_default_max_stale() -> float:
+    """attnBroadcastDefaultMaxStale (PAB:112)."""
+    return 0.04
+
+
+def sigma_schedule(steps: int, shift: float) -> list[float]:
+    """sigmaSchedule (H3Layout.swift:175-182)."""
+    out = np.zeros(steps + 1, dtype=np.float64)
+    check(_lib.load().wx_sigma_schedule(steps, shift, out.ctypes.data))
+    return out.tolist()
+
+
+class SparsePolicy:
+    OFF, MIX, SPATIAL, TEMPORAL = 0, 1, 2, 3
+
+
+def sparse_mode_for_layer(layer: int, n_layers: int, policy: int) -> int:
+    """sparseModeForLayer (H3Layout.swift:896-906): 0 dense, 1 spatial, 2 temporal."""
+    return _lib.load().wx_sparse_mode_for_layer(layer, n_layers, policy)
+
+
+class H3AttnBroadcast:
+    """PAB cache (PAB:36-52): one device slot [S, hidden] per block, allocated on first refresh."""
+
+    def __init__(self, count: int):
+        self.blocks: list[Optional[torch.Tensor]] = [None] * count
+        self.cached_sigma = math.inf
+
+    def reset(self) -> None:
+        self.blocks = [None] * len(self.blocks)
+        self.cached_sigma = math.inf
+
+    def slot(self, bi: int, rows: int, hidden: int, device) -> torch.Tensor:
+        t = self.blocks[bi]
+        if t is None or t.shape != (rows, hidden):
+            t = torch.empty((rows, hidden), dtype=torch.bfloat16, device=device)
+            self.blocks[bi] = t
+        return t
+
+
+# ------------------------------------------------------------------------ DiT blocks
+@dataclass
+class H3DiTConfig:
+    hidden: int = 3072
+    heads: int = 24
+    head_dim: int = 128
+    ffn: int = 12288
+    mlp_kind: int = MLP_GELU
+    rot: int = 96
+    eps: float = 1e-6
+    layers: int = 48
+
+    def c(self) -> DitConfig:
+        return DitConfig(self.hidden, self.heads, self.head_dim, self.ffn, self.mlp_kind, self.rot, self.eps, 0)
+
+
+@dataclass
+class H3BlockWeights:
+    qkv: MfLinear
+    out: MfLinear
+    fc1: MfLinear
+    fc2: MfLinear
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    norm1: torch.Tensor
+    norm2: torch.Tensor
+
+    def c(self) -> BlockWeights:
+        return BlockWeights(self.qkv.qweight(), self.out.qweight(), self.fc1.qweight(), self.fc2.qweight(),
+                            _p(self.q_norm), _p(self.k_norm), _p(self.norm1), _p(self.norm2))
+
+
+class H3DiTBlocks:
+    """The block loop of H3DiT.forward (H3Transformer.swift:1078-1159) on libwx.
+
+    ``mods[bi]`` = six [num_mod_rows, hidden] bf16 tables (shift/scale/gate MSA, shift/scale/gate MLP)."""
+
+    def __init__(self, cfg: H3DiTConfig, blocks: list[H3BlockWeights]):
+        self.cfg = cfg
+        self.blocks = blocks
+        self._c = cfg.c()
+        self._wc = [b.c() for b in blocks]
+        self._scratch: Optional[torch.Tensor] = None
+
+    def scratch(self, S: int, device) -> torch.Tensor:
+        need = int(_lib.load().wx_dit_block_scratch_bytes(C.byref(self._c), S))
+        if self._scratch is None or self._scratch.numel() < need or self._scratch.device != torch.device(device):
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=device)
+        return self._scratch
+
+    def block_forward(self, bi: int, h: torch.Tensor, mods: Sequence[torch.Tensor], rowmap: torch.Tensor,
+                      cos: torch.Tensor, sin: torch.Tensor, spec: Optional[SparseSpec],
+                      pab_slot: Optional[torch.Tensor] = None, refresh: bool = True) -> torch.Tensor:
+        """One block, h [S, hidden] updated in place."""
+        _need_bf16_cuda(h, cos, sin, *mods)
+        S = h.shape[0]
+        scr = self.scratch(S, h.device)
+        bm = BlockMods(*[_p(m) for m in mods])
+        sp = spec if spec is not None else dense_spec()
+        context(h.device.index).call("wx_dit_block_forward", C.byref(self._c), C.byref(self._wc[bi]), C.byref(bm),
+                                     _p(rowmap), _p(h), S, _p(cos), _p(sin), C.byref(sp), _p(pab_slot),
+                                     int(refresh), _p(scr))
+        return h
+
+    def forward(self, h: torch.Tensor, mods: Sequence[Sequence[torch.Tensor]], rowmap: torch.Tensor,
+                cos: torch.Tensor, sin: torch.Tensor, sparse_cfg: Optional[H3SolAttnConfig], g: int,
+                policy: int = SparsePolicy.MIX, attn_bcast: Optional[H3AttnBroadcast] = None,
+                attn_refresh: bool = True, sigma: Optional[float] = None) -> torch.Tensor:
+        """All blocks in order; the PAB slot of block bi is written on refresh, read on reuse."""
+        n = len(self.blocks)
+        for bi in range(n):
+            mode = sparse_mode_for_layer(bi, n, policy) if sparse_cfg is not None else 0
+            spec = sparse_cfg.spec(g) if mode != 0 else None
+            slot = None
+            refresh = True
+            if attn_bcast is not None:
+                cached = attn_bcast.blocks[bi]
+                refresh = attn_refresh or cached is None
+                slot = attn_bcast.slot(bi, h.shape[0], self.cfg.hidden, h.device)
+            self.block_forward(bi, h, mods[bi], rowmap, cos, sin, spec, slot, refresh)
+        if attn_bcast is not None and attn_refresh and sigma is not None:
+            attn_bcast.cached_sigma = sigma
+        return h
