@@ -1,0 +1,508 @@
+#!/usr/bin/env python
+"""Benchmark of the video-DiT denoising step (BASELINE.json metric:
+"DiT denoising s/step (720p x 121f, 6-bit, 1/2/4/8 B200); qGEMM TFLOP/s % peak").
+
+Workload (default ``--config c5``): one full-size
+synthetic 720p x 121-frame step of the 48-block 6-bit H3-style DiT:
+S = 512 text + 4 x 3600 reference-image rows + 111600 video rows (31x45x80) = 126512,
+hidden 3072, 24 x 128 heads, FFN 12288 GELU, AdaLN modulation, attention policy
+"mix" (dense anchors {0,1,24,25,46,47}, other layers block top-k 25 % over
+128-row blocks, strip rows [0, 14912) exact), PAB over the 4-step window of
+sigmaSchedule(4, shift 12) with maxStale 0.06 (refresh {0,1,3}, reuse {2}).
+A bench "step" is one denoising step (patch embed, 48 blocks, final head,
+Euler update); K timed steps follow W warm-up steps along the window.
+
+Random-init weights quantized to 6 bits on the GPU, synthetic latents: no
+checkpoint or dataset is used. Every kernel on the timed path is libwx
+(sm_100a); torch only allocates buffers and copies host data.
+
+``--impl reference`` times the reference algorithm's CPU restatement (the
+oracle; the reference's own Swift/MLX/Metal path cannot run on this box) on
+bounded samples of the same workload and reports the same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "DiT denoising s/step (720p x 121f, 6-bit); qGEMM TFLOP/s % peak"
+PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+
+CONFIGS = {
+    # full-size 720p x 121f with reference-image conditioning
+    "c5": dict(text=512, refs=4, ref_rows=3600, grid=(31, 45, 80), hidden=3072, heads=24, ffn=12288, layers=48,
+               text_dim=4096),
+    # half-size step
+    "c4": dict(text=512, refs=0, ref_rows=0, grid=(31, 23, 40), hidden=3072, heads=24, ffn=12288, layers=48,
+               text_dim=4096),
+    # development geometry (seconds on one GPU)
+    "tiny": dict(text=64, refs=1, ref_rows=192, grid=(3, 8, 16), hidden=512, heads=4, ffn=1024, layers=4,
+                 text_dim=512),
+}
+PATCH_DIM = 96          # latent channels x 2 x 2 patch
+TOPK_DENSITY = 0.25
+SHIFT = 12.0
+WINDOW = 4              # sampler steps in the PAB window
+PAB_K = 2
+PAB_MAX_STALE = 0.06    # lifts the reference default 0.04 so step 2 is reused (|dsigma| = 0.0499)
+EPS = 1e-6
+ROT = 96                # 3 axes x 16 inverse frequencies x 2
+
+
+def geometry(name: str) -> dict:
+    c = dict(CONFIGS[name])
+    t, hh, ww = c["grid"]
+    c["video"] = t * hh * ww
+    c["g"] = c["text"] + c["refs"] * c["ref_rows"]
+    c["S"] = c["g"] + c["video"]
+    c["inner"] = c["heads"] * 128
+    c["name"] = name
+    return c
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return dict(PEAKS_FALLBACK), "fallback"
+
+
+# ------------------------------------------------------------------ work model
+def step_flops(c: dict, refresh: bool) -> dict:
+    """Algorithmic FLOPs of one step: GEMMs (2MNK) and attention (4*hd per query-key pair)."""
+    S, hdn, inner, ffn, L = c["S"], c["hidden"], c["inner"], c["ffn"], c["layers"]
+    mlp = 2 * S * (hdn * ffn + ffn * hdn)
+    attn_proj = 2 * S * (hdn * 3 * inner + inner * hdn)
+    gemm = L * (mlp + (attn_proj if refresh else 0))
+    attn = 0.0
+    if refresh:
+        for layer in range(L):
+            attn += attention_flops(c, dense=_is_dense(layer, L))
+    return dict(gemm=gemm, attn=attn)
+
+
+def _is_dense(layer: int, n: int) -> bool:
+    mid = n // 2
+    return layer < 2 or layer + 2 >= n or layer == mid or layer == mid + 1
+
+
+def attention_flops(c: dict, dense: bool) -> float:
+    S, g, H = c["S"], c["g"], c["heads"]
+    if dense:
+        pairs = S * S
+    else:
+        L = S - g
+        nb = (L + 127) // 128
+        keep = min(math.ceil(TOPK_DENSITY * nb), nb - 1) + 1
+        # kept key rows per video row: strip + keep blocks (the ragged last block counted full: <0.1 %)
+        pairs = g * S + L * (g + min(keep * 128, L))
+    return 4.0 * 128 * H * pairs
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if not self.proc:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["nvidia-smi unavailable"])
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return dict(sm_mhz=None, sm_max_mhz=None, reasons=["no samples"])
+        return dict(sm_mhz=float(np.median(sm)), sm_max_mhz=max(smax), samples=len(sm),
+                    power_w_max=max(power) if power else None, reasons=sorted(reasons))
+
+
+# ------------------------------------------------------------------ model
+class Model:
+    def __init__(self, c: dict, device, seed: int = 1234 + 5):
+        import torch
+        from wuxianhuabu_b200 import h3
+        self.c = c
+        self.dev = device
+        g = torch.Generator(device=device).manual_seed(seed)
+        hdn, inner, ffn, L = c["hidden"], c["inner"], c["ffn"], c["layers"]
+
+        def qlin(n, k):
+            w = torch.randn((n, k), device=device, generator=g) * 0.02
+            b = (torch.randn((n,), device=device, generator=g) * 0.02).to(torch.bfloat16)
+            m = h3.MfLinear.quantize(w, bits=6, group=64, bias=b)
+            del w
+            return m
+
+        def norm(n):
+            return (1.0 + 0.02 * torch.randn((n,), device=device, generator=g)).to(torch.bfloat16)
+
+        blocks = []
+        for _ in range(L):
+            blocks.append(h3.H3BlockWeights(qlin(3 * inner, hdn), qlin(hdn, inner), qlin(ffn, hdn), qlin(hdn, ffn),
+                                            norm(128), norm(128), norm(hdn), norm(hdn)))
+        torch.cuda.synchronize()
+        self.cfg = h3.H3DiTConfig(hidden=hdn, heads=c["heads"], head_dim=128, ffn=ffn, mlp_kind=h3.MLP_GELU, rot=ROT,
+                                  eps=EPS, layers=L)
+        self.dit = h3.H3DiTBlocks(self.cfg, blocks)
+        # AdaLN tables (precomputeAdaln output): 6 x [12, hidden] per block, rows = t_row*3 + modality
+        self.mods = [[(0.05 * torch.randn((12, hdn), device=device, generator=g)).to(torch.bfloat16)
+                      for _ in range(6)] for _ in range(L)]
+        self.final_norm = norm(hdn)
+        self.final_mods = [(0.05 * torch.randn((4, hdn), device=device, generator=g)).to(torch.bfloat16)
+                           for _ in range(2)]
+        self.w_embed = torch.randn((PATCH_DIM, hdn), device=device, generator=g) * (1 / math.sqrt(PATCH_DIM))
+        self.b_embed = torch.zeros((hdn,), device=device)
+        self.w_out = torch.randn((hdn, PATCH_DIM), device=device, generator=g) * (1 / math.sqrt(hdn))
+        self.b_out = torch.zeros((PATCH_DIM,), device=device)
+        # refined text states (condition_proj output, computed once per generation)
+        self.text = torch.randn((c["text"], hdn), device=device, generator=g).to(torch.bfloat16)
+        self.gen = g
+
+
+class Runner:
+    """Device-resident sampler step over the packed sequence."""
+
+    def __init__(self, model: Model):
+        import torch
+        from wuxianhuabu_b200 import h3
+        self.m = model
+        c = model.c
+        dev = model.dev
+        self.h3 = h3
+        S, g, hdn = c["S"], c["g"], c["hidden"]
+        nv = c["refs"] * c["ref_rows"] + c["video"]  # rows through the patch embed (cond rows + video)
+        self.n_embed = nv
+        self.x_in = torch.randn((nv, PATCH_DIM), device=dev, generator=model.gen)  # [cond ; videoX] fp32
+        self.video_x = self.x_in[c["refs"] * c["ref_rows"]:]
+        self.h = torch.empty((S, hdn), dtype=torch.bfloat16, device=dev)
+        self.emb32 = torch.empty((nv, hdn), dtype=torch.float32, device=dev)
+        self.head32 = torch.empty((c["video"], hdn), dtype=torch.float32, device=dev)
+        self.head16 = torch.empty((c["video"], hdn), dtype=torch.bfloat16, device=dev)
+        self.vel = torch.empty((c["video"], PATCH_DIM), dtype=torch.float32, device=dev)
+        self.cos, self.sin = self._rope(c, dev)
+        self.sigmas = h3.sigma_schedule(WINDOW, SHIFT)
+        self.plan = h3.attn_broadcast_plan(self.sigmas, PAB_K, PAB_MAX_STALE)
+        self.rowmaps = [self._rowmap(c, i, dev) for i in range(WINDOW)]
+        self.pab = h3.H3AttnBroadcast(c["layers"])
+        self.sparse = h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False)
+        self.ctx = h3.context(dev.index)
+
+    @staticmethod
+    def _rope(c, dev):
+        """buildRope (H3Layout.swift:725-740): angles = concat(t*inv, h*inv, w*inv) for 16 inverse frequencies."""
+        import torch
+        t, hh, ww = c["grid"]
+        pos = []
+        pos.append(torch.zeros((c["text"], 3)))
+        for r in range(c["refs"]):
+            n = c["ref_rows"]
+            side_w = n // hh if n % hh == 0 else n
+            idx = torch.arange(n)
+            pos.append(torch.stack([torch.full((n,), -1.0 - r), (idx // side_w).float(), (idx % side_w).float()], 1))
+        ti, hi, wi = torch.meshgrid(torch.arange(t), torch.arange(hh), torch.arange(ww), indexing="ij")
+        pos.append(torch.stack([ti.flatten(), hi.flatten(), wi.flatten()], 1).float())
+        P = torch.cat(pos, 0).to(dev)
+        inv = 1.0 / (10000.0 ** (torch.arange(16, device=dev, dtype=torch.float32) * 2 / 32))
+        ang = (P[:, :, None] * inv[None, None, :]).reshape(P.shape[0], 48)
+        return ang.cos().to(torch.bfloat16).contiguous(), ang.sin().to(torch.bfloat16).contiguous()
+
+    @staticmethod
+    def _rowmap(c, i, dev):
+        """buildTimestepPlanGlobal + buildRowModMap: text/video rows use the step's t row, cond rows the aug t."""
+        import torch
+        from wuxianhuabu_b200 import h3
+        t_row, cond_row = i % 4, 3
+        g_text, g = c["text"], c["g"]
+        runs = [h3.ModRun(0, g_text, t_row * 3 + 0)]
+        if g > g_text:
+            runs.append(h3.ModRun(g_text, g, cond_row * 3 + 1))
+        runs.append(h3.ModRun(g, c["S"], t_row * 3 + 2))
+        m = h3.H3FusedKernels.build_row_mod_map(c["S"], runs)
+        return torch.from_numpy(m.view(np.int32)).to(dev)
+
+    def step(self, i: int) -> None:
+        """One sampler step (H3Pipeline.swift:1398-1445) at window position i."""
+        h3, m, c = self.h3, self.m, self.m.c
+        pos = i % WINDOW
+        refresh = self.plan[pos]
+        dsigma = self.sigmas[pos + 1] - self.sigmas[pos]
+        ctx = self.ctx
+        ctx.sync_stream()
+        # patch embed (fp32 island, H3Transformer.swift:1036-1039) -> bf16 packed stream
+        ctx.call("wx_dense_f32", self.x_in.data_ptr(), self.n_embed, PATCH_DIM, m.w_embed.data_ptr(), c["hidden"],
+                 m.b_embed.data_ptr(), self.emb32.data_ptr())
+        ctx.call("wx_f32_to_bf16", self.emb32.data_ptr(), self.emb32.numel(), self.h[c["text"]:].data_ptr())
+        self.h[:c["text"]].copy_(m.text)
+        rm = self.rowmaps[pos]
+        m.dit.forward(self.h, m.mods, rm, self.cos, self.sin, self.sparse, c["g"], policy=h3.SparsePolicy.MIX,
+                      attn_bcast=self.pab, attn_refresh=refresh, sigma=self.sigmas[pos])
+        # final head on the video rows (H3Transformer.swift:1192-1203) + Euler (H3Pipeline.swift:1436-1443)
+        hv = self.h[c["g"]:]
+        ctx.call("wx_norm_modscale", hv.data_ptr(), c["video"], c["hidden"], m.final_norm.data_ptr(),
+                 m.final_mods[0][pos].data_ptr(), m.final_mods[1][pos].data_ptr(), None, EPS, self.head16.data_ptr())
+        ctx.call("wx_bf16_to_f32", self.head16.data_ptr(), self.head16.numel(), self.head32.data_ptr())
+        ctx.call("wx_dense_f32", self.head32.data_ptr(), c["video"], c["hidden"], m.w_out.data_ptr(), PATCH_DIM,
+                 m.b_out.data_ptr(), self.vel.data_ptr())
+        ctx.call("wx_euler_update", self.video_x.data_ptr(), self.vel.data_ptr(), self.vel.numel(), float(dsigma))
+
+
+# ------------------------------------------------------------------ CPU baseline
+def cpu_sample(c: dict, rows: int = 64, att_rows: int = 32, seed: int = 99) -> dict:
+    """Bounded sample of the step on the host cores with the oracle (the reference
+    algorithm restated in C): the four 6-bit linears on `rows` rows, the row kernels,
+    and one head's attention for `att_rows` strip rows (dense) and `att_rows` video
+    rows (strip + top-k kept blocks). Extrapolated to s/step over the PAB window."""
+    from oracle import oracle as O
+    hdn, inner, ffn, S, g, H = c["hidden"], c["inner"], c["ffn"], c["S"], c["g"], c["heads"]
+    t0 = time.perf_counter()
+    lin = {}
+    for i, (name, n, k) in enumerate([("qkv", 3 * inner, hdn), ("out", hdn, inner), ("fc1", ffn, hdn),
+                                      ("fc2", hdn, ffn)]):
+        lin[name] = O.quantize(O.normal_f32((n, k), seed, i, std=0.02))
+    x = O.normal_bf16((rows, hdn), seed, 10)
+    xi = O.normal_bf16((rows, inner), seed, 11)
+    xf = O.normal_bf16((rows, ffn), seed, 12)
+    q = O.normal_bf16((S, 1, 128), seed, 13)
+    k = O.normal_bf16((S, 1, 128), seed, 14)
+    v = O.normal_bf16((S, 1, 128), seed, 15)
+    prep = time.perf_counter() - t0
+
+    def tm(fn):
+        a = time.perf_counter()
+        fn()
+        return time.perf_counter() - a
+
+    # each oracle qlinear call expands its whole weight once (a per-layer cost) and then
+    # does per-row work: split the two so the extrapolation scales only the row part
+    t_dq = {n: tm(lambda n=n, k=k: O.dequantize(*lin[n], k)) for n, k in
+            (("qkv", hdn), ("out", inner), ("fc1", hdn), ("fc2", ffn))}
+    t_qkv = tm(lambda: O.qlinear(x, *lin["qkv"])) - t_dq["qkv"]
+    t_out = tm(lambda: O.qlinear(xi, *lin["out"])) - t_dq["out"]
+    t_fc1 = tm(lambda: O.qlinear(x, *lin["fc1"], epilogue=O.EPI_GELU)) - t_dq["fc1"]
+    t_fc2 = tm(lambda: O.qlinear(xf, *lin["fc2"])) - t_dq["fc2"]
+    w1 = O.normal_bf16((hdn,), seed, 16)
+    mods = O.normal_bf16((4, hdn), seed, 17)
+    rm = np.zeros(rows, np.uint32)
+    t_norm = tm(lambda: O.norm_modscale(x, w1, mods, mods, rm, EPS))
+    scale = float(1 / np.sqrt(128))
+    t_route = tm(lambda: O.topk_route(q, k, v, g, scale, TOPK_DENSITY))
+    route = O.topk_route(q, k, v, g, scale, TOPK_DENSITY)
+    route.update(g=g, block=128)
+    t_strip = tm(lambda: O.attention_rows(q, k, v, g, scale, 0, att_rows, route=route))
+    t_video = tm(lambda: O.attention_rows(q, k, v, g, scale, g, g + att_rows, route=route))
+    # extrapolation to the full step
+    per_row = lambda t: t / rows
+    gemm_attn_rows = per_row(t_qkv) + per_row(t_out) * (inner / inner)
+    gemm_mlp_rows = per_row(t_fc1) + per_row(t_fc2)
+    rowops = per_row(t_norm) * 4  # norm1, norm2, q/k rope (~norm cost), gate
+    attn_sparse = H * (t_strip / att_rows * g + t_video / att_rows * (S - g)) + H * t_route
+    attn_dense = H * (t_strip / att_rows * S)
+    L = c["layers"]
+    n_dense = sum(1 for lyr in range(L) if _is_dense(lyr, L))
+    dq_attn = t_dq["qkv"] + t_dq["out"]
+    dq_mlp = t_dq["fc1"] + t_dq["fc2"]
+    refresh_step = (L * (S * (gemm_attn_rows + gemm_mlp_rows + rowops) + dq_attn + dq_mlp)
+                    + n_dense * attn_dense + (L - n_dense) * attn_sparse)
+    reuse_step = L * (S * (gemm_mlp_rows + rowops * 0.5) + dq_mlp)
+    plan = [True, True, False, True]
+    s_per_step = sum(refresh_step if r else reuse_step for r in plan) / len(plan)
+    sampled = t_qkv + t_out + t_fc1 + t_fc2 + sum(t_dq.values()) * 2 + t_norm + t_route + t_strip + t_video
+    return dict(value=s_per_step, sampled_s=sampled, prep_s=prep,
+                sample=(f"oracle (C, OpenMP) on {rows} rows through the 4 six-bit linears + row kernels and 1 of {H} "
+                        f"heads' attention for {att_rows} strip + {att_rows} video query rows at S={S}; "
+                        f"extrapolated linearly in rows/heads/layers over the PAB window {plan}"))
+
+
+# ------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
+    ap.add_argument("--config", default="c5", choices=list(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    c = geometry(args.config)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    base_cfg = dict(workload=f"{args.config}: " + ("720p x 121f step, 4 ref images, PAB window" if args.config == "c5"
+                                                   else "DiT step"),
+                    S=c["S"], strip_rows=c["g"], video_rows=c["video"], layers=c["layers"], hidden=c["hidden"],
+                    heads=c["heads"], ffn=c["ffn"], weights="6-bit affine g64", attention="mix: dense anchors + top-k 25% (128 blocks)",
+                    pab=dict(k=PAB_K, max_stale=PAB_MAX_STALE, window=WINDOW), global_batch=1, seq_len=c["S"],
+                    parallelism=f"ulysses{world}" if world > 1 else "single", l2="inputs larger than L2 (h 0.78 GB, weights 4.4 GB)")
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import oracle as O
+        O.build()
+        vals = []
+        for i in range(args.warmup + args.steps):
+            r = cpu_sample(c)
+            if i >= args.warmup:
+                vals.append(r["value"])
+        v = float(np.mean(vals))
+        line = dict(metric=METRIC, value=v, unit="s/step", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
+                    ms_per_step=v * 1e3, higher_is_better=False, scaling="strong", vs_baseline=None, dtype="bf16",
+                    data="synthetic", config=base_cfg, impl="reference",
+                    cpu_baseline=dict(value=v, unit="s/step", cores=O.num_threads(), kind="port", sample=r["sample"]),
+                    e2e=dict(value=v, unit="s/step", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
+                    note="reference = the oracle's C restatement of the reference's MLX/Metal algorithm; "
+                         "Swift/MLX/Metal cannot run on this box")
+        print(json.dumps(line))
+        return
+
+    import torch
+    if world > 1:
+        raise SystemExit("multi-GPU Ulysses step is not available in this build")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from wuxianhuabu_b200 import h3
+    peaks, peaks_kind = load_peaks()
+    model = Model(c, dev)
+    run = Runner(model)
+    ctx = run.ctx
+    lib = ctx.lib
+    # warm-up along the window
+    for i in range(args.warmup):
+        run.step(i)
+    torch.cuda.synchronize()
+    ctx.check_device()
+    # timed region (device-resident inputs)
+    clocks = ClockSampler(local)
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    lib.wx_ctx_profile_enable(ctx.h, 1)
+    n0 = lib.wx_ctx_launch_count(ctx.h)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.warmup, args.warmup + args.steps):
+        run.step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    n1 = lib.wx_ctx_launch_count(ctx.h)
+    clk = clocks.stop()
+    import ctypes
+    ms = (ctypes.c_double * 6)()
+    cnt = (ctypes.c_int64 * 6)()
+    lib.wx_ctx_profile_read(ctx.h, ms, cnt, 6)
+    lib.wx_ctx_profile_enable(ctx.h, 0)
+    ctx.check_device()
+    total_ms = e0.elapsed_time(e1)
+    s_per_step = total_ms / 1e3 / args.steps
+    positions = [i % WINDOW for i in range(args.warmup, args.warmup + args.steps)]
+    n_refresh = sum(1 for p in positions if run.plan[p])
+    fl = [step_flops(c, run.plan[p]) for p in positions]
+    gemm_flops = sum(f["gemm"] for f in fl)
+    attn_flops = sum(f["attn"] for f in fl)
+    kinds = ["qgemm", "attention", "routing", "row_kernels", "dequant", "other"]
+    prof = {k: dict(ms=float(ms[i]), launches=int(cnt[i])) for i, k in enumerate(kinds)}
+    attn_ms = prof["attention"]["ms"]
+    gemm_ms = prof["qgemm"]["ms"]
+    attn_launches = max(1, prof["attention"]["launches"])
+    peak_t = peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"])
+    ach_attn = attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms > 0 else 0.0
+    ach_gemm = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+    dominant = "attention" if attn_ms >= gemm_ms else "qgemm"
+    if dominant == "attention":
+        roof = dict(kernel="flash_attn_kernel (tcgen05 sparse/dense flash attention)", bound="tensor",
+                    achieved=ach_attn, peak=peak_t, unit="TFLOP/s", frac=ach_attn / peak_t,
+                    flops_per_launch=attn_flops / attn_launches, avg_launch_ms=attn_ms / attn_launches,
+                    traffic=None, peak_kind=f"{peaks_kind} sustained bf16")
+    else:
+        roof = dict(kernel="gemm_bf16_tc_kernel", bound="tensor", achieved=ach_gemm, peak=peak_t, unit="TFLOP/s",
+                    frac=ach_gemm / peak_t, traffic=None, peak_kind=f"{peaks_kind} sustained bf16")
+    line = dict(metric=METRIC, value=s_per_step, unit="s/step", n_gpus=world, steps=args.steps, warmup=args.warmup,
+                ms_per_step=s_per_step * 1e3, higher_is_better=False, scaling="strong", vs_baseline=None,
+                dtype="bf16", data="synthetic", config=dict(base_cfg, refresh_steps=n_refresh,
+                                                            reuse_steps=args.steps - n_refresh),
+                roofline=roof,
+                qgemm=dict(tflops=ach_gemm, frac=ach_gemm / peak_t, ms=gemm_ms, launches=prof["qgemm"]["launches"],
+                           flops=gemm_flops, peak_kind=f"{peaks_kind} sustained bf16"),
+                kernel_ms=prof, gpu_launches=int(n1 - n0), clocks=clk)
+    # e2e through the public API with host buffers (pinned H2D of the latent, D2H of the updated latent)
+    if not args.no_e2e:
+        host_in = torch.empty(run.video_x.shape, dtype=torch.float32, pin_memory=True)
+        host_in.copy_(run.video_x)
+        host_out = torch.empty_like(host_in, pin_memory=True)
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for i in range(args.warmup, args.warmup + args.steps):
+            run.video_x.copy_(host_in, non_blocking=True)
+            run.step(i)
+            host_out.copy_(run.video_x, non_blocking=True)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e2e = f0.elapsed_time(f1) / 1e3 / args.steps
+        nbytes = run.video_x.numel() * 4
+        line["e2e"] = dict(value=e2e, unit="s/step", h2d_bytes_per_step=nbytes, d2h_bytes_per_step=nbytes,
+                           finite=bool(torch.isfinite(host_out).all().item()))
+    if not args.no_cpu_baseline and rank == 0:
+        from oracle import oracle as O
+        O.build()
+        r = cpu_sample(c)
+        line["cpu_baseline"] = dict(value=r["value"], unit="s/step", cores=O.num_threads(), kind="port",
+                                    sample=r["sample"], sampled_s=r["sampled_s"])
+    if rank == 0:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -127,7 +127,16 @@ const char* wx_last_error(wx_ctx* ctx);
 int wx_ctx_check_device(wx_ctx* ctx);
 /* bytes currently held by the context workspace arena */
 size_t wx_ctx_workspace_bytes(wx_ctx* ctx);
+/* number of kernels this context has launched so far */
+int64_t wx_ctx_launch_count(wx_ctx* ctx);
 int wx_version(void);
+/* Device timing by kernel class (0 qGEMM, 1 flash attention, 2 routing + list
+ * build, 3 row kernels, 4 weight dequant, 5 other): while enabled, CUDA events
+ * bracket each launch on the context stream. enable(…, 0/1) clears the record;
+ * read() synchronises, returns the summed milliseconds and launch counts of the
+ * first nkinds classes since the last enable/read, and clears the record. */
+int wx_ctx_profile_enable(wx_ctx* ctx, int enable);
+int wx_ctx_profile_read(wx_ctx* ctx, double* ms, int64_t* launches, int nkinds);
 
 /* ---------------------------------------------------- quantized linear */
 /* Affine group quantization of fp32 w [n, k] (the offline step of

@@ -35,6 +35,8 @@ _SIGS = {
                               _vp, _vp, _vp, _vp, _vp]),
     "wxo_sparse_attention": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i64, _i32, _f32, _vp, _vp, _vp, _vp,
                                     _i32, _vp, _i64]),
+    "wxo_sparse_attention_rows": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i64, _i32, _f32, _vp, _vp, _vp,
+                                         _vp, _i32, _i64, _i64, _vp, _i64]),
     "wxo_dense_f32": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "wxo_num_threads": (_i32, []),
 }
@@ -203,6 +205,19 @@ def sparse_attention(q, k, v, g: int, scale: float, block: int = 64, route=None,
                                         _ptr(route["sel"]), _ptr(route["cm"]), _ptr(route["vsum"]),
                                         _ptr(route["lens"]), int(tail), _ptr(out), H * hd), "attention")
     return out
+
+
+def attention_rows(q, k, v, g: int, scale: float, row0: int, row1: int, block: int = 128, route=None,
+                   tail: bool = False):
+    """Attention output for query rows [row0, row1) only; q/k/v [S, H, hd] uint16."""
+    S, H, hd = q.shape
+    out = np.zeros((S, H, hd), dtype=np.uint16)
+    r = route or {}
+    _chk(lib().wxo_sparse_attention_rows(_ptr(q), _ptr(k), _ptr(v), H * hd, S, H, hd, g if route else 0, block,
+                                         scale, _ptr(r.get("sel")), _ptr(r.get("cm")), _ptr(r.get("vsum")),
+                                         _ptr(r.get("lens")), int(tail), row0, row1, _ptr(out), H * hd),
+         "attention_rows")
+    return out[row0:row1]
 
 
 def dense_f32(x, w, b=None):

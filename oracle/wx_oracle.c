@@ -380,6 +380,18 @@ int wxo_sol_route(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64
   return 0;
 }
 
+typedef struct {
+  float s;
+  int j;
+} scored_idx;
+
+static int cmp_scored_desc(const void* a, const void* b) {
+  const scored_idx* x = (const scored_idx*)a;
+  const scored_idx* y = (const scored_idx*)b;
+  if (x->s != y->s) return x->s > y->s ? -1 : 1;
+  return x->j < y->j ? -1 : (x->j > y->j);
+}
+
 int wxo_topk_route(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t row_stride,
                    int64_t S, int H, int hd, int64_t g, int block, float scale, float density,
                    uint8_t* sel, float* scores, uint16_t* cm, uint16_t* vsum, float* lens) {
@@ -403,16 +415,20 @@ int wxo_topk_route(const uint16_t* q, const uint16_t* k, const uint16_t* v, int6
         cm[((int64_t)h * nb + i) * nb + j] = wxo_f2bf(sr[j]);
       }
       uint8_t* selr = sel + ((int64_t)h * nb + i) * nb;
-      /* rank of j among the off-diagonal blocks: higher score first, lower index on ties */
+      /* order the off-diagonal blocks: higher score first, lower index on ties */
+      scored_idx* ord = (scored_idx*)malloc((size_t)nb * sizeof(scored_idx));
+      int n = 0;
       for (int j = 0; j < nb; ++j) {
-        if (j == i) { selr[j] = 1; continue; }
-        int rank = 0;
-        for (int t = 0; t < nb; ++t) {
-          if (t == i || t == j) continue;
-          if (sr[t] > sr[j] || (sr[t] == sr[j] && t < j)) ++rank;
+        selr[j] = (uint8_t)(j == i);
+        if (j != i) {
+          ord[n].s = sr[j];
+          ord[n].j = j;
+          ++n;
         }
-        selr[j] = (uint8_t)(rank < keep);
       }
+      qsort(ord, (size_t)n, sizeof(scored_idx), cmp_scored_desc);
+      for (int t = 0; t < keep && t < n; ++t) selr[ord[t].j] = 1;
+      free(ord);
     }
   free(qc);
   free(kc);
@@ -446,13 +462,22 @@ int wxo_sparse_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v
                          int64_t S, int H, int hd, int64_t g, int block, float scale,
                          const uint8_t* sel, const uint16_t* cm, const uint16_t* vsum,
                          const float* lens, int tail, uint16_t* out, int64_t out_stride) {
-  if (hd > 256 || S <= 0) return -1;
+  return wxo_sparse_attention_rows(q, k, v, row_stride, S, H, hd, g, block, scale, sel, cm, vsum, lens, tail,
+                                   0, S, out, out_stride);
+}
+
+int wxo_sparse_attention_rows(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t row_stride,
+                              int64_t S, int H, int hd, int64_t g, int block, float scale,
+                              const uint8_t* sel, const uint16_t* cm, const uint16_t* vsum,
+                              const float* lens, int tail, int64_t row0, int64_t row1,
+                              uint16_t* out, int64_t out_stride) {
+  if (hd > 256 || S <= 0 || row0 < 0 || row1 > S || row0 > row1) return -1;
   if (sel && (S <= g || block <= 0)) return -1;
   const int64_t L = S - g;
   const int nb = sel ? (int)((L + block - 1) / block) : 0;
 #pragma omp parallel for collapse(2) schedule(dynamic, 8)
   for (int h = 0; h < H; ++h)
-    for (int64_t s = 0; s < S; ++s) {
+    for (int64_t s = row0; s < row1; ++s) {
       soft_state st;
       st.m = -INFINITY;
       st.l = 0.f;

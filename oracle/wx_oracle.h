@@ -121,6 +121,14 @@ int wxo_sparse_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v
                          const uint8_t* sel, const uint16_t* cm, const uint16_t* vsum,
                          const float* lens, int tail, uint16_t* out, int64_t out_stride);
 
+/* the same for query rows [row0, row1) only (bounded CPU-baseline samples);
+ * out rows outside the range are not written */
+int wxo_sparse_attention_rows(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t row_stride,
+                              int64_t S, int H, int hd, int64_t g, int block, float scale,
+                              const uint8_t* sel, const uint16_t* cm, const uint16_t* vsum,
+                              const float* lens, int tail, int64_t row0, int64_t row1,
+                              uint16_t* out, int64_t out_stride);
+
 /* fp32 dense linear y[m][n] = sum_k x[m][k]*w[k][n] + b[n] (H3TensorOps.denseLinear,
  * the fp32 patch-embed / final-head islands, H3Transformer.swift:1036-1039, 1192-1203) */
 int wxo_dense_f32(const float* x, int64_t m, int64_t k, const float* w, int64_t n,

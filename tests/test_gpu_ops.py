@@ -158,10 +158,10 @@ def test_qk_norm_rope_packed_qkv_in_place(torch_mod):
     rq = O.qk_norm_rope(np.ascontiguousarray(qkv[:, :inner].reshape(S, H, hd)), qw, cos, sin, rot, eps)
     rk = O.qk_norm_rope(np.ascontiguousarray(qkv[:, inner:2 * inner].reshape(S, H, hd)), kw, cos, sin, rot, eps)
     t = to_torch_bf16(qkv)
+    keep = [to_torch_bf16(a) for a in (qw, kw, cos, sin)]  # alive until the kernel has run
     ctx = h3.context()
-    ctx.call("wx_qk_norm_rope_qkv", t.data_ptr(), S, H, hd, to_torch_bf16(qw).data_ptr(),
-             to_torch_bf16(kw).data_ptr(), to_torch_bf16(cos).data_ptr(), to_torch_bf16(sin).data_ptr(), rot,
-             float(eps))
+    ctx.call("wx_qk_norm_rope_qkv", t.data_ptr(), S, H, hd, *[a.data_ptr() for a in keep], rot, float(eps))
+    torch.cuda.synchronize()
     out = to_np_bf16(t)
     assert_close(f32(out[:, :inner]), f32(rq.reshape(S, inner)), rel=1e-2, cos=0.99999, what="q")
     assert_close(f32(out[:, inner:2 * inner]), f32(rk.reshape(S, inner)), rel=1e-2, cos=0.99999, what="k")

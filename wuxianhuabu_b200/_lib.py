@@ -72,6 +72,9 @@ _SIGS = {
     "wx_last_error": (C.c_char_p, [_vp]),
     "wx_ctx_check_device": (_i32, [_vp]),
     "wx_ctx_workspace_bytes": (C.c_size_t, [_vp]),
+    "wx_ctx_launch_count": (_i64, [_vp]),
+    "wx_ctx_profile_enable": (_i32, [_vp, _i32]),
+    "wx_ctx_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "wx_quantize_affine": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "wx_dequantize_affine": (_i32, [_vp, C.POINTER(QWeight), _vp]),
     "wx_qlinear": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),

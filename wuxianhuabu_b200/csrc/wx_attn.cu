@@ -708,6 +708,7 @@ static int run_routing(wx_ctx* ctx, const void* q, const void* k, const void* v,
   auto Q = static_cast<const __nv_bfloat16*>(q);
   auto K = static_cast<const __nv_bfloat16*>(k);
   auto V = static_cast<const __nv_bfloat16*>(v);
+  ProfScope prof(ctx, kProfRoute);
   block_stats_kernel<<<dim3(a.nb, a.H), a.hd, 0, ctx->stream>>>(Q, K, V, rs, a.S, a.hd, a.g, a.block, a.nb, qc, kc,
                                                                   vsum, lens);
   int st = launch_status(ctx, "block_stats");
@@ -720,7 +721,7 @@ static int run_routing(wx_ctx* ctx, const void* q, const void* k, const void* v,
   dim3 sg((a.nb + 31) / 32, (a.nb + 7) / 8, a.H);
   score_kernel<<<sg, 256, 0, ctx->stream>>>(qc, kc, a.nb, a.hd, scale, spec->mode, thr, spec->sink_start,
                                            spec->sink_end, cm, sel, scores);
-  st = launch_status(ctx, "score");
+  st = launch_status(ctx, "score", spec->mode == WX_SPARSE_SOL ? 3 : 1);
   if (st) return st;
   if (spec->mode == WX_SPARSE_TOPK) {
     int P = 1;
@@ -760,7 +761,10 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
       base + c.take((size_t)a.H * a.nvt * (size_t)((a.nb + a.qpb - 1) / a.qpb + 1) * 16));
   WorkItem* items = reinterpret_cast<WorkItem*>(base + c.take((size_t)a.H * (a.nst + a.nvt) * sizeof(WorkItem)));
   const bool tail = !a.dense && spec->tail && cm && vsum && lens;
+  const int64_t n_items = (int64_t)a.H * (a.nst + a.nvt);
   int st;
+  {
+  ProfScope prof(ctx, kProfRoute);
   if (!a.dense) {
     if (tail) {
       tail_kernel<<<dim3(a.nb, a.H), a.hd, 0, ctx->stream>>>(sel, cm, vsum, lens, a.nb, a.hd, tT, tL, tC);
@@ -772,12 +776,13 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
     scan_kernel<<<1, 1024, 0, ctx->stream>>>(counts, a.H * a.nvt, offsets);
     list_fill_kernel<<<blocks, 256, 0, ctx->stream>>>(sel, a.H, a.nb, a.nvt, a.qpb, a.block, a.g, a.S, offsets,
                                                       entries);
-    if ((st = launch_status(ctx, "list build"))) return st;
+    if ((st = launch_status(ctx, "list build", 3))) return st;
   }
-  const int64_t n_items = (int64_t)a.H * (a.nst + a.nvt);
+
   items_kernel<<<(unsigned)((n_items + 127) / 128), 128, 0, ctx->stream>>>(a.H, a.nst, a.nvt, a.S, a.g, a.dense,
                                                                              a.qpb, a.nb, offsets, items);
   if ((st = launch_status(ctx, "items"))) return st;
+  }
 
   const int64_t cols = (int64_t)a.H * a.hd;
   CUtensorMap tq, tk, tv;
@@ -803,6 +808,7 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   p.out_stride = os;
   p.err = ctx->dev_err;
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
+  ProfScope prof(ctx, kProfAttn);
   flash_attn_kernel<<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
   return launch_status(ctx, "flash_attn");
 }

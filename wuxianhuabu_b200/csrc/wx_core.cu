@@ -84,10 +84,34 @@ int make_tmap_bf16_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t 
   return WX_OK;
 }
 
-int launch_status(wx_ctx* ctx, const char* what) {
+int launch_status(wx_ctx* ctx, const char* what, int n) {
+  ctx->launches += n;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
   return WX_OK;
+}
+
+static cudaEvent_t pool_event(wx_ctx* c) {
+  if (!c->prof_pool.empty()) {
+    cudaEvent_t e = c->prof_pool.back();
+    c->prof_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+ProfScope::ProfScope(wx_ctx* ctx, int kind) : c(ctx) {
+  if (!c || !c->prof) return;
+  wx_ctx::ProfRec r{kind, pool_event(c), pool_event(c)};
+  cudaEventRecord(r.a, c->stream);
+  c->prof_recs.push_back(r);
+  idx = (int)c->prof_recs.size() - 1;
+}
+
+ProfScope::~ProfScope() {
+  if (idx >= 0) cudaEventRecord(c->prof_recs[idx].b, c->stream);
 }
 
 // ------------------------------------------------------------ fp32 islands
@@ -180,6 +204,11 @@ int wx_ctx_destroy(wx_ctx* ctx) {
   if (!ctx) return WX_OK;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  for (auto& r : ctx->prof_recs) {
+    cudaEventDestroy(r.a);
+    cudaEventDestroy(r.b);
+  }
+  for (auto e : ctx->prof_pool) cudaEventDestroy(e);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   delete ctx;
@@ -195,6 +224,39 @@ int wx_ctx_set_stream(wx_ctx* ctx, void* stream) {
 const char* wx_last_error(wx_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
 
 size_t wx_ctx_workspace_bytes(wx_ctx* ctx) { return ctx ? ctx->ws_bytes : 0; }
+
+int64_t wx_ctx_launch_count(wx_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+int wx_ctx_profile_enable(wx_ctx* ctx, int enable) {
+  if (!ctx) return WX_ERR_INVALID;
+  for (auto& r : ctx->prof_recs) {
+    ctx->prof_pool.push_back(r.a);
+    ctx->prof_pool.push_back(r.b);
+  }
+  ctx->prof_recs.clear();
+  ctx->prof = enable != 0;
+  return WX_OK;
+}
+
+int wx_ctx_profile_read(wx_ctx* ctx, double* ms, int64_t* launches, int nkinds) {
+  if (!ctx || !ms || !launches || nkinds <= 0) return WX_ERR_INVALID;
+  WX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  for (int k = 0; k < nkinds; ++k) {
+    ms[k] = 0.0;
+    launches[k] = 0;
+  }
+  for (auto& r : ctx->prof_recs) {
+    float t = 0.f;
+    if (r.kind < nkinds && cudaEventElapsedTime(&t, r.a, r.b) == cudaSuccess) {
+      ms[r.kind] += t;
+      launches[r.kind] += 1;
+    }
+    ctx->prof_pool.push_back(r.a);
+    ctx->prof_pool.push_back(r.b);
+  }
+  ctx->prof_recs.clear();
+  return WX_OK;
+}
 
 int wx_ctx_check_device(wx_ctx* ctx) {
   if (!ctx) return WX_ERR_INVALID;

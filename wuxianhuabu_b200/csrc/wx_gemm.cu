@@ -273,6 +273,7 @@ static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap&
   p.tiles_n = p.N / BN;
   p.num_tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(p.num_tiles, ctx->num_sms);
+  ProfScope prof(ctx, kProfGemm);
   gemm_bf16_tc_kernel<BN><<<grid, kGemmThreads, L::kBytes, ctx->stream>>>(ta, tb, p);
   return launch_status(ctx, "gemm_bf16_tc");
 }

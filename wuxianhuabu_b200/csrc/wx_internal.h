@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <vector>
 
 #include "../../include/wx_api.h"
 
@@ -17,6 +18,15 @@ struct wx_ctx {
   void* ws = nullptr;             // workspace arena
   size_t ws_bytes = 0;
   std::string last_error;
+  int64_t launches = 0;  // kernels launched through this context
+  // per-kernel-class device timing (wx_ctx_profile_enable / _read)
+  bool prof = false;
+  struct ProfRec {
+    int kind;
+    cudaEvent_t a, b;
+  };
+  std::vector<ProfRec> prof_recs;
+  std::vector<cudaEvent_t> prof_pool;
 };
 
 namespace wx {
@@ -55,7 +65,20 @@ struct Carve {
 int make_tmap_bf16_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t rows,
                       uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows);
 
-int launch_status(wx_ctx* ctx, const char* what);
+// checks the last launch(es) and counts `n` kernel launches on the context
+int launch_status(wx_ctx* ctx, const char* what, int n = 1);
+
+enum ProfKind { kProfGemm = 0, kProfAttn = 1, kProfRoute = 2, kProfRow = 3, kProfDequant = 4, kProfOther = 5,
+                kProfKinds = 6 };
+
+// Records CUDA events around the launches of one kernel class on the
+// context stream while profiling is enabled (no-op otherwise).
+struct ProfScope {
+  wx_ctx* c;
+  int idx = -1;
+  ProfScope(wx_ctx* ctx, int kind);
+  ~ProfScope();
+};
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

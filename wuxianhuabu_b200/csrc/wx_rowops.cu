@@ -296,6 +296,7 @@ int launch_swiglu(wx_ctx* ctx, const void* t, int64_t m, int64_t F, int64_t ldt,
 }
 
 int launch_dequant(wx_ctx* ctx, const wx_qweight* w, void* out) {
+  ProfScope prof(ctx, kProfDequant);
   dequant_kernel<<<grid_for(w->n * (w->k / 8), 256, ctx->num_sms), 256, 0, ctx->stream>>>(
       w->wq, static_cast<const __nv_bfloat16*>(w->scales), static_cast<const __nv_bfloat16*>(w->biases),
       w->n, w->k, w->group, w->bits, static_cast<__nv_bfloat16*>(out));
@@ -315,6 +316,7 @@ int launch_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, void* out,
   const int64_t rows = S * nparts * H;
   if (rows == 0) return WX_OK;
   const unsigned grid = (unsigned)((rows + 7) / 8);
+  ProfScope prof(ctx, kProfRow);
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto O = static_cast<__nv_bfloat16*>(out);
   auto W0 = static_cast<const __nv_bfloat16*>(w0);
@@ -333,6 +335,7 @@ int launch_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, void* out,
 int launch_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w,
                          const void* shift, const void* scale, const uint32_t* rowmap, float eps, void* out) {
   if (S == 0) return WX_OK;
+  ProfScope prof(ctx, kProfRow);
   norm_modscale_kernel<<<(unsigned)((S + 7) / 8), 256, 0, ctx->stream>>>(
       static_cast<const __nv_bfloat16*>(x), S, (int)hidden, static_cast<const __nv_bfloat16*>(w),
       static_cast<const __nv_bfloat16*>(shift), static_cast<const __nv_bfloat16*>(scale), rowmap, eps,
@@ -344,6 +347,7 @@ int launch_mod_gate(wx_ctx* ctx, const void* x, const void* other, const void* g
                     int64_t S, int64_t hidden, void* out) {
   if (S == 0) return WX_OK;
   const int64_t total = (hidden % 8 == 0) ? S * hidden / 8 : S * hidden;
+  ProfScope prof(ctx, kProfRow);
   mod_gate_kernel<<<grid_for(total, 256, ctx->num_sms), 256, 0, ctx->stream>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(other),
       static_cast<const __nv_bfloat16*>(gate), rowmap, S, (int)hidden, static_cast<__nv_bfloat16*>(out));
