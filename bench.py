@@ -364,6 +364,83 @@ def cpu_sample(c: dict, rows: int = 64, att_rows: int = 32, seed: int = 99) -> d
                         f"extrapolated linearly in rows/heads/layers over the PAB window {plan}"))
 
 
+# ------------------------------------------------------------------ kernel-level configs
+def run_c3(args, seq: int) -> dict:
+    """standalone block-sparse attention (24 x 128 heads,
+    128-row blocks, diagonal + top-k 25 %, g = 0, no tail), routing included."""
+    import torch
+    from wuxianhuabu_b200 import h3
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1234 + 2)
+    H = 24
+    q, k, v = [torch.randn((seq, H, 128), device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
+    out = torch.empty_like(q)
+    cfg = h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False)
+    scale = float(1 / math.sqrt(128))
+    ctx = h3.context(0)
+    for _ in range(args.warmup):
+        h3.H3SolAttn.forward(q, k, v, 0, scale, cfg, out=out)
+    torch.cuda.synchronize()
+    import ctypes
+    ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        h3.H3SolAttn.forward(q, k, v, 0, scale, cfg, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = (ctypes.c_double * 6)()
+    cnt = (ctypes.c_int64 * 6)()
+    ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 6)
+    ctx.check_device()
+    nb = (seq + 127) // 128
+    keep = min(math.ceil(TOPK_DENSITY * nb), nb - 1) + 1
+    flops = 4.0 * 128 * H * seq * min(keep * 128, seq)
+    peaks, kind = load_peaks()
+    per_call = e0.elapsed_time(e1) / args.steps
+    flash_ms = ms[1] / max(1, cnt[1])
+    ach = flops / (flash_ms / 1e3) / 1e12
+    pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    return dict(metric="sparse attention ms/call (c3)", value=per_call, unit="ms/call", config=dict(
+        workload=f"c3: SOL top-k 25% attention, S={seq}, 24x128 heads", S=seq), higher_is_better=False,
+        roofline=dict(kernel="flash_attn_kernel", bound="tensor", achieved=ach, peak=pk, unit="TFLOP/s",
+                      frac=ach / pk, avg_launch_ms=flash_ms, flops_per_launch=flops, peak_kind=f"{kind} burst bf16"),
+        routing_ms=ms[2] / max(1, args.steps))
+
+
+def run_c2(args) -> dict:
+    """the 6-bit quantized linear sweep."""
+    import torch
+    from wuxianhuabu_b200 import h3
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1234 + 1)
+    peaks, kind = load_peaks()
+    pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    res = []
+    for (K, N) in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]:
+        lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02)
+        for M in (256, 4096, 28520, 111600):
+            x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+            for _ in range(max(1, args.warmup)):
+                lin(x, out=y)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            reps = max(1, args.steps)
+            for _ in range(reps):
+                lin(x, out=y)
+            e1.record()
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1) / reps / 1e3
+            fl = 2.0 * M * N * K
+            byts = 2 * M * K + 0.75 * N * K + 4 * N * (K // 64) + 2 * M * N
+            res.append(dict(M=M, K=K, N=N, ms=t * 1e3, tflops=fl / t / 1e12, frac=fl / t / 1e12 / pk,
+                            gbs=byts / t / 1e9))
+            del x, y
+    return dict(metric="6-bit qGEMM sweep (c2)", unit="TFLOP/s", peak=pk, peak_kind=f"{kind} burst bf16", sweep=res)
+
+
 # ------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -371,10 +448,16 @@ def main():
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
-    ap.add_argument("--config", default="c5", choices=list(CONFIGS))
+    ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c3", "c3full", "c2"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
+    if args.config in ("c3", "c3full", "c2"):
+        import torch
+        torch.cuda.set_device(0)
+        r = run_c2(args) if args.config == "c2" else run_c3(args, 28520 if args.config == "c3" else 111600)
+        print(json.dumps(r))
+        return
     c = geometry(args.config)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
