@@ -154,6 +154,21 @@ int wx_qlinear(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qwei
                int epilogue, const void* gate, const void* resid, const uint32_t* rowmap,
                void* y, int64_t ldy, void* y_raw);
 
+/* No counterpart in the reference. wx_qlinear for callers that cannot allocate
+ * device memory (a host whose engine or restricted allocator owns every device
+ * allocation, or a plugin handed only a stream and tensors): it takes a
+ * cudaStream_t instead of a context and allocates nothing. The expanded bf16
+ * weight lives in a 64 MiB static device array inside libwx, created on every
+ * GPU that loads the library and held until exit, so w->n * w->k may be at
+ * most 33,554,432; larger weights, and WX_EPI_SWIGLU, are rejected
+ * (WX_ERR_INVALID / WX_ERR_UNSUPPORTED). The first call on a device looks up
+ * the array's address (cudaGetSymbolAddress); make that first call before any
+ * stream capture. All calls share the array: calls that overlap on the GPU
+ * race. Other arguments and results are those of wx_qlinear. */
+int wx_qlinear_noalloc(void* stream, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                       int epilogue, const void* gate, const void* resid, const uint32_t* rowmap,
+                       void* y, int64_t ldy, void* y_raw);
+
 /* ------------------------------------------------------ fused row ops */
 /* H3FusedKernels.fusedRmsnormRope (网络算子-融合-RMSNormRoPE-通用.swift:111-129):
  * rows (s, h) of head_dim at x[s*x_stride + h*head_dim]; cos/sin [S, rot/2] bf16;

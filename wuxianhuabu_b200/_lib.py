@@ -78,6 +78,7 @@ _SIGS = {
     "wx_quantize_affine": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "wx_dequantize_affine": (_i32, [_vp, C.POINTER(QWeight), _vp]),
     "wx_qlinear": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "wx_qlinear_noalloc": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
     "wx_qk_norm_rope": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _i32, _f32, _vp, _i64]),
     "wx_qk_norm_rope_qkv": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _f32]),
     "wx_norm_modscale": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _f32, _vp]),
