@@ -305,7 +305,9 @@ __global__ void list_fill_kernel(const uint8_t* __restrict__ sel, int H, int nb,
   }
 }
 
-// thread per item: strip/dense items first (all heads), then video tiles
+// thread per item: strip/dense items first (the heaviest), then video tiles;
+// head-major within each group so that the CTAs resident at one time share
+// one head's K/V in L2
 __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int dense_all, int qpb, int nb,
                              const int* __restrict__ offsets, WorkItem* __restrict__ items) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
@@ -316,8 +318,8 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
   it.pad0 = it.pad1 = it.pad2 = 0;
   const int kt_all = (int)((S + 127) / 128);
   if (i < n_strip) {
-    const int t = (int)(i / H);
-    it.head = (int)(i % H);
+    const int t = (int)(i % nst);
+    it.head = (int)(i / nst);
     it.q_start = t * 128;
     const int64_t lim = dense_all ? S : g;
     it.q_rows = (int)min64(128, lim - (int64_t)t * 128);
@@ -328,8 +330,8 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
     it.implicit_end = (int)S;
   } else {
     const int64_t j = i - n_strip;
-    const int t = (int)(j / H);
-    const int h = (int)(j % H);
+    const int t = (int)(j % nvt);
+    const int h = (int)(j / nvt);
     it.head = h;
     it.q_start = (int)(g + (int64_t)t * 128);
     it.q_rows = (int)min64(128, S - it.q_start);
@@ -345,288 +347,7 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
 }
 
 // ------------------------------------------------------------ 5. flash kernel
-constexpr int kAttnThreads = 192;
-constexpr int kTileBytes = 128 * 128 * 2;  // one 128x128 bf16 operand tile
-constexpr int kAttnSmem = 6 * kTileBytes + 256 + 1024;
-
-struct AttnParams {
-  const WorkItem* items;
-  const int4* entries;
-  const float* tailT;
-  const float* tailL;
-  const float* tailC;
-  int nqb;
-  int H;
-  float sl2;  // softmax scale * log2(e)
-  __nv_bfloat16* out;
-  int64_t out_stride;
-  int* err;
-};
-
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ void kv_entry(const WorkItem& it, const int4* entries, int j, int& s0, int& s1,
-                                         int& w0, int& w1) {
-  if (j < it.n_implicit) {
-    s0 = j * 128;
-    s1 = s0 + 64;
-    w0 = max(0, min(64, it.implicit_end - s0)) | (3 << 8);
-    w1 = max(0, min(64, it.implicit_end - s1)) | (3 << 8);
-  } else {
-    const int4 e = entries[it.list_begin + (j - it.n_implicit)];
-    s0 = e.x;
-    s1 = e.y;
-    w0 = e.z;
-    w1 = e.w;
-  }
-}
-
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                      const __grid_constant__ CUtensorMap tmV, AttnParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK[2] = {smem + kTileBytes, smem + 3 * kTileBytes};
-  uint8_t* sV[2] = {smem + 2 * kTileBytes, smem + 4 * kTileBytes};
-  uint8_t* sP = smem + 5 * kTileBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 6 * kTileBytes);
-  // q_full, kv_full[2], kv_empty[2], s_full[2], p_full, o_done
-  const uint32_t q_full = smem_u32(bars + 0);
-  const uint32_t kv_full[2] = {smem_u32(bars + 1), smem_u32(bars + 2)};
-  const uint32_t kv_empty[2] = {smem_u32(bars + 3), smem_u32(bars + 4)};
-  const uint32_t s_full[2] = {smem_u32(bars + 5), smem_u32(bars + 6)};
-  const uint32_t p_full = smem_u32(bars + 7);
-  const uint32_t o_done = smem_u32(bars + 8);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const WorkItem it = p.items[blockIdx.x];
-  const int n_kv = it.n_implicit + it.list_len;
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(kv_full[i], 1);
-      mbar_init(kv_empty[i], 1);
-      mbar_init(s_full[i], 1);
-    }
-    mbar_init(p_full, 128);
-    mbar_init(o_done, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // S0: cols [0,128), S1: [128,256), O: [256,384)
-  const int hcol = it.head * 128;
-
-  if (warp == 0) {
-    if (lane == 0 && n_kv > 0) {
-      prefetch_tmap(&tmQ);
-      prefetch_tmap(&tmK);
-      prefetch_tmap(&tmV);
-      mbar_arrive_expect_tx(q_full, kTileBytes);
-      for (int ch = 0; ch < 2; ++ch)
-        for (int rh = 0; rh < 2; ++rh)
-          tma_load_2d(smem_u32(sQ + ch * 16384 + rh * 8192), &tmQ, q_full, hcol + ch * 64, it.q_start + rh * 64);
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(kv_empty[st], ((j >> 1) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
-        int s0, s1, w0, w1;
-        kv_entry(it, p.entries, j, s0, s1, w0, w1);
-        mbar_arrive_expect_tx(kv_full[st], 2 * kTileBytes);
-        for (int ch = 0; ch < 2; ++ch) {
-          const uint32_t ko = smem_u32(sK[st] + ch * 16384), vo = smem_u32(sV[st] + ch * 16384);
-          tma_load_2d(ko, &tmK, kv_full[st], hcol + ch * 64, s0);
-          tma_load_2d(ko + 8192, &tmK, kv_full[st], hcol + ch * 64, s1);
-          tma_load_2d(vo, &tmV, kv_full[st], hcol + ch * 64, s0);
-          tma_load_2d(vo + 8192, &tmV, kv_full[st], hcol + ch * 64, s1);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0 && n_kv > 0) {
-      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);  // B = V, MN-major
-      const uint32_t qa = smem_u32(sQ), pa = smem_u32(sP);
-      bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutFull, abort_flag);
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(kv_full[st], (j >> 1) & 1, p.err, kDevTimeoutFull, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t ka = smem_u32(sK[st]);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tmem + st * 128, smem_desc_sw128(qa + off, 16, 1024), smem_desc_sw128(ka + off, 16, 1024),
-                    idesc_s, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(s_full[st]);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) break;
-        if (!mbar_wait(p_full, j & 1, p.err, kDevTimeoutSoftmax, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t va = smem_u32(sV[j & 1]);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = smem_desc_sw128(pa + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = smem_desc_sw128(va + kk * 2048, 16384, 1024);
-          umma_bf16(tmem + 256, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(o_done);
-        umma_commit(kv_empty[j & 1]);
-      }
-    }
-  } else {
-    // softmax / correction / epilogue warps: thread owns TMEM lane (= q row) r
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const int qh = r >> 6;
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      int s0, s1, w0, w1;
-      kv_entry(it, p.entries, j, s0, s1, w0, w1);
-      const int b = j & 1;
-      if (!mbar_wait(s_full[b], (j >> 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      float sv[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float t[32];
-        tmem_ld32(tmem + lane_addr + b * 128 + c * 32, t);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = t[i];
-      }
-      tmem_wait_ld();
-      const int len0 = w0 & 0xFF, len1 = w1 & 0xFF;
-      const bool on0 = (w0 >> (8 + qh)) & 1, on1 = (w1 >> (8 + qh)) & 1;
-      const int lim0 = on0 ? len0 : 0, lim1 = on1 ? len1 : 0;
-      float rmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const bool valid = (c < 64) ? (c < lim0) : ((c - 64) < lim1);
-        sv[c] = valid ? sv[c] * p.sl2 : -INFINITY;
-        rmax = fmaxf(rmax, sv[c]);
-      }
-      const float m_new = fmaxf(m, rmax);
-      if (j > 0) {
-        if (!mbar_wait(o_done, (j - 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
-      bool need = false;
-      if (j == 0) {
-        m = m_new;
-      } else {
-        need = m_new > m + 8.0f;
-      }
-      if (__any_sync(0xffffffffu, need)) {
-        const float alpha = need ? ex2(m - m_new) : 1.0f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float t[32];
-          tmem_ld32(tmem + lane_addr + 256 + c * 32, t);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) t[i] *= alpha;
-          tmem_st32(tmem + lane_addr + 256 + c * 32, t);
-        }
-        tmem_wait_st();
-        l *= alpha;
-        if (need) m = m_new;
-      }
-      const float mu = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
-      uint8_t* prow = sP + r * 128;
-#pragma unroll
-      for (int cc = 0; cc < 16; ++cc) {
-        float pv[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = ex2(sv[cc * 8 + e] - mu);
-          rs += pv[e];
-        }
-        const uint4 pk = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]),
-                                    pack_bf16x2(pv[4], pv[5]), pack_bf16x2(pv[6], pv[7]));
-        const int atom = cc >> 3, c8 = cc & 7;
-        *reinterpret_cast<uint4*>(prow + atom * 16384 + ((c8 ^ (r & 7)) << 4)) = pk;
-      }
-      l += rs;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok && n_kv > 0) ok = mbar_wait(o_done, (n_kv - 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag);
-    tc_fence_after();
-    // epilogue: tail term, normalisation, bf16 store
-    const int ti = qh == 0 ? it.tail0 : it.tail1;
-    float a1 = 1.f, a2 = 0.f, lt = l;
-    const float* T = nullptr;
-    if (p.tailT && ti >= 0) {
-      const int64_t o = (int64_t)it.head * p.nqb + ti;
-      const float C2 = p.tailC[o] * 1.4426950408889634f;
-      if (C2 > -INFINITY) {
-        const float M2 = fmaxf(m, C2);
-        a1 = (m == -INFINITY) ? 0.f : ex2(m - M2);
-        a2 = ex2(C2 - M2);
-        lt = l * a1 + p.tailL[o] * a2;
-        T = p.tailT + o * 128;
-      }
-    }
-    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-    const bool row_ok = ok && r < it.q_rows;
-    __nv_bfloat16* orow = p.out + (int64_t)(it.q_start + r) * p.out_stride + hcol;
-#pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      float t[32];
-      tmem_ld32(tmem + lane_addr + 256 + c * 32, t);
-      tmem_wait_ld();
-      if (n_kv == 0) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) t[i] = 0.f;
-      }
-      if (T) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) t[i] = t[i] * a1 + T[c * 32 + i] * a2;
-      }
-      if (row_ok) {
-#pragma unroll
-        for (int i = 0; i < 32; i += 8)
-          *reinterpret_cast<uint4*>(orow + c * 32 + i) =
-              make_uint4(pack_bf16x2(t[i] * inv, t[i + 1] * inv), pack_bf16x2(t[i + 2] * inv, t[i + 3] * inv),
-                         pack_bf16x2(t[i + 4] * inv, t[i + 5] * inv), pack_bf16x2(t[i + 6] * inv, t[i + 7] * inv));
-      }
-    }
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
+#include "wx_flash.cuh"
 
 // ------------------------------------------------------------- host driver
 struct AttnGeom {
