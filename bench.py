@@ -208,35 +208,48 @@ class Model:
         # refined text states (condition_proj output, computed once per generation)
         self.text = torch.randn((c["text"], hdn), device=device, generator=g).to(torch.bfloat16)
         self.gen = g
+        self.h3dit = h3.H3DiT(self.dit, self.mods, self.w_embed, self.b_embed, self.final_norm, self.w_out,
+                              self.b_out)
 
 
 class Runner:
-    """Device-resident sampler step over the packed sequence."""
+    """Device-resident sampler step over this rank's rows of the packed sequence
+    (all rows on one GPU; S/P rows per rank under Ulysses sequence parallelism)."""
 
-    def __init__(self, model: Model):
+    def __init__(self, model: Model, rank: int = 0, world: int = 1):
         import torch
         from wuxianhuabu_b200 import h3
         self.m = model
         c = model.c
         dev = model.dev
         self.h3 = h3
-        S, g, hdn = c["S"], c["g"], c["hidden"]
-        nv = c["refs"] * c["ref_rows"] + c["video"]  # rows through the patch embed (cond rows + video)
-        self.n_embed = nv
-        self.x_in = torch.randn((nv, PATCH_DIM), device=dev, generator=model.gen)  # [cond ; videoX] fp32
-        self.video_x = self.x_in[c["refs"] * c["ref_rows"]:]
-        self.h = torch.empty((S, hdn), dtype=torch.bfloat16, device=dev)
-        self.emb32 = torch.empty((nv, hdn), dtype=torch.float32, device=dev)
-        self.head32 = torch.empty((c["video"], hdn), dtype=torch.float32, device=dev)
-        self.head16 = torch.empty((c["video"], hdn), dtype=torch.bfloat16, device=dev)
-        self.vel = torch.empty((c["video"], PATCH_DIM), dtype=torch.float32, device=dev)
-        self.cos, self.sin = self._rope(c, dev)
+        S, g, hdn, text = c["S"], c["g"], c["hidden"], c["text"]
+        self.rows = S // world
+        self.row0 = rank * self.rows
+        r1 = self.row0 + self.rows
+        # packed rows [text, S) come from the patch embed; the latent x_in covers them
+        self.x_in = torch.randn((S - text, PATCH_DIM), device=dev, generator=model.gen)  # [cond ; videoX] fp32
+        self.t0, self.t1 = self.row0, min(r1, text)            # local text rows
+        self.e0, self.e1 = max(self.row0, text), r1            # local embedded rows
+        self.v0, self.v1 = max(self.row0, g), r1               # local video rows
+        self.n_embed = max(0, self.e1 - self.e0)
+        nvl = max(0, self.v1 - self.v0)
+        self.video_x = self.x_in[self.v0 - text:self.v1 - text]
+        self.h = torch.empty((self.rows, hdn), dtype=torch.bfloat16, device=dev)
+        self.emb32 = torch.empty((max(1, self.n_embed), hdn), dtype=torch.float32, device=dev)
+        self.head32 = torch.empty((max(1, nvl), hdn), dtype=torch.float32, device=dev)
+        self.head16 = torch.empty((max(1, nvl), hdn), dtype=torch.bfloat16, device=dev)
+        self.vel = torch.empty((max(1, nvl), PATCH_DIM), dtype=torch.float32, device=dev)
+        self.nvl = nvl
+        cos, sin = self._rope(c, dev)
+        self.cos, self.sin = cos[self.row0:r1].contiguous(), sin[self.row0:r1].contiguous()
         self.sigmas = h3.sigma_schedule(WINDOW, SHIFT)
         self.plan = h3.attn_broadcast_plan(self.sigmas, PAB_K, PAB_MAX_STALE)
-        self.rowmaps = [self._rowmap(c, i, dev) for i in range(WINDOW)]
+        self.rowmaps = [self._rowmap(c, i, dev)[self.row0:r1].contiguous() for i in range(WINDOW)]
         self.pab = h3.H3AttnBroadcast(c["layers"])
         self.sparse = h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False)
         self.ctx = h3.context(dev.index)
+        self.S = S
 
     @staticmethod
     def _rope(c, dev):
@@ -272,29 +285,13 @@ class Runner:
         return torch.from_numpy(m.view(np.int32)).to(dev)
 
     def step(self, i: int) -> None:
-        """One sampler step (H3Pipeline.swift:1398-1445) at window position i."""
-        h3, m, c = self.h3, self.m, self.m.c
+        """One sampler step (H3Pipeline.swift:1398-1445) at window position i: one native
+        call (wx_dit_step) running patch embed, 48 blocks, final head and Euler update."""
+        m, c = self.m, self.m.c
         pos = i % WINDOW
-        refresh = self.plan[pos]
-        dsigma = self.sigmas[pos + 1] - self.sigmas[pos]
-        ctx = self.ctx
-        ctx.sync_stream()
-        # patch embed (fp32 island, H3Transformer.swift:1036-1039) -> bf16 packed stream
-        ctx.call("wx_dense_f32", self.x_in.data_ptr(), self.n_embed, PATCH_DIM, m.w_embed.data_ptr(), c["hidden"],
-                 m.b_embed.data_ptr(), self.emb32.data_ptr())
-        ctx.call("wx_f32_to_bf16", self.emb32.data_ptr(), self.emb32.numel(), self.h[c["text"]:].data_ptr())
-        self.h[:c["text"]].copy_(m.text)
-        rm = self.rowmaps[pos]
-        m.dit.forward(self.h, m.mods, rm, self.cos, self.sin, self.sparse, c["g"], policy=h3.SparsePolicy.MIX,
-                      attn_bcast=self.pab, attn_refresh=refresh, sigma=self.sigmas[pos])
-        # final head on the video rows (H3Transformer.swift:1192-1203) + Euler (H3Pipeline.swift:1436-1443)
-        hv = self.h[c["g"]:]
-        ctx.call("wx_norm_modscale", hv.data_ptr(), c["video"], c["hidden"], m.final_norm.data_ptr(),
-                 m.final_mods[0][pos].data_ptr(), m.final_mods[1][pos].data_ptr(), None, EPS, self.head16.data_ptr())
-        ctx.call("wx_bf16_to_f32", self.head16.data_ptr(), self.head16.numel(), self.head32.data_ptr())
-        ctx.call("wx_dense_f32", self.head32.data_ptr(), c["video"], c["hidden"], m.w_out.data_ptr(), PATCH_DIM,
-                 m.b_out.data_ptr(), self.vel.data_ptr())
-        ctx.call("wx_euler_update", self.video_x.data_ptr(), self.vel.data_ptr(), self.vel.numel(), float(dsigma))
+        m.h3dit.step(self.S, c["text"], c["g"], m.text, self.x_in, self.rowmaps[pos], self.cos, self.sin,
+                     m.final_mods[0][pos], m.final_mods[1][pos], self.sparse, self.h3.SparsePolicy.MIX, self.pab,
+                     self.plan[pos], self.sigmas[pos + 1] - self.sigmas[pos], sigma=self.sigmas[pos])
 
 
 # ------------------------------------------------------------------ CPU baseline
@@ -491,20 +488,67 @@ def main():
         return
 
     import torch
-    if world > 1:
-        raise SystemExit("multi-GPU Ulysses step is not available in this build")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     from wuxianhuabu_b200 import h3
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+
+        def bcast(obj):
+            box = [obj]
+            dist.broadcast_object_list(box, src=0)
+            return box[0]
+        h3.init_sequence_parallel(world, rank, bcast)
+    try:
+        line = run_step_bench(args, c, base_cfg, dev, world, rank, local, dist)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def _max_over_ranks(x: float, dist) -> float:
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(x: float, dist) -> float:
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
+    import ctypes
+    import torch
     peaks, peaks_kind = load_peaks()
     model = Model(c, dev)
-    run = Runner(model)
+    run = Runner(model, rank, world)
     ctx = run.ctx
     lib = ctx.lib
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+            torch.cuda.synchronize()
+
     # warm-up along the window
     for i in range(args.warmup):
         run.step(i)
-    torch.cuda.synchronize()
+    sync_all()
     ctx.check_device()
     # timed region (device-resident inputs)
     clocks = ClockSampler(local)
@@ -512,29 +556,29 @@ def main():
     stream = torch.cuda.current_stream()
     lib.wx_ctx_profile_enable(ctx.h, 1)
     n0 = lib.wx_ctx_launch_count(ctx.h)
-    torch.cuda.synchronize()
+    sync_all()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.warmup, args.warmup + args.steps):
         run.step(i)
     e1.record(stream)
-    torch.cuda.synchronize()
+    sync_all()
     n1 = lib.wx_ctx_launch_count(ctx.h)
     clk = clocks.stop()
-    import ctypes
     ms = (ctypes.c_double * 6)()
     cnt = (ctypes.c_int64 * 6)()
     lib.wx_ctx_profile_read(ctx.h, ms, cnt, 6)
     lib.wx_ctx_profile_enable(ctx.h, 0)
     ctx.check_device()
-    total_ms = e0.elapsed_time(e1)
+    total_ms = _max_over_ranks(e0.elapsed_time(e1), dist)
     s_per_step = total_ms / 1e3 / args.steps
     positions = [i % WINDOW for i in range(args.warmup, args.warmup + args.steps)]
     n_refresh = sum(1 for p in positions if run.plan[p])
     fl = [step_flops(c, run.plan[p]) for p in positions]
-    gemm_flops = sum(f["gemm"] for f in fl)
-    attn_flops = sum(f["attn"] for f in fl)
-    kinds = ["qgemm", "attention", "routing", "row_kernels", "dequant", "other"]
+    # work done by this rank: 1/world of every GEMM row and of every attention head
+    gemm_flops = sum(f["gemm"] for f in fl) / world
+    attn_flops = sum(f["attn"] for f in fl) / world
+    kinds = ["qgemm", "attention", "routing", "row_kernels", "dequant", "collectives"]
     prof = {k: dict(ms=float(ms[i]), launches=int(cnt[i])) for i, k in enumerate(kinds)}
     attn_ms = prof["attention"]["ms"]
     gemm_ms = prof["qgemm"]["ms"]
@@ -542,29 +586,29 @@ def main():
     peak_t = peaks.get("bf16_tflops_sustained", PEAKS_FALLBACK["bf16_tflops_sustained"])
     ach_attn = attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms > 0 else 0.0
     ach_gemm = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
-    dominant = "attention" if attn_ms >= gemm_ms else "qgemm"
-    if dominant == "attention":
+    if attn_ms >= gemm_ms:
         roof = dict(kernel="flash_attn_kernel (tcgen05 sparse/dense flash attention)", bound="tensor",
                     achieved=ach_attn, peak=peak_t, unit="TFLOP/s", frac=ach_attn / peak_t,
                     flops_per_launch=attn_flops / attn_launches, avg_launch_ms=attn_ms / attn_launches,
-                    traffic=None, peak_kind=f"{peaks_kind} sustained bf16")
+                    traffic=None, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True)
     else:
         roof = dict(kernel="gemm_bf16_tc_kernel", bound="tensor", achieved=ach_gemm, peak=peak_t, unit="TFLOP/s",
-                    frac=ach_gemm / peak_t, traffic=None, peak_kind=f"{peaks_kind} sustained bf16")
+                    frac=ach_gemm / peak_t, traffic=None, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True)
     line = dict(metric=METRIC, value=s_per_step, unit="s/step", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=s_per_step * 1e3, higher_is_better=False, scaling="strong", vs_baseline=None,
                 dtype="bf16", data="synthetic", config=dict(base_cfg, refresh_steps=n_refresh,
                                                             reuse_steps=args.steps - n_refresh),
                 roofline=roof,
                 qgemm=dict(tflops=ach_gemm, frac=ach_gemm / peak_t, ms=gemm_ms, launches=prof["qgemm"]["launches"],
-                           flops=gemm_flops, peak_kind=f"{peaks_kind} sustained bf16"),
-                kernel_ms=prof, gpu_launches=int(n1 - n0), clocks=clk)
-    # e2e through the public API with host buffers (pinned H2D of the latent, D2H of the updated latent)
+                           flops=gemm_flops, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True),
+                kernel_ms=prof, gpu_launches=int(_sum_over_ranks(n1 - n0, dist)), clocks=clk)
+    # e2e through the public API with host buffers (pinned H2D of each rank's latent rows,
+    # D2H of the updated rows)
     if not args.no_e2e:
         host_in = torch.empty(run.video_x.shape, dtype=torch.float32, pin_memory=True)
         host_in.copy_(run.video_x)
         host_out = torch.empty_like(host_in, pin_memory=True)
-        torch.cuda.synchronize()
+        sync_all()
         f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         f0.record(stream)
         for i in range(args.warmup, args.warmup + args.steps):
@@ -572,19 +616,19 @@ def main():
             run.step(i)
             host_out.copy_(run.video_x, non_blocking=True)
         f1.record(stream)
-        torch.cuda.synchronize()
-        e2e = f0.elapsed_time(f1) / 1e3 / args.steps
-        nbytes = run.video_x.numel() * 4
+        sync_all()
+        e2e = _max_over_ranks(f0.elapsed_time(f1), dist) / 1e3 / args.steps
+        nbytes = int(_sum_over_ranks(run.video_x.numel() * 4, dist))
+        finite = _sum_over_ranks(float(not bool(torch.isfinite(host_out).all().item())), dist) == 0
         line["e2e"] = dict(value=e2e, unit="s/step", h2d_bytes_per_step=nbytes, d2h_bytes_per_step=nbytes,
-                           finite=bool(torch.isfinite(host_out).all().item()))
-    if not args.no_cpu_baseline and rank == 0:
+                           finite=finite)
+    if not args.no_cpu_baseline and rank == 0 and world == 1:
         from oracle import oracle as O
         O.build()
         r = cpu_sample(c)
         line["cpu_baseline"] = dict(value=r["value"], unit="s/step", cores=O.num_threads(), kind="port",
                                     sample=r["sample"], sampled_s=r["sampled_s"])
-    if rank == 0:
-        print(json.dumps(line))
+    return line
 
 
 if __name__ == "__main__":

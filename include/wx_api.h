@@ -242,6 +242,96 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
                          const void* cos_t, const void* sin_t, const wx_sparse_spec* spec,
                          void* pab_slot, int refresh, void* scratch);
 
+/* ------------------------------------------- Ulysses sequence parallelism */
+/* No counterpart in the reference (single device; SURVEY of the reference: no
+ * DP/TP/SP). Rank `rank` of P owns rows [row0, row0 + rows) of the packed
+ * sequence (S/P each) for every row-local op, and heads [head0, head0 + heads)
+ * (H/P each) for attention over the whole sequence. Before attention each rank
+ * sends peer r a chunk of qkv_chunk elements = [rows][3][heads*head_dim] (q|k|v
+ * of r's heads for the sender's rows) and receives [S][3*heads*head_dim], the
+ * packed q|k|v of its own heads; after attention it sends peer r the rows of r
+ * ([rows][heads*head_dim], out_chunk elements) and gathers its rows of every
+ * head. S % P == 0 and H % P == 0 are required. */
+typedef struct wx_sp_plan {
+  int64_t S;
+  int64_t rows;
+  int64_t row0;
+  int32_t P;
+  int32_t rank;
+  int32_t H;
+  int32_t heads;
+  int32_t head0;
+  int32_t head_dim;
+  int64_t qkv_chunk;
+  int64_t out_chunk;
+} wx_sp_plan;
+int wx_sp_make_plan(int64_t S, int H, int head_dim, int P, int rank, wx_sp_plan* out);
+/* NCCL bootstrap: rank 0 creates the 128-byte id, every rank passes it to
+ * wx_ctx_init_comm (NCCL is loaded at run time, reusing a copy already loaded
+ * into the process). */
+int wx_comm_unique_id(void* id128);
+int wx_ctx_init_comm(wx_ctx* ctx, int nranks, int rank, const void* id128);
+/* WX_ERR_CUDA if NCCL reported an asynchronous error on the communicator */
+int wx_ctx_comm_check(wx_ctx* ctx);
+/* aborts the communicator (pending collectives return); the context keeps working on one GPU */
+int wx_ctx_comm_abort(wx_ctx* ctx);
+int64_t wx_dit_block_sp_scratch_bytes(const wx_dit_config* cfg, int64_t S, int P);
+/* wx_dit_block_forward on this rank's rows of an S-row sequence (the context's
+ * communicator decides P and the rank): h/rowmap/cos/sin/pab_slot are the
+ * local rows; spec->g counts strip rows of the whole sequence. Refresh steps
+ * run two all-to-alls around attention; reuse steps communicate nothing. */
+int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_weights* w,
+                            const wx_block_mods* mods, const uint32_t* rowmap, void* h, int64_t S,
+                            const void* cos_t, const void* sin_t, const wx_sparse_spec* spec,
+                            void* pab_slot, int refresh, void* scratch);
+
+/* ------------------------------------------------------- sampler step */
+/* Weights of the DiT around the blocks (H3DiT, H3Transformer.swift:1022-1203). */
+typedef struct wx_dit_model {
+  const wx_dit_config* cfg;
+  int32_t n_blocks;
+  int32_t patch_dim;           /* latent features per packed row (96) */
+  const wx_block_weights* blocks; /* [n_blocks] */
+  const wx_block_mods* mods;      /* [n_blocks] AdaLN tables (precomputeAdaln output) */
+  const float* embed_w;        /* [patch_dim, hidden] fp32 patch embed */
+  const float* embed_b;        /* [hidden] */
+  const void* final_norm;      /* [hidden] bf16 */
+  const float* out_w;          /* [hidden, patch_dim] fp32 final projection */
+  const float* out_b;          /* [patch_dim] */
+} wx_dit_model;
+
+/* One sampler step (the loop body of H3Pipeline.swift:1398-1445): packed rows
+ * [0, text_rows) are text states, rows [text_rows, S) come from the patch embed
+ * of `latents` ([S - text_rows, patch_dim] fp32: reference/cond rows, then the
+ * video latent), rows [video_start, S) are denoised: final head, negated
+ * velocity, and latents[video rows] += -v * dsigma in place. Layers follow
+ * sparse_mode_for_layer(policy); `spec` is used on the sparse layers. PAB:
+ * pab_slots[bi] ([rows, hidden] each, or pab_slots NULL) are written when
+ * `refresh` and read otherwise. Under sequence parallelism the context's rank
+ * handles rows [rank*S/P, (rank+1)*S/P): rowmap/cos/sin/pab slots are those
+ * rows, text_states and latents are whole. */
+typedef struct wx_dit_step_args {
+  int64_t S;
+  int64_t text_rows;
+  int64_t video_start;
+  const void* text_states;     /* [text_rows, hidden] bf16 */
+  float* latents;              /* [S - text_rows, patch_dim] fp32 */
+  const uint32_t* rowmap;      /* [rows] */
+  const void* cos_t;           /* [rows, rot/2] bf16 */
+  const void* sin_t;
+  const void* final_shift;     /* [hidden] bf16, this step's row of the final AdaLN table */
+  const void* final_scale;
+  const wx_sparse_spec* spec;
+  int32_t policy;              /* 0 off (all dense), 1 mix, 2 spatial, 3 temporal */
+  int32_t refresh;
+  void* const* pab_slots;
+  float dsigma;
+  int32_t reserved;
+  void* scratch;               /* wx_dit_step_scratch_bytes */
+} wx_dit_step_args;
+int64_t wx_dit_step_scratch_bytes(wx_ctx* ctx, const wx_dit_model* m, int64_t S);
+int wx_dit_step(wx_ctx* ctx, const wx_dit_model* m, const wx_dit_step_args* a);
+
 /* fp32 dense linear y = x*w + b (H3TensorOps.denseLinear: patch embed and final
  * head islands, H3Transformer.swift:1036-1039, 1192-1203); w [k, n] fp32. */
 int wx_dense_f32(wx_ctx* ctx, const float* x, int64_t m, int64_t k, const float* w, int64_t n,

@@ -61,6 +61,26 @@ class ModRun(C.Structure):
     _fields_ = [("start", C.c_uint32), ("end", C.c_uint32), ("mod_row", C.c_uint32)]
 
 
+class SpPlan(C.Structure):
+    _fields_ = [("S", C.c_int64), ("rows", C.c_int64), ("row0", C.c_int64), ("P", C.c_int32), ("rank", C.c_int32),
+                ("H", C.c_int32), ("heads", C.c_int32), ("head0", C.c_int32), ("head_dim", C.c_int32),
+                ("qkv_chunk", C.c_int64), ("out_chunk", C.c_int64)]
+
+
+class DitModel(C.Structure):
+    _fields_ = [("cfg", C.POINTER(DitConfig)), ("n_blocks", C.c_int32), ("patch_dim", C.c_int32),
+                ("blocks", C.POINTER(BlockWeights)), ("mods", C.POINTER(BlockMods)), ("embed_w", C.c_void_p),
+                ("embed_b", C.c_void_p), ("final_norm", C.c_void_p), ("out_w", C.c_void_p), ("out_b", C.c_void_p)]
+
+
+class StepArgs(C.Structure):
+    _fields_ = [("S", C.c_int64), ("text_rows", C.c_int64), ("video_start", C.c_int64), ("text_states", C.c_void_p),
+                ("latents", C.c_void_p), ("rowmap", C.c_void_p), ("cos_t", C.c_void_p), ("sin_t", C.c_void_p),
+                ("final_shift", C.c_void_p), ("final_scale", C.c_void_p), ("spec", C.POINTER(SparseSpec)),
+                ("policy", C.c_int32), ("refresh", C.c_int32), ("pab_slots", C.POINTER(C.c_void_p)),
+                ("dsigma", C.c_float), ("reserved", C.c_int32), ("scratch", C.c_void_p)]
+
+
 _vp, _i64, _i32, _f32, _f64, _u32 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_double, C.c_uint32
 
 # name -> (restype, argtypes)
@@ -100,6 +120,16 @@ _SIGS = {
     "wx_dit_block_scratch_bytes": (_i64, [C.POINTER(DitConfig), _i64]),
     "wx_dit_block_forward": (_i32, [_vp, C.POINTER(DitConfig), C.POINTER(BlockWeights), C.POINTER(BlockMods), _vp,
                                     _vp, _i64, _vp, _vp, C.POINTER(SparseSpec), _vp, _i32, _vp]),
+    "wx_sp_make_plan": (_i32, [_i64, _i32, _i32, _i32, _i32, C.POINTER(SpPlan)]),
+    "wx_comm_unique_id": (_i32, [_vp]),
+    "wx_ctx_init_comm": (_i32, [_vp, _i32, _i32, _vp]),
+    "wx_ctx_comm_check": (_i32, [_vp]),
+    "wx_ctx_comm_abort": (_i32, [_vp]),
+    "wx_dit_block_sp_scratch_bytes": (_i64, [C.POINTER(DitConfig), _i64, _i32]),
+    "wx_dit_block_forward_sp": (_i32, [_vp, C.POINTER(DitConfig), C.POINTER(BlockWeights), C.POINTER(BlockMods),
+                                       _vp, _vp, _i64, _vp, _vp, C.POINTER(SparseSpec), _vp, _i32, _vp]),
+    "wx_dit_step_scratch_bytes": (_i64, [_vp, C.POINTER(DitModel), _i64]),
+    "wx_dit_step": (_i32, [_vp, C.POINTER(DitModel), C.POINTER(StepArgs)]),
     "wx_dense_f32": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "wx_bf16_to_f32": (_i32, [_vp, _vp, _i64, _vp]),
     "wx_f32_to_bf16": (_i32, [_vp, _vp, _i64, _vp]),

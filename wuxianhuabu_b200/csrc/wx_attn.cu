@@ -350,6 +350,17 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
 #include "wx_flash.cuh"
 
 // ------------------------------------------------------------- host driver
+// Share of the softmax exponentials taken by the FMA-pipe polynomial (pairs out of
+// every 4; tuning knob WX_EXP_POLY_PAIRS = 0, 1 or 2, read once).
+static int exp_poly_pairs() {
+  static int v = [] {
+    const char* e = getenv("WX_EXP_POLY_PAIRS");
+    int x = e ? atoi(e) : 0;
+    return x < 0 ? 0 : (x > 2 ? 2 : x);
+  }();
+  return v;
+}
+
 struct AttnGeom {
   int64_t S, g;
   int H, hd, block, nb, nvt, nst, qpb;
@@ -512,7 +523,9 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   if ((st = make_tmap_bf16_2d(ctx, &tv, v, (uint64_t)a.S, (uint64_t)cols, (uint64_t)rs, 64, 64))) return st;
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(flash_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    cudaError_t e = cudaSuccess;
+    for (auto fn : {flash_attn_kernel<0>, flash_attn_kernel<1>, flash_attn_kernel<2>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
     if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
     attr = true;
   }
@@ -530,7 +543,13 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   p.err = ctx->dev_err;
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
   ProfScope prof(ctx, kProfAttn);
-  flash_attn_kernel<<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
+  const int poly = exp_poly_pairs();
+  if (poly == 0)
+    flash_attn_kernel<0><<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
+  else if (poly == 2)
+    flash_attn_kernel<2><<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
+  else
+    flash_attn_kernel<1><<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
   return launch_status(ctx, "flash_attn");
 }
 

@@ -204,6 +204,7 @@ int wx_ctx_destroy(wx_ctx* ctx) {
   if (!ctx) return WX_OK;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  sp_destroy_comm(ctx);
   for (auto& r : ctx->prof_recs) {
     cudaEventDestroy(r.a);
     cudaEventDestroy(r.b);

@@ -43,6 +43,36 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe for a pair of arguments: x = j + f with j = round(x) and
+// f in [-1/2, 1/2]; 2^f from a degree-3 polynomial fitted by least squares (in
+// relative error, at Chebyshev nodes) with max relative error 7.8e-5 — far below
+// the bf16 rounding P goes through — and j added to the exponent bits. Arguments
+// are clamped at -125 so that masked (-inf) scores give a negligible 2^-125.
+// Used for part of each row so that the MUFU pipe and the FMA pipe share the work.
+// POLY (template argument of the kernel) = pairs of every 4 evaluated this way.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 magic = make_float2(12582912.f, 12582912.f);  // 1.5 * 2^23: rounds to an integer
+  const float2 t = __fadd2_rn(x, magic);
+  const float2 jf = __fadd2_rn(t, make_float2(-12582912.f, -12582912.f));
+  const float2 f = __ffma2_rn(jf, make_float2(-1.f, -1.f), x);
+  float2 q = __ffma2_rn(make_float2(0.05508868396282196f, 0.05508868396282196f), f,
+                        make_float2(0.24260404706001282f, 0.24260404706001282f));
+  q = __ffma2_rn(q, f, make_float2(0.6932762265205383f, 0.6932762265205383f));
+  q = __ffma2_rn(q, f, make_float2(0.9999289512634277f, 0.9999289512634277f));
+  // bits(t) = 0x4B400000 + j, and 0x4B400000 << 23 vanishes mod 2^32
+  return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
+// three-input max (sm_100)
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // key tile j of a work item: two 64-row halves (start row, valid length | q-half mask << 8)
 __device__ __forceinline__ int4 kv_entry(const WorkItem& it, const int4* entries, int j) {
   if (j < it.n_implicit) {
@@ -53,6 +83,7 @@ __device__ __forceinline__ int4 kv_entry(const WorkItem& it, const int4* entries
   return __ldg(entries + it.list_begin + (j - it.n_implicit));
 }
 
+template <int POLY>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     flash_attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, AttnParams p) {
@@ -65,14 +96,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   auto sV = [&](int st) { return sbase + (uint32_t)(2 + 2 * st) * kTileBytes; };
   auto sP = [&](int b) { return sbase + (uint32_t)(5 + b) * kTileBytes; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kAttnBarOffset);
-  // q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], o_done[2]
+  // q_full, k_full[2], k_empty[2], s_full[2], p_full[2], o_done[2], v_full[2], v_empty[2]
   const uint32_t q_full = smem_u32(bars + 0);
-  auto kv_full = [&](int i) { return smem_u32(bars + 1 + i); };
-  auto kv_empty = [&](int i) { return smem_u32(bars + 3 + i); };
+  auto k_full = [&](int i) { return smem_u32(bars + 1 + i); };
+  auto k_empty = [&](int i) { return smem_u32(bars + 3 + i); };
+  auto v_full = [&](int i) { return smem_u32(bars + 11 + i); };
+  auto v_empty = [&](int i) { return smem_u32(bars + 13 + i); };
   auto s_full = [&](int i) { return smem_u32(bars + 5 + i); };
   auto p_full = [&](int i) { return smem_u32(bars + 7 + i); };
   auto o_done = [&](int i) { return smem_u32(bars + 9 + i); };
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -82,8 +115,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(kv_full(i), 1);
-      mbar_init(kv_empty(i), 1);
+      mbar_init(k_full(i), 1);
+      mbar_init(k_empty(i), 1);
+      mbar_init(v_full(i), 1);
+      mbar_init(v_empty(i), 1);
       mbar_init(s_full(i), 1);
       mbar_init(o_done(i), 1);
       mbar_init(p_full(i), 128);
@@ -115,14 +150,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int st = j & 1;
         const int4 cur = e;
         if (j + 1 < n_kv) e = kv_entry(it, p.entries, j + 1);
-        if (!mbar_wait(kv_empty(st), ((j >> 1) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(kv_full(st), 2 * kTileBytes);
+        // K of stage st is free once S_{j-2} is done, V once PV_{j-2} is done
+        if (!mbar_wait(k_empty(st), ((j >> 1) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full(st), kTileBytes);
         for (int ch = 0; ch < 2; ++ch) {
-          const uint32_t ko = sK(st) + ch * 16384, vo = sV(st) + ch * 16384;
-          tma_load_2d(ko, &tmK, kv_full(st), hcol + ch * 64, cur.x);
-          tma_load_2d(ko + 8192, &tmK, kv_full(st), hcol + ch * 64, cur.y);
-          tma_load_2d(vo, &tmV, kv_full(st), hcol + ch * 64, cur.x);
-          tma_load_2d(vo + 8192, &tmV, kv_full(st), hcol + ch * 64, cur.y);
+          const uint32_t ko = sK(st) + ch * 16384;
+          tma_load_2d(ko, &tmK, k_full(st), hcol + ch * 64, cur.x);
+          tma_load_2d(ko + 8192, &tmK, k_full(st), hcol + ch * 64, cur.y);
+        }
+        if (!mbar_wait(v_empty(st), ((j >> 1) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full(st), kTileBytes);
+        for (int ch = 0; ch < 2; ++ch) {
+          const uint32_t vo = sV(st) + ch * 16384;
+          tma_load_2d(vo, &tmV, v_full(st), hcol + ch * 64, cur.x);
+          tma_load_2d(vo + 8192, &tmV, v_full(st), hcol + ch * 64, cur.y);
         }
       }
     }
@@ -133,7 +174,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = mbar_wait(q_full, 0, p.err, kDevTimeoutFull, abort_flag);
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!mbar_wait(kv_full(st), (j >> 1) & 1, p.err, kDevTimeoutFull, abort_flag)) return false;
+        if (!mbar_wait(k_full(st), (j >> 1) & 1, p.err, kDevTimeoutFull, abort_flag)) return false;
         tc_fence_after();
         const uint32_t ka = sK(st);
 #pragma unroll
@@ -143,12 +184,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(s_full(st));
+        umma_commit(k_empty(st));
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < n_kv && ok; ++j) {
         if (j + 1 < n_kv && !issue_s(j + 1)) break;
         if (!mbar_wait(p_full(j & 1), (j >> 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag)) break;
+        if (!mbar_wait(v_full(j & 1), (j >> 1) & 1, p.err, kDevTimeoutFull, abort_flag)) break;
         tc_fence_after();
         const uint32_t va = sV(j & 1), pa = sP(j & 1);
 #pragma unroll
@@ -158,7 +201,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           umma_bf16(tmem + 256, ad, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(o_done(j & 1));
-        umma_commit(kv_empty(j & 1));
+        umma_commit(v_empty(j & 1));
       }
     }
   } else {
@@ -202,9 +245,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!valid) sv[c] = -INFINITY;
         }
       }
-      float rmax = sv[0];
+      float rmax = fmaxf(sv[0], sv[1]);
 #pragma unroll
-      for (int c = 1; c < 128; ++c) rmax = fmaxf(rmax, sv[c]);
+      for (int c = 2; c < 128; c += 2) rmax = max3f(rmax, sv[c], sv[c + 1]);
       const float m_new = fmaxf(m, rmax);
       bool need = false;
       if (j == 0) {
@@ -241,15 +284,27 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
       const float mu = (m == -INFINITY) ? 0.f : m * p.sl2;
-      float rs = 0.f;
+      // p = 2^(s*scale*log2e - m*scale*log2e): packed fp32x2 FMA for the argument,
+      // MUFU ex2, packed fp32x2 adds for the row sum
+      const float2 sl2x2 = make_float2(p.sl2, p.sl2);
+      const float2 nmu2 = make_float2(-mu, -mu);
+      float2 rs2 = make_float2(0.f, 0.f);
       const uint32_t prow = sP(b) + r * 128;
 #pragma unroll
       for (int cc = 0; cc < 16; ++cc) {
         float pv[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          pv[q] = ex2(fmaf(sv[cc * 8 + q], p.sl2, -mu));
-          rs += pv[q];
+        for (int q = 0; q < 4; ++q) {
+          const float2 a = __ffma2_rn(make_float2(sv[cc * 8 + 2 * q], sv[cc * 8 + 2 * q + 1]), sl2x2, nmu2);
+          if (q < POLY) {
+            const float2 e2 = ex2_poly2(a);
+            pv[2 * q] = e2.x;
+            pv[2 * q + 1] = e2.y;
+          } else {
+            pv[2 * q] = ex2(a.x);
+            pv[2 * q + 1] = ex2(a.y);
+          }
+          rs2 = __fadd2_rn(rs2, make_float2(pv[2 * q], pv[2 * q + 1]));
         }
         const int atom = cc >> 3, c8 = cc & 7;
         const uint32_t addr = prow + atom * 16384 + ((c8 ^ (r & 7)) << 4);
@@ -257,7 +312,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                      "r"(pack_bf16x2(pv[2], pv[3])), "r"(pack_bf16x2(pv[4], pv[5])), "r"(pack_bf16x2(pv[6], pv[7]))
                      : "memory");
       }
-      l += rs;
+      l += rs2.x + rs2.y;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full(b));

@@ -19,6 +19,10 @@ struct wx_ctx {
   size_t ws_bytes = 0;
   std::string last_error;
   int64_t launches = 0;  // kernels launched through this context
+  // sequence-parallel group (Ulysses): NCCL communicator, size, rank
+  void* comm = nullptr;
+  int sp_size = 1;
+  int sp_rank = 0;
   // per-kernel-class device timing (wx_ctx_profile_enable / _read)
   bool prof = false;
   struct ProfRec {
@@ -64,6 +68,9 @@ struct Carve {
 // box `box_cols` x `box_rows`, 128-byte swizzle, zero fill out of bounds.
 int make_tmap_bf16_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t rows,
                       uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows);
+
+// releases the NCCL communicator of a context (no-op without one)
+void sp_destroy_comm(wx_ctx* ctx);
 
 // checks the last launch(es) and counts `n` kernel launches on the context
 int launch_status(wx_ctx* ctx, const char* what, int n = 1);

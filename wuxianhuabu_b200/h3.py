@@ -49,6 +49,7 @@ class Context:
         if not torch.cuda.is_available():
             raise RuntimeError("libwx needs a CUDA device (sm_100a); no CPU fallback exists")
         self.device = device
+        self.sp_size, self.sp_rank = 1, 0
         h = C.c_void_p()
         st = self.lib.wx_ctx_create(device, C.byref(h))
         if st != 0:
@@ -378,10 +379,35 @@ class H3BlockWeights:
                             _p(self.q_norm), _p(self.k_norm), _p(self.norm1), _p(self.norm2))
 
 
+def sp_plan(S: int, H: int, head_dim: int, P: int, rank: int) -> _lib.SpPlan:
+    """Ulysses partition (wx_sp_make_plan): this rank's rows and heads."""
+    plan = _lib.SpPlan()
+    check(_lib.load().wx_sp_make_plan(S, H, head_dim, P, rank, C.byref(plan)))
+    return plan
+
+
+def init_sequence_parallel(world: int, rank: int, broadcast_id) -> None:
+    """Create the NCCL communicator of this process's context. ``broadcast_id(bytes_or_None)``
+    returns rank 0's 128-byte id on every rank (e.g. torch.distributed.broadcast_object_list)."""
+    lib = _lib.load()
+    uid = None
+    if rank == 0:
+        buf = (C.c_uint8 * 128)()
+        check(lib.wx_comm_unique_id(buf))
+        uid = bytes(buf)
+    uid = broadcast_id(uid)
+    buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+    ctx = context()
+    check(lib.wx_ctx_init_comm(ctx.h, world, rank, buf), ctx.h)
+    ctx.sp_size, ctx.sp_rank = world, rank
+
+
 class H3DiTBlocks:
     """The block loop of H3DiT.forward (H3Transformer.swift:1078-1159) on libwx.
 
-    ``mods[bi]`` = six [num_mod_rows, hidden] bf16 tables (shift/scale/gate MSA, shift/scale/gate MLP)."""
+    ``mods[bi]`` = six [num_mod_rows, hidden] bf16 tables (shift/scale/gate MSA, shift/scale/gate MLP).
+    With a sequence-parallel context (init_sequence_parallel) h, rowmap, cos/sin and the PAB
+    slots are this rank's rows and ``S_total`` is the length of the whole sequence."""
 
     def __init__(self, cfg: H3DiTConfig, blocks: list[H3BlockWeights]):
         self.cfg = cfg
@@ -390,30 +416,44 @@ class H3DiTBlocks:
         self._wc = [b.c() for b in blocks]
         self._scratch: Optional[torch.Tensor] = None
 
-    def scratch(self, S: int, device) -> torch.Tensor:
-        need = int(_lib.load().wx_dit_block_scratch_bytes(C.byref(self._c), S))
+    def scratch(self, S: int, device, P: int = 1) -> torch.Tensor:
+        lib = _lib.load()
+        need = int(lib.wx_dit_block_scratch_bytes(C.byref(self._c), S) if P == 1 else
+                   lib.wx_dit_block_sp_scratch_bytes(C.byref(self._c), S, P))
+        if need <= 0:
+            raise WxError(_lib.WX_ERR_INVALID, f"no block plan for S={S} over {P} ranks")
         if self._scratch is None or self._scratch.numel() < need or self._scratch.device != torch.device(device):
+            self._scratch = None
             self._scratch = torch.empty(need, dtype=torch.uint8, device=device)
         return self._scratch
 
     def block_forward(self, bi: int, h: torch.Tensor, mods: Sequence[torch.Tensor], rowmap: torch.Tensor,
                       cos: torch.Tensor, sin: torch.Tensor, spec: Optional[SparseSpec],
-                      pab_slot: Optional[torch.Tensor] = None, refresh: bool = True) -> torch.Tensor:
-        """One block, h [S, hidden] updated in place."""
+                      pab_slot: Optional[torch.Tensor] = None, refresh: bool = True,
+                      S_total: Optional[int] = None) -> torch.Tensor:
+        """One block, h [rows, hidden] updated in place."""
         _need_bf16_cuda(h, cos, sin, *mods)
-        S = h.shape[0]
-        scr = self.scratch(S, h.device)
+        ctx = context(h.device.index)
+        P = getattr(ctx, "sp_size", 1)
         bm = BlockMods(*[_p(m) for m in mods])
         sp = spec if spec is not None else dense_spec()
-        context(h.device.index).call("wx_dit_block_forward", C.byref(self._c), C.byref(self._wc[bi]), C.byref(bm),
-                                     _p(rowmap), _p(h), S, _p(cos), _p(sin), C.byref(sp), _p(pab_slot),
-                                     int(refresh), _p(scr))
+        if P == 1:
+            S = h.shape[0]
+            scr = self.scratch(S, h.device)
+            ctx.call("wx_dit_block_forward", C.byref(self._c), C.byref(self._wc[bi]), C.byref(bm), _p(rowmap),
+                     _p(h), S, _p(cos), _p(sin), C.byref(sp), _p(pab_slot), int(refresh), _p(scr))
+        else:
+            S = S_total if S_total is not None else h.shape[0] * P
+            scr = self.scratch(S, h.device, P)
+            ctx.call("wx_dit_block_forward_sp", C.byref(self._c), C.byref(self._wc[bi]), C.byref(bm), _p(rowmap),
+                     _p(h), S, _p(cos), _p(sin), C.byref(sp), _p(pab_slot), int(refresh), _p(scr))
         return h
 
     def forward(self, h: torch.Tensor, mods: Sequence[Sequence[torch.Tensor]], rowmap: torch.Tensor,
                 cos: torch.Tensor, sin: torch.Tensor, sparse_cfg: Optional[H3SolAttnConfig], g: int,
                 policy: int = SparsePolicy.MIX, attn_bcast: Optional[H3AttnBroadcast] = None,
-                attn_refresh: bool = True, sigma: Optional[float] = None) -> torch.Tensor:
+                attn_refresh: bool = True, sigma: Optional[float] = None,
+                S_total: Optional[int] = None) -> torch.Tensor:
         """All blocks in order; the PAB slot of block bi is written on refresh, read on reuse."""
         n = len(self.blocks)
         for bi in range(n):
@@ -425,7 +465,56 @@ class H3DiTBlocks:
                 cached = attn_bcast.blocks[bi]
                 refresh = attn_refresh or cached is None
                 slot = attn_bcast.slot(bi, h.shape[0], self.cfg.hidden, h.device)
-            self.block_forward(bi, h, mods[bi], rowmap, cos, sin, spec, slot, refresh)
+            self.block_forward(bi, h, mods[bi], rowmap, cos, sin, spec, slot, refresh, S_total=S_total)
         if attn_bcast is not None and attn_refresh and sigma is not None:
             attn_bcast.cached_sigma = sigma
         return h
+
+
+class H3DiT:
+    """H3DiT (H3Transformer.swift:1022-1203) around the blocks: patch embed, final head,
+    and the sampler step of H3Pipeline.swift:1398-1445 as one native call (wx_dit_step)."""
+
+    def __init__(self, blocks: H3DiTBlocks, mods: Sequence[Sequence[torch.Tensor]], embed_w: torch.Tensor,
+                 embed_b: torch.Tensor, final_norm: torch.Tensor, out_w: torch.Tensor, out_b: torch.Tensor):
+        self.blocks = blocks
+        self.mods = [list(m) for m in mods]
+        self._bw = (BlockWeights * len(blocks.blocks))(*blocks._wc)
+        self._bm = (BlockMods * len(self.mods))(*[BlockMods(*[_p(t) for t in m]) for m in self.mods])
+        self.embed_w, self.embed_b, self.final_norm, self.out_w, self.out_b = embed_w, embed_b, final_norm, out_w, out_b
+        self.patch_dim = embed_w.shape[0]
+        self._m = _lib.DitModel(C.pointer(blocks._c), len(blocks.blocks), self.patch_dim, self._bw, self._bm,
+                                _p(embed_w), _p(embed_b), _p(final_norm), _p(out_w), _p(out_b))
+        self._scratch: Optional[torch.Tensor] = None
+
+    def step(self, S: int, text_rows: int, video_start: int, text_states: torch.Tensor, latents: torch.Tensor,
+             rowmap: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, final_shift: torch.Tensor,
+             final_scale: torch.Tensor, sparse_cfg: Optional[H3SolAttnConfig], policy: int,
+             attn_bcast: Optional[H3AttnBroadcast], attn_refresh: bool, dsigma: float,
+             sigma: Optional[float] = None) -> torch.Tensor:
+        """One denoising step; latents [S - text_rows, patch] fp32 are updated in place."""
+        ctx = context(latents.device.index)
+        lib = ctx.lib
+        need = int(lib.wx_dit_step_scratch_bytes(ctx.h, C.byref(self._m), S))
+        if need <= 0:
+            raise WxError(_lib.WX_ERR_INVALID, f"no step plan for S={S}")
+        if self._scratch is None or self._scratch.numel() < need:
+            self._scratch = None
+            self._scratch = torch.empty(need, dtype=torch.uint8, device=latents.device)
+        slots = None
+        rows = S // getattr(ctx, "sp_size", 1)
+        refresh = attn_refresh
+        if attn_bcast is not None:
+            refresh = attn_refresh or any(b is None for b in attn_bcast.blocks)
+            ptrs = [attn_bcast.slot(bi, rows, self.blocks.cfg.hidden, latents.device).data_ptr()
+                    for bi in range(len(self.blocks.blocks))]
+            slots = (C.c_void_p * len(ptrs))(*ptrs)
+        spec = sparse_cfg.spec(video_start) if sparse_cfg is not None else None
+        args = _lib.StepArgs(S, text_rows, video_start, _p(text_states), _p(latents), _p(rowmap), _p(cos), _p(sin),
+                             _p(final_shift), _p(final_scale), C.pointer(spec) if spec is not None else None,
+                             policy if sparse_cfg is not None else SparsePolicy.OFF, int(refresh), slots,
+                             float(dsigma), 0, _p(self._scratch))
+        ctx.call("wx_dit_step", C.byref(self._m), C.byref(args))
+        if attn_bcast is not None and refresh and sigma is not None:
+            attn_bcast.cached_sigma = sigma
+        return latents
