@@ -245,9 +245,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!valid) sv[c] = -INFINITY;
         }
       }
-      float rmax = fmaxf(sv[0], sv[1]);
+      // row max: four independent chains (one softmax warp per SMSP has no other warp to hide latency)
+      float mx[4];
 #pragma unroll
-      for (int c = 2; c < 128; c += 2) rmax = max3f(rmax, sv[c], sv[c + 1]);
+      for (int k = 0; k < 4; ++k) mx[k] = fmaxf(sv[2 * k], sv[2 * k + 1]);
+#pragma unroll
+      for (int c = 8; c < 128; c += 8) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mx[k] = max3f(mx[k], sv[c + 2 * k], sv[c + 2 * k + 1]);
+      }
+      const float rmax = max3f(fmaxf(mx[0], mx[1]), mx[2], mx[3]);
       const float m_new = fmaxf(m, rmax);
       bool need = false;
       if (j == 0) {
@@ -288,7 +295,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // MUFU ex2, packed fp32x2 adds for the row sum
       const float2 sl2x2 = make_float2(p.sl2, p.sl2);
       const float2 nmu2 = make_float2(-mu, -mu);
-      float2 rs2 = make_float2(0.f, 0.f);
+      float2 rs2[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) rs2[q] = make_float2(0.f, 0.f);
       const uint32_t prow = sP(b) + r * 128;
 #pragma unroll
       for (int cc = 0; cc < 16; ++cc) {
@@ -304,7 +313,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             pv[2 * q] = ex2(a.x);
             pv[2 * q + 1] = ex2(a.y);
           }
-          rs2 = __fadd2_rn(rs2, make_float2(pv[2 * q], pv[2 * q + 1]));
+          rs2[q] = __fadd2_rn(rs2[q], make_float2(pv[2 * q], pv[2 * q + 1]));
         }
         const int atom = cc >> 3, c8 = cc & 7;
         const uint32_t addr = prow + atom * 16384 + ((c8 ^ (r & 7)) << 4);
@@ -312,7 +321,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                      "r"(pack_bf16x2(pv[2], pv[3])), "r"(pack_bf16x2(pv[4], pv[5])), "r"(pack_bf16x2(pv[6], pv[7]))
                      : "memory");
       }
-      l += rs2.x + rs2.y;
+      {
+        const float2 a = __fadd2_rn(rs2[0], rs2[1]), c2 = __fadd2_rn(rs2[2], rs2[3]);
+        const float2 t = __fadd2_rn(a, c2);
+        l += t.x + t.y;
+      }
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full(b));
