@@ -53,7 +53,9 @@ def test_dequant_reference_4bit_fixture(torch_mod):
     assert np.array_equal(to_np_bf16(m.dequantized_weight()), d["expect"])
 
 
-SHAPES = [(1, 128, 192), (77, 256, 384), (128, 512, 512), (300, 1024, 3072), (256, 3072, 256)]
+SHAPES = [(1, 128, 192), (77, 256, 384), (128, 512, 512), (300, 1024, 3072), (256, 3072, 256),
+          # small M takes the fused path (weights expanded in shared memory, split-K):
+          (256, 3072, 3072), (257, 1024, 1024), (512, 1024, 3072), (600, 512, 256)]
 
 
 @pytest.mark.parametrize("m,k,n", SHAPES)

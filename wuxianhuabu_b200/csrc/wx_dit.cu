@@ -48,7 +48,9 @@ static BlockLayout block_layout(const wx_dit_config* c, int64_t S) {
   L.f1 = off; off += al((size_t)S * c->ffn * 2);
   size_t wmax = std::max(std::max(3 * inner * (size_t)c->hidden, inner * (size_t)c->hidden),
                          std::max(fc1_n * (size_t)c->hidden, (size_t)c->ffn * c->hidden));
-  L.wd = off; off += al(wmax * 2);
+  // expanded weight of the two-pass GEMM, or the fp32 split-K accumulator of the small-M path
+  const size_t nmax = std::max(std::max(3 * inner, (size_t)c->hidden), fc1_n);
+  L.wd = off; off += al(std::max(wmax * 2, qlinear_ws_need(S, (int64_t)nmax, 1)));
   L.sw = off; off += c->mlp_kind == WX_MLP_SWIGLU ? al((size_t)S * fc1_n * 2) : 0;
   // the widest attention plan this geometry can need (SOL 64-blocks with g = 0)
   wx_sparse_spec sol{};

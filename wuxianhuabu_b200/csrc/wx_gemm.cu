@@ -23,6 +23,18 @@
 namespace wx {
 
 int launch_dequant(wx_ctx* ctx, const wx_qweight* w, void* out);
+bool fused_eligible(const wx_qweight* w, int64_t M, int epilogue);
+int qlinear_fused(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const wx_qweight* w, int epilogue,
+                  const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw,
+                  void* scratch);
+// WX_QGEMM_TWO_PASS=1 disables the fused small-M path (A/B measurements), read once
+static bool force_two_pass() {
+  static bool v = [] {
+    const char* e = getenv("WX_QGEMM_TWO_PASS");
+    return e && atoi(e) != 0;
+  }();
+  return v;
+}
 int launch_swiglu(wx_ctx* ctx, const void* t, int64_t m, int64_t F, int64_t ldt, void* y, int64_t ldy);
 bool qweight_ok(const wx_qweight* w);
 
@@ -317,6 +329,9 @@ int gemm_bf16(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd
 int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,
                          const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
                          void* y_raw, void* wd, void* swiglu_tmp) {
+  // small M is weight-bandwidth bound: expand the weights in shared memory instead
+  if (fused_eligible(w, m, epilogue) && !force_two_pass())
+    return qlinear_fused(ctx, x, m, lda, w, epilogue, gate, resid, rowmap, y, ldy, y_raw, wd);
   int st = launch_dequant(ctx, w, wd);
   if (st) return st;
   if (epilogue == WX_EPI_SWIGLU) {
@@ -329,7 +344,8 @@ int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, con
 }
 
 size_t qlinear_scratch_bytes(const wx_qweight* w, int64_t m, int epilogue) {
-  size_t b = ((size_t)w->n * w->k * 2 + 255) & ~size_t(255);
+  size_t b = qlinear_ws_need(m, w->n, w->k);
+  b = (b + 255) & ~size_t(255);
   if (epilogue == WX_EPI_SWIGLU) b += ((size_t)m * w->n * 2 + 255) & ~size_t(255);
   return b;
 }
@@ -351,6 +367,6 @@ extern "C" int wx_qlinear(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, co
   if (!ws) return st;
   uint8_t* base = static_cast<uint8_t*>(ws);
   void* wd = base;
-  void* tmp = base + (((size_t)w->n * w->k * 2 + 255) & ~size_t(255));
+  void* tmp = base + ((qlinear_ws_need(m, w->n, w->k) + 255) & ~size_t(255));
   return qlinear_with_scratch(ctx, x, m, lda, w, epilogue, gate, resid, rowmap, y, ldy, y_raw, wd, tmp);
 }

@@ -87,6 +87,15 @@ struct ProfScope {
   ~ProfScope();
 };
 
+// Scratch of one quantized linear: the expanded bf16 weight of the two-pass
+// GEMM, or (small M, at most 512 rows) the fp32 partials of up to 4 K splits
+// of the shared-memory dequant path.
+inline size_t qlinear_ws_need(int64_t m, int64_t n, int64_t k) {
+  const size_t two_pass = (size_t)n * k * 2;
+  const size_t fused = m <= 512 ? (size_t)4 * m * n * 4 : 0;
+  return two_pass > fused ? two_pass : fused;
+}
+
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace wx
