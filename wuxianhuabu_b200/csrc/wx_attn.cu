@@ -348,6 +348,7 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
 
 // ------------------------------------------------------------ 5. flash kernel
 #include "wx_flash.cuh"
+#include "wx_flash2.cuh"
 
 // ------------------------------------------------------------- host driver
 // Share of the softmax exponentials taken by the FMA-pipe polynomial (pairs out of
@@ -357,6 +358,17 @@ static int exp_poly_pairs() {
     const char* e = getenv("WX_EXP_POLY_PAIRS");
     int x = e ? atoi(e) : 0;
     return x < 0 ? 0 : (x > 2 ? 2 : x);
+  }();
+  return v;
+}
+
+// Flash kernel variant (tuning knob WX_ATTN_KERNEL, read once): 1 = one CTA per SM
+// with double-buffered S/P (flash_attn_kernel), 2 = two CTAs per SM with P in
+// TMEM (flash_attn2_kernel).
+static int attn_kernel_variant() {
+  static int v = [] {
+    const char* e = getenv("WX_ATTN_KERNEL");
+    return (e && atoi(e) == 1) ? 1 : 2;
   }();
   return v;
 }
@@ -526,6 +538,8 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
     cudaError_t e = cudaSuccess;
     for (auto fn : {flash_attn_kernel<0>, flash_attn_kernel<1>, flash_attn_kernel<2>})
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    for (auto fn : {flash_attn2_kernel<0>, flash_attn2_kernel<1>, flash_attn2_kernel<2>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA2Smem);
     if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
     attr = true;
   }
@@ -544,6 +558,15 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
   ProfScope prof(ctx, kProfAttn);
   const int poly = exp_poly_pairs();
+  if (attn_kernel_variant() == 2) {
+    if (poly == 0)
+      flash_attn2_kernel<0><<<(unsigned)n_items, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
+    else if (poly == 2)
+      flash_attn2_kernel<2><<<(unsigned)n_items, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
+    else
+      flash_attn2_kernel<1><<<(unsigned)n_items, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
+    return launch_status(ctx, "flash_attn2");
+  }
   if (poly == 0)
     flash_attn_kernel<0><<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
   else if (poly == 2)
