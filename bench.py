@@ -414,9 +414,14 @@ def run_c2(args) -> dict:
     peaks, kind = load_peaks()
     pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
     res = []
-    for (K, N) in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]:
+    shapes = [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]
+    ms_list = (256, 4096, 28520, 111600)
+    if args.shape:  # one point "M,K,N" of the sweep (profiling runs)
+        M0, K0, N0 = (int(v) for v in args.shape.split(","))
+        shapes, ms_list = [(K0, N0)], (M0,)
+    for (K, N) in shapes:
         lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02)
-        for M in (256, 4096, 28520, 111600):
+        for M in ms_list:
             x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
             y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
             for _ in range(max(1, args.warmup)):
@@ -446,6 +451,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
     ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c3", "c3full", "c2"])
+    ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
