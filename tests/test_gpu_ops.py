@@ -128,10 +128,13 @@ def test_qlinear_large_vs_torch_fp32(torch_mod, m, k, n):
     assert err < 1e-2 and cos > 0.9999, (err, cos)
 
 
-@pytest.mark.parametrize("hd,rot,eps", [(128, 96, 1e-5), (64, 64, 1e-6), (128, 128, 1e-6)])
-def test_qk_norm_rope(torch_mod, hd, rot, eps):
+# (128, *, *) with rot/2 % 4 == 0 takes the 8-heads-per-warp kernel (H=11: a ragged head group);
+# rot 100 and head_dim 64 take the warp-per-row kernel
+@pytest.mark.parametrize("hd,rot,eps,H", [(128, 96, 1e-5, 3), (64, 64, 1e-6, 3), (128, 128, 1e-6, 3),
+                                          (128, 128, 1e-6, 11), (128, 100, 1e-6, 3), (128, 0, 1e-6, 3)])
+def test_qk_norm_rope(torch_mod, hd, rot, eps, H):
     from wuxianhuabu_b200 import h3
-    S, H = 333, 3
+    S = 333
     x = O.normal_bf16((S, H, hd), 41, hd)
     w = O.normal_bf16((hd,), 41, 2, mean=1.0, std=0.1)
     cos = O.normal_bf16((S, rot // 2), 41, 3)

@@ -20,6 +20,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
+#include <stdio.h>
 
 #include <algorithm>
 
@@ -313,6 +314,7 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t n_strip = (int64_t)H * nst;
   const int64_t n_items = n_strip + (int64_t)H * nvt;
+  if (i == 0) items[n_items].q_start = 0;  // work counter of the persistent flash kernel
   if (i >= n_items) return;
   WorkItem it;
   it.pad0 = it.pad1 = it.pad2 = 0;
@@ -349,6 +351,7 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
 // ------------------------------------------------------------ 5. flash kernel
 #include "wx_flash.cuh"
 #include "wx_flash2.cuh"
+#include "wx_flash4.cuh"
 
 // ------------------------------------------------------------- host driver
 // Share of the softmax exponentials taken by the FMA-pipe polynomial (pairs out of
@@ -364,11 +367,13 @@ static int exp_poly_pairs() {
 
 // Flash kernel variant (tuning knob WX_ATTN_KERNEL, read once): 1 = one CTA per SM
 // with double-buffered S/P (flash_attn_kernel), 2 = two CTAs per SM with P in
-// TMEM (flash_attn2_kernel).
+// TMEM (flash_attn2_kernel, the default), 4 = persistent, softmax split over two
+// warpgroups, two MMA issuers (flash_attn4_kernel).
 static int attn_kernel_variant() {
   static int v = [] {
     const char* e = getenv("WX_ATTN_KERNEL");
-    return (e && atoi(e) == 1) ? 1 : 2;
+    const int x = e ? atoi(e) : 2;
+    return (x == 1 || x == 4) ? x : 2;
   }();
   return v;
 }
@@ -403,7 +408,7 @@ static size_t list_bytes(const AttnGeom& a) {
   c.take((size_t)a.H * a.nvt * 4);            // counts
   c.take(((size_t)a.H * a.nvt + 1) * 4);      // offsets
   c.take((size_t)a.H * a.nvt * (size_t)((a.nb + a.qpb - 1) / a.qpb + 1) * 16);  // entries (worst case)
-  c.take((size_t)a.H * (a.nst + a.nvt) * sizeof(WorkItem));
+  c.take(((size_t)a.H * (a.nst + a.nvt) + 1) * sizeof(WorkItem));  // + work counter
   return c.off;
 }
 
@@ -491,6 +496,24 @@ static int run_routing(wx_ctx* ctx, const void* q, const void* k, const void* v,
   return WX_OK;
 }
 
+// The register split of flash_attn4_kernel (setmaxnreg) must fit the register
+// file the launch reserves: check the compiled per-thread count once.
+static bool flash4_regs_ok(int poly) {
+  static int ok[3] = {-1, -1, -1};
+  const int i = poly < 0 ? 0 : (poly > 2 ? 2 : poly);
+  if (ok[i] < 0) {
+    cudaFuncAttributes fa{};
+    const void* fn = i == 0 ? (const void*)flash_attn4_kernel<0>
+                            : (i == 1 ? (const void*)flash_attn4_kernel<1> : (const void*)flash_attn4_kernel<2>);
+    ok[i] = cudaFuncGetAttributes(&fa, fn) == cudaSuccess &&
+            fa.numRegs * kA4Threads >= kA4RegsLow * 128 + kA4RegsHigh * 256;
+    if (!ok[i])
+      fprintf(stderr, "wx: flash_attn4 register split does not fit %d registers/thread; using flash_attn2\n",
+              fa.numRegs);
+  }
+  return ok[i] == 1;
+}
+
 static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, const AttnGeom& a,
                      const wx_sparse_spec* spec, float scale, const uint8_t* sel, const __nv_bfloat16* cm,
                      const __nv_bfloat16* vsum, const float* lens, uint8_t* base, void* out, int64_t os) {
@@ -503,7 +526,8 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   int* offsets = reinterpret_cast<int*>(base + c.take(((size_t)a.H * a.nvt + 1) * 4));
   int4* entries = reinterpret_cast<int4*>(
       base + c.take((size_t)a.H * a.nvt * (size_t)((a.nb + a.qpb - 1) / a.qpb + 1) * 16));
-  WorkItem* items = reinterpret_cast<WorkItem*>(base + c.take((size_t)a.H * (a.nst + a.nvt) * sizeof(WorkItem)));
+  WorkItem* items =
+      reinterpret_cast<WorkItem*>(base + c.take(((size_t)a.H * (a.nst + a.nvt) + 1) * sizeof(WorkItem)));
   const bool tail = !a.dense && spec->tail && cm && vsum && lens;
   const int64_t n_items = (int64_t)a.H * (a.nst + a.nvt);
   int st;
@@ -540,6 +564,8 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
     for (auto fn : {flash_attn2_kernel<0>, flash_attn2_kernel<1>, flash_attn2_kernel<2>})
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA2Smem);
+    for (auto fn : {flash_attn4_kernel<0>, flash_attn4_kernel<1>, flash_attn4_kernel<2>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA4Smem);
     if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
     attr = true;
   }
@@ -555,9 +581,23 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = os;
   p.err = ctx->dev_err;
+
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
   ProfScope prof(ctx, kProfAttn);
   const int poly = exp_poly_pairs();
+  if (attn_kernel_variant() == 4 && flash4_regs_ok(poly)) {
+    // persistent: one CTA per SM, items fetched dynamically, softmax split over two warpgroups
+    const unsigned grid = (unsigned)std::min<int64_t>(ctx->num_sms, n_items);
+    int* counter = reinterpret_cast<int*>(items + n_items);
+    const int ni = (int)n_items;
+    if (poly == 0)
+      flash_attn4_kernel<0><<<grid, kA4Threads, kA4Smem, ctx->stream>>>(tq, tk, tv, p, ni, counter);
+    else if (poly == 2)
+      flash_attn4_kernel<2><<<grid, kA4Threads, kA4Smem, ctx->stream>>>(tq, tk, tv, p, ni, counter);
+    else
+      flash_attn4_kernel<1><<<grid, kA4Threads, kA4Smem, ctx->stream>>>(tq, tk, tv, p, ni, counter);
+    return launch_status(ctx, "flash_attn4");
+  }
   if (attn_kernel_variant() == 2) {
     if (poly == 0)
       flash_attn2_kernel<0><<<(unsigned)n_items, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);

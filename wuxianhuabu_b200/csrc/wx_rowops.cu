@@ -93,6 +93,73 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   }
 }
 
+// Same operation for head_dim 128 with rot/2 a multiple of 4, sized for HBM:
+// one warp per (s, part, group of up to 8 heads). Every load of the group
+// (8 rows x 256 B, plus the position's cos/sin) is issued before any use, so a
+// warp keeps ~2.5 KB in flight instead of one 256-B row, and the rotation
+// partner (j +- rot/2) comes from lane +- rot/8 by shuffle.
+constexpr int kRopeHeads = 8;
+__global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
+    const __nv_bfloat16* x, int64_t x_stride, __nv_bfloat16* out,
+    int64_t out_stride, int64_t part_off, int nparts, int64_t S, int H, int n_groups,
+    const __nv_bfloat16* __restrict__ w0, const __nv_bfloat16* __restrict__ w1,
+    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int rot, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t task = (int64_t)blockIdx.x * 8 + warp;
+  if (task >= S * nparts * n_groups) return;
+  const int g = (int)(task % n_groups);
+  const int part = (int)((task / n_groups) % nparts);
+  const int64_t s = task / ((int64_t)n_groups * nparts);
+  const int h0 = g * kRopeHeads;
+  const int nh = min(kRopeHeads, H - h0);
+  const int64_t xoff = s * x_stride + part * part_off + (int64_t)h0 * 128 + lane * 4;
+  const int64_t ooff = s * out_stride + part * part_off + (int64_t)h0 * 128 + lane * 4;
+  uint2 raw[kRopeHeads];
+#pragma unroll
+  for (int i = 0; i < kRopeHeads; ++i)
+    if (i < nh) raw[i] = *reinterpret_cast<const uint2*>(x + xoff + i * 128);  // may alias out (in place)
+  const int rh = rot >> 1;
+  const int j0 = lane * 4;
+  const bool rotated = j0 < rot;
+  const bool first = j0 < rh;
+  uint2 cr = make_uint2(0, 0), sr = make_uint2(0, 0);
+  if (rotated) {
+    const int64_t t = s * rh + (first ? j0 : j0 - rh);
+    cr = __ldg(reinterpret_cast<const uint2*>(cos_t + t));
+    sr = __ldg(reinterpret_cast<const uint2*>(sin_t + t));
+  }
+  const uint2 wr = __ldg(reinterpret_cast<const uint2*>((part == 0 ? w0 : w1) + j0));
+  const float wv[4] = {bf16_lo(wr.x), bf16_hi(wr.x), bf16_lo(wr.y), bf16_hi(wr.y)};
+  const float c[4] = {bf16_lo(cr.x), bf16_hi(cr.x), bf16_lo(cr.y), bf16_hi(cr.y)};
+  const float sn[4] = {bf16_lo(sr.x), bf16_hi(sr.x), bf16_lo(sr.y), bf16_hi(sr.y)};
+  const int partner = first ? lane + (rh >> 2) : lane - (rh >> 2);
+  const int src = rotated ? partner : lane;
+#pragma unroll
+  for (int i = 0; i < kRopeHeads; ++i) {
+    if (i >= nh) break;
+    const float xv[4] = {bf16_lo(raw[i].x), bf16_hi(raw[i].x), bf16_lo(raw[i].y), bf16_hi(raw[i].y)};
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += xv[e] * xv[e];
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / 128.f + eps);
+    float nv[4], o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) nv[e] = round_bf16(xv[e] * rstd * wv[e]);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float pv = __shfl_sync(0xffffffffu, nv[e], src);
+      if (!rotated)
+        o[e] = nv[e];
+      else if (first)
+        o[e] = nv[e] * c[e] - pv * sn[e];
+      else
+        o[e] = nv[e] * c[e] + pv * sn[e];
+    }
+    *reinterpret_cast<uint2*>(out + ooff + i * 128) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+  }
+}
+
 // ----------------------------------------------------------------- K4
 // h3_fused_norm_modscale (fused:133-168): one warp per row, two passes over
 // the row (the second pass hits L1).
@@ -323,6 +390,18 @@ int launch_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, void* out,
   auto W1 = static_cast<const __nv_bfloat16*>(w1);
   auto C = static_cast<const __nv_bfloat16*>(cos_t);
   auto Sn = static_cast<const __nv_bfloat16*>(sin_t);
+  const int rh = rot >> 1;
+  const bool vec_ok = hd == 128 && rh % 4 == 0 && x_stride % 4 == 0 && out_stride % 4 == 0 && part_off % 4 == 0 &&
+                      (reinterpret_cast<uintptr_t>(x) & 7) == 0 && (reinterpret_cast<uintptr_t>(out) & 7) == 0 &&
+                      (reinterpret_cast<uintptr_t>(w0) & 7) == 0 && (nparts < 2 || (reinterpret_cast<uintptr_t>(w1) & 7) == 0) &&
+                      (rot == 0 || ((reinterpret_cast<uintptr_t>(cos_t) & 7) == 0 && (reinterpret_cast<uintptr_t>(sin_t) & 7) == 0));
+  if (vec_ok) {
+    const int n_groups = (H + kRopeHeads - 1) / kRopeHeads;
+    const int64_t tasks = S * nparts * n_groups;
+    qk_norm_rope_vec_kernel<<<(unsigned)((tasks + 7) / 8), 256, 0, ctx->stream>>>(
+        X, x_stride, O, out_stride, part_off, nparts, S, H, n_groups, W0, W1, C, Sn, rot, eps);
+    return launch_status(ctx, "qk_norm_rope");
+  }
   if (hd == 128)
     qk_norm_rope_kernel<128><<<grid, 256, 0, ctx->stream>>>(X, x_stride, O, out_stride, part_off, nparts, S,
                                                              H, W0, W1, C, Sn, rot, eps);
