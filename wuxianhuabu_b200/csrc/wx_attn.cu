@@ -309,19 +309,35 @@ __global__ void list_fill_kernel(const uint8_t* __restrict__ sel, int H, int nb,
 // thread per item: strip/dense items first (the heaviest), then video tiles;
 // head-major within each group so that the CTAs resident at one time share
 // one head's K/V in L2
+// Item order: first the PAIRED strip / dense items (pair p = items 2p, 2p+1: two
+// consecutive query tiles of one head, both walking every key tile), then the
+// unpaired strip tile of each head when the head has an odd number, then the
+// video items (head-major). npair_h = pairs per head (0 when pairing is off).
 __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int dense_all, int qpb, int nb,
-                             const int* __restrict__ offsets, WorkItem* __restrict__ items) {
+                             int npair_h, const int* __restrict__ offsets, WorkItem* __restrict__ items) {
   const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
   const int64_t n_strip = (int64_t)H * nst;
   const int64_t n_items = n_strip + (int64_t)H * nvt;
   if (i == 0) items[n_items].q_start = 0;  // work counter of the persistent flash kernel
   if (i >= n_items) return;
+  const int64_t n_paired = 2 * (int64_t)H * npair_h;
+  const int n_rest = nst - 2 * npair_h;  // unpaired strip tiles per head
   WorkItem it;
   it.pad0 = it.pad1 = it.pad2 = 0;
   const int kt_all = (int)((S + 127) / 128);
-  if (i < n_strip) {
-    const int t = (int)(i % nst);
-    it.head = (int)(i / nst);
+  int strip_h = -1, strip_t = 0;
+  if (i < n_paired) {
+    const int64_t pr = i >> 1;
+    strip_h = (int)(pr / npair_h);
+    strip_t = 2 * (int)(pr % npair_h) + (int)(i & 1);
+  } else if (i < n_strip) {
+    const int64_t r = i - n_paired;
+    strip_h = (int)(r / n_rest);
+    strip_t = 2 * npair_h + (int)(r % n_rest);
+  }
+  if (strip_h >= 0) {
+    const int t = strip_t;
+    it.head = strip_h;
     it.q_start = t * 128;
     const int64_t lim = dense_all ? S : g;
     it.q_rows = (int)min64(128, lim - (int64_t)t * 128);
@@ -352,6 +368,7 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
 #include "wx_flash.cuh"
 #include "wx_flash2.cuh"
 #include "wx_flash4.cuh"
+#include "wx_flash5.cuh"
 
 // ------------------------------------------------------------- host driver
 // Share of the softmax exponentials taken by the FMA-pipe polynomial (pairs out of
@@ -514,6 +531,28 @@ static bool flash4_regs_ok(int poly) {
   return ok[i] == 1;
 }
 
+static bool flash_pair_regs_ok(int poly) {
+  static int ok[3] = {-1, -1, -1};
+  const int i = poly < 0 ? 0 : (poly > 2 ? 2 : poly);
+  if (ok[i] < 0) {
+    cudaFuncAttributes fa{};
+    const void* fn = i == 0 ? (const void*)flash_attn_pair_kernel<0>
+                            : (i == 1 ? (const void*)flash_attn_pair_kernel<1> : (const void*)flash_attn_pair_kernel<2>);
+    ok[i] = cudaFuncGetAttributes(&fa, fn) == cudaSuccess &&
+            fa.numRegs * kA5Threads >= kA4RegsLow * 128 + kA4RegsHigh * 256;
+  }
+  return ok[i] == 1;
+}
+
+// Pair strip / dense query tiles that walk the same key tiles (WX_ATTN_PAIRS, read once; 0 = off).
+static int attn_pairs() {
+  static int v = [] {
+    const char* e = getenv("WX_ATTN_PAIRS");
+    return (e && atoi(e) == 0) ? 0 : 1;
+  }();
+  return v;
+}
+
 static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, const AttnGeom& a,
                      const wx_sparse_spec* spec, float scale, const uint8_t* sel, const __nv_bfloat16* cm,
                      const __nv_bfloat16* vsum, const float* lens, uint8_t* base, void* out, int64_t os) {
@@ -530,6 +569,9 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
       reinterpret_cast<WorkItem*>(base + c.take(((size_t)a.H * (a.nst + a.nvt) + 1) * sizeof(WorkItem)));
   const bool tail = !a.dense && spec->tail && cm && vsum && lens;
   const int64_t n_items = (int64_t)a.H * (a.nst + a.nvt);
+  // strip / dense query tiles walk every key tile: pair them to share K/V loads
+  const int npair_h = attn_pairs() ? a.nst / 2 : 0;
+  const int64_t n_pairs = (int64_t)a.H * npair_h;
   int st;
   {
   ProfScope prof(ctx, kProfRoute);
@@ -548,7 +590,7 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   }
 
   items_kernel<<<(unsigned)((n_items + 127) / 128), 128, 0, ctx->stream>>>(a.H, a.nst, a.nvt, a.S, a.g, a.dense,
-                                                                             a.qpb, a.nb, offsets, items);
+                                                                             a.qpb, a.nb, npair_h, offsets, items);
   if ((st = launch_status(ctx, "items"))) return st;
   }
 
@@ -566,6 +608,8 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA2Smem);
     for (auto fn : {flash_attn4_kernel<0>, flash_attn4_kernel<1>, flash_attn4_kernel<2>})
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA4Smem);
+    for (auto fn : {flash_attn_pair_kernel<0>, flash_attn_pair_kernel<1>, flash_attn_pair_kernel<2>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA5Smem);
     if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
     attr = true;
   }
@@ -585,11 +629,26 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
   ProfScope prof(ctx, kProfAttn);
   const int poly = exp_poly_pairs();
+  if (n_pairs > 0) {
+    if (!flash_pair_regs_ok(poly)) return set_error(ctx, WX_ERR_CUDA, "flash_attn_pair: register split does not fit");
+    if (poly == 0)
+      flash_attn_pair_kernel<0><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p);
+    else if (poly == 2)
+      flash_attn_pair_kernel<2><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p);
+    else
+      flash_attn_pair_kernel<1><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p);
+    if ((st = launch_status(ctx, "flash_attn_pair"))) return st;
+  }
+  // the remaining (unpaired) items
+  WorkItem* const items_all = items;
+  const int64_t n_rest = n_items - 2 * n_pairs;
+  p.items = items + 2 * n_pairs;
+  if (n_rest == 0) return WX_OK;
   if (attn_kernel_variant() == 4 && flash4_regs_ok(poly)) {
     // persistent: one CTA per SM, items fetched dynamically, softmax split over two warpgroups
-    const unsigned grid = (unsigned)std::min<int64_t>(ctx->num_sms, n_items);
-    int* counter = reinterpret_cast<int*>(items + n_items);
-    const int ni = (int)n_items;
+    const unsigned grid = (unsigned)std::min<int64_t>(ctx->num_sms, n_rest);
+    int* counter = reinterpret_cast<int*>(items_all + n_items);
+    const int ni = (int)n_rest;
     if (poly == 0)
       flash_attn4_kernel<0><<<grid, kA4Threads, kA4Smem, ctx->stream>>>(tq, tk, tv, p, ni, counter);
     else if (poly == 2)
@@ -600,19 +659,19 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   }
   if (attn_kernel_variant() == 2) {
     if (poly == 0)
-      flash_attn2_kernel<0><<<(unsigned)n_items, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
+      flash_attn2_kernel<0><<<(unsigned)n_rest, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
     else if (poly == 2)
-      flash_attn2_kernel<2><<<(unsigned)n_items, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
+      flash_attn2_kernel<2><<<(unsigned)n_rest, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
     else
-      flash_attn2_kernel<1><<<(unsigned)n_items, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
+      flash_attn2_kernel<1><<<(unsigned)n_rest, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
     return launch_status(ctx, "flash_attn2");
   }
   if (poly == 0)
-    flash_attn_kernel<0><<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
+    flash_attn_kernel<0><<<(unsigned)n_rest, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
   else if (poly == 2)
-    flash_attn_kernel<2><<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
+    flash_attn_kernel<2><<<(unsigned)n_rest, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
   else
-    flash_attn_kernel<1><<<(unsigned)n_items, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
+    flash_attn_kernel<1><<<(unsigned)n_rest, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
   return launch_status(ctx, "flash_attn");
 }
 

@@ -1,0 +1,322 @@
+// wx_flash5.cuh — flash-attention kernel for PAIRS of query tiles that walk the
+// same key tiles (strip rows and dense layers: every key of the sequence), so
+// each K/V tile is loaded once for 256 query rows (included by wx_attn.cu after
+// wx_flash.cuh and wx_flash4.cuh, whose helpers it shares).
+//
+// One CTA per pair (head, q tiles A and B). Per key tile t the tensor pipe runs
+// S_X = Q_X K^T and O_X += P_X V for X in {A, B} (2048 cycles); the shared K/V
+// tile (64 KB) halves the load traffic per FLOP of the single-tile kernels.
+//   TMEM (512 columns): S/P_A [0,128), S/P_B [128,256), O_A [256,384), O_B [384,512);
+//   P_X overwrites the first 64 columns of S_X as packed bf16.
+//   Shared memory: Q_A, Q_B, K ring of 3, V ring of 2 (32 KB tiles, SW128).
+//   Warp 0: TMA producer. Warp 1 / warp 2: MMA issuer of slot A / B (one
+//   thread each: S_X(t), then after P_X(t) the PV_X(t), then S_X(t+1) — the
+//   tensor pipe runs one thread's MMAs in issue order, so S_X(t+1) cannot
+//   overwrite P_X(t) before PV_X(t) has read it). Warp 3: idle.
+//   Warps 4-7 / 8-11: softmax + epilogue of slot A / B (thread r owns row r).
+// The exponential phases of the two slots' softmaxes take turns (A(t) after
+// B(t-1), B(t) after A(t)); the TMEM loads and row max of one slot overlap the
+// exponentials of the other, and the tensor pipe runs PV and the next S meanwhile.
+#pragma once
+
+constexpr int kA5Threads = 384;
+constexpr int kA5KStages = 3;
+constexpr int kA5VStages = 2;
+constexpr int kA5BarOff = (2 + kA5KStages + kA5VStages) * kTileBytes;
+constexpr int kA5Smem = kA5BarOff + 512 + 1024;
+static_assert(kA5Threads == kA4Threads, "uses the register split of flash_attn4_kernel (kA4RegsLow/High)");
+
+enum : int {
+  kB5QFull = 0,
+  kB5KFull = 1,   // [3]
+  kB5KEmpty = 4,  // [3] count 2 (both slots' S)
+  kB5VFull = 7,   // [2]
+  kB5VEmpty = 9,  // [2] count 2 (both slots' PV)
+  kB5SFull = 11,  // [2] per slot
+  kB5PFull = 13,  // [2] per slot, count 128
+  kB5OFull = 15,  // [2] per slot
+  kB5Drain = 17,  // [2] per slot
+  kB5Count = 19
+};
+
+template <int POLY>
+__global__ void __launch_bounds__(kA5Threads, 1)
+    flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  auto sQ = [&](int X) { return sbase + (uint32_t)X * kTileBytes; };
+  auto sK = [&](int s) { return sbase + (uint32_t)(2 + s) * kTileBytes; };
+  auto sV = [&](int s) { return sbase + (uint32_t)(2 + kA5KStages + s) * kTileBytes; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kA5BarOff);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the pair: items 2b and 2b+1 (same head, same key stream)
+  const WorkItem itA = p.items[2 * blockIdx.x];
+  const int n_kv = item_tiles(itA);
+  const int hcol = itA.head * 128;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kB5Count; ++i) {
+      uint32_t c = 1;
+      if (i == kB5KEmpty || i == kB5KEmpty + 1 || i == kB5KEmpty + 2 || i == kB5VEmpty || i == kB5VEmpty + 1) c = 2;
+      if (i == kB5PFull || i == kB5PFull + 1) c = 128;
+      mbar_init(bar(i), c);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    reg_dealloc4();
+    if (lane == 0 && n_kv > 0) {
+      // ------------------------------------------------------------ producer
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      bool ok = true;
+      uint32_t nk = 0, nv = 0;
+      mbar_arrive_expect_tx(bar(kB5QFull), 2 * kTileBytes);
+      for (int X = 0; X < 2; ++X) {
+        const int q0 = p.items[2 * blockIdx.x + X].q_start;
+        for (int ch = 0; ch < 2; ++ch)
+          for (int rh = 0; rh < 2; ++rh)
+            tma_load_2d(sQ(X) + ch * 16384 + rh * 8192, &tmQ, bar(kB5QFull), hcol + ch * 64, q0 + rh * 64);
+      }
+      auto load = [&](bool is_k, int j) -> bool {
+        const uint32_t cnt = is_k ? nk : nv;
+        const int ns = is_k ? kA5KStages : kA5VStages;
+        const uint32_t s = cnt % ns, par = ((cnt / ns) & 1) ^ 1u;
+        const uint32_t full = bar((is_k ? kB5KFull : kB5VFull) + s);
+        if (!mbar_wait(bar((is_k ? kB5KEmpty : kB5VEmpty) + s), par, p.err, kDevTimeoutEmpty, abort_flag))
+          return false;
+        const int4 e = kv_entry(itA, p.entries, j);
+        const uint32_t dst = is_k ? sK(s) : sV(s);
+        const CUtensorMap* tm = is_k ? &tmK : &tmV;
+        mbar_arrive_expect_tx(full, kTileBytes);
+        for (int ch = 0; ch < 2; ++ch) {
+          tma_load_2d(dst + ch * 16384, tm, full, hcol + ch * 64, e.x);
+          tma_load_2d(dst + ch * 16384 + 8192, tm, full, hcol + ch * 64, e.y);
+        }
+        if (is_k) ++nk; else ++nv;
+        return true;
+      };
+      // consumption order of each issuer: K(0), V(0), K(1), V(1), ... with the K
+      // ring two tiles ahead of the V ring
+      ok = load(true, 0) && (n_kv < 2 || load(true, 1));
+      for (int t = 0; t < n_kv && ok; ++t) {
+        ok = load(false, t);
+        if (ok && t + 2 < n_kv) ok = load(true, t + 2);
+      }
+      if (!ok) {  // let copies already issued land before the CTA exits
+        mbar_drain(bar(kB5QFull), 0);
+        for (uint32_t i = nk > kA5KStages ? nk - kA5KStages : 0; i < nk; ++i)
+          mbar_drain(bar(kB5KFull + i % kA5KStages), (i / kA5KStages) & 1);
+        for (uint32_t i = nv > kA5VStages ? nv - kA5VStages : 0; i < nv; ++i)
+          mbar_drain(bar(kB5VFull + i % kA5VStages), (i / kA5VStages) & 1);
+      }
+    }
+  } else if (warp == 1 || warp == 2) {
+    reg_dealloc4();
+    if (lane == 0 && n_kv > 0) {
+      // ------------------------------------------------------------ MMA issuer of slot X
+      const int X = warp - 1;
+      constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);  // A = P from TMEM, B = V MN-major
+      const uint32_t tS = tmem + (uint32_t)(X * 128);
+      const uint32_t tO = tmem + 256 + (uint32_t)(X * 128);
+      bool ok = mbar_wait(bar(kB5QFull), 0, p.err, kDevTimeoutFull, abort_flag);
+      bool issued = false;
+      const uint64_t dq = opaque64(smem_desc_sw128(sQ(X), 16, 1024));
+      for (int t = 0; t < n_kv && ok; ++t) {
+        const uint32_t ks = (uint32_t)t % kA5KStages, vs = (uint32_t)t % kA5VStages;
+        if (!mbar_wait(bar(kB5KFull + ks), ((uint32_t)t / kA5KStages) & 1, p.err, kDevTimeoutFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t dk = opaque64(smem_desc_sw128(sK(ks), 16, 1024));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          umma_bf16(tS, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        issued = true;
+        umma_commit(bar(kB5SFull + X));
+        umma_commit(bar(kB5KEmpty + ks));
+        if (!mbar_wait(bar(kB5PFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag) ||
+            !mbar_wait(bar(kB5VFull + vs), ((uint32_t)t / kA5VStages) & 1, p.err, kDevTimeoutFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t dv = opaque64(smem_desc_sw128(sV(vs), 16384, 1024));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_bf16_ts(tO, tS + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(bar(kB5VEmpty + vs));
+      }
+      if (ok) umma_commit(bar(kB5OFull + X));
+      if (issued) {  // every MMA of this thread completes before TMEM is released
+        umma_commit(bar(kB5Drain + X));
+        mbar_drain(bar(kB5Drain + X), 0);
+      }
+    }
+  } else if (warp == 3) {
+    reg_dealloc4();
+  } else {
+    reg_alloc4();
+    // ------------------------------------------------ softmax + epilogue of slot X
+    const int X = (warp - 4) >> 2;
+    const WorkItem it = p.items[2 * blockIdx.x + X];
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qh = r >> 6;
+    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
+    const uint32_t tS = tmem + lane_addr + (uint32_t)(X * 128);
+    const uint32_t tO = tmem + lane_addr + 256 + (uint32_t)(X * 128);
+    float m = -INFINITY;
+    float l = 0.f;
+    bool ok = true;
+    int4 e = n_kv > 0 ? kv_entry(it, p.entries, 0) : make_int4(0, 0, 0, 0);
+    for (int t = 0; t < n_kv; ++t) {
+      const int4 cur = e;
+      if (t + 1 < n_kv) e = kv_entry(it, p.entries, t + 1);
+      if (!mbar_wait(bar(kB5SFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float v[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(v + c * 32));
+      tmem_wait_ld();
+      const int lim0 = ((cur.z >> (8 + qh)) & 1) ? (cur.z & 0xFF) : 0;
+      const int lim1 = ((cur.w >> (8 + qh)) & 1) ? (cur.w & 0xFF) : 0;
+      if (__any_sync(0xffffffffu, lim0 != 64 || lim1 != 64)) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if ((i & 63) >= ((i < 64) ? lim0 : lim1)) v[i] = -INFINITY;
+      }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < 128; i += 8) {
+        mx[0] = max3f(mx[0], v[i], v[i + 1]);
+        mx[1] = max3f(mx[1], v[i + 2], v[i + 3]);
+        mx[2] = max3f(mx[2], v[i + 4], v[i + 5]);
+        mx[3] = max3f(mx[3], v[i + 6], v[i + 7]);
+      }
+      const float m_new = fmaxf(m, max3f(fmaxf(mx[0], mx[1]), mx[2], mx[3]));
+      bool need = false;
+      if (t == 0) {
+        m = m_new;
+      } else {
+        need = (m_new - m) * p.sl2 > 8.0f;
+      }
+      const bool any_need = __any_sync(0xffffffffu, need);
+      float alpha = 1.0f;
+      if (need) {
+        alpha = ex2((m - m_new) * p.sl2);
+        m = m_new;
+      }
+      // The exponential phases of the two slots take turns (A(0), B(0), A(1),
+      // B(1), ...): run together they would share the MUFU pipe while the tensor
+      // pipe idles; in turns, each overlaps the other slot's TMEM loads, row max,
+      // PV and next S.
+      const bool turn = X == 0 ? (t == 0 || mbar_wait(bar(kB5PFull + 1), ((uint32_t)t - 1) & 1, p.err,
+                                                       kDevTimeoutSoftmax, abort_flag))
+                               : mbar_wait(bar(kB5PFull + 0), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag);
+      if (!turn) {
+        ok = false;
+        break;
+      }
+      const float mu = (m == -INFINITY) ? 0.f : m * p.sl2;
+      const float2 sl2x2 = make_float2(p.sl2, p.sl2);
+      const float2 nmu2 = make_float2(-mu, -mu);
+      float2 rs2[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) rs2[q] = make_float2(0.f, 0.f);
+      // p = 2^(s*scale*log2e - m) as packed bf16 over the first 64 S columns (read above)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 a = __ffma2_rn(make_float2(v[32 * c + 2 * i], v[32 * c + 2 * i + 1]), sl2x2, nmu2);
+          float2 pv;
+          if ((i & 3) < POLY) {
+            pv = ex2_poly2(a);
+          } else {
+            pv = make_float2(ex2(a.x), ex2(a.y));
+          }
+          rs2[i & 3] = __fadd2_rn(rs2[i & 3], pv);
+          pk[i] = pack_bf16x2(pv.x, pv.y);
+        }
+        tmem_st16(tS + c * 16, pk);
+      }
+      if (any_need) {
+        // PV_X(t-1) completed before S_X(t) (in-order tensor pipe): O_X is stable
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      tmem_wait_st();
+      {
+        const float2 a = __fadd2_rn(rs2[0], rs2[1]), c2 = __fadd2_rn(rs2[2], rs2[3]);
+        const float2 u = __fadd2_rn(a, c2);
+        l = l * alpha + (u.x + u.y);
+      }
+      tc_fence_before();
+      mbar_arrive(bar(kB5PFull + X));
+    }
+    if (ok && n_kv > 0) ok = mbar_wait(bar(kB5OFull + X), 0, p.err, kDevTimeoutSoftmax, abort_flag);
+    tc_fence_after();
+    // epilogue: O / l -> bf16 rows (pairs are formed only from items without a tail term)
+    const float inv = l > 0.f ? 1.0f / l : 0.f;
+    const bool row_ok = ok && r < it.q_rows;
+    __nv_bfloat16* orow = p.out + (int64_t)(it.q_start + r) * p.out_stride + it.head * 128;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      if (n_kv > 0) {
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      if (row_ok) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 8)
+          *reinterpret_cast<uint4*>(orow + c * 32 + i) =
+              make_uint4(pack_bf16x2(o[i] * inv, o[i + 1] * inv), pack_bf16x2(o[i + 2] * inv, o[i + 3] * inv),
+                         pack_bf16x2(o[i + 4] * inv, o[i + 5] * inv), pack_bf16x2(o[i + 6] * inv, o[i + 7] * inv));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
