@@ -75,6 +75,29 @@ typedef struct wx_sparse_spec {
 } wx_sparse_spec;
 
 /* one DiT block's weights (H3BlockW / H3AttnW / H3MlpW, H3Transformer.swift:405-660) */
+/* One LoRA adapter of a linear (LoraRef, H3Common.swift:407-411): the layer adds
+ * scale * ((x A) B) (loraDelta, H3Common.swift:424-433). a [k, r] and b [r, n] bf16,
+ * row-major (the reference's [in, r] and [r, out]). */
+typedef struct wx_lora {
+  const void* a;
+  const void* b;
+  int32_t r;
+  float scale;
+} wx_lora;
+
+/* The adapters of one linear packed as an extension of the GEMM's K dimension:
+ * y = x W^T + t bt^T with t = x at^T ([m, R] bf16, computed per call), so the
+ * delta accumulates in the same fp32 accumulator as the base product.
+ * at [R, k] = scale_i * A_i^T stacked over adapters; bt [n, R] = B_i^T side by side;
+ * R = sum r_i rounded up to 64 (zero padding). Built by wx_lora_pack_build. */
+typedef struct wx_lora_pack {
+  void* at;
+  void* bt;
+  int64_t R;
+  int64_t n;
+  int64_t k;
+} wx_lora_pack;
+
 typedef struct wx_block_weights {
   wx_qweight qkv; /* hidden -> 3*inner */
   wx_qweight out; /* inner -> hidden */
@@ -84,6 +107,10 @@ typedef struct wx_block_weights {
   const void* k_norm;
   const void* norm1; /* [hidden] bf16 */
   const void* norm2;
+  /* LoRA of qkv / out / fc1 / fc2 (H3LoraFile entries, H3Common.swift:436-496;
+   * attached in production, H3Pipeline.swift:680-687); NULL = none. Each pack's
+   * R must not exceed wx_dit_config.lora_rank. */
+  const wx_lora_pack* lora[4];
 } wx_block_weights;
 
 /* model geometry (H3Config, H3Common.swift:78-139) */
@@ -95,7 +122,7 @@ typedef struct wx_dit_config {
   int32_t mlp_kind; /* wx_mlp_kind */
   int32_t rot;      /* rotated dims (rotHalf*2); dims [rot, head_dim) pass through */
   float eps;        /* RMSNorm epsilon */
-  int32_t reserved;
+  int32_t lora_rank; /* largest packed LoRA rank R of any linear (0 = no LoRA); sizes scratch */
 } wx_dit_config;
 
 /* AdaLN modulation tables of one block, each [num_mod_rows, hidden] bf16:
@@ -153,6 +180,20 @@ int wx_dequantize_affine(wx_ctx* ctx, const wx_qweight* w, void* w_out);
 int wx_qlinear(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
                int epilogue, const void* gate, const void* resid, const uint32_t* rowmap,
                void* y, int64_t ldy, void* y_raw);
+
+/* Bytes of the packed LoRA operands of a linear [n, k] with `count` adapters:
+ * *R = sum r_i rounded up to 64, *at_bytes = R*k*2, *bt_bytes = n*R*2. */
+int wx_lora_pack_bytes(int64_t n, int64_t k, const wx_lora* l, int count, int64_t* R, size_t* at_bytes,
+                       size_t* bt_bytes);
+/* Build the packed operands (device buffers at, bt of wx_lora_pack_bytes' sizes)
+ * from adapters in device memory; at = bf16(scale_i * A_i^T), bt = B_i^T. */
+int wx_lora_pack_build(wx_ctx* ctx, int64_t n, int64_t k, const wx_lora* l, int count, wx_lora_pack* out);
+/* wx_qlinear plus the LoRA delta (MfLinear.forward with lora.hasAdapters,
+ * H3Common.swift:369-375): two MMA passes into one accumulator, then the epilogue.
+ * lora NULL = wx_qlinear. WX_EPI_SWIGLU is supported. */
+int wx_qlinear_lora(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                    const wx_lora_pack* lora, int epilogue, const void* gate, const void* resid,
+                    const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw);
 
 /* No counterpart in the reference. wx_qlinear for callers that cannot allocate
  * device memory (a host whose engine or restricted allocator owns every device

@@ -136,6 +136,40 @@ def qlinear(x, wq, sc, bi, bits=6, group=64, bias=None, epilogue=EPI_NONE, gate=
     return (y, raw) if want_raw else y
 
 
+def lora_delta(x, loras):
+    """loraDelta (H3Common.swift:424-433) with the reference's bf16 intermediates:
+    sum_i bf16(bf16(bf16(x A_i) B_i) * scale_i), accumulated in bf16. x [m, k] bf16 bits;
+    loras = [(a [k, r] bf16 bits, b [r, n] bf16 bits, scale)]. Returns fp32 values."""
+    xf = bf16_to_f32(np.ascontiguousarray(x, dtype=np.uint16))
+    acc = None
+    for a, b, scale in loras:
+        xa = bf16_to_f32(f32_to_bf16(xf @ bf16_to_f32(a)))
+        d = bf16_to_f32(f32_to_bf16(xa @ bf16_to_f32(b)))
+        d = bf16_to_f32(f32_to_bf16(d * np.float32(bf16_to_f32(f32_to_bf16(np.float32(scale))))))
+        acc = d if acc is None else bf16_to_f32(f32_to_bf16(acc + d))
+    return acc
+
+
+def qlinear_lora(x, wq, sc, bi, loras, bits=6, group=64, bias=None, epilogue=EPI_NONE, gate=None, resid=None,
+                 rowmap=None, want_raw=False):
+    """MfLinear.forward with adapters (H3Common.swift:341-375): bf16(qmm + bias) + delta, rounded,
+    then the epilogue (GELU, or resid + y * gate[rowmap[r]]) in fp32 with one bf16 rounding.
+    want_raw: also return the linear's output before the epilogue."""
+    base = bf16_to_f32(qlinear(x, wq, sc, bi, bits, group, bias))
+    y = bf16_to_f32(f32_to_bf16(base + lora_delta(x, loras)))
+    if epilogue == EPI_NONE:
+        out = f32_to_bf16(y)
+    elif epilogue == EPI_GELU:
+        c = np.float32(0.7978845608028654)
+        out = f32_to_bf16(np.float32(0.5) * y * (np.float32(1) + np.tanh(c * (y + np.float32(0.044715) * y ** 3))))
+    elif epilogue == EPI_GATE_RESID:
+        g = bf16_to_f32(gate)[np.asarray(rowmap, dtype=np.int64)]
+        out = f32_to_bf16(bf16_to_f32(resid) + y * g)
+    else:
+        raise ValueError("qlinear_lora: unsupported epilogue")
+    return (out, f32_to_bf16(y)) if want_raw else out
+
+
 # --------------------------------------------------------------------------- row ops
 def qk_norm_rope(x: np.ndarray, w, cos, sin, rot: int, eps: float) -> np.ndarray:
     """x [S, H, hd] uint16 (contiguous)."""
@@ -238,15 +272,23 @@ def num_threads() -> int:
 def block_forward(h, w, mods, rowmap, cos, sin, cfg, route_fn=None, at_cached=None, refresh=True):
     """One H3 DiT block (H3Transformer.swift:1078-1159) composed from the oracle ops.
 
-    w: dict of quantized triples qkv/out/fc1/fc2 (wq, sc, bi, bias) and norms; mods: 6 tables;
+    w: dict of quantized triples qkv/out/fc1/fc2 (wq, sc, bi, bias) and norms, optionally
+    w["lora"][name] = [(a, b, scale), ...] (loraDelta, H3Common.swift:424-433); mods: 6 tables;
     route_fn(q, k, v) -> route dict or None for dense. Returns (h_new, at)."""
     S, hidden = h.shape
     H, hd = cfg["heads"], cfg["head_dim"]
     inner = H * hd
     eps = cfg["eps"]
+    lora = w.get("lora", {})
+
+    def lin(name, x, **kw):  # quantized linear, with its LoRA adapters when attached
+        if lora.get(name):
+            return qlinear_lora(x, *w[name][:3], lora[name], bias=w[name][3], **kw)
+        return qlinear(x, *w[name][:3], bias=w[name][3], **kw)
+
     if refresh or at_cached is None:
         m1 = norm_modscale(h, w["norm1"], mods[0], mods[1], rowmap, eps)
-        qkv = qlinear(m1, *w["qkv"][:3], bias=w["qkv"][3])
+        qkv = lin("qkv", m1)
         q = qkv[:, :inner].reshape(S, H, hd)
         k = qkv[:, inner:2 * inner].reshape(S, H, hd)
         v = np.ascontiguousarray(qkv[:, 2 * inner:].reshape(S, H, hd))
@@ -259,14 +301,13 @@ def block_forward(h, w, mods, rowmap, cos, sin, cfg, route_fn=None, at_cached=No
         else:
             att = sparse_attention(q, k, v, route["g"], float(scale), block=route["block"], route=route,
                                    tail=route["tail"])
-        ha, at = qlinear(att.reshape(S, inner), *w["out"][:3], bias=w["out"][3], epilogue=EPI_GATE_RESID,
-                         gate=mods[2], resid=h, rowmap=rowmap, want_raw=True)
+        ha, at = lin("out", att.reshape(S, inner), epilogue=EPI_GATE_RESID, gate=mods[2], resid=h, rowmap=rowmap,
+                     want_raw=True)
     else:
         at = at_cached
         ha = mod_gate(h, at, mods[2], rowmap)
     m2 = norm_modscale(ha, w["norm2"], mods[3], mods[4], rowmap, eps)
     act = EPI_SWIGLU if cfg.get("mlp_kind", 0) == 1 else EPI_GELU
-    f1 = qlinear(m2, *w["fc1"][:3], bias=w["fc1"][3], epilogue=act)
-    hn = qlinear(f1, *w["fc2"][:3], bias=w["fc2"][3], epilogue=EPI_GATE_RESID, gate=mods[5], resid=ha,
-                 rowmap=rowmap)
+    f1 = lin("fc1", m2, epilogue=act)
+    hn = lin("fc2", f1, epilogue=EPI_GATE_RESID, gate=mods[5], resid=ha, rowmap=rowmap)
     return hn, at

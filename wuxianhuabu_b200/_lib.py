@@ -42,14 +42,23 @@ class SparseSpec(C.Structure):
                 ("tail", C.c_int32), ("reserved", C.c_int32)]
 
 
+class Lora(C.Structure):
+    _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("r", C.c_int32), ("scale", C.c_float)]
+
+
+class LoraPack(C.Structure):
+    _fields_ = [("at", C.c_void_p), ("bt", C.c_void_p), ("R", C.c_int64), ("n", C.c_int64), ("k", C.c_int64)]
+
+
 class BlockWeights(C.Structure):
     _fields_ = [("qkv", QWeight), ("out", QWeight), ("fc1", QWeight), ("fc2", QWeight),
-                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("norm1", C.c_void_p), ("norm2", C.c_void_p)]
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("norm1", C.c_void_p), ("norm2", C.c_void_p),
+                ("lora", C.POINTER(LoraPack) * 4)]
 
 
 class DitConfig(C.Structure):
     _fields_ = [("hidden", C.c_int64), ("heads", C.c_int32), ("head_dim", C.c_int32), ("ffn", C.c_int64),
-                ("mlp_kind", C.c_int32), ("rot", C.c_int32), ("eps", C.c_float), ("reserved", C.c_int32)]
+                ("mlp_kind", C.c_int32), ("rot", C.c_int32), ("eps", C.c_float), ("lora_rank", C.c_int32)]
 
 
 class BlockMods(C.Structure):
@@ -98,6 +107,11 @@ _SIGS = {
     "wx_quantize_affine": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "wx_dequantize_affine": (_i32, [_vp, C.POINTER(QWeight), _vp]),
     "wx_qlinear": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "wx_lora_pack_bytes": (_i32, [_i64, _i64, C.POINTER(Lora), _i32, C.POINTER(_i64), C.POINTER(C.c_size_t),
+                                  C.POINTER(C.c_size_t)]),
+    "wx_lora_pack_build": (_i32, [_vp, _i64, _i64, C.POINTER(Lora), _i32, C.POINTER(LoraPack)]),
+    "wx_qlinear_lora": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), C.POINTER(LoraPack), _i32, _vp, _vp, _vp,
+                               _vp, _i64, _vp]),
     "wx_qlinear_noalloc": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
     "wx_qk_norm_rope": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _i32, _f32, _vp, _i64]),
     "wx_qk_norm_rope_qkv": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _f32]),

@@ -30,7 +30,7 @@ int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void
                            int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os, void* scratch);
 
 struct BlockLayout {
-  size_t m, qkv, att, at, ha, f1, wd, sw, attn, total;
+  size_t m, qkv, att, at, ha, f1, wd, sw, lt, attn, total;
 };
 
 static size_t al(size_t b) { return (b + 255) & ~size_t(255); }
@@ -52,6 +52,7 @@ static BlockLayout block_layout(const wx_dit_config* c, int64_t S) {
   const size_t nmax = std::max(std::max(3 * inner, (size_t)c->hidden), fc1_n);
   L.wd = off; off += al(std::max(wmax * 2, qlinear_ws_need(S, (int64_t)nmax, 1)));
   L.sw = off; off += c->mlp_kind == WX_MLP_SWIGLU ? al((size_t)S * fc1_n * 2) : 0;
+  L.lt = off; off += al((size_t)S * (size_t)std::max(0, c->lora_rank) * 2);  // x at^T of a LoRA pack
   // the widest attention plan this geometry can need (SOL 64-blocks with g = 0)
   wx_sparse_spec sol{};
   sol.mode = WX_SPARSE_SOL;
@@ -66,6 +67,14 @@ static BlockLayout block_layout(const wx_dit_config* c, int64_t S) {
   L.attn = off; off += al(std::max(a1, std::max(a2, a3)));
   L.total = off;
   return L;
+}
+
+// every attached LoRA pack matches its linear and fits the scratch sized by cfg->lora_rank
+bool lora_packs_ok(const wx_dit_config* cfg, const wx_block_weights* w) {
+  const wx_qweight* q[4] = {&w->qkv, &w->out, &w->fc1, &w->fc2};
+  for (int i = 0; i < 4; ++i)
+    if (w->lora[i] && (!lora_pack_ok(w->lora[i], q[i]) || w->lora[i]->R > cfg->lora_rank)) return false;
+  return true;
 }
 
 }  // namespace wx
@@ -95,6 +104,7 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
                         mods->gate_mlp);
   WX_CHECK_ARG(ctx, cfg->rot >= 0 && cfg->rot <= cfg->head_dim && (cfg->rot == 0 || (cos_t && sin_t)));
   WX_CHECK_ARG(ctx, pab_slot || refresh);
+  WX_CHECK_ARG(ctx, lora_packs_ok(cfg, w));
   const BlockLayout L = block_layout(cfg, S);
   uint8_t* base = static_cast<uint8_t*>(scratch);
   void* m = base + L.m;
@@ -104,6 +114,7 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
   void* f1 = base + L.f1;
   void* wd = base + L.wd;
   void* sw = base + L.sw;
+  void* lt = base + L.lt;
   int st;
   if (refresh || !pab_slot) {
     // m1 = norm1(h) * (scaleMSA + 1) + shiftMSA
@@ -111,8 +122,8 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
                                    cfg->eps, m)))
       return st;
     // qkv = qkv_proj(m1)
-    if ((st = qlinear_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
-                                   3 * inner, nullptr, wd, nullptr)))
+    if ((st = qlinear_lora_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
+                                   3 * inner, nullptr, wd, lt, nullptr)))
       return st;
     // per-head RMSNorm + RoPE of q and k, in place
     if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, S, cfg->heads, cfg->head_dim,
@@ -126,8 +137,8 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
       return st;
     // at = out_proj(att) (-> PAB slot); hAttn = h + at * gateMSA
     void* at_dst = pab_slot ? pab_slot : base + L.at;
-    if ((st = qlinear_with_scratch(ctx, att, S, inner, &w->out, WX_EPI_GATE_RESID, mods->gate_msa, h, rowmap, ha,
-                                   cfg->hidden, at_dst, wd, nullptr)))
+    if ((st = qlinear_lora_with_scratch(ctx, att, S, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID, mods->gate_msa, h, rowmap, ha,
+                                   cfg->hidden, at_dst, wd, lt, nullptr)))
       return st;
   } else {
     // PAB reuse: at = cache[bi]; hAttn = h + at * gateMSA (current step's gate)
@@ -139,12 +150,12 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
     return st;
   // fc1 + activation
   const int act = cfg->mlp_kind == WX_MLP_SWIGLU ? WX_EPI_SWIGLU : WX_EPI_GELU;
-  if ((st = qlinear_with_scratch(ctx, m, S, cfg->hidden, &w->fc1, act, nullptr, nullptr, nullptr, f1, cfg->ffn,
-                                 nullptr, wd, sw)))
+  if ((st = qlinear_lora_with_scratch(ctx, m, S, cfg->hidden, &w->fc1, w->lora[2], act, nullptr, nullptr, nullptr, f1, cfg->ffn,
+                                 nullptr, wd, lt, sw)))
     return st;
   // h = hAttn + fc2(f1) * gateMLP
-  return qlinear_with_scratch(ctx, f1, S, cfg->ffn, &w->fc2, WX_EPI_GATE_RESID, mods->gate_mlp, ha, rowmap, h,
-                              cfg->hidden, nullptr, wd, nullptr);
+  return qlinear_lora_with_scratch(ctx, f1, S, cfg->ffn, &w->fc2, w->lora[3], WX_EPI_GATE_RESID, mods->gate_mlp, ha, rowmap, h,
+                              cfg->hidden, nullptr, wd, lt, nullptr);
 }
 
 }  // extern "C"

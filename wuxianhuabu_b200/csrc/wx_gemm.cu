@@ -46,6 +46,7 @@ constexpr int kGroupM = 16;
 
 struct GemmParams {
   int M, N, K;
+  int K2;  // extra K columns read through the second operand pair (LoRA: t [M,K2], bt [N,K2]); 0 = none
   int tiles_m, tiles_n, num_tiles;
   __nv_bfloat16* y;
   int64_t ldy;
@@ -85,6 +86,7 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                         GemmParams p) {
   using L = GemmSmem<BN>;
   extern __shared__ uint8_t smem_raw[];
@@ -115,6 +117,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (p.K2 > 0) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 2 * BN);
@@ -124,7 +130,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int kblocks = p.K / kGemmBK;
+  // K blocks of the main operands, then of the extension pair (same stage layout)
+  const int kblocks1 = p.K / kGemmBK;
+  const int kblocks = kblocks1 + p.K2 / kGemmBK;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -141,8 +149,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
           mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
           const uint32_t sa = smem_u32(smem + stage * L::kStageBytes);
-          tma_load_2d(sa, &tmA, full_bar(stage), kb * kGemmBK, mb * kGemmBM);
-          tma_load_2d(sa + L::kABytes, &tmB, full_bar(stage), kb * kGemmBK, nb * BN);
+          if (kb < kblocks1) {
+            tma_load_2d(sa, &tmA, full_bar(stage), kb * kGemmBK, mb * kGemmBM);
+            tma_load_2d(sa + L::kABytes, &tmB, full_bar(stage), kb * kGemmBK, nb * BN);
+          } else {
+            tma_load_2d(sa, &tmA2, full_bar(stage), (kb - kblocks1) * kGemmBK, mb * kGemmBM);
+            tma_load_2d(sa + L::kABytes, &tmB2, full_bar(stage), (kb - kblocks1) * kGemmBK, nb * BN);
+          }
           if (++stage == kGemmStages) {
             stage = 0;
             phase ^= 1u;
@@ -272,7 +285,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 template <int BN>
-static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p) {
+static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
+                          const CUtensorMap& tb2, GemmParams& p) {
   using L = GemmSmem<BN>;
   static bool attr_done = false;
   if (!attr_done) {
@@ -286,31 +300,41 @@ static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap&
   p.num_tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(p.num_tiles, ctx->num_sms);
   ProfScope prof(ctx, kProfGemm);
-  gemm_bf16_tc_kernel<BN><<<grid, kGemmThreads, L::kBytes, ctx->stream>>>(ta, tb, p);
+  gemm_bf16_tc_kernel<BN><<<grid, kGemmThreads, L::kBytes, ctx->stream>>>(ta, tb, ta2, tb2, p);
   return launch_status(ctx, "gemm_bf16_tc");
 }
 
-// bf16 GEMM core: Y = X · Wd^T with X [M,K] (pitch lda), Wd [N,K] (pitch K)
-int gemm_bf16(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd, int64_t N, int64_t K,
-              const void* bias, int epi, const void* gate, const void* resid, const uint32_t* rowmap, void* y,
-              int64_t ldy, void* y_raw) {
+// bf16 GEMM core: Y = X · Wd^T (+ T · Bt^T when k2 > 0) with X [M,K] (pitch lda),
+// Wd [N,K] (pitch K), T [M,k2] (pitch k2), Bt [N,k2] (pitch k2)
+int gemm_bf16_ext(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd, int64_t N, int64_t K,
+                  const void* t, const void* bt, int64_t k2, const void* bias, int epi, const void* gate,
+                  const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw) {
   if (M == 0) return WX_OK;
-  if (K % kGemmBK != 0 || N % 64 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+  if (K % kGemmBK != 0 || k2 % kGemmBK != 0 || N % 64 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX ||
+      k2 > INT32_MAX)
     return set_error(ctx, WX_ERR_UNSUPPORTED, "gemm needs K %% 64 == 0 and N %% 64 == 0 (M=%lld N=%lld K=%lld)",
                      (long long)M, (long long)N, (long long)K);
   if (!aligned16(y) || ldy % 8 != 0 || (bias && !aligned16(bias)) ||
       (epi == WX_EPI_GATE_RESID && (!aligned16(gate) || !aligned16(resid) || (y_raw && !aligned16(y_raw)))))
     return set_error(ctx, WX_ERR_INVALID, "gemm outputs/epilogue operands need 16-byte alignment");
   const int BN = (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64);
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, ta2, tb2;
   int st = make_tmap_bf16_2d(ctx, &ta, x, (uint64_t)M, (uint64_t)K, (uint64_t)lda, kGemmBK, kGemmBM);
   if (st) return st;
   st = make_tmap_bf16_2d(ctx, &tb, wd, (uint64_t)N, (uint64_t)K, (uint64_t)K, kGemmBK, BN);
   if (st) return st;
+  if (k2 > 0) {
+    if ((st = make_tmap_bf16_2d(ctx, &ta2, t, (uint64_t)M, (uint64_t)k2, (uint64_t)k2, kGemmBK, kGemmBM))) return st;
+    if ((st = make_tmap_bf16_2d(ctx, &tb2, bt, (uint64_t)N, (uint64_t)k2, (uint64_t)k2, kGemmBK, BN))) return st;
+  } else {
+    ta2 = ta;
+    tb2 = tb;
+  }
   GemmParams p{};
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
+  p.K2 = (int)k2;
   p.y = static_cast<__nv_bfloat16*>(y);
   p.ldy = ldy;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
@@ -320,27 +344,61 @@ int gemm_bf16(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd
   p.rowmap = rowmap;
   p.y_raw = static_cast<__nv_bfloat16*>(y_raw);
   p.err = ctx->dev_err;
-  if (BN == 256) return launch_gemm_bn<256>(ctx, ta, tb, p);
-  if (BN == 128) return launch_gemm_bn<128>(ctx, ta, tb, p);
-  return launch_gemm_bn<64>(ctx, ta, tb, p);
+  if (BN == 256) return launch_gemm_bn<256>(ctx, ta, tb, ta2, tb2, p);
+  if (BN == 128) return launch_gemm_bn<128>(ctx, ta, tb, ta2, tb2, p);
+  return launch_gemm_bn<64>(ctx, ta, tb, ta2, tb2, p);
 }
 
-// Full quantized linear: dequant into scratch `wd` (N*K bf16), then GEMM.
-int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,
-                         const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
-                         void* y_raw, void* wd, void* swiglu_tmp) {
+int gemm_bf16(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd, int64_t N, int64_t K,
+              const void* bias, int epi, const void* gate, const void* resid, const uint32_t* rowmap, void* y,
+              int64_t ldy, void* y_raw) {
+  return gemm_bf16_ext(ctx, x, M, lda, wd, N, K, nullptr, nullptr, 0, bias, epi, gate, resid, rowmap, y, ldy,
+                       y_raw);
+}
+
+int gemm_bf16_ext(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd, int64_t N, int64_t K,
+                  const void* t, const void* bt, int64_t k2, const void* bias, int epi, const void* gate,
+                  const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw);
+
+bool lora_pack_ok(const wx_lora_pack* l, const wx_qweight* w) {
+  return l && l->at && l->bt && l->R > 0 && l->R % 64 == 0 && l->n == w->n && l->k == w->k && aligned16(l->at) &&
+         aligned16(l->bt);
+}
+
+// Full quantized linear: dequant into scratch `wd` (N*K bf16), then GEMM; with a
+// LoRA pack, t = x at^T first and the GEMM runs R extra K columns over (t, bt).
+int qlinear_lora_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                              const wx_lora_pack* lora, int epilogue, const void* gate, const void* resid,
+                              const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw, void* wd, void* t,
+                              void* swiglu_tmp) {
   // small M is weight-bandwidth bound: expand the weights in shared memory instead
-  if (fused_eligible(w, m, epilogue) && !force_two_pass())
+  if (!lora && fused_eligible(w, m, epilogue) && !force_two_pass())
     return qlinear_fused(ctx, x, m, lda, w, epilogue, gate, resid, rowmap, y, ldy, y_raw, wd);
   int st = launch_dequant(ctx, w, wd);
   if (st) return st;
+  const int64_t R = lora ? lora->R : 0;
+  if (R > 0) {
+    // t = x (scale A)^T-packed: [m, R], the A operand of the extension columns
+    if ((st = gemm_bf16(ctx, x, m, lda, lora->at, R, w->k, nullptr, WX_EPI_NONE, nullptr, nullptr, nullptr, t, R,
+                        nullptr)))
+      return st;
+  }
+  const void* bt = R > 0 ? lora->bt : nullptr;
   if (epilogue == WX_EPI_SWIGLU) {
-    st = gemm_bf16(ctx, x, m, lda, wd, w->n, w->k, w->bias, WX_EPI_NONE, nullptr, nullptr, nullptr, swiglu_tmp,
-                   w->n, nullptr);
+    st = gemm_bf16_ext(ctx, x, m, lda, wd, w->n, w->k, t, bt, R, w->bias, WX_EPI_NONE, nullptr, nullptr, nullptr,
+                       swiglu_tmp, w->n, nullptr);
     if (st) return st;
     return launch_swiglu(ctx, swiglu_tmp, m, w->n / 2, w->n, y, ldy);
   }
-  return gemm_bf16(ctx, x, m, lda, wd, w->n, w->k, w->bias, epilogue, gate, resid, rowmap, y, ldy, y_raw);
+  return gemm_bf16_ext(ctx, x, m, lda, wd, w->n, w->k, t, bt, R, w->bias, epilogue, gate, resid, rowmap, y, ldy,
+                       y_raw);
+}
+
+int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,
+                         const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
+                         void* y_raw, void* wd, void* swiglu_tmp) {
+  return qlinear_lora_with_scratch(ctx, x, m, lda, w, nullptr, epilogue, gate, resid, rowmap, y, ldy, y_raw, wd,
+                                   nullptr, swiglu_tmp);
 }
 
 size_t qlinear_scratch_bytes(const wx_qweight* w, int64_t m, int epilogue) {
@@ -353,6 +411,27 @@ size_t qlinear_scratch_bytes(const wx_qweight* w, int64_t m, int epilogue) {
 }  // namespace wx
 
 using namespace wx;
+
+extern "C" int wx_qlinear_lora(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                               const wx_lora_pack* lora, int epilogue, const void* gate, const void* resid,
+                               const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw) {
+  if (!lora) return wx_qlinear(ctx, x, m, lda, w, epilogue, gate, resid, rowmap, y, ldy, y_raw);
+  WX_CHECK_ARG(ctx, ctx && x && y && qweight_ok(w) && m >= 0 && lda >= w->k);
+  WX_CHECK_ARG(ctx, lora_pack_ok(lora, w));
+  WX_CHECK_ARG(ctx, epilogue >= WX_EPI_NONE && epilogue <= WX_EPI_SWIGLU);
+  WX_CHECK_ARG(ctx, epilogue != WX_EPI_GATE_RESID || (gate && resid));
+  WX_CHECK_ARG(ctx, epilogue != WX_EPI_SWIGLU || w->n % 2 == 0);
+  WX_CHECK_ARG(ctx, ldy >= (epilogue == WX_EPI_SWIGLU ? w->n / 2 : w->n));
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t b_wd = al((size_t)w->n * w->k * 2), b_t = al((size_t)m * lora->R * 2);
+  const size_t b_sw = epilogue == WX_EPI_SWIGLU ? al((size_t)m * w->n * 2) : 0;
+  int st = WX_OK;
+  void* ws = workspace(ctx, b_wd + b_t + b_sw, &st);
+  if (!ws) return st;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  return qlinear_lora_with_scratch(ctx, x, m, lda, w, lora, epilogue, gate, resid, rowmap, y, ldy, y_raw, base,
+                                   base + b_wd, base + b_wd + b_t);
+}
 
 extern "C" int wx_qlinear(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,
                           const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,

@@ -98,4 +98,14 @@ inline size_t qlinear_ws_need(int64_t m, int64_t n, int64_t k) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Quantized linear with an optional LoRA pack (nullptr = none): `wd` holds the
+// expanded weight (qlinear_ws_need bytes), `t` the [m, lora->R] bf16 product
+// x at^T, `swiglu_tmp` the [m, n] pre-activation of WX_EPI_SWIGLU.
+int qlinear_lora_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                              const wx_lora_pack* lora, int epilogue, const void* gate, const void* resid,
+                              const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw, void* wd, void* t,
+                              void* swiglu_tmp);
+bool lora_pack_ok(const wx_lora_pack* l, const wx_qweight* w);
+bool lora_packs_ok(const wx_dit_config* cfg, const wx_block_weights* w);
+
 }  // namespace wx

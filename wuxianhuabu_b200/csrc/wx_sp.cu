@@ -141,7 +141,7 @@ static unsigned grid_units(wx_ctx* ctx, int64_t total) {
 }
 
 struct SpLayout {
-  size_t m, qkv, send, recv, attf, ret, att, at, ha, f1, wd, sw, attn, total;
+  size_t m, qkv, send, recv, attf, ret, att, at, ha, f1, wd, sw, lt, attn, total;
 };
 
 static size_t al(size_t b) { return (b + 255) & ~size_t(255); }
@@ -169,6 +169,7 @@ static SpLayout sp_layout(const wx_dit_config* c, int64_t S, int P) {
   const size_t nmax = std::max(std::max(3 * inner, (size_t)c->hidden), fc1_n);
   L.wd = off; off += al(std::max(wmax * 2, qlinear_ws_need(rows, (int64_t)nmax, 1)));
   L.sw = off; off += c->mlp_kind == WX_MLP_SWIGLU ? al((size_t)rows * fc1_n * 2) : 0;
+  L.lt = off; off += al((size_t)rows * (size_t)std::max(0, c->lora_rank) * 2);  // x at^T of a LoRA pack
   wx_sparse_spec sol{};
   sol.mode = WX_SPARSE_SOL;
   sol.block = 64;
@@ -281,6 +282,7 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
   WX_CHECK_ARG(ctx, qweight_ok(&w->fc1) && w->fc1.k == cfg->hidden && w->fc1.n == fc1_n);
   WX_CHECK_ARG(ctx, qweight_ok(&w->fc2) && w->fc2.k == cfg->ffn && w->fc2.n == cfg->hidden);
   WX_CHECK_ARG(ctx, pab_slot || refresh);
+  WX_CHECK_ARG(ctx, lora_packs_ok(cfg, w));
   const int64_t rows = S / P;
   const int Hl = cfg->heads / P;
   const int hd = cfg->head_dim;
@@ -290,6 +292,7 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
   void* ha = base + L.ha;
   void* f1 = base + L.f1;
   void* wd = base + L.wd;
+  void* lt = base + L.lt;
   int st;
   if (refresh || !pab_slot) {
     void* qkv = base + L.qkv;
@@ -301,8 +304,8 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
     if ((st = launch_norm_modscale(ctx, h, rows, cfg->hidden, w->norm1, mods->shift_msa, mods->scale_msa, rowmap,
                                    cfg->eps, m)))
       return st;
-    if ((st = qlinear_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
-                                   3 * inner, nullptr, wd, nullptr)))
+    if ((st = qlinear_lora_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
+                                   3 * inner, nullptr, wd, lt, nullptr)))
       return st;
     if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, rows, cfg->heads, hd, w->q_norm,
                                   w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
@@ -325,8 +328,8 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
     sp_unpack_out_kernel<<<grid_units(ctx, un_units), 256, 0, ctx->stream>>>(ret, rows, P, Hl, hd, att);
     if ((st = launch_status(ctx, "sp_unpack_out"))) return st;
     void* at_dst = pab_slot ? pab_slot : base + L.at;
-    if ((st = qlinear_with_scratch(ctx, att, rows, inner, &w->out, WX_EPI_GATE_RESID, mods->gate_msa, h, rowmap, ha,
-                                   cfg->hidden, at_dst, wd, nullptr)))
+    if ((st = qlinear_lora_with_scratch(ctx, att, rows, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID, mods->gate_msa, h, rowmap, ha,
+                                   cfg->hidden, at_dst, wd, lt, nullptr)))
       return st;
   } else {
     if ((st = launch_mod_gate(ctx, h, pab_slot, mods->gate_msa, rowmap, rows, cfg->hidden, ha))) return st;
@@ -335,11 +338,11 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
                                  cfg->eps, m)))
     return st;
   const int act = cfg->mlp_kind == WX_MLP_SWIGLU ? WX_EPI_SWIGLU : WX_EPI_GELU;
-  if ((st = qlinear_with_scratch(ctx, m, rows, cfg->hidden, &w->fc1, act, nullptr, nullptr, nullptr, f1, cfg->ffn,
-                                 nullptr, wd, base + L.sw)))
+  if ((st = qlinear_lora_with_scratch(ctx, m, rows, cfg->hidden, &w->fc1, w->lora[2], act, nullptr, nullptr,
+                                      nullptr, f1, cfg->ffn, nullptr, wd, lt, base + L.sw)))
     return st;
-  return qlinear_with_scratch(ctx, f1, rows, cfg->ffn, &w->fc2, WX_EPI_GATE_RESID, mods->gate_mlp, ha, rowmap, h,
-                              cfg->hidden, nullptr, wd, nullptr);
+  return qlinear_lora_with_scratch(ctx, f1, rows, cfg->ffn, &w->fc2, w->lora[3], WX_EPI_GATE_RESID, mods->gate_mlp, ha, rowmap, h,
+                              cfg->hidden, nullptr, wd, lt, nullptr);
 }
 
 }  // extern "C"

@@ -26,13 +26,14 @@ import torch
 
 from . import _lib
 from ._lib import (EPI_GATE_RESID, EPI_GELU, EPI_NONE, EPI_SWIGLU, MLP_GELU, MLP_SWIGLU, SPARSE_DENSE, SPARSE_SOL,
-                   SPARSE_TOPK, BlockMods, BlockWeights, DitConfig, ModRun, QWeight, SparseSpec, WxError, check)
+                   SPARSE_TOPK, BlockMods, BlockWeights, DitConfig, Lora, LoraPack, ModRun, QWeight, SparseSpec, WxError,
+                   check)
 
 __all__ = [
     "Context", "context", "MfLinear", "H3FusedKernels", "H3SolAttnConfig", "H3SolAttn", "H3AttnBroadcast",
     "attn_broadcast_refresh", "attn_broadcast_must_refresh", "attn_broadcast_plan",
     "attn_broadcast_default_max_stale", "sigma_schedule", "sparse_mode_for_layer", "SparsePolicy",
-    "H3DiTConfig", "H3BlockWeights", "H3DiTBlocks", "ModRun", "WxError",
+    "H3DiTConfig", "H3BlockWeights", "H3DiTBlocks", "ModRun", "WxError", "LoraRef",
     "EPI_NONE", "EPI_GELU", "EPI_GATE_RESID", "EPI_SWIGLU",
 ]
 
@@ -92,6 +93,14 @@ def _need_bf16_cuda(*ts: Optional[torch.Tensor]) -> None:
 
 
 # --------------------------------------------------------------------------- MfLinear
+@dataclass
+class LoraRef:
+    """LoraRef (H3Common.swift:407-411): the layer adds scale * ((x a) b)."""
+    a: torch.Tensor  # [in, r] bf16
+    b: torch.Tensor  # [r, out] bf16
+    scale: float
+
+
 class MfLinear:
     """6-bit (2..8-bit) MLX-affine group-quantized linear layer (H3Common.swift:283-404).
 
@@ -108,6 +117,35 @@ class MfLinear:
         self.out_dim = w.shape[0]
         self.bits = 32 * w.shape[1] // in_dim
         self.group_size = in_dim // scales.shape[1]
+        self.lora: list[LoraRef] = []  # LoraSlot.refs (H3Common.swift:413-417)
+        self._pack = None
+
+    def set_lora(self, refs: Sequence["LoraRef"]) -> None:
+        """LoraSlot.set (H3Common.swift:416): attach adapters (empty = detach)."""
+        self.lora = list(refs)
+        self._pack = None
+
+    def lora_pack(self) -> Optional[LoraPack]:
+        """The adapters packed as the GEMM's K extension (wx_lora_pack_build), built once."""
+        if not self.lora:
+            return None
+        if self._pack is None:
+            lib = _lib.load()
+            dev = self.w.device
+            for r in self.lora:
+                _need_bf16_cuda(r.a, r.b)
+            arr = (Lora * len(self.lora))(*[Lora(_p(r.a.contiguous()), _p(r.b.contiguous()), r.a.shape[1],
+                                                 float(r.scale)) for r in self.lora])
+            R, ab, bb = C.c_int64(), C.c_size_t(), C.c_size_t()
+            check(lib.wx_lora_pack_bytes(self.out_dim, self.in_dim, arr, len(self.lora), C.byref(R), C.byref(ab),
+                                         C.byref(bb)))
+            at = torch.empty(ab.value // 2, dtype=torch.bfloat16, device=dev)
+            bt = torch.empty(bb.value // 2, dtype=torch.bfloat16, device=dev)
+            pack = LoraPack(_p(at), _p(bt), 0, 0, 0)
+            context(dev.index).call("wx_lora_pack_build", self.out_dim, self.in_dim, arr, len(self.lora),
+                                    C.byref(pack))
+            self._pack = (pack, at, bt)
+        return self._pack[0]
 
     @classmethod
     def quantize(cls, w_f32: torch.Tensor, bits: int = 6, group: int = 64,
@@ -145,8 +183,13 @@ class MfLinear:
         n_out = self.out_dim // 2 if epilogue == EPI_SWIGLU else self.out_dim
         y = out if out is not None else torch.empty((m, n_out), dtype=torch.bfloat16, device=x.device)
         qw = self.qweight()
-        context(x.device.index).call("wx_qlinear", _p(x2), m, x2.stride(0), C.byref(qw), epilogue, _p(gate),
-                                     _p(resid), _p(rowmap), _p(y), y.stride(0), _p(y_raw))
+        pack = self.lora_pack()
+        if pack is not None:  # quantizedMM + bias + loraDelta (:358-375)
+            context(x.device.index).call("wx_qlinear_lora", _p(x2), m, x2.stride(0), C.byref(qw), C.byref(pack),
+                                         epilogue, _p(gate), _p(resid), _p(rowmap), _p(y), y.stride(0), _p(y_raw))
+        else:
+            context(x.device.index).call("wx_qlinear", _p(x2), m, x2.stride(0), C.byref(qw), epilogue, _p(gate),
+                                         _p(resid), _p(rowmap), _p(y), y.stride(0), _p(y_raw))
         return y.reshape(*x.shape[:-1], n_out)
 
     __call__ = forward
@@ -359,8 +402,9 @@ class H3DiTConfig:
     eps: float = 1e-6
     layers: int = 48
 
-    def c(self) -> DitConfig:
-        return DitConfig(self.hidden, self.heads, self.head_dim, self.ffn, self.mlp_kind, self.rot, self.eps, 0)
+    def c(self, lora_rank: int = 0) -> DitConfig:
+        return DitConfig(self.hidden, self.heads, self.head_dim, self.ffn, self.mlp_kind, self.rot, self.eps,
+                         lora_rank)
 
 
 @dataclass
@@ -374,9 +418,15 @@ class H3BlockWeights:
     norm1: torch.Tensor
     norm2: torch.Tensor
 
+    def linears(self) -> list[MfLinear]:
+        return [self.qkv, self.out, self.fc1, self.fc2]
+
     def c(self) -> BlockWeights:
+        packs = [lin.lora_pack() for lin in self.linears()]
+        ptrs = (C.POINTER(LoraPack) * 4)(*[C.pointer(pk) if pk is not None else C.POINTER(LoraPack)()
+                                           for pk in packs])
         return BlockWeights(self.qkv.qweight(), self.out.qweight(), self.fc1.qweight(), self.fc2.qweight(),
-                            _p(self.q_norm), _p(self.k_norm), _p(self.norm1), _p(self.norm2))
+                            _p(self.q_norm), _p(self.k_norm), _p(self.norm1), _p(self.norm2), ptrs)
 
 
 def sp_plan(S: int, H: int, head_dim: int, P: int, rank: int) -> _lib.SpPlan:
@@ -412,8 +462,10 @@ class H3DiTBlocks:
     def __init__(self, cfg: H3DiTConfig, blocks: list[H3BlockWeights]):
         self.cfg = cfg
         self.blocks = blocks
-        self._c = cfg.c()
         self._wc = [b.c() for b in blocks]
+        # scratch for x at^T of the widest attached LoRA pack
+        rank = max([lin.lora_pack().R for b in blocks for lin in b.linears() if lin.lora] or [0])
+        self._c = cfg.c(int(rank))
         self._scratch: Optional[torch.Tensor] = None
 
     def scratch(self, S: int, device, P: int = 1) -> torch.Tensor:
