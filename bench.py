@@ -421,6 +421,10 @@ def run_c2(args) -> dict:
         shapes, ms_list = [(K0, N0)], (M0,)
     for (K, N) in shapes:
         lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02)
+        if args.lora > 0:  # one adapter of rank args.lora (the LoRA row: a K extension of the GEMM)
+            a = (torch.randn((K, args.lora), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            b = (torch.randn((args.lora, N), device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            lin.set_lora([h3.LoraRef(a, b, 1.0)])
         for M in ms_list:
             x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
             y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
@@ -438,7 +442,7 @@ def run_c2(args) -> dict:
             fl = 2.0 * M * N * K
             byts = 2 * M * K + 0.75 * N * K + 4 * N * (K // 64) + 2 * M * N
             res.append(dict(M=M, K=K, N=N, ms=t * 1e3, tflops=fl / t / 1e12, frac=fl / t / 1e12 / pk,
-                            gbs=byts / t / 1e9))
+                            gbs=byts / t / 1e9, lora_rank=args.lora))
             del x, y
     return dict(metric="6-bit qGEMM sweep (c2)", unit="TFLOP/s", peak=pk, peak_kind=f"{kind} burst bf16", sweep=res)
 
@@ -452,6 +456,7 @@ def main():
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
     ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c3", "c3full", "c2"])
     ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
+    ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
