@@ -210,6 +210,36 @@ int wx_qlinear_noalloc(void* stream, const void* x, int64_t m, int64_t lda, cons
                        int epilogue, const void* gate, const void* resid, const uint32_t* rowmap,
                        void* y, int64_t ldy, void* y_raw);
 
+/* ------------------------------------------------------ checkpoints */
+/* Safetensors container (H3Weights, H3Common.swift:180-261): the file is mapped
+ * read-only, the header parsed once, tensors copied to device memory on demand. */
+typedef struct wx_st_file wx_st_file;
+typedef struct wx_st_info {
+  char dtype[8];      /* safetensors dtype name: "BF16", "F32", "U32", ... */
+  int32_t ndim;
+  int64_t shape[8];
+  uint64_t offset;    /* byte offset in the file */
+  uint64_t nbytes;
+  const void* host;   /* the bytes in the mapping (valid until wx_st_close) */
+} wx_st_info;
+int wx_st_open(const char* path, wx_st_file** out);
+int wx_st_close(wx_st_file* f);
+/* message of the last wx_st_* failure of this thread */
+const char* wx_st_last_error(void);
+int64_t wx_st_count(const wx_st_file* f);
+/* name of tensor i, 0 <= i < wx_st_count (valid until wx_st_close) */
+const char* wx_st_name(const wx_st_file* f, int64_t i);
+/* WX_ERR_INVALID when the name is absent (H3Weights.get returning nil) */
+int wx_st_find(const wx_st_file* f, const char* name, wx_st_info* out);
+/* copy a tensor's bytes to device memory on the context stream (returns when done) */
+int wx_st_upload(wx_ctx* ctx, const wx_st_file* f, const char* name, void* dst, uint64_t dst_bytes);
+/* H3Weights.getQuantized + MfLinear.load geometry (H3Common.swift:243-258, 311-338):
+ * prefix.weight (U32 [n, k*bits/32]) with prefix.scales/.biases or
+ * prefix.weight.scales/.weight.biases ([n, k/group]); bits = 32*w_cols/in_features,
+ * group = in_features/s_cols; bias->dtype[0] == 0 when prefix.bias is absent. */
+int wx_st_find_qlinear(const wx_st_file* f, const char* prefix, int64_t in_features, wx_st_info* wq,
+                       wx_st_info* scales, wx_st_info* biases, wx_st_info* bias, int32_t* bits, int32_t* group);
+
 /* ------------------------------------------------------ fused row ops */
 /* H3FusedKernels.fusedRmsnormRope (网络算子-融合-RMSNormRoPE-通用.swift:111-129):
  * rows (s, h) of head_dim at x[s*x_stride + h*head_dim]; cos/sin [S, rot/2] bf16;

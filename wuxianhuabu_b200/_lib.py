@@ -42,6 +42,11 @@ class SparseSpec(C.Structure):
                 ("tail", C.c_int32), ("reserved", C.c_int32)]
 
 
+class StInfo(C.Structure):
+    _fields_ = [("dtype", C.c_char * 8), ("ndim", C.c_int32), ("shape", C.c_int64 * 8), ("offset", C.c_uint64),
+                ("nbytes", C.c_uint64), ("host", C.c_void_p)]
+
+
 class Lora(C.Structure):
     _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("r", C.c_int32), ("scale", C.c_float)]
 
@@ -113,6 +118,15 @@ _SIGS = {
     "wx_qlinear_lora": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), C.POINTER(LoraPack), _i32, _vp, _vp, _vp,
                                _vp, _i64, _vp]),
     "wx_qlinear_noalloc": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "wx_st_open": (_i32, [C.c_char_p, C.POINTER(_vp)]),
+    "wx_st_close": (_i32, [_vp]),
+    "wx_st_last_error": (C.c_char_p, []),
+    "wx_st_count": (_i64, [_vp]),
+    "wx_st_name": (C.c_char_p, [_vp, _i64]),
+    "wx_st_find": (_i32, [_vp, C.c_char_p, C.POINTER(StInfo)]),
+    "wx_st_upload": (_i32, [_vp, _vp, C.c_char_p, _vp, C.c_uint64]),
+    "wx_st_find_qlinear": (_i32, [_vp, C.c_char_p, _i64, C.POINTER(StInfo), C.POINTER(StInfo), C.POINTER(StInfo),
+                                  C.POINTER(StInfo), C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "wx_qk_norm_rope": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _i32, _f32, _vp, _i64]),
     "wx_qk_norm_rope_qkv": (_i32, [_vp, _vp, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _i32, _f32]),
     "wx_norm_modscale": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _f32, _vp]),

@@ -26,14 +26,14 @@ import torch
 
 from . import _lib
 from ._lib import (EPI_GATE_RESID, EPI_GELU, EPI_NONE, EPI_SWIGLU, MLP_GELU, MLP_SWIGLU, SPARSE_DENSE, SPARSE_SOL,
-                   SPARSE_TOPK, BlockMods, BlockWeights, DitConfig, Lora, LoraPack, ModRun, QWeight, SparseSpec, WxError,
-                   check)
+                   SPARSE_TOPK, BlockMods, BlockWeights, DitConfig, Lora, LoraPack, ModRun, QWeight, SparseSpec, StInfo,
+                   WxError, check)
 
 __all__ = [
     "Context", "context", "MfLinear", "H3FusedKernels", "H3SolAttnConfig", "H3SolAttn", "H3AttnBroadcast",
     "attn_broadcast_refresh", "attn_broadcast_must_refresh", "attn_broadcast_plan",
     "attn_broadcast_default_max_stale", "sigma_schedule", "sparse_mode_for_layer", "SparsePolicy",
-    "H3DiTConfig", "H3BlockWeights", "H3DiTBlocks", "ModRun", "WxError", "LoraRef",
+    "H3DiTConfig", "H3BlockWeights", "H3DiTBlocks", "ModRun", "WxError", "LoraRef", "H3Weights", "load_block",
     "EPI_NONE", "EPI_GELU", "EPI_GATE_RESID", "EPI_SWIGLU",
 ]
 
@@ -570,3 +570,101 @@ class H3DiT:
         if attn_bcast is not None and refresh and sigma is not None:
             attn_bcast.cached_sigma = sigma
         return latents
+
+
+# ------------------------------------------------------------------------ checkpoints
+_ST_DTYPES = {"BF16": torch.bfloat16, "F16": torch.float16, "F32": torch.float32, "I32": torch.int32,
+              "U32": torch.int32, "I64": torch.int64, "U8": torch.uint8, "I8": torch.int8, "BOOL": torch.bool}
+
+
+class H3Weights:
+    """H3Weights (H3Common.swift:180-261): a memory-mapped safetensors file whose tensors are
+    copied to the GPU on demand (wx_st_*). U32 tensors come back as int32 (same bits)."""
+
+    def __init__(self, path: str):
+        self._lib = _lib.load()
+        h = C.c_void_p()
+        st = self._lib.wx_st_open(str(path).encode(), C.byref(h))
+        if st != 0:
+            raise WxError(st, self._lib.wx_st_last_error().decode(errors="replace"))
+        self._h = h
+        self.path = str(path)
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.wx_st_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def keys(self) -> list[str]:
+        n = self._lib.wx_st_count(self._h)
+        return [self._lib.wx_st_name(self._h, i).decode() for i in range(n)]
+
+    def info(self, key: str) -> Optional[StInfo]:
+        inf = StInfo()
+        return inf if self._lib.wx_st_find(self._h, key.encode(), C.byref(inf)) == 0 else None
+
+    def contains(self, key: str) -> bool:
+        return self.info(key) is not None
+
+    def _upload(self, key: str, inf: StInfo, device) -> torch.Tensor:
+        dt = _ST_DTYPES.get(inf.dtype.decode())
+        if dt is None:
+            raise WxError(_lib.WX_ERR_UNSUPPORTED, f"{key}: dtype {inf.dtype.decode()} not supported")
+        shape = [inf.shape[i] for i in range(inf.ndim)]
+        t = torch.empty(shape, dtype=dt, device=device)
+        context(t.device.index).call("wx_st_upload", self._h, key.encode(), _p(t), t.numel() * t.element_size())
+        return t
+
+    def get(self, key: str, device=None) -> Optional[torch.Tensor]:
+        """H3Weights.get (:229-235): the tensor on the GPU, or None when absent."""
+        inf = self.info(key)
+        if inf is None:
+            return None
+        return self._upload(key, inf, device if device is not None else torch.device("cuda", torch.cuda.current_device()))
+
+    def get_linear(self, prefix: str, in_features: int, device=None) -> MfLinear:
+        """MfLinear.load (H3Common.swift:311-338) of a quantized linear; either naming variant
+        of the triple (getQuantized, :243-258)."""
+        infos = [StInfo() for _ in range(4)]
+        bits, group = C.c_int32(), C.c_int32()
+        st = self._lib.wx_st_find_qlinear(self._h, prefix.encode(), in_features, *[C.byref(i) for i in infos],
+                                          C.byref(bits), C.byref(group))
+        if st != 0:
+            raise WxError(st, self._lib.wx_st_last_error().decode(errors="replace"))
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        names = [prefix + ".weight"]
+        for suf in (".scales", ".biases"):
+            names.append(prefix + suf if self.contains(prefix + suf) else prefix + ".weight" + suf)
+        w, sc, bi = [self._upload(n, i, dev) for n, i in zip(names, infos[:3])]
+        bias = self._upload(prefix + ".bias", infos[3], dev) if infos[3].dtype else None
+        if sc.dtype != torch.bfloat16:
+            sc, bi = sc.to(torch.bfloat16), bi.to(torch.bfloat16)
+        if bias is not None and bias.dtype != torch.bfloat16:
+            bias = bias.to(torch.bfloat16)
+        return MfLinear(w, sc, bi, in_features, bias)
+
+
+def load_block(w: H3Weights, idx: int, cfg: H3DiTConfig, device=None) -> H3BlockWeights:
+    """H3DiTBlock.load (H3Transformer.swift:648-660): blocks.{idx}.{norm1,norm2}.weight,
+    attn.{qkv_proj,q_norm,k_norm,out_proj}, mlp.{fc1,fc2}."""
+    p = f"blocks.{idx}"
+    inner = cfg.heads * cfg.head_dim
+
+    def need(key):
+        t = w.get(key, device)
+        if t is None:
+            raise WxError(_lib.WX_ERR_INVALID, f"missing weight: {key}")
+        return t.to(torch.bfloat16) if t.dtype != torch.bfloat16 else t
+    return H3BlockWeights(w.get_linear(p + ".attn.qkv_proj", cfg.hidden, device),
+                          w.get_linear(p + ".attn.out_proj", inner, device),
+                          w.get_linear(p + ".mlp.fc1", cfg.hidden, device),
+                          w.get_linear(p + ".mlp.fc2", cfg.ffn, device),
+                          need(p + ".attn.q_norm.weight"), need(p + ".attn.k_norm.weight"),
+                          need(p + ".norm1.weight"), need(p + ".norm2.weight"))
