@@ -50,7 +50,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     mbar_init(v_full, 1);
     mbar_init(v_empty, 1);
     mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    mbar_init(p_full, 4);  // one arrival per softmax warp
     mbar_init(o_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -224,7 +224,8 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         l += t.x + t.y;
       }
       tc_fence_before();
-      mbar_arrive(p_full);
+      __syncwarp();  // the warp's TMEM stores are complete: one arrival per warp
+      if (lane == 0) mbar_arrive(p_full);
     }
     // the last PV: o_done completes once per tile and every earlier PV precedes S_{n-1}
     if (ok && n_kv > 0) ok = mbar_wait(o_done, (n_kv - 1) & 1, p.err, kDevTimeoutSoftmax, abort_flag);

@@ -22,6 +22,10 @@
 constexpr int kA5Threads = 384;
 constexpr int kA5KStages = 3;
 constexpr int kA5VStages = 2;
+#ifndef WX_A5_TURN_CHUNK
+#define WX_A5_TURN_CHUNK 2
+#endif
+constexpr int kA5TurnChunk = WX_A5_TURN_CHUNK;  // exponential chunks (of 4) after which the turn passes
 constexpr int kA5BarOff = (2 + kA5KStages + kA5VStages) * kTileBytes;
 constexpr int kA5Smem = kA5BarOff + 512 + 1024;
 static_assert(kA5Threads == kA4Threads, "uses the register split of flash_attn4_kernel (kA4RegsLow/High)");
@@ -33,10 +37,11 @@ enum : int {
   kB5VFull = 7,   // [2]
   kB5VEmpty = 9,  // [2] count 2 (both slots' PV)
   kB5SFull = 11,  // [2] per slot
-  kB5PFull = 13,  // [2] per slot, count 128
+  kB5PFull = 13,  // [2] per slot, count 4 (one per softmax warp)
   kB5OFull = 15,  // [2] per slot
   kB5Drain = 17,  // [2] per slot
-  kB5Count = 19
+  kB5Turn = 19,   // [2] per slot, count 4: this slot's exponentials (all but the tail) are issued
+  kB5Count = 21
 };
 
 template <int POLY>
@@ -64,7 +69,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
     for (int i = 0; i < kB5Count; ++i) {
       uint32_t c = 1;
       if (i == kB5KEmpty || i == kB5KEmpty + 1 || i == kB5KEmpty + 2 || i == kB5VEmpty || i == kB5VEmpty + 1) c = 2;
-      if (i == kB5PFull || i == kB5PFull + 1) c = 128;
+      if (i == kB5PFull || i == kB5PFull + 1 || i == kB5Turn || i == kB5Turn + 1) c = 4;  // one per softmax warp
       mbar_init(bar(i), c);
     }
     *abort_flag = 0;
@@ -140,12 +145,9 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       bool ok = mbar_wait(bar(kB5QFull), 0, p.err, kDevTimeoutFull, abort_flag);
       bool issued = false;
       const uint64_t dq = opaque64(smem_desc_sw128(sQ(X), 16, 1024));
-      for (int t = 0; t < n_kv && ok; ++t) {
-        const uint32_t ks = (uint32_t)t % kA5KStages, vs = (uint32_t)t % kA5VStages;
-        if (!mbar_wait(bar(kB5KFull + ks), ((uint32_t)t / kA5KStages) & 1, p.err, kDevTimeoutFull, abort_flag)) {
-          ok = false;
-          break;
-        }
+      // S(t) into S/P_X; its K tile must have landed (k_full waited by the caller)
+      auto issue_s = [&](int t) {
+        const uint32_t ks = (uint32_t)t % kA5KStages;
         tc_fence_after();
         const uint64_t dk = opaque64(smem_desc_sw128(sK(ks), 16, 1024));
 #pragma unroll
@@ -156,8 +158,19 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         issued = true;
         umma_commit(bar(kB5SFull + X));
         umma_commit(bar(kB5KEmpty + ks));
-        if (!mbar_wait(bar(kB5PFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag) ||
-            !mbar_wait(bar(kB5VFull + vs), ((uint32_t)t / kA5VStages) & 1, p.err, kDevTimeoutFull, abort_flag)) {
+      };
+      auto k_ready = [&](int t) {
+        return mbar_wait(bar(kB5KFull + (uint32_t)t % kA5KStages), ((uint32_t)t / kA5KStages) & 1, p.err,
+                         kDevTimeoutFull, abort_flag);
+      };
+      if (ok && (ok = k_ready(0))) issue_s(0);
+      for (int t = 0; t < n_kv && ok; ++t) {
+        const uint32_t vs = (uint32_t)t % kA5VStages;
+        // V(t) and K(t+1) are waited for before P(t): once the softmax hands over P(t),
+        // PV(t) and S(t+1) go out back to back with no barrier wait between them
+        if (!mbar_wait(bar(kB5VFull + vs), ((uint32_t)t / kA5VStages) & 1, p.err, kDevTimeoutFull, abort_flag) ||
+            (t + 1 < n_kv && !k_ready(t + 1)) ||
+            !mbar_wait(bar(kB5PFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
           ok = false;
           break;
         }
@@ -167,6 +180,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         for (int kk = 0; kk < 8; ++kk)
           umma_bf16_ts(tO, tS + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
         umma_commit(bar(kB5VEmpty + vs));
+        if (t + 1 < n_kv) issue_s(t + 1);
       }
       if (ok) umma_commit(bar(kB5OFull + X));
       if (issued) {  // every MMA of this thread completes before TMEM is released
@@ -235,9 +249,11 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       // B(1), ...): run together they would share the MUFU pipe while the tensor
       // pipe idles; in turns, each overlaps the other slot's TMEM loads, row max,
       // PV and next S.
-      const bool turn = X == 0 ? (t == 0 || mbar_wait(bar(kB5PFull + 1), ((uint32_t)t - 1) & 1, p.err,
+      // The turn passes when the other slot has issued all but its last chunk of
+      // exponentials, so the two phases overlap only in their tails.
+      const bool turn = X == 0 ? (t == 0 || mbar_wait(bar(kB5Turn + 1), ((uint32_t)t - 1) & 1, p.err,
                                                        kDevTimeoutSoftmax, abort_flag))
-                               : mbar_wait(bar(kB5PFull + 0), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag);
+                               : mbar_wait(bar(kB5Turn + 0), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag);
       if (!turn) {
         ok = false;
         break;
@@ -265,6 +281,10 @@ __global__ void __launch_bounds__(kA5Threads, 1)
           pk[i] = pack_bf16x2(pv.x, pv.y);
         }
         tmem_st16(tS + c * 16, pk);
+        if (c == kA5TurnChunk) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(kB5Turn + X));
+        }
       }
       if (any_need) {
         // PV_X(t-1) completed before S_X(t) (in-order tensor pipe): O_X is stable
@@ -285,7 +305,8 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         l = l * alpha + (u.x + u.y);
       }
       tc_fence_before();
-      mbar_arrive(bar(kB5PFull + X));
+      __syncwarp();  // the warp's TMEM stores are complete: one arrival per warp (4, not 128 atomics)
+      if (lane == 0) mbar_arrive(bar(kB5PFull + X));
     }
     if (ok && n_kv > 0) ok = mbar_wait(bar(kB5OFull + X), 0, p.err, kDevTimeoutSoftmax, abort_flag);
     tc_fence_after();
