@@ -536,12 +536,23 @@ static bool flash_pair_regs_ok(int poly) {
   const int i = poly < 0 ? 0 : (poly > 2 ? 2 : poly);
   if (ok[i] < 0) {
     cudaFuncAttributes fa{};
-    const void* fn = i == 0 ? (const void*)flash_attn_pair_kernel<0>
-                            : (i == 1 ? (const void*)flash_attn_pair_kernel<1> : (const void*)flash_attn_pair_kernel<2>);
+    // the DUO instantiations share the register split and compile to the same budget
+    const void* fn = i == 0 ? (const void*)flash_attn_pair_kernel<0, false>
+                            : (i == 1 ? (const void*)flash_attn_pair_kernel<1, false>
+                                      : (const void*)flash_attn_pair_kernel<2, false>);
     ok[i] = cudaFuncGetAttributes(&fa, fn) == cudaSuccess &&
             fa.numRegs * kA5Threads >= kA4RegsLow * 128 + kA4RegsHigh * 256;
   }
   return ok[i] == 1;
+}
+
+// Two routed items per CTA (flash_attn_pair_kernel<.., true>; WX_ATTN_DUO, read once; 0 = off).
+static int attn_duo() {
+  static int v = [] {
+    const char* e = getenv("WX_ATTN_DUO");
+    return (e && atoi(e) == 0) ? 0 : 1;
+  }();
+  return v;
 }
 
 // Pair strip / dense query tiles that walk the same key tiles (WX_ATTN_PAIRS, read once; 0 = off).
@@ -608,7 +619,8 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA2Smem);
     for (auto fn : {flash_attn4_kernel<0>, flash_attn4_kernel<1>, flash_attn4_kernel<2>})
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA4Smem);
-    for (auto fn : {flash_attn_pair_kernel<0>, flash_attn_pair_kernel<1>, flash_attn_pair_kernel<2>})
+    for (auto fn : {flash_attn_pair_kernel<0, false>, flash_attn_pair_kernel<1, false>, flash_attn_pair_kernel<2, false>,
+                    flash_attn_pair_kernel<0, true>, flash_attn_pair_kernel<1, true>, flash_attn_pair_kernel<2, true>})
       if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA5Smem);
     if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
     attr = true;
@@ -631,12 +643,13 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   const int poly = exp_poly_pairs();
   if (n_pairs > 0) {
     if (!flash_pair_regs_ok(poly)) return set_error(ctx, WX_ERR_CUDA, "flash_attn_pair: register split does not fit");
+    const int np2 = (int)(2 * n_pairs);
     if (poly == 0)
-      flash_attn_pair_kernel<0><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p);
+      flash_attn_pair_kernel<0, false><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, np2);
     else if (poly == 2)
-      flash_attn_pair_kernel<2><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p);
+      flash_attn_pair_kernel<2, false><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, np2);
     else
-      flash_attn_pair_kernel<1><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p);
+      flash_attn_pair_kernel<1, false><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, np2);
     if ((st = launch_status(ctx, "flash_attn_pair"))) return st;
   }
   // the remaining (unpaired) items
@@ -644,6 +657,18 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   const int64_t n_rest = n_items - 2 * n_pairs;
   p.items = items + 2 * n_pairs;
   if (n_rest == 0) return WX_OK;
+  if (attn_kernel_variant() == 2 && attn_duo() && flash_pair_regs_ok(poly)) {
+    // two independent (routed) items per CTA, their exponential phases taking turns
+    const unsigned grid = (unsigned)((n_rest + 1) / 2);
+    const int nr = (int)n_rest;
+    if (poly == 0)
+      flash_attn_pair_kernel<0, true><<<grid, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, nr);
+    else if (poly == 2)
+      flash_attn_pair_kernel<2, true><<<grid, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, nr);
+    else
+      flash_attn_pair_kernel<1, true><<<grid, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, nr);
+    return launch_status(ctx, "flash_attn_duo");
+  }
   if (attn_kernel_variant() == 4 && flash4_regs_ok(poly)) {
     // persistent: one CTA per SM, items fetched dynamically, softmax split over two warpgroups
     const unsigned grid = (unsigned)std::min<int64_t>(ctx->num_sms, n_rest);

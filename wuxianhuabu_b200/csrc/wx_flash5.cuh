@@ -14,9 +14,16 @@
 //   tensor pipe runs one thread's MMAs in issue order, so S_X(t+1) cannot
 //   overwrite P_X(t) before PV_X(t) has read it). Warp 3: idle.
 //   Warps 4-7 / 8-11: softmax + epilogue of slot A / B (thread r owns row r).
+//   (DUO: warp 3 loads V while warp 0 loads Q and K.)
 // The exponential phases of the two slots' softmaxes take turns (A(t) after
 // B(t-1), B(t) after A(t)); the TMEM loads and row max of one slot overlap the
 // exponentials of the other, and the tensor pipe runs PV and the next S meanwhile.
+//
+// DUO = true runs the same schedule for two INDEPENDENT work items (the routed
+// video query tiles, whose key lists differ): each slot streams its own K and V
+// (one buffer each: Q_A, Q_B, K_A, V_A, K_B, V_B), slots may have different tile
+// counts (the turn is not awaited from a slot that has finished), and the
+// epilogue adds the SOL tail term.
 #pragma once
 
 constexpr int kA5Threads = 384;
@@ -44,31 +51,37 @@ enum : int {
   kB5Count = 21
 };
 
-template <int POLY>
+template <int POLY, bool DUO>
 __global__ void __launch_bounds__(kA5Threads, 1)
     flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                           const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+                           const __grid_constant__ CUtensorMap tmV, AttnParams p, int n_items) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   auto sQ = [&](int X) { return sbase + (uint32_t)X * kTileBytes; };
+  // shared K ring / V ring, or (DUO) K_X at tile 2 + 2X and V_X at tile 3 + 2X
   auto sK = [&](int s) { return sbase + (uint32_t)(2 + s) * kTileBytes; };
-  auto sV = [&](int s) { return sbase + (uint32_t)(2 + kA5KStages + s) * kTileBytes; };
+  auto sV = [&](int s) { return sbase + (uint32_t)((DUO ? 3 : 2 + kA5KStages) + s) * kTileBytes; };
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kA5BarOff);
   auto bar = [&](int i) { return smem_u32(bars + i); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the pair: items 2b and 2b+1 (same head, same key stream)
+  // the pair: items 2b and 2b+1 (shared mode: same head and key stream; DUO: any two
+  // items, the second absent when n_items is odd)
+  const bool has_b = 2 * (int)blockIdx.x + 1 < n_items;
   const WorkItem itA = p.items[2 * blockIdx.x];
-  const int n_kv = item_tiles(itA);
+  const int nA = item_tiles(itA);
+  const int nB = has_b ? item_tiles(p.items[2 * blockIdx.x + 1]) : 0;
+  const int n_kv = DUO ? (nA > nB ? nA : nB) : nA;  // tiles of the longer slot
   const int hcol = itA.head * 128;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kB5Count; ++i) {
       uint32_t c = 1;
-      if (i == kB5KEmpty || i == kB5KEmpty + 1 || i == kB5KEmpty + 2 || i == kB5VEmpty || i == kB5VEmpty + 1) c = 2;
+      if (!DUO && (i == kB5KEmpty || i == kB5KEmpty + 1 || i == kB5KEmpty + 2 || i == kB5VEmpty || i == kB5VEmpty + 1))
+        c = 2;
       if (i == kB5PFull || i == kB5PFull + 1 || i == kB5Turn || i == kB5Turn + 1) c = 4;  // one per softmax warp
       mbar_init(bar(i), c);
     }
@@ -92,52 +105,78 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
       bool ok = true;
-      uint32_t nk = 0, nv = 0;
-      mbar_arrive_expect_tx(bar(kB5QFull), 2 * kTileBytes);
-      for (int X = 0; X < 2; ++X) {
-        const int q0 = p.items[2 * blockIdx.x + X].q_start;
+      uint32_t nk = 0, nv = 0, nk_b = 0;  // loads issued (DUO: K of slot A, K of slot B)
+      const int nslots = (DUO && !has_b) ? 1 : 2;
+      mbar_arrive_expect_tx(bar(kB5QFull), nslots * kTileBytes);
+      for (int X = 0; X < nslots; ++X) {
+        const WorkItem w = p.items[2 * blockIdx.x + X];
         for (int ch = 0; ch < 2; ++ch)
           for (int rh = 0; rh < 2; ++rh)
-            tma_load_2d(sQ(X) + ch * 16384 + rh * 8192, &tmQ, bar(kB5QFull), hcol + ch * 64, q0 + rh * 64);
+            tma_load_2d(sQ(X) + ch * 16384 + rh * 8192, &tmQ, bar(kB5QFull), w.head * 128 + ch * 64,
+                        w.q_start + rh * 64);
       }
-      auto load = [&](bool is_k, int j) -> bool {
-        const uint32_t cnt = is_k ? nk : nv;
-        const int ns = is_k ? kA5KStages : kA5VStages;
-        const uint32_t s = cnt % ns, par = ((cnt / ns) & 1) ^ 1u;
-        const uint32_t full = bar((is_k ? kB5KFull : kB5VFull) + s);
-        if (!mbar_wait(bar((is_k ? kB5KEmpty : kB5VEmpty) + s), par, p.err, kDevTimeoutEmpty, abort_flag))
-          return false;
-        const int4 e = kv_entry(itA, p.entries, j);
-        const uint32_t dst = is_k ? sK(s) : sV(s);
-        const CUtensorMap* tm = is_k ? &tmK : &tmV;
+      auto tile_load = [&](const CUtensorMap* tm, uint32_t dst, uint32_t full, int hc, int4 e) {
         mbar_arrive_expect_tx(full, kTileBytes);
         for (int ch = 0; ch < 2; ++ch) {
-          tma_load_2d(dst + ch * 16384, tm, full, hcol + ch * 64, e.x);
-          tma_load_2d(dst + ch * 16384 + 8192, tm, full, hcol + ch * 64, e.y);
+          tma_load_2d(dst + ch * 16384, tm, full, hc + ch * 64, e.x);
+          tma_load_2d(dst + ch * 16384 + 8192, tm, full, hc + ch * 64, e.y);
         }
-        if (is_k) ++nk; else ++nv;
-        return true;
       };
-      // consumption order of each issuer: K(0), V(0), K(1), V(1), ... with the K
-      // ring two tiles ahead of the V ring
-      ok = load(true, 0) && (n_kv < 2 || load(true, 1));
-      for (int t = 0; t < n_kv && ok; ++t) {
-        ok = load(false, t);
-        if (ok && t + 2 < n_kv) ok = load(true, t + 2);
+      if constexpr (!DUO) {
+        auto load = [&](bool is_k, int j) -> bool {
+          const uint32_t cnt = is_k ? nk : nv;
+          const int ns = is_k ? kA5KStages : kA5VStages;
+          const uint32_t s = cnt % ns, par = ((cnt / ns) & 1) ^ 1u;
+          if (!mbar_wait(bar((is_k ? kB5KEmpty : kB5VEmpty) + s), par, p.err, kDevTimeoutEmpty, abort_flag))
+            return false;
+          tile_load(is_k ? &tmK : &tmV, is_k ? sK(s) : sV(s), bar((is_k ? kB5KFull : kB5VFull) + s), hcol,
+                    kv_entry(itA, p.entries, j));
+          if (is_k) ++nk; else ++nv;
+          return true;
+        };
+        // consumption order of each issuer: K(0), V(0), K(1), V(1), ... with the K
+        // ring two tiles ahead of the V ring
+        ok = load(true, 0) && (n_kv < 2 || load(true, 1));
+        for (int t = 0; t < n_kv && ok; ++t) {
+          ok = load(false, t);
+          if (ok && t + 2 < n_kv) ok = load(true, t + 2);
+        }
+      } else {
+        // one K buffer per slot: K_X(t) waits for S_X(t-1). The V loads come from warp 3
+        // so that a slow V never holds back the next K.
+        const WorkItem itB = p.items[2 * blockIdx.x + (has_b ? 1 : 0)];
+        for (int t = 0; t < n_kv && ok; ++t) {
+          for (int X = 0; X < 2 && ok; ++X) {
+            if (t >= (X == 0 ? nA : nB)) continue;
+            const WorkItem& w = X == 0 ? itA : itB;
+            if (!mbar_wait(bar(kB5KEmpty + X), ((uint32_t)t & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tile_load(&tmK, sK(2 * X), bar(kB5KFull + X), w.head * 128, kv_entry(w, p.entries, t));
+            (X == 0 ? nk : nk_b) = (uint32_t)t + 1;
+          }
+        }
       }
       if (!ok) {  // let copies already issued land before the CTA exits
         mbar_drain(bar(kB5QFull), 0);
-        for (uint32_t i = nk > kA5KStages ? nk - kA5KStages : 0; i < nk; ++i)
-          mbar_drain(bar(kB5KFull + i % kA5KStages), (i / kA5KStages) & 1);
-        for (uint32_t i = nv > kA5VStages ? nv - kA5VStages : 0; i < nv; ++i)
-          mbar_drain(bar(kB5VFull + i % kA5VStages), (i / kA5VStages) & 1);
+        if constexpr (!DUO) {
+          for (uint32_t i = nk > kA5KStages ? nk - kA5KStages : 0; i < nk; ++i)
+            mbar_drain(bar(kB5KFull + i % kA5KStages), (i / kA5KStages) & 1);
+          for (uint32_t i = nv > kA5VStages ? nv - kA5VStages : 0; i < nv; ++i)
+            mbar_drain(bar(kB5VFull + i % kA5VStages), (i / kA5VStages) & 1);
+        } else {
+          if (nk) mbar_drain(bar(kB5KFull), (nk - 1) & 1);
+          if (nk_b) mbar_drain(bar(kB5KFull + 1), (nk_b - 1) & 1);
+        }
       }
     }
   } else if (warp == 1 || warp == 2) {
     reg_dealloc4();
-    if (lane == 0 && n_kv > 0) {
+    const int X = warp - 1;
+    const int nX = X == 0 ? nA : nB;
+    if (lane == 0 && nX > 0) {
       // ------------------------------------------------------------ MMA issuer of slot X
-      const int X = warp - 1;
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
       constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);  // A = P from TMEM, B = V MN-major
       const uint32_t tS = tmem + (uint32_t)(X * 128);
@@ -145,11 +184,17 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       bool ok = mbar_wait(bar(kB5QFull), 0, p.err, kDevTimeoutFull, abort_flag);
       bool issued = false;
       const uint64_t dq = opaque64(smem_desc_sw128(sQ(X), 16, 1024));
+      // buffer, barrier offset and phase of K(t) / V(t) for this slot
+      auto kbuf = [&](int t) { return DUO ? 2 * X : t % kA5KStages; };
+      auto kpar = [&](int t) { return DUO ? ((uint32_t)t & 1) : (((uint32_t)t / kA5KStages) & 1); };
+      auto kbar = [&](int t) { return DUO ? X : t % kA5KStages; };
+      auto vbuf = [&](int t) { return DUO ? 2 * X : t % kA5VStages; };
+      auto vpar = [&](int t) { return DUO ? ((uint32_t)t & 1) : (((uint32_t)t / kA5VStages) & 1); };
+      auto vbar = [&](int t) { return DUO ? X : t % kA5VStages; };
       // S(t) into S/P_X; its K tile must have landed (k_full waited by the caller)
       auto issue_s = [&](int t) {
-        const uint32_t ks = (uint32_t)t % kA5KStages;
         tc_fence_after();
-        const uint64_t dk = opaque64(smem_desc_sw128(sK(ks), 16, 1024));
+        const uint64_t dk = opaque64(smem_desc_sw128(sK(kbuf(t)), 16, 1024));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
@@ -157,30 +202,28 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         }
         issued = true;
         umma_commit(bar(kB5SFull + X));
-        umma_commit(bar(kB5KEmpty + ks));
+        umma_commit(bar(kB5KEmpty + kbar(t)));
       };
       auto k_ready = [&](int t) {
-        return mbar_wait(bar(kB5KFull + (uint32_t)t % kA5KStages), ((uint32_t)t / kA5KStages) & 1, p.err,
-                         kDevTimeoutFull, abort_flag);
+        return mbar_wait(bar(kB5KFull + kbar(t)), kpar(t), p.err, kDevTimeoutFull, abort_flag);
       };
       if (ok && (ok = k_ready(0))) issue_s(0);
-      for (int t = 0; t < n_kv && ok; ++t) {
-        const uint32_t vs = (uint32_t)t % kA5VStages;
+      for (int t = 0; t < nX && ok; ++t) {
         // V(t) and K(t+1) are waited for before P(t): once the softmax hands over P(t),
         // PV(t) and S(t+1) go out back to back with no barrier wait between them
-        if (!mbar_wait(bar(kB5VFull + vs), ((uint32_t)t / kA5VStages) & 1, p.err, kDevTimeoutFull, abort_flag) ||
-            (t + 1 < n_kv && !k_ready(t + 1)) ||
+        if (!mbar_wait(bar(kB5VFull + vbar(t)), vpar(t), p.err, kDevTimeoutFull, abort_flag) ||
+            (t + 1 < nX && !k_ready(t + 1)) ||
             !mbar_wait(bar(kB5PFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint64_t dv = opaque64(smem_desc_sw128(sV(vs), 16384, 1024));
+        const uint64_t dv = opaque64(smem_desc_sw128(sV(vbuf(t)), 16384, 1024));
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           umma_bf16_ts(tO, tS + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(bar(kB5VEmpty + vs));
-        if (t + 1 < n_kv) issue_s(t + 1);
+        umma_commit(bar(kB5VEmpty + vbar(t)));
+        if (t + 1 < nX) issue_s(t + 1);
       }
       if (ok) umma_commit(bar(kB5OFull + X));
       if (issued) {  // every MMA of this thread completes before TMEM is released
@@ -190,11 +233,42 @@ __global__ void __launch_bounds__(kA5Threads, 1)
     }
   } else if (warp == 3) {
     reg_dealloc4();
+    if (DUO && lane == 0 && n_kv > 0) {
+      // ------------------------------------------------------------ V producer (DUO)
+      // one V buffer per slot: V_X(t) waits for PV_X(t-1)
+      bool ok = true;
+      uint32_t nv_a = 0, nv_b = 0;
+      const WorkItem itB = p.items[2 * blockIdx.x + (has_b ? 1 : 0)];
+      for (int t = 0; t < n_kv && ok; ++t) {
+        for (int X = 0; X < 2 && ok; ++X) {
+          if (t >= (X == 0 ? nA : nB)) continue;
+          const WorkItem& w = X == 0 ? itA : itB;
+          if (!mbar_wait(bar(kB5VEmpty + X), ((uint32_t)t & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int4 e = kv_entry(w, p.entries, t);
+          const uint32_t full = bar(kB5VFull + X), dst = sV(2 * X);
+          mbar_arrive_expect_tx(full, kTileBytes);
+          for (int ch = 0; ch < 2; ++ch) {
+            tma_load_2d(dst + ch * 16384, &tmV, full, w.head * 128 + ch * 64, e.x);
+            tma_load_2d(dst + ch * 16384 + 8192, &tmV, full, w.head * 128 + ch * 64, e.y);
+          }
+          (X == 0 ? nv_a : nv_b) = (uint32_t)t + 1;
+        }
+      }
+      if (!ok) {
+        if (nv_a) mbar_drain(bar(kB5VFull), (nv_a - 1) & 1);
+        if (nv_b) mbar_drain(bar(kB5VFull + 1), (nv_b - 1) & 1);
+      }
+    }
   } else {
     reg_alloc4();
     // ------------------------------------------------ softmax + epilogue of slot X
     const int X = (warp - 4) >> 2;
-    const WorkItem it = p.items[2 * blockIdx.x + X];
+    const bool present = X == 0 || has_b;
+    const WorkItem it = p.items[2 * blockIdx.x + (present ? X : 0)];
+    const int nX = X == 0 ? nA : nB;
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int qh = r >> 6;
@@ -204,10 +278,10 @@ __global__ void __launch_bounds__(kA5Threads, 1)
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    int4 e = n_kv > 0 ? kv_entry(it, p.entries, 0) : make_int4(0, 0, 0, 0);
-    for (int t = 0; t < n_kv; ++t) {
+    int4 e = nX > 0 ? kv_entry(it, p.entries, 0) : make_int4(0, 0, 0, 0);
+    for (int t = 0; t < nX; ++t) {
       const int4 cur = e;
-      if (t + 1 < n_kv) e = kv_entry(it, p.entries, t + 1);
+      if (t + 1 < nX) e = kv_entry(it, p.entries, t + 1);
       if (!mbar_wait(bar(kB5SFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
         ok = false;
         break;
@@ -251,9 +325,12 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       // PV and next S.
       // The turn passes when the other slot has issued all but its last chunk of
       // exponentials, so the two phases overlap only in their tails.
-      const bool turn = X == 0 ? (t == 0 || mbar_wait(bar(kB5Turn + 1), ((uint32_t)t - 1) & 1, p.err,
-                                                       kDevTimeoutSoftmax, abort_flag))
-                               : mbar_wait(bar(kB5Turn + 0), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag);
+      // (A slot whose partner has no tile at that index does not wait.)
+      const bool turn = X == 0 ? (t == 0 || t - 1 >= nB ||
+                                  mbar_wait(bar(kB5Turn + 1), ((uint32_t)t - 1) & 1, p.err, kDevTimeoutSoftmax,
+                                            abort_flag))
+                               : (t >= nA ||
+                                  mbar_wait(bar(kB5Turn + 0), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag));
       if (!turn) {
         ok = false;
         break;
@@ -308,21 +385,40 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       __syncwarp();  // the warp's TMEM stores are complete: one arrival per warp (4, not 128 atomics)
       if (lane == 0) mbar_arrive(bar(kB5PFull + X));
     }
-    if (ok && n_kv > 0) ok = mbar_wait(bar(kB5OFull + X), 0, p.err, kDevTimeoutSoftmax, abort_flag);
+    if (ok && nX > 0) ok = mbar_wait(bar(kB5OFull + X), 0, p.err, kDevTimeoutSoftmax, abort_flag);
     tc_fence_after();
-    // epilogue: O / l -> bf16 rows (pairs are formed only from items without a tail term)
-    const float inv = l > 0.f ? 1.0f / l : 0.f;
-    const bool row_ok = ok && r < it.q_rows;
+    // epilogue: O / l (with the SOL tail term for routed items) -> bf16 rows
+    const int ti = qh == 0 ? it.tail0 : it.tail1;
+    float a1 = 1.f, a2 = 0.f, lt = l;
+    const float* T = nullptr;
+    if (DUO && p.tailT && ti >= 0) {
+      const float ms = m * p.sl2;
+      const int64_t o = (int64_t)it.head * p.nqb + ti;
+      const float C2 = p.tailC[o] * 1.4426950408889634f;
+      if (C2 > -INFINITY) {
+        const float M2 = fmaxf(ms, C2);
+        a1 = (m == -INFINITY) ? 0.f : ex2(ms - M2);
+        a2 = ex2(C2 - M2);
+        lt = l * a1 + p.tailL[o] * a2;
+        T = p.tailT + o * 128;
+      }
+    }
+    const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+    const bool row_ok = ok && present && r < it.q_rows;
     __nv_bfloat16* orow = p.out + (int64_t)(it.q_start + r) * p.out_stride + it.head * 128;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 4 && present; ++c) {
       float o[32];
-      if (n_kv > 0) {
+      if (nX > 0) {
         tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      if (T) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = o[i] * a1 + T[c * 32 + i] * a2;
       }
       if (row_ok) {
 #pragma unroll
