@@ -641,6 +641,21 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
   ProfScope prof(ctx, kProfAttn);
   const int poly = exp_poly_pairs();
+  // The paired (strip / dense) items are few and long, the routed ones many and short:
+  // the routed kernel runs on a side stream so that its CTAs fill the SMs left idle by
+  // the last, partial wave of paired CTAs.
+  const int64_t n_rest_all = n_items - 2 * n_pairs;
+  const bool side = n_pairs > 0 && n_rest_all > 0 && attn_kernel_variant() == 2 && attn_duo();
+  if (side) {
+    if (!ctx->aux) {
+      cudaError_t e = cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->fork, cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&ctx->join, cudaEventDisableTiming);
+      if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "side stream: %s", cudaGetErrorString(e));
+    }
+    cudaEventRecord(ctx->fork, ctx->stream);  // after the routing / item kernels
+    cudaStreamWaitEvent(ctx->aux, ctx->fork, 0);
+  }
   if (n_pairs > 0) {
     if (!flash_pair_regs_ok(poly)) return set_error(ctx, WX_ERR_CUDA, "flash_attn_pair: register split does not fit");
     const int np2 = (int)(2 * n_pairs);
@@ -661,13 +676,19 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
     // two independent (routed) items per CTA, their exponential phases taking turns
     const unsigned grid = (unsigned)((n_rest + 1) / 2);
     const int nr = (int)n_rest;
+    cudaStream_t sm = side ? ctx->aux : ctx->stream;
     if (poly == 0)
-      flash_attn_pair_kernel<0, true><<<grid, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, nr);
+      flash_attn_pair_kernel<0, true><<<grid, kA5Threads, kA5Smem, sm>>>(tq, tk, tv, p, nr);
     else if (poly == 2)
-      flash_attn_pair_kernel<2, true><<<grid, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, nr);
+      flash_attn_pair_kernel<2, true><<<grid, kA5Threads, kA5Smem, sm>>>(tq, tk, tv, p, nr);
     else
-      flash_attn_pair_kernel<1, true><<<grid, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, nr);
-    return launch_status(ctx, "flash_attn_duo");
+      flash_attn_pair_kernel<1, true><<<grid, kA5Threads, kA5Smem, sm>>>(tq, tk, tv, p, nr);
+    st = launch_status(ctx, "flash_attn_duo");
+    if (side) {  // join: the context stream continues after both kernels
+      cudaEventRecord(ctx->join, ctx->aux);
+      cudaStreamWaitEvent(ctx->stream, ctx->join, 0);
+    }
+    return st;
   }
   if (attn_kernel_variant() == 4 && flash4_regs_ok(poly)) {
     // persistent: one CTA per SM, items fetched dynamically, softmax split over two warpgroups

@@ -210,6 +210,9 @@ int wx_ctx_destroy(wx_ctx* ctx) {
     cudaEventDestroy(r.b);
   }
   for (auto e : ctx->prof_pool) cudaEventDestroy(e);
+  if (ctx->aux) cudaStreamDestroy(ctx->aux);
+  if (ctx->fork) cudaEventDestroy(ctx->fork);
+  if (ctx->join) cudaEventDestroy(ctx->join);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   delete ctx;

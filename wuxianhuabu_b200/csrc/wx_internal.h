@@ -31,6 +31,10 @@ struct wx_ctx {
   };
   std::vector<ProfRec> prof_recs;
   std::vector<cudaEvent_t> prof_pool;
+  // side stream for independent kernels that run concurrently with the context
+  // stream (forked and joined with the two events); created on first use
+  cudaStream_t aux = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
 };
 
 namespace wx {
