@@ -61,6 +61,28 @@ def test_topk_route_bit_exact(H, g, S):
     assert np.array_equal(got["sel"].cpu().numpy(), ref["sel"])
 
 
+@pytest.mark.parametrize("pattern", ["all_equal", "two_levels", "signed_zero"])
+def test_topk_route_ties_bit_exact(pattern):
+    """Many equal block scores: the selection must break ties by the lower block index."""
+    h3 = _h3()
+    H, g, S = 2, 0, 128 * 23 + 17
+    q, k, v = _qkv(S, H, 900)
+    kf = O.bf16_to_f32(k)
+    if pattern == "all_equal":
+        kf[:] = kf[0:1]
+    elif pattern == "two_levels":
+        kf[:] = np.where((np.arange(S) // 128 % 3 == 0)[:, None, None], kf[0:1], kf[1:2])
+    else:  # zero keys give +0 / -0 scores that must compare equal
+        kf[:] = 0.0
+    k = O.f32_to_bf16(kf)
+    scale = float(1 / np.sqrt(HD))
+    ref = O.topk_route(q, k, v, g, scale, 0.25)
+    cfg = h3.H3SolAttnConfig(block=128, topk_ratio=0.25, tail=False)
+    got = h3.H3SolAttn.route(*_dev(q, k, v), g, scale, cfg)
+    assert np.array_equal(got["scores"].cpu().numpy().view(np.uint32), ref["scores"].view(np.uint32))
+    assert np.array_equal(got["sel"].cpu().numpy(), ref["sel"])
+
+
 @pytest.mark.parametrize("S,H", [(64, 1), (300, 2), (1000, 3), (129, 2)])
 def test_dense_attention(S, H):
     h3 = _h3()

@@ -90,86 +90,169 @@ __global__ void thr_kernel(const float* __restrict__ qc, const float* __restrict
 
 // grid (ceil(nb/32), ceil(nb/8), H), block 256 = 32 key blocks x 8 query blocks.
 // cm = bf16(fma-chain(qc, kc) * scale); mode 1: SOL selection, mode 2: f32 scores.
+// grid (ceil(nb/64), ceil(nb/64), H), block 256: a 64x64 tile of block scores per
+// CTA, 4x4 per thread (register tiling), head_dim in chunks of 32 through shared
+// memory. Every score keeps the sequential fp32 order over d (d = 0, 1, ...) of
+// the reference restatement, so the decisions stay bit-exact.
 __global__ void __launch_bounds__(256) score_kernel(const float* __restrict__ qc, const float* __restrict__ kc,
                                                     int nb, int hd, float scale, int mode,
                                                     const float* __restrict__ thr, int sink_start, int sink_end,
                                                     __nv_bfloat16* __restrict__ cm, uint8_t* __restrict__ sel,
                                                     float* __restrict__ scores) {
-  __shared__ float ks[32][129];
-  __shared__ float qs[8][128];
+  constexpr int T = 64, DC = 32;
+  __shared__ float qs[T][DC + 1];
+  __shared__ float ks[T][DC + 1];
   const int h = blockIdx.z;
-  const int kb0 = blockIdx.x * 32, qb0 = blockIdx.y * 8;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < 32 * hd; i += 256) {
-    const int r = i / hd, d = i % hd;
-    ks[r][d] = (kb0 + r < nb) ? kc[((int64_t)h * nb + kb0 + r) * hd + d] : 0.f;
+  const int qb0 = blockIdx.y * T, kb0 = blockIdx.x * T;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int d0 = 0; d0 < hd; d0 += DC) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < T * DC; i += 256) {
+      const int r = i / DC, d = i % DC;
+      qs[r][d] = (qb0 + r < nb) ? qc[((int64_t)h * nb + qb0 + r) * hd + d0 + d] : 0.f;
+      ks[r][d] = (kb0 + r < nb) ? kc[((int64_t)h * nb + kb0 + r) * hd + d0 + d] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int d = 0; d < DC; ++d) {
+      float qv[4], kv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) qv[i] = qs[ty * 4 + i][d];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) kv[j] = ks[tx + 16 * j][d];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(qv[i], kv[j], acc[i][j]);
+    }
   }
-  for (int i = threadIdx.x; i < 8 * hd; i += 256) {
-    const int r = i / hd, d = i % hd;
-    qs[r][d] = (qb0 + r < nb) ? qc[((int64_t)h * nb + qb0 + r) * hd + d] : 0.f;
-  }
-  __syncthreads();
-  const int qb = qb0 + ty, kb = kb0 + tx;
-  if (qb >= nb || kb >= nb) return;
-  float acc = 0.f;
-  for (int d = 0; d < hd; ++d) acc = __fmaf_rn(qs[ty][d], ks[tx][d], acc);
-  const float sc = __fmul_rn(acc, scale);
-  const __nv_bfloat16 c = __float2bfloat16_rn(sc);
-  const int64_t idx = ((int64_t)h * nb + qb) * nb + kb;
-  cm[idx] = c;
-  if (mode == WX_SPARSE_SOL) {
-    bool s = __bfloat162float(c) > thr[(int64_t)h * nb + qb];
-    if (abs(qb - kb) <= 1) s = true;
-    if (kb >= sink_start && kb < sink_end) s = true;
-    sel[idx] = (uint8_t)s;
-  } else {
-    scores[idx] = sc;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qb = qb0 + ty * 4 + i;
+    if (qb >= nb) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int kb = kb0 + tx + 16 * j;
+      if (kb >= nb) continue;
+      const float sc = __fmul_rn(acc[i][j], scale);
+      const __nv_bfloat16 c = __float2bfloat16_rn(sc);
+      const int64_t idx = ((int64_t)h * nb + qb) * nb + kb;
+      cm[idx] = c;
+      if (mode == WX_SPARSE_SOL) {
+        bool s2 = __bfloat162float(c) > thr[(int64_t)h * nb + qb];
+        if (abs(qb - kb) <= 1) s2 = true;
+        if (kb >= sink_start && kb < sink_end) s2 = true;
+        sel[idx] = (uint8_t)s2;
+      } else {
+        scores[idx] = sc;
+      }
+    }
   }
 }
 
-// grid (nb, H), block 512: bitonic sort of (valid desc, score desc, index asc)
-__global__ void __launch_bounds__(512) topk_select_kernel(const float* __restrict__ scores, int nb, int P, int keep,
+// grid (nb, H), block 256: the `keep` best off-diagonal blocks of row (h, qb) in the
+// order (score desc, block index asc), plus the diagonal. Scores become order-
+// preserving 32-bit keys (-0 folded into +0, so equal floats get equal keys); a
+// radix select over 4 digits of 8 bits finds the keep-th key T; every key > T is
+// kept, and of the keys == T the lowest block indices, in order, fill the rest.
+__device__ __forceinline__ uint32_t score_key(float x) {
+  const uint32_t u = __float_as_uint(__fadd_rn(x, 0.0f));
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(256) topk_select_kernel(const float* __restrict__ scores, int nb, int keep,
                                                           uint8_t* __restrict__ sel) {
-  extern __shared__ uint8_t tsm[];
-  float* key = reinterpret_cast<float*>(tsm);
-  int* idx = reinterpret_cast<int*>(tsm + (size_t)P * 4);
+  extern __shared__ uint32_t keys[];  // [nb]; 0 = not a candidate (diagonal / padding)
+  __shared__ int hist[256];
+  __shared__ uint32_t s_prefix, s_mask;
+  __shared__ int s_need;
+  __shared__ int s_wsum[8];
   const int qb = blockIdx.x, h = blockIdx.y;
   const float* row = scores + ((int64_t)h * nb + qb) * nb;
-  for (int i = threadIdx.x; i < P; i += blockDim.x) {
-    const bool valid = i < nb && i != qb;
-    key[i] = valid ? row[i] : 0.f;
-    idx[i] = valid ? i : (0x40000000 | i);  // invalid entries sort last
+  for (int i = threadIdx.x; i < nb; i += blockDim.x) keys[i] = (i == qb) ? 0u : score_key(row[i]);
+  if (threadIdx.x == 0) {
+    s_prefix = 0;
+    s_mask = 0;
+    s_need = keep;
   }
   __syncthreads();
-  // "a before b" ordering
-  auto before = [](float ka, int ia, float kb_, int ib) {
-    const bool va = ia < 0x40000000, vb = ib < 0x40000000;
-    if (va != vb) return va;
-    if (ka != kb_) return ka > kb_;
-    return ia < ib;
-  };
-  for (int size = 2; size <= P; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = threadIdx.x; i < P; i += blockDim.x) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool up = (i & size) == 0;
-          const bool ij = before(key[i], idx[i], key[j], idx[j]);
-          if (up ? !ij : ij) {
-            float tk = key[i]; key[i] = key[j]; key[j] = tk;
-            int ti = idx[i]; idx[i] = idx[j]; idx[j] = ti;
+  for (int shift = 24; shift >= 0 && keep > 0; shift -= 8) {
+    hist[threadIdx.x] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix, mask = s_mask;
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+      const uint32_t k = keys[i];
+      if (k && (k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      // lane l owns bins [8l, 8l+8): find the bin where the count from the top reaches `need`
+      const int lane = threadIdx.x;
+      int local = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) local += hist[lane * 8 + b];
+      int suf = local;  // inclusive suffix sum over lanes >= lane
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_down_sync(0xffffffffu, suf, o);
+        if (lane + o < 32) suf += v;
+      }
+      const int above = suf - local;  // candidates in the bins of lanes > lane
+      const int need = s_need;
+      const bool here = above < need && above + local >= need;  // exactly one lane
+      if (here) {
+        int cum = above;
+        for (int b = 7; b >= 0; --b) {
+          const int cnt = hist[lane * 8 + b];
+          if (cum + cnt >= need) {
+            s_prefix = prefix | ((uint32_t)(lane * 8 + b) << shift);
+            s_need = need - cum;
+            break;
           }
+          cum += cnt;
         }
       }
-      __syncthreads();
+      if (lane == 0) s_mask = mask | (255u << shift);
     }
+    __syncthreads();
   }
-  uint8_t* srow = sel + ((int64_t)h * nb + qb) * nb;
-  for (int i = threadIdx.x; i < nb; i += blockDim.x) srow[i] = (i == qb) ? 1 : 0;
+  // keys > T are kept; of keys == T the first s_need in index order
+  const uint32_t T = s_prefix;
+  const int need_eq = s_need;
+  const int per = (nb + blockDim.x - 1) / blockDim.x;
+  const int i0 = threadIdx.x * per, i1 = min(nb, i0 + per);
+  int eq = 0;
+  for (int i = i0; i < i1; ++i) eq += (keep > 0 && keys[i] == T && keys[i]) ? 1 : 0;
+  // exclusive prefix of eq over threads (index order)
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int incl = eq;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_wsum[wid] = incl;
   __syncthreads();
-  for (int i = threadIdx.x; i < keep; i += blockDim.x) {
-    const int id = idx[i];
-    if (id < 0x40000000) srow[id] = 1;
+  int before = incl - eq;
+  for (int w = 0; w < wid; ++w) before += s_wsum[w];
+  uint8_t* srow = sel + ((int64_t)h * nb + qb) * nb;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t k = keys[i];
+    bool keepit = (i == qb);
+    if (keep > 0 && k) {
+      if (k > T) {
+        keepit = true;
+      } else if (k == T) {
+        keepit = before < need_eq;
+        ++before;
+      }
+    }
+    srow[i] = (uint8_t)keepit;
   }
 }
 
@@ -484,23 +567,21 @@ static int run_routing(wx_ctx* ctx, const void* q, const void* k, const void* v,
     thr_kernel<<<(unsigned)((hnb + 127) / 128), 128, 0, ctx->stream>>>(qc, kvar, a.H, a.nb, a.hd, scale,
                                                                         spec->tau, thr);
   }
-  dim3 sg((a.nb + 31) / 32, (a.nb + 7) / 8, a.H);
+  if (a.hd % 32 != 0) return set_error(ctx, WX_ERR_UNSUPPORTED, "routing needs head_dim %% 32 == 0");
+  dim3 sg((a.nb + 63) / 64, (a.nb + 63) / 64, a.H);
   score_kernel<<<sg, 256, 0, ctx->stream>>>(qc, kc, a.nb, a.hd, scale, spec->mode, thr, spec->sink_start,
                                            spec->sink_end, cm, sel, scores);
   st = launch_status(ctx, "score", spec->mode == WX_SPARSE_SOL ? 3 : 1);
   if (st) return st;
   if (spec->mode == WX_SPARSE_TOPK) {
-    int P = 1;
-    while (P < a.nb) P <<= 1;
-    if (P > 8192) return set_error(ctx, WX_ERR_UNSUPPORTED, "top-k router supports at most 8192 blocks");
+    if (a.nb > 16384) return set_error(ctx, WX_ERR_UNSUPPORTED, "top-k router supports at most 16384 blocks");
     double want = ceil((double)spec->density * (double)a.nb);
     int keep = (int)std::min<double>(want, a.nb - 1);
     if (keep < 0) keep = 0;
-    const size_t smem = (size_t)P * 8;
-    if (smem > 48 * 1024) {
+    const size_t smem = (size_t)a.nb * 4;
+    if (smem > 48 * 1024)
       cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    }
-    topk_select_kernel<<<dim3(a.nb, a.H), 512, smem, ctx->stream>>>(scores, a.nb, P, keep, sel);
+    topk_select_kernel<<<dim3(a.nb, a.H), 256, smem, ctx->stream>>>(scores, a.nb, keep, sel);
     st = launch_status(ctx, "topk_select");
     if (st) return st;
   }
