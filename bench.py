@@ -362,9 +362,10 @@ def cpu_sample(c: dict, rows: int = 1024, att_rows: int = 384, seed: int = 99) -
 
 
 # ------------------------------------------------------------------ kernel-level configs
-def run_c3(args, seq: int) -> dict:
+def run_c3(args, seq: int, dense: bool = False) -> dict:
     """standalone block-sparse attention (24 x 128 heads,
-    128-row blocks, diagonal + top-k 25 %, g = 0, no tail), routing included."""
+    128-row blocks, diagonal + top-k 25 %, g = 0, no tail), routing included.
+    dense=True: the dense attention of the dense layers and strip rows at the same size."""
     import torch
     from wuxianhuabu_b200 import h3
     dev = torch.device("cuda", 0)
@@ -372,7 +373,7 @@ def run_c3(args, seq: int) -> dict:
     H = 24
     q, k, v = [torch.randn((seq, H, 128), device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
     out = torch.empty_like(q)
-    cfg = h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False)
+    cfg = None if dense else h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False)
     scale = float(1 / math.sqrt(128))
     ctx = h3.context(0)
     for _ in range(args.warmup):
@@ -392,17 +393,21 @@ def run_c3(args, seq: int) -> dict:
     ctx.check_device()
     nb = (seq + 127) // 128
     keep = min(math.ceil(TOPK_DENSITY * nb), nb - 1) + 1
-    flops = 4.0 * 128 * H * seq * min(keep * 128, seq)
+    flops = 4.0 * 128 * H * seq * (seq if dense else min(keep * 128, seq))
     peaks, kind = load_peaks()
     per_call = e0.elapsed_time(e1) / args.steps
     flash_ms = ms[1] / max(1, cnt[1])
     ach = flops / (flash_ms / 1e3) / 1e12
     pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
-    return dict(metric="sparse attention ms/call (c3)", value=per_call, unit="ms/call", config=dict(
-        workload=f"c3: SOL top-k 25% attention, S={seq}, 24x128 heads", S=seq), higher_is_better=False,
-        roofline=dict(kernel="flash_attn_kernel", bound="tensor", achieved=ach, peak=pk, unit="TFLOP/s",
-                      frac=ach / pk, avg_launch_ms=flash_ms, flops_per_launch=flops, peak_kind=f"{kind} burst bf16"),
-        routing_ms=ms[2] / max(1, args.steps))
+    kernel = ("flash_attn_pair_kernel<0, false> (paired query tiles, shared K/V)" if dense else
+              "flash_attn_pair_kernel<0, true> (duo: two routed query tiles per CTA)")
+    what = "dense attention" if dense else "SOL top-k 25% attention"
+    return dict(metric=f"{'dense' if dense else 'sparse'} attention ms/call (c3)", value=per_call, unit="ms/call",
+                config=dict(workload=f"c3: {what}, S={seq}, 24x128 heads", S=seq), higher_is_better=False,
+                roofline=dict(kernel=kernel, bound="tensor", achieved=ach, peak=pk, unit="TFLOP/s",
+                              frac=ach / pk, avg_launch_ms=flash_ms, flops_per_launch=flops,
+                              peak_kind=f"{kind} burst bf16"),
+                routing_ms=ms[2] / max(1, args.steps))
 
 
 def run_c2(args) -> dict:
@@ -454,16 +459,17 @@ def main():
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
-    ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c3", "c3full", "c2"])
+    ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c3", "c3full", "c3dense", "c2"])
     ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
-    if args.config in ("c3", "c3full", "c2"):
+    if args.config in ("c3", "c3full", "c3dense", "c2"):
         import torch
         torch.cuda.set_device(0)
-        r = run_c2(args) if args.config == "c2" else run_c3(args, 28520 if args.config == "c3" else 111600)
+        r = (run_c2(args) if args.config == "c2" else
+             run_c3(args, 111600 if args.config == "c3full" else 28520, dense=args.config == "c3dense"))
         print(json.dumps(r))
         return
     c = geometry(args.config)
