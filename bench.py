@@ -604,7 +604,7 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     ach_attn = attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms > 0 else 0.0
     ach_gemm = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
     if attn_ms >= gemm_ms:
-        roof = dict(kernel="flash_attn_kernel (tcgen05 sparse/dense flash attention)", bound="tensor",
+        roof = dict(kernel="flash_attn_pair_kernel <paired> + <duo> (tcgen05 sparse/dense flash attention)", bound="tensor",
                     achieved=ach_attn, peak=peak_t, unit="TFLOP/s", frac=ach_attn / peak_t,
                     flops_per_launch=attn_flops / attn_launches, avg_launch_ms=attn_ms / attn_launches,
                     traffic=None, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True)
