@@ -415,6 +415,57 @@ int wx_f32_to_bf16(wx_ctx* ctx, const float* x, int64_t n, void* y);
  * negated velocity of H3DiT.forward (:1188): x[i] += (-v[i]) * dsigma */
 int wx_euler_update(wx_ctx* ctx, float* x, const float* v, int64_t n, float dsigma);
 
+/* ------------------------------------------------ conditioning (per generation) */
+/* Dense MfLinear (H3Common.swift:304-308, 361-366): w [k, n] bf16 stored
+ * pre-transposed; y = bf16(bf16(x w) + bias). */
+typedef struct wx_dense_bf16 {
+  const void* w;    /* [k, n] bf16 */
+  const void* bias; /* [n] bf16 or NULL */
+  int64_t k;
+  int64_t n;
+} wx_dense_bf16;
+/* y [m, n] = the dense linear of x [m, k]; for the few rows of an AdaLN table */
+int wx_linear_bf16(wx_ctx* ctx, const void* x, int64_t m, const wx_dense_bf16* w, void* y);
+/* H3TimeEmbedder.forward (H3Transformer.swift:287-302): ts (host, m <= 64) ->
+ * temb [m, dim] fp32 = dense(silu(dense(sinusoid(ts), w_in [freq_dim, dim], b_in)),
+ * w_out [dim, dim], b_out); sinusoid row = [cos(t f_j) | sin(t f_j)],
+ * f_j = exp(-ln(10000) j / (freq_dim/2)). */
+int wx_time_embed(wx_ctx* ctx, const double* ts, int m, int freq_dim, const float* w_in, const float* b_in,
+                  int64_t dim, const float* w_out, const float* b_out, float* temb);
+/* H3AdalnLUT.coeffs (H3Transformer.swift:338-349): row round(t (n_rows-1))
+ * (ties away from zero, clamped) of t_table [n_rows, rank] fp32, as bf16 [m, rank]. */
+int wx_adaln_lut_coeffs(wx_ctx* ctx, const double* ts, int m, const float* t_table, int64_t n_rows, int rank,
+                        void* coeffs);
+/* MLX silu on a bf16 array: y = bf16(x * bf16(sigmoid(x))) */
+int wx_silu_bf16(wx_ctx* ctx, const void* x, int64_t n, void* y);
+/* H3AdalnW.forward (H3Transformer.swift:392-403) of one block (expand 6,
+ * modalities 3) or of the final layer (expand 2, modalities 1): temb [m, k]
+ * bf16 (SiLU applied first when apply_silu) through the adaln_proj linear,
+ * quantized `qw` (+ optional LoRA pack) or dense `dw` (exactly one), then split:
+ * tables[e] [m*modalities, hidden] bf16, row t*modalities + tag
+ * = y[t, (tag*expand + e)*hidden : +hidden]. Block tables feed wx_block_mods
+ * (shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = tables[0..5]);
+ * final tables are [shift, scale]. */
+int wx_adaln_tables(wx_ctx* ctx, const void* temb, int64_t m, int64_t k, int apply_silu, const wx_qweight* qw,
+                    const wx_lora_pack* lora, const wx_dense_bf16* dw, int expand, int modalities,
+                    void* const* tables);
+/* rmsNormLast (H3Common.swift:502-508): out = bf16(x * rsqrt(mean(x^2) + eps) * w) */
+int wx_rms_norm(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w, float eps, void* out);
+/* One token-refiner block (H3DiT.refineText loop body, H3Transformer.swift:1003-1010;
+ * weights H3RefinerBlockW :676-700, in a wx_block_weights): h [L, hidden] in place,
+ * h += attn(rmsNorm(h, norm1)) with per-head q/k RMSNorm, no RoPE and dense
+ * attention; h += mlp(rmsNorm(h, norm2)) (cfg->mlp_kind). */
+int64_t wx_refiner_scratch_bytes(const wx_dit_config* cfg, int64_t L);
+int wx_refiner_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_weights* w, void* h, int64_t L,
+                             void* scratch);
+/* H3DiT.refineText (H3Transformer.swift:993-1016): text [L, text_dim] bf16 ->
+ * out [L, hidden]; identity copy when text_dim == hidden; else condition_proj
+ * (+ LoRA), the n_blocks refiner blocks, and the final RMSNorm when final_norm. */
+int64_t wx_refine_text_scratch_bytes(const wx_dit_config* cfg, int64_t L, int64_t text_dim);
+int wx_refine_text(wx_ctx* ctx, const wx_dit_config* cfg, const wx_qweight* condition_proj,
+                   const wx_lora_pack* condition_lora, const wx_block_weights* blocks, int n_blocks,
+                   const void* final_norm, const void* text, int64_t L, int64_t text_dim, void* out, void* scratch);
+
 #ifdef __cplusplus
 }
 #endif

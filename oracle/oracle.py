@@ -311,3 +311,129 @@ def block_forward(h, w, mods, rowmap, cos, sin, cfg, route_fn=None, at_cached=No
     f1 = lin("fc1", m2, epilogue=act)
     hn = lin("fc2", f1, epilogue=EPI_GATE_RESID, gate=mods[5], resid=ha, rowmap=rowmap)
     return hn, at
+
+
+# ------------------------------------------------------------ conditioning (per generation)
+def timestep_sinusoid(ts, dim: int = 256) -> np.ndarray:
+    """H3TimeEmbedder.forward's host loop (H3Transformer.swift:288-299): row i =
+    [cos(t_i f_j) | sin(t_i f_j)], f_j = exp(-ln(10000) j / half), in double, stored fp32."""
+    half = dim // 2
+    j = np.arange(half, dtype=np.float64)
+    freq = np.exp(-np.log(10000.0) * j / half)
+    arg = np.asarray(ts, dtype=np.float64)[:, None] * freq[None, :]
+    return np.concatenate([np.cos(arg), np.sin(arg)], axis=1).astype(np.float32)
+
+
+def sigmoid_mlx(x: np.ndarray) -> np.ndarray:
+    """MLX's sigmoid: y = 1 / (1 + exp(-|x|)), mirrored for x < 0 (fp32)."""
+    x = np.asarray(x, dtype=np.float32)
+    y = (np.float32(1) / (np.float32(1) + np.exp(-np.abs(x)))).astype(np.float32)
+    return np.where(x < 0, np.float32(1) - y, y).astype(np.float32)
+
+
+def silu_f32(x: np.ndarray) -> np.ndarray:
+    x = np.asarray(x, dtype=np.float32)
+    return (x * sigmoid_mlx(x)).astype(np.float32)
+
+
+def silu_bf16(x: np.ndarray) -> np.ndarray:
+    """silu on a bf16 array as MLX composes it: bf16(x * bf16(sigmoid(x)))."""
+    xf = bf16_to_f32(x)
+    s = bf16_to_f32(f32_to_bf16(sigmoid_mlx(xf)))
+    return f32_to_bf16(xf * s)
+
+
+def time_embed(ts, w_in, b_in, w_out, b_out, freq_dim: int = 256) -> np.ndarray:
+    """H3TimeEmbedder.forward (H3Transformer.swift:287-302): [m, out] fp32."""
+    h1 = silu_f32(dense_f32(timestep_sinusoid(ts, freq_dim), w_in, b_in))
+    return dense_f32(h1, w_out, b_out)
+
+
+def lut_rows(ts, n_rows: int) -> np.ndarray:
+    """H3AdalnLUT.coeffs row index (H3Transformer.swift:340-345): Double.rounded() (ties away
+    from zero) of t·(n-1), clamped to [0, n-1]."""
+    x = np.asarray(ts, dtype=np.float64) * (n_rows - 1)
+    r = np.where(x < 0, -np.floor(-x + 0.5), np.floor(x + 0.5))
+    return np.clip(r, 0, n_rows - 1).astype(np.int64)
+
+
+def lut_coeffs(ts, t_table: np.ndarray) -> np.ndarray:
+    return f32_to_bf16(np.asarray(t_table, dtype=np.float32)[lut_rows(ts, t_table.shape[0])])
+
+
+def linear_bf16(x, w, bias=None) -> np.ndarray:
+    """Dense MfLinear (H3Common.swift:361-366): bf16(bf16(x w) + bias), w [in, out] bf16."""
+    acc = bf16_to_f32(x).astype(np.float64) @ bf16_to_f32(w).astype(np.float64)
+    y = bf16_to_f32(f32_to_bf16(acc.astype(np.float32)))
+    if bias is not None:
+        y = y + bf16_to_f32(bias)[None, :]
+    return f32_to_bf16(y.astype(np.float32))
+
+
+def adaln_split(y: np.ndarray, expand: int, modalities: int) -> list:
+    """H3AdalnW.forward's reshape + split (H3Transformer.swift:397-403): y [m, modalities·expand·hidden]
+    -> expand tables [m·modalities, hidden]."""
+    m, n = y.shape
+    hidden = n // (expand * modalities)
+    v = y.reshape(m * modalities, expand * hidden)
+    return [np.ascontiguousarray(v[:, e * hidden:(e + 1) * hidden]) for e in range(expand)]
+
+
+def adaln_tables(t_emb, expand: int, modalities: int, apply_silu: bool, q=None, dense=None, lora=None):
+    """H3AdalnW.forward (H3Transformer.swift:392-404): q = (wq, sc, bi, bias) quantized linear
+    (with optional LoRA adapters), or dense = (w [in, out], bias)."""
+    x = silu_bf16(t_emb) if apply_silu else np.ascontiguousarray(t_emb)
+    if q is not None:
+        wq, sc, bi, bias = q
+        y = qlinear_lora(x, wq, sc, bi, lora, bias=bias) if lora else qlinear(x, wq, sc, bi, bias=bias)
+    else:
+        y = linear_bf16(x, dense[0], dense[1])
+    return adaln_split(y, expand, modalities)
+
+
+def rms_norm(x, w, eps: float) -> np.ndarray:
+    """rmsNormLast (H3Common.swift:502-508): bf16(x * rsqrt(mean(x^2) + eps) * w), the same
+    arithmetic as the fused norm with zero modulation (bf16(n)·(0+1)+0 is exact)."""
+    x = np.ascontiguousarray(x)
+    zero = np.zeros((1, x.shape[1]), dtype=np.uint16)
+    return norm_modscale(x, w, zero, zero, None, eps)
+
+
+def refiner_block_forward(h, w, cfg):
+    """One token-refiner block (H3DiT.refineText loop body, H3Transformer.swift:1003-1010):
+    h += attn(rmsNorm(h, norm1)) with q/k RMSNorm and no RoPE, dense attention;
+    h += mlp(rmsNorm(h, norm2)). Residual adds are bf16(h + bf16(branch))."""
+    L, hidden = h.shape
+    H, hd = cfg["heads"], cfg["head_dim"]
+    inner = H * hd
+    eps = cfg["eps"]
+    lora = w.get("lora", {})
+    ones = f32_to_bf16(np.ones((1, hidden), dtype=np.float32))
+
+    def lin(name, x, **kw):
+        if lora.get(name):
+            return qlinear_lora(x, *w[name][:3], lora[name], bias=w[name][3], **kw)
+        return qlinear(x, *w[name][:3], bias=w[name][3], **kw)
+
+    n1 = rms_norm(h, w["norm1"], eps)
+    qkv = lin("qkv", n1)
+    q = qk_norm_rope(qkv[:, :inner].reshape(L, H, hd), w["q_norm"], None, None, 0, eps)
+    k = qk_norm_rope(qkv[:, inner:2 * inner].reshape(L, H, hd), w["k_norm"], None, None, 0, eps)
+    v = np.ascontiguousarray(qkv[:, 2 * inner:].reshape(L, H, hd))
+    att = sparse_attention(q, k, v, 0, float(1.0 / np.sqrt(np.float64(hd))))
+    ha = lin("out", att.reshape(L, inner), epilogue=EPI_GATE_RESID, gate=ones, resid=h)
+    n2 = rms_norm(ha, w["norm2"], eps)
+    act = EPI_SWIGLU if cfg.get("mlp_kind", 0) == 1 else EPI_GELU
+    f1 = lin("fc1", n2, epilogue=act)
+    return lin("fc2", f1, epilogue=EPI_GATE_RESID, gate=ones, resid=ha)
+
+
+def refine_text(text, cfg, condition_proj=None, blocks=(), final_norm=None, cp_lora=None):
+    """H3DiT.refineText (H3Transformer.swift:993-1016); condition_proj = (wq, sc, bi, bias)."""
+    if text.shape[1] == cfg["hidden"]:
+        return np.array(text, copy=True)
+    wq, sc, bi, bias = condition_proj
+    h = qlinear_lora(text, wq, sc, bi, cp_lora, bias=bias) if cp_lora else qlinear(text, wq, sc, bi, bias=bias)
+    for b in blocks:
+        h = refiner_block_forward(h, b, cfg)
+    return rms_norm(h, final_norm, cfg["eps"]) if final_norm is not None else h

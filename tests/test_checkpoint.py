@@ -146,3 +146,69 @@ def test_load_block_runs_like_in_memory_weights(tmp_path):
         x = to_torch_bf16(O.normal_bf16((300, k), 6, 1))
         assert torch.equal(lin(x), mem(x)), name
     w.close()
+
+
+@pytest.mark.gpu
+def test_load_conditioning_weights(tmp_path):
+    """time_embedder, a quantized and a dense (folded) adaln_proj, condition_proj, one
+    token-refiner block and its final norm, read through the H3DiT.load names
+    (H3Transformer.swift:762-807) and run against the oracle."""
+    from tests._util import assert_close, f32, to_np_bf16, to_torch_bf16
+    from wuxianhuabu_b200 import h3
+    hidden, heads, ffn, ted, text_dim, rank = 256, 2, 512, 384, 384, 8
+    inner = heads * 128
+    t, qref = {}, {}
+    t["time_embedder.proj_in.weight"] = O.normal_f32((256, ted), 9, 1, std=0.05)
+    t["time_embedder.proj_in.bias"] = O.normal_f32((ted,), 9, 2, std=0.05)
+    t["time_embedder.proj_out.weight"] = O.normal_f32((ted, ted), 9, 3, std=0.02)
+    t["time_embedder.proj_out.bias"] = O.normal_f32((ted,), 9, 4, std=0.02)
+    lins = [("blocks.0.adaln_proj.linear", 18 * hidden, ted), ("condition_proj", hidden, text_dim),
+            ("token_refiner.blocks.0.attn.qkv_proj", 3 * inner, hidden),
+            ("token_refiner.blocks.0.attn.out_proj", hidden, inner),
+            ("token_refiner.blocks.0.mlp.fc1", 2 * ffn, hidden), ("token_refiner.blocks.0.mlp.fc2", hidden, ffn)]
+    for i, (p, n, k) in enumerate(lins):
+        wq, sc, bi = O.quantize(O.normal_f32((n, k), 9, 10 + i, std=0.02))
+        bias = O.normal_bf16((n,), 9, 20 + i, std=0.02)
+        t[p + ".weight"], t[p + ".scales"], t[p + ".biases"], t[p + ".bias"] = wq, sc, bi, bias
+        qref[p] = (wq, sc, bi, bias)
+    dense_w = O.normal_bf16((18 * hidden, rank), 9, 30, std=0.1)  # [out, in] as stored
+    t["blocks.1.adaln_proj.linear.weight"] = dense_w
+    for nm in ("attn.q_norm", "attn.k_norm"):
+        t[f"token_refiner.blocks.0.{nm}.weight"] = O.normal_bf16((128,), 9, 31, mean=1.0, std=0.02)
+    for nm in ("norm1", "norm2"):
+        t[f"token_refiner.blocks.0.{nm}.weight"] = O.normal_bf16((hidden,), 9, 32, mean=1.0, std=0.02)
+    t["token_refiner.final_norm.weight"] = O.normal_bf16((hidden,), 9, 33, mean=1.0, std=0.02)
+    path = tmp_path / "cond.safetensors"
+    write_safetensors(path, t, metadata={"format": "mlx"})
+    w = h3.H3Weights(path)
+    cfg = h3.H3DiTConfig(hidden=hidden, heads=heads, head_dim=128, ffn=ffn, mlp_kind=h3.MLP_SWIGLU, rot=0,
+                         eps=1e-5, layers=2)
+    ts = [1000.0, 500.0]
+    emb = h3.load_time_embedder(w, 256, ted)
+    temb = O.f32_to_bf16(O.time_embed(ts, *[t["time_embedder." + k] for k in
+                                            ("proj_in.weight", "proj_in.bias", "proj_out.weight", "proj_out.bias")]))
+    ad_q = h3.load_adaln(w, "blocks.0.adaln_proj", ted, 6, 3)
+    assert isinstance(ad_q.linear, h3.MfLinear)
+    tables = h3.precompute_adaln(ts, [ad_q], None, hidden, embedder=emb)
+    for got, ref in zip(tables.blocks[0], O.adaln_tables(temb, 6, 3, True, q=qref["blocks.0.adaln_proj.linear"])):
+        assert_close(f32(to_np_bf16(got)), f32(ref), rel=2e-2, cos=0.9999, what="loaded adaln table")
+    ad_d = h3.load_adaln(w, "blocks.1.adaln_proj", ted, 6, 3)
+    assert isinstance(ad_d.linear, h3.DenseLinear) and ad_d.linear.in_dim == rank
+    c = O.normal_bf16((2, rank), 9, 40)
+    for got, ref in zip(ad_d(to_torch_bf16(c), apply_silu=False),
+                        O.adaln_tables(c, 6, 3, False, dense=(np.ascontiguousarray(dense_w.T), None))):
+        assert_close(f32(to_np_bf16(got)), f32(ref), rel=1e-2, cos=0.9999, what="dense adaln table")
+    refiner = h3.load_text_refiner(w, cfg, text_dim)
+    assert refiner.condition_proj is not None and len(refiner.blocks) == 1 and refiner.final_norm is not None
+    text = O.normal_bf16((96, text_dim), 9, 41)
+    got = refiner(to_torch_bf16(text))
+    h3.context().check_device()
+    blk = {"qkv": qref["token_refiner.blocks.0.attn.qkv_proj"], "out": qref["token_refiner.blocks.0.attn.out_proj"],
+           "fc1": qref["token_refiner.blocks.0.mlp.fc1"], "fc2": qref["token_refiner.blocks.0.mlp.fc2"],
+           "q_norm": t["token_refiner.blocks.0.attn.q_norm.weight"],
+           "k_norm": t["token_refiner.blocks.0.attn.k_norm.weight"],
+           "norm1": t["token_refiner.blocks.0.norm1.weight"], "norm2": t["token_refiner.blocks.0.norm2.weight"]}
+    want = O.refine_text(text, dict(hidden=hidden, heads=heads, head_dim=128, eps=1e-5, mlp_kind=1),
+                         qref["condition_proj"], [blk], t["token_refiner.final_norm.weight"])
+    assert_close(f32(to_np_bf16(got)), f32(want), rel=2e-2, cos=0.999, what="loaded refiner")
+    w.close()

@@ -124,3 +124,34 @@ def test_pab_reuse_equals_refresh_with_same_inputs():
     blk.block_forward(0, h3_, md2, rm, c, s, None, pab_slot=slot, refresh=False)
     assert not torch.equal(h1, h3_)
     h3.context().check_device()
+
+
+@pytest.mark.parametrize("sparse", [None, dict(block=128, topk_ratio=0.25, tail=False)])
+def test_block_real_h3_geometry_swiglu(sparse):
+    """The production H3 geometry (H3Config, H3Common.swift:78-89): hidden 5376, 56 heads of
+    128 (inner 7168 != hidden), SwiGLU FFN 14336 (fc1 N = 28672), eps 1e-5, rot 96."""
+    import torch
+    from wuxianhuabu_b200 import h3
+    hidden, heads, ffn, rot, eps = 5376, 56, 14336, 96, 1e-5
+    g, S = 128, 512
+    w, mods, h, cos, sin, rowmap = make_block(12, hidden, heads, ffn, 1, S, rot)
+    cfgd = dict(heads=heads, head_dim=128, eps=eps, rot=rot, mlp_kind=1)
+    scale = float(1 / np.sqrt(np.float32(128)))
+
+    def route_fn(q, k, v):
+        if sparse is None:
+            return None
+        r = O.topk_route(q, k, v, g, scale, sparse["topk_ratio"])
+        r.update(g=g, block=128, tail=False)
+        return r
+
+    ref, ref_at = O.block_forward(h, w, mods, rowmap, cos, sin, cfgd, route_fn=route_fn)
+    blk = gpu_block(w, hidden, heads, ffn, 1, rot, eps)
+    ht = to_torch_bf16(h)
+    spec = None if sparse is None else h3.H3SolAttnConfig(**sparse).spec(g)
+    slot = torch.empty((S, hidden), dtype=torch.bfloat16, device="cuda")
+    blk.block_forward(0, ht, [to_torch_bf16(m) for m in mods], torch.from_numpy(rowmap.view(np.int32)).cuda(),
+                      to_torch_bf16(cos), to_torch_bf16(sin), spec, pab_slot=slot, refresh=True)
+    h3.context().check_device()
+    assert_close(f32(to_np_bf16(slot)), f32(ref_at), rel=2e-2, cos=0.999, what="real geometry at")
+    assert_close(f32(to_np_bf16(ht)), f32(ref), rel=2e-2, cos=0.999, what="real geometry h")

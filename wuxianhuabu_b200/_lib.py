@@ -95,6 +95,10 @@ class StepArgs(C.Structure):
                 ("dsigma", C.c_float), ("reserved", C.c_int32), ("scratch", C.c_void_p)]
 
 
+class DenseBf16(C.Structure):
+    _fields_ = [("w", C.c_void_p), ("bias", C.c_void_p), ("k", C.c_int64), ("n", C.c_int64)]
+
+
 _vp, _i64, _i32, _f32, _f64, _u32 = C.c_void_p, C.c_int64, C.c_int, C.c_float, C.c_double, C.c_uint32
 
 # name -> (restype, argtypes)
@@ -162,6 +166,18 @@ _SIGS = {
     "wx_bf16_to_f32": (_i32, [_vp, _vp, _i64, _vp]),
     "wx_f32_to_bf16": (_i32, [_vp, _vp, _i64, _vp]),
     "wx_euler_update": (_i32, [_vp, _vp, _vp, _i64, _f32]),
+    "wx_linear_bf16": (_i32, [_vp, _vp, _i64, C.POINTER(DenseBf16), _vp]),
+    "wx_time_embed": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "wx_adaln_lut_coeffs": (_i32, [_vp, _vp, _i32, _vp, _i64, _i32, _vp]),
+    "wx_silu_bf16": (_i32, [_vp, _vp, _i64, _vp]),
+    "wx_adaln_tables": (_i32, [_vp, _vp, _i64, _i64, _i32, C.POINTER(QWeight), C.POINTER(LoraPack),
+                               C.POINTER(DenseBf16), _i32, _i32, _vp]),
+    "wx_rms_norm": (_i32, [_vp, _vp, _i64, _i64, _vp, _f32, _vp]),
+    "wx_refiner_scratch_bytes": (_i64, [C.POINTER(DitConfig), _i64]),
+    "wx_refiner_block_forward": (_i32, [_vp, C.POINTER(DitConfig), C.POINTER(BlockWeights), _vp, _i64, _vp]),
+    "wx_refine_text_scratch_bytes": (_i64, [C.POINTER(DitConfig), _i64, _i64]),
+    "wx_refine_text": (_i32, [_vp, C.POINTER(DitConfig), C.POINTER(QWeight), C.POINTER(LoraPack),
+                              C.POINTER(BlockWeights), _i32, _vp, _vp, _i64, _i64, _vp, _vp]),
 }
 
 _lib = None

@@ -162,7 +162,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
 
 // ----------------------------------------------------------------- K4
 // h3_fused_norm_modscale (fused:133-168): one warp per row, two passes over
-// the row (the second pass hits L1).
+// the row (the second pass hits L1). MOD = false is rmsNormLast
+// (H3Common.swift:502-508): bf16(x * rstd * w) with no modulation tables.
+template <bool MOD>
 __global__ void __launch_bounds__(256) norm_modscale_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t S, int hidden, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ shift, const __nv_bfloat16* __restrict__ scale,
@@ -172,8 +174,8 @@ __global__ void __launch_bounds__(256) norm_modscale_kernel(
   if (r >= S) return;
   const __nv_bfloat16* xr = x + r * hidden;
   const int64_t mr = rowmap ? (int64_t)rowmap[r] : 0;
-  const __nv_bfloat16* sh = shift + mr * hidden;
-  const __nv_bfloat16* sc = scale + mr * hidden;
+  const __nv_bfloat16* sh = MOD ? shift + mr * hidden : nullptr;
+  const __nv_bfloat16* sc = MOD ? scale + mr * hidden : nullptr;
   __nv_bfloat16* orow = out + r * hidden;
   const bool vec = (hidden % 256) == 0;
   float ss = 0.f;
@@ -199,26 +201,32 @@ __global__ void __launch_bounds__(256) norm_modscale_kernel(
     for (int j = lane * 8; j < hidden; j += 256) {
       uint4 xv = *reinterpret_cast<const uint4*>(xr + j);
       uint4 wv = *reinterpret_cast<const uint4*>(w + j);
-      uint4 hv = *reinterpret_cast<const uint4*>(sh + j);
-      uint4 cv = *reinterpret_cast<const uint4*>(sc + j);
       const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w}, wu[4] = {wv.x, wv.y, wv.z, wv.w};
-      const uint32_t hu[4] = {hv.x, hv.y, hv.z, hv.w}, cu[4] = {cv.x, cv.y, cv.z, cv.w};
       uint32_t ou[4];
+      if constexpr (MOD) {
+        uint4 hv = *reinterpret_cast<const uint4*>(sh + j);
+        uint4 cv = *reinterpret_cast<const uint4*>(sc + j);
+        const uint32_t hu[4] = {hv.x, hv.y, hv.z, hv.w}, cu[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        float n0 = round_bf16(bf16_lo(xu[q]) * rstd * bf16_lo(wu[q]));
-        float n1 = round_bf16(bf16_hi(xu[q]) * rstd * bf16_hi(wu[q]));
-        float o0 = n0 * (bf16_lo(cu[q]) + 1.0f) + bf16_lo(hu[q]);
-        float o1 = n1 * (bf16_hi(cu[q]) + 1.0f) + bf16_hi(hu[q]);
-        ou[q] = pack_bf16x2(o0, o1);
+        for (int q = 0; q < 4; ++q) {
+          float n0 = round_bf16(bf16_lo(xu[q]) * rstd * bf16_lo(wu[q]));
+          float n1 = round_bf16(bf16_hi(xu[q]) * rstd * bf16_hi(wu[q]));
+          float o0 = n0 * (bf16_lo(cu[q]) + 1.0f) + bf16_lo(hu[q]);
+          float o1 = n1 * (bf16_hi(cu[q]) + 1.0f) + bf16_hi(hu[q]);
+          ou[q] = pack_bf16x2(o0, o1);
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          ou[q] = pack_bf16x2(bf16_lo(xu[q]) * rstd * bf16_lo(wu[q]), bf16_hi(xu[q]) * rstd * bf16_hi(wu[q]));
       }
       *reinterpret_cast<uint4*>(orow + j) = make_uint4(ou[0], ou[1], ou[2], ou[3]);
     }
   } else {
     for (int j = lane; j < hidden; j += 32) {
       float nv = round_bf16(__bfloat162float(xr[j]) * rstd * __bfloat162float(w[j]));
-      float o = nv * (__bfloat162float(sc[j]) + 1.0f) + __bfloat162float(sh[j]);
-      orow[j] = __float2bfloat16_rn(o);
+      if constexpr (MOD) nv = nv * (__bfloat162float(sc[j]) + 1.0f) + __bfloat162float(sh[j]);
+      orow[j] = __float2bfloat16_rn(nv);
     }
   }
 }
@@ -415,7 +423,8 @@ int launch_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, 
                          const void* shift, const void* scale, const uint32_t* rowmap, float eps, void* out) {
   if (S == 0) return WX_OK;
   ProfScope prof(ctx, kProfRow);
-  norm_modscale_kernel<<<(unsigned)((S + 7) / 8), 256, 0, ctx->stream>>>(
+  auto kern = shift ? norm_modscale_kernel<true> : norm_modscale_kernel<false>;
+  kern<<<(unsigned)((S + 7) / 8), 256, 0, ctx->stream>>>(
       static_cast<const __nv_bfloat16*>(x), S, (int)hidden, static_cast<const __nv_bfloat16*>(w),
       static_cast<const __nv_bfloat16*>(shift), static_cast<const __nv_bfloat16*>(scale), rowmap, eps,
       static_cast<__nv_bfloat16*>(out));
@@ -481,6 +490,12 @@ int wx_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, cons
   WX_CHECK_ARG(ctx, hidden % 256 != 0 || (aligned16(x) && aligned16(w) && aligned16(shift) &&
                                           aligned16(scale) && aligned16(out)));
   return launch_norm_modscale(ctx, x, S, hidden, w, shift, scale, rowmap, eps, out);
+}
+
+int wx_rms_norm(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w, float eps, void* out) {
+  WX_CHECK_ARG(ctx, ctx && x && w && out && S >= 0 && hidden > 0 && hidden < (1 << 30));
+  WX_CHECK_ARG(ctx, hidden % 256 != 0 || (aligned16(x) && aligned16(w) && aligned16(out)));
+  return launch_norm_modscale(ctx, x, S, hidden, w, nullptr, nullptr, nullptr, eps, out);
 }
 
 int wx_mod_gate(wx_ctx* ctx, const void* x, const void* other, const void* gate, const uint32_t* rowmap,

@@ -35,6 +35,8 @@ __all__ = [
     "attn_broadcast_default_max_stale", "sigma_schedule", "sparse_mode_for_layer", "SparsePolicy",
     "H3DiTConfig", "H3BlockWeights", "H3DiTBlocks", "ModRun", "WxError", "LoraRef", "H3Weights", "load_block",
     "EPI_NONE", "EPI_GELU", "EPI_GATE_RESID", "EPI_SWIGLU",
+    "DenseLinear", "H3TimeEmbedder", "H3AdalnLUT", "H3AdalnW", "H3AdalnTables", "precompute_adaln",
+    "H3TextRefiner", "rms_norm", "load_refiner_block", "load_text_refiner", "load_time_embedder", "load_adaln",
 ]
 
 
@@ -572,6 +574,201 @@ class H3DiT:
         return latents
 
 
+# ------------------------------------------------------------ conditioning (per generation)
+class DenseLinear:
+    """The dense branch of MfLinear (H3Common.swift:304-308, 361-366): ``w`` [in, out] bf16
+    stored pre-transposed, optional ``bias`` [out]; forward = bf16(bf16(x w) + bias)."""
+
+    def __init__(self, w: torch.Tensor, bias: Optional[torch.Tensor] = None):
+        _need_bf16_cuda(w, bias)
+        self.w, self.bias = w.contiguous(), bias
+        self.in_dim, self.out_dim = w.shape
+
+    def c(self) -> _lib.DenseBf16:
+        return _lib.DenseBf16(_p(self.w), _p(self.bias), self.in_dim, self.out_dim)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        _need_bf16_cuda(x)
+        x2 = x.reshape(-1, self.in_dim).contiguous()
+        y = torch.empty((x2.shape[0], self.out_dim), dtype=torch.bfloat16, device=x.device)
+        dw = self.c()
+        context(x.device.index).call("wx_linear_bf16", _p(x2), x2.shape[0], C.byref(dw), _p(y))
+        return y.reshape(*x.shape[:-1], self.out_dim)
+
+    __call__ = forward
+
+
+class H3TimeEmbedder:
+    """H3TimeEmbedder (H3Transformer.swift:255-302), the fp32 island: sinusoid of the
+    timesteps → proj_in → SiLU → proj_out. Weights fp32 [in, out] as the reference stores them."""
+
+    def __init__(self, input_dim: int, out_dim: int, proj_in_w: torch.Tensor, proj_in_b: Optional[torch.Tensor],
+                 proj_out_w: torch.Tensor, proj_out_b: Optional[torch.Tensor]):
+        for t in (proj_in_w, proj_in_b, proj_out_w, proj_out_b):
+            if t is not None and (not t.is_cuda or t.dtype != torch.float32):
+                raise WxError(_lib.WX_ERR_INVALID, "time embedder weights must be CUDA fp32 tensors")
+        self.input_dim, self.out_dim = input_dim, out_dim
+        self.proj_in_w, self.proj_in_b = proj_in_w.contiguous(), proj_in_b
+        self.proj_out_w, self.proj_out_b = proj_out_w.contiguous(), proj_out_b
+
+    def forward(self, t_vals: Sequence[float]) -> torch.Tensor:
+        """t_vals → [m, out_dim] fp32 (the caller casts to bf16, as precomputeAdaln does)."""
+        m = len(t_vals)
+        ts = (C.c_double * m)(*[float(t) for t in t_vals])
+        out = torch.empty((m, self.out_dim), dtype=torch.float32, device=self.proj_in_w.device)
+        context(out.device.index).call("wx_time_embed", ts, m, self.input_dim, _p(self.proj_in_w),
+                                       _p(self.proj_in_b), self.out_dim, _p(self.proj_out_w), _p(self.proj_out_b),
+                                       _p(out))
+        return out
+
+    __call__ = forward
+
+
+class H3AdalnLUT:
+    """H3AdalnLUT (H3Transformer.swift:319-350): lookup-table time modulation of pruned /
+    fused checkpoints; ``t_table`` [n, rank] fp32 (basis and mean are kept for reference only)."""
+
+    def __init__(self, basis: Optional[torch.Tensor], mean: Optional[torch.Tensor], t_table: torch.Tensor):
+        if not t_table.is_cuda or t_table.dtype != torch.float32:
+            raise WxError(_lib.WX_ERR_INVALID, "adaln_t_table must be a CUDA fp32 tensor")
+        self.basis, self.mean, self.t_table = basis, mean, t_table.contiguous()
+        self.rank = t_table.shape[1]
+
+    def coeffs(self, ts: Sequence[float]) -> torch.Tensor:
+        """coeffs(ts).asType(bf16): [m, rank] rows round(t·(n-1)) of the table."""
+        m = len(ts)
+        arr = (C.c_double * m)(*[float(t) for t in ts])
+        out = torch.empty((m, self.rank), dtype=torch.bfloat16, device=self.t_table.device)
+        context(out.device.index).call("wx_adaln_lut_coeffs", arr, m, _p(self.t_table), self.t_table.shape[0],
+                                       self.rank, _p(out))
+        return out
+
+
+class H3AdalnW:
+    """H3AdalnW (H3Transformer.swift:353-404): ``linear`` (quantized MfLinear, optionally with
+    LoRA, or DenseLinear for folded LUT checkpoints) [time_embed_dim → expand·modalities·hidden];
+    forward splits it into ``expand`` tables of [m·modalities, hidden]."""
+
+    def __init__(self, linear, expand: int, modalities: int):
+        self.linear, self.expand, self.modalities = linear, expand, modalities
+
+    def forward(self, t_emb: torch.Tensor, apply_silu: bool = True) -> list[torch.Tensor]:
+        _need_bf16_cuda(t_emb)
+        t_emb = t_emb.contiguous()
+        m, k = t_emb.shape
+        n = self.linear.out_dim
+        hidden = n // (self.expand * self.modalities)
+        tabs = [torch.empty((m * self.modalities, hidden), dtype=torch.bfloat16, device=t_emb.device)
+                for _ in range(self.expand)]
+        ptrs = (C.c_void_p * self.expand)(*[t.data_ptr() for t in tabs])
+        qw = pack = dw = None
+        if isinstance(self.linear, MfLinear):
+            qw = self.linear.qweight()
+            pack = self.linear.lora_pack()
+        else:
+            dw = self.linear.c()
+        context(t_emb.device.index).call("wx_adaln_tables", _p(t_emb), m, k, int(apply_silu),
+                                         C.byref(qw) if qw is not None else None,
+                                         C.byref(pack) if pack is not None else None,
+                                         C.byref(dw) if dw is not None else None, self.expand, self.modalities, ptrs)
+        return tabs
+
+    __call__ = forward
+
+
+@dataclass
+class H3AdalnTables:
+    """H3AdalnTables (H3Transformer.swift:406-411)."""
+    ts: list
+    blocks: list  # [layer][6] each [t·modalities, hidden]
+    final: list   # [2] each [t, hidden]
+
+
+def precompute_adaln(ts: Sequence[float], block_adalns: Sequence[Optional[H3AdalnW]],
+                     final_adaln: Optional[H3AdalnW], hidden: int, embedder: Optional[H3TimeEmbedder] = None,
+                     lut: Optional[H3AdalnLUT] = None, device=None) -> H3AdalnTables:
+    """H3DiT.precomputeAdaln (H3Transformer.swift:957-988): the t-embedding (LUT coefficients,
+    no SiLU; or the time embedder, SiLU in the adaln forward) folded into every block's six
+    tables and the final layer's two. Absent (ablated) block modulation gives zero tables
+    (the reference allocates them with ts.count rows; here they get ts.count·3 rows so that
+    every mod row a plan can address exists — the values are the same zeros)."""
+    if lut is not None:
+        t_emb, apply_silu = lut.coeffs(ts), False
+    elif embedder is not None:
+        t_emb, apply_silu = embedder(ts), True
+        src = t_emb
+        t_emb = torch.empty(src.shape, dtype=torch.bfloat16, device=src.device)
+        context(src.device.index).call("wx_f32_to_bf16", _p(src), src.numel(), _p(t_emb))
+    else:
+        raise WxError(_lib.WX_ERR_INVALID, "precompute_adaln needs the time embedder or the LUT")
+    dev = t_emb.device if device is None else device
+    blocks = []
+    for ad in block_adalns:
+        if ad is None:
+            zero = torch.zeros((len(ts) * 3, hidden), dtype=torch.bfloat16, device=dev)
+            blocks.append([zero] * 6)
+        else:
+            blocks.append(ad(t_emb, apply_silu))
+    final = final_adaln(t_emb, apply_silu) if final_adaln is not None else []
+    return H3AdalnTables(list(ts), blocks, final)
+
+
+class H3TextRefiner:
+    """H3DiT.refineText (H3Transformer.swift:993-1016) on libwx: condition_proj [text_dim →
+    hidden], the token-refiner blocks (H3RefinerBlockW, :676-700; same weight set as a DiT
+    block, used without modulation or RoPE, dense attention), then the final RMSNorm.
+    Text states already ``hidden`` wide come back unchanged, as in the reference."""
+
+    def __init__(self, cfg: H3DiTConfig, condition_proj: Optional[MfLinear], blocks: Sequence[H3BlockWeights],
+                 final_norm: Optional[torch.Tensor]):
+        self.cfg = cfg
+        self.condition_proj = condition_proj
+        self.blocks = list(blocks)
+        self.final_norm = final_norm
+        self._wc = [b.c() for b in self.blocks]
+        lins = [lin for b in self.blocks for lin in b.linears()] + ([condition_proj] if condition_proj else [])
+        rank = max([lin.lora_pack().R for lin in lins if lin.lora] or [0])
+        self._c = cfg.c(int(rank))
+        self._bw = (BlockWeights * max(1, len(self._wc)))(*self._wc)
+
+    def block_forward(self, bi: int, h: torch.Tensor) -> torch.Tensor:
+        """One refiner block, h [L, hidden] updated in place."""
+        _need_bf16_cuda(h)
+        lib = _lib.load()
+        L = h.shape[0]
+        need = int(lib.wx_refiner_scratch_bytes(C.byref(self._c), L))
+        scr = torch.empty(need, dtype=torch.uint8, device=h.device)
+        context(h.device.index).call("wx_refiner_block_forward", C.byref(self._c), C.byref(self._wc[bi]), _p(h), L,
+                                     _p(scr))
+        return h
+
+    def forward(self, text_states: torch.Tensor) -> torch.Tensor:
+        _need_bf16_cuda(text_states, self.final_norm)
+        x = text_states.contiguous()
+        L, text_dim = x.shape
+        lib = _lib.load()
+        out = torch.empty((L, self.cfg.hidden), dtype=torch.bfloat16, device=x.device)
+        need = int(lib.wx_refine_text_scratch_bytes(C.byref(self._c), L, text_dim))
+        scr = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+        qw = self.condition_proj.qweight() if self.condition_proj is not None else None
+        pack = self.condition_proj.lora_pack() if self.condition_proj is not None else None
+        context(x.device.index).call("wx_refine_text", C.byref(self._c), C.byref(qw) if qw is not None else None,
+                                     C.byref(pack) if pack is not None else None, self._bw, len(self._wc),
+                                     _p(self.final_norm), _p(x), L, text_dim, _p(out), _p(scr))
+        return out
+
+    __call__ = forward
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """rmsNormLast (H3Common.swift:502-508) over the last axis."""
+    _need_bf16_cuda(x, weight)
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    out = torch.empty_like(x2)
+    context(x.device.index).call("wx_rms_norm", _p(x2), x2.shape[0], x2.shape[1], _p(weight), float(eps), _p(out))
+    return out.reshape(x.shape)
+
+
 # ------------------------------------------------------------------------ checkpoints
 _ST_DTYPES = {"BF16": torch.bfloat16, "F16": torch.float16, "F32": torch.float32, "I32": torch.int32,
               "U32": torch.int32, "I64": torch.int64, "U8": torch.uint8, "I8": torch.int8, "BOOL": torch.bool}
@@ -668,3 +865,64 @@ def load_block(w: H3Weights, idx: int, cfg: H3DiTConfig, device=None) -> H3Block
                           w.get_linear(p + ".mlp.fc2", cfg.ffn, device),
                           need(p + ".attn.q_norm.weight"), need(p + ".attn.k_norm.weight"),
                           need(p + ".norm1.weight"), need(p + ".norm2.weight"))
+
+
+def _need_bf16(w: H3Weights, key: str, device=None) -> torch.Tensor:
+    t = w.get(key, device)
+    if t is None:
+        raise WxError(_lib.WX_ERR_INVALID, f"missing weight: {key}")
+    return t.to(torch.bfloat16) if t.dtype != torch.bfloat16 else t
+
+
+def load_refiner_block(w: H3Weights, idx: int, cfg: H3DiTConfig, device=None) -> H3BlockWeights:
+    """H3RefinerBlockW.load (H3Transformer.swift:690-699): token_refiner.blocks.{idx}.*"""
+    p = f"token_refiner.blocks.{idx}"
+    inner = cfg.heads * cfg.head_dim
+    return H3BlockWeights(w.get_linear(p + ".attn.qkv_proj", cfg.hidden, device),
+                          w.get_linear(p + ".attn.out_proj", inner, device),
+                          w.get_linear(p + ".mlp.fc1", cfg.hidden, device),
+                          w.get_linear(p + ".mlp.fc2", cfg.ffn, device),
+                          _need_bf16(w, p + ".attn.q_norm.weight", device),
+                          _need_bf16(w, p + ".attn.k_norm.weight", device),
+                          _need_bf16(w, p + ".norm1.weight", device), _need_bf16(w, p + ".norm2.weight", device))
+
+
+def load_text_refiner(w: H3Weights, cfg: H3DiTConfig, text_dim: int, device=None) -> H3TextRefiner:
+    """The text-side weights of H3DiT.load (H3Transformer.swift:792-807): condition_proj
+    when present, token_refiner.blocks.0.. while their qkv_proj exists, and
+    token_refiner.final_norm.weight when present."""
+    cp = w.get_linear("condition_proj", text_dim, device) if w.contains("condition_proj.weight") else None
+    blocks = []
+    while (w.contains(f"token_refiner.blocks.{len(blocks)}.attn.qkv_proj.weight")
+           or w.contains(f"token_refiner.blocks.{len(blocks)}.attn.qkv_proj.scales")):
+        blocks.append(load_refiner_block(w, len(blocks), cfg, device))
+    fn = w.get("token_refiner.final_norm.weight", device)
+    if fn is not None and fn.dtype != torch.bfloat16:
+        fn = fn.to(torch.bfloat16)
+    return H3TextRefiner(cfg, cp, blocks, fn)
+
+
+def load_time_embedder(w: H3Weights, input_dim: int = 256, out_dim: int = 2688, device=None) -> H3TimeEmbedder:
+    """H3TimeEmbedder.load (H3Transformer.swift:274-286); weights kept fp32 [in, out]."""
+    def f32(key):
+        t = w.get(key, device)
+        return None if t is None else (t if t.dtype == torch.float32 else t.to(torch.float32))
+    win, wout = f32("time_embedder.proj_in.weight"), f32("time_embedder.proj_out.weight")
+    if win is None or wout is None:
+        raise WxError(_lib.WX_ERR_INVALID, "missing weight: time_embedder.proj_in.weight / proj_out.weight")
+    return H3TimeEmbedder(input_dim, out_dim, win, f32("time_embedder.proj_in.bias"), wout,
+                          f32("time_embedder.proj_out.bias"))
+
+
+def load_adaln(w: H3Weights, prefix: str, time_embed_dim: int, expand: int, modalities: int,
+               device=None) -> H3AdalnW:
+    """H3AdalnW.load (H3Transformer.swift:366-382): {prefix}.linear quantized (in =
+    time_embed_dim), or dense [out, in] stored transposed to [in, out] as MfLinear.load does."""
+    if w.contains(prefix + ".linear.scales") or w.contains(prefix + ".linear.weight.scales"):
+        return H3AdalnW(w.get_linear(prefix + ".linear", time_embed_dim, device), expand, modalities)
+    raw = w.get(prefix + ".linear.weight", device)
+    if raw is None:
+        raise WxError(_lib.WX_ERR_INVALID, f"missing weight: {prefix}.linear.weight")
+    bias = w.get(prefix + ".linear.bias", device)
+    wt = raw.to(torch.bfloat16).t().contiguous()  # raw [out, in] -> [in, out]
+    return H3AdalnW(DenseLinear(wt, bias.to(torch.bfloat16) if bias is not None else None), expand, modalities)
