@@ -454,8 +454,9 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
 #include "wx_flash5.cuh"
 
 // ------------------------------------------------------------- host driver
-// Share of the softmax exponentials taken by the FMA-pipe polynomial (pairs out of
-// every 4; tuning knob WX_EXP_POLY_PAIRS = 0, 1 or 2, read once).
+// Share of the softmax exponentials taken by the FMA-pipe polynomial (tuning knob
+// WX_EXP_POLY_PAIRS = 0, 1 or 2, read once): pairs out of every 4 in flash_attn2 /
+// flash_attn4, out of every 8 in the paired and duo kernels.
 static int exp_poly_pairs() {
   static int v = [] {
     const char* e = getenv("WX_EXP_POLY_PAIRS");

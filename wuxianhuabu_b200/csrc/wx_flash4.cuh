@@ -32,8 +32,8 @@ constexpr int kA4Prefetch = 4;  // key tiles ahead whose K/V boxes are prefetche
 // Q[1] | K[3] | V[3] | barriers + queue + partial row sums
 constexpr int kA4BarOff = (kA4QStages + kA4KStages + kA4VStages) * kTileBytes;
 constexpr int kA4Smem = kA4BarOff + 2048 + 1024;
-constexpr int kA4RegsLow = 80;    // warps 0-3 after setmaxnreg.dec
-constexpr int kA4RegsHigh = 200;  // warps 4-11 after setmaxnreg.inc
+constexpr int kA4RegsLow = 72;    // warps 0-3 after setmaxnreg.dec
+constexpr int kA4RegsHigh = 216;  // warps 4-11 after setmaxnreg.inc (72*128 + 216*256 = 168*384)
 static_assert(kA4RegsLow * 128 + kA4RegsHigh * 256 <= 168 * kA4Threads, "register split exceeds the launch");
 
 enum : int {

@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         for (int i = 0; i < 16; ++i) {
           const float2 a = __ffma2_rn(make_float2(v[32 * c + 2 * i], v[32 * c + 2 * i + 1]), sl2x2, nmu2);
           float2 pv;
-          if ((i & 3) < POLY) {
+          if ((i & 7) < POLY) {  // POLY pairs of every 8 on the FMA pipe
             pv = ex2_poly2(a);
           } else {
             pv = make_float2(ex2(a.x), ex2(a.y));
