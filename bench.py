@@ -42,14 +42,14 @@ PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=
 
 CONFIGS = {
     # full-size 720p x 121f with reference-image conditioning
-    "c5": dict(text=512, refs=4, ref_rows=3600, grid=(31, 45, 80), hidden=3072, heads=24, ffn=12288, layers=48,
-               text_dim=4096),
+    "c5": dict(text=512, refs=4, ref_rows=3600, ref_hw=(120, 120), grid=(31, 45, 80), hidden=3072, heads=24,
+               ffn=12288, layers=48, text_dim=4096),
     # half-size step
-    "c4": dict(text=512, refs=0, ref_rows=0, grid=(31, 23, 40), hidden=3072, heads=24, ffn=12288, layers=48,
-               text_dim=4096),
+    "c4": dict(text=512, refs=0, ref_rows=0, ref_hw=(0, 0), grid=(31, 23, 40), hidden=3072, heads=24, ffn=12288,
+               layers=48, text_dim=4096),
     # development geometry (seconds on one GPU)
-    "tiny": dict(text=64, refs=1, ref_rows=192, grid=(3, 8, 16), hidden=512, heads=4, ffn=1024, layers=4,
-                 text_dim=512),
+    "tiny": dict(text=64, refs=1, ref_rows=192, ref_hw=(24, 32), grid=(3, 8, 16), hidden=512, heads=4, ffn=1024,
+                 layers=4, text_dim=512),
 }
 PATCH_DIM = 96          # latent channels x 2 x 2 patch
 TOPK_DENSITY = 0.25
@@ -256,22 +256,16 @@ class Runner:
 
     @staticmethod
     def _rope(c, dev):
-        """buildRope (H3Layout.swift:725-740): angles = concat(t*inv, h*inv, w*inv) for 16 inverse frequencies."""
+        """Position ids of the packed layout (text, reference images, target video; H3Layout.swift
+        PackedLayout) and buildRope (:725-740) through libwx, with the 16 inverse frequencies
+        1/10000^(2j/32) standing in for the checkpoint's inv_freq."""
         import torch
+        from wuxianhuabu_b200 import h3
         t, hh, ww = c["grid"]
-        pos = []
-        pos.append(torch.zeros((c["text"], 3)))
-        for r in range(c["refs"]):
-            n = c["ref_rows"]
-            side_w = n // hh if n % hh == 0 else n
-            idx = torch.arange(n)
-            pos.append(torch.stack([torch.full((n,), -1.0 - r), (idx // side_w).float(), (idx % side_w).float()], 1))
-        ti, hi, wi = torch.meshgrid(torch.arange(t), torch.arange(hh), torch.arange(ww), indexing="ij")
-        pos.append(torch.stack([ti.flatten(), hi.flatten(), wi.flatten()], 1).float())
-        P = torch.cat(pos, 0).to(dev)
-        inv = 1.0 / (10000.0 ** (torch.arange(16, device=dev, dtype=torch.float32) * 2 / 32))
-        ang = (P[:, :, None] * inv[None, None, :]).reshape(P.shape[0], 48)
-        return ang.cos().to(torch.bfloat16).contiguous(), ang.sin().to(torch.bfloat16).contiguous()
+        pos = h3.packed_positions(c["text"], [c["ref_hw"]] * c["refs"], t, 2 * hh, 2 * ww)
+        assert pos.shape[0] == c["S"]
+        inv = (1.0 / (10000.0 ** (np.arange(16, dtype=np.float64) * 2 / 32))).astype(np.float32)
+        return h3.build_rope(pos, torch.from_numpy(inv).to(dev))
 
     @staticmethod
     def _rowmap(c, i, dev):

@@ -415,6 +415,24 @@ int wx_f32_to_bf16(wx_ctx* ctx, const float* x, int64_t n, void* y);
  * negated velocity of H3DiT.forward (:1188): x[i] += (-v[i]) * dsigma */
 int wx_euler_update(wx_ctx* ctx, float* x, const float* v, int64_t n, float dsigma);
 
+/* ---------------------------------------------- RoPE tables (per generation) */
+/* axisFromSqrtArea (H3Layout.swift:188-194): n = dim/patch coordinates
+ * (i*ratio/n + (1-ratio)/2)*32, ratio = dim/sqrt_area, written to out (cap
+ * values); returns n (out NULL: only n) or a negative status. */
+int wx_axis_from_sqrt_area(uint32_t dim, uint32_t patch, double sqrt_area, double* out, int cap);
+/* videoTSpan (H3Layout.swift:197-200): 5/3 * [1,4,4,4,4][k % 5] */
+double wx_video_t_span(int k);
+/* videoTGrid (H3Layout.swift:202-210): out[i] = origin + sum_{j<i} span(j) */
+int wx_video_t_grid(uint32_t n, double origin, double* out);
+/* writeFrameGrid (H3Layout.swift:683-694): rows [row, row + nh*nw) of pos [S,3]
+ * (host doubles) get (t, h_axis[a], w_axis[b]), b fastest. */
+int wx_write_frame_grid(double* pos, int64_t row, double t, const double* h_axis, int nh, const double* w_axis,
+                        int nw);
+/* buildRope (H3Layout.swift:725-740): pos [S,3] fp32 and inv_freq [nf] fp32 on
+ * the device -> cos_t / sin_t [S, 3*nf] bf16, column a*nf + f = pos[s][a]*inv[f]. */
+int wx_build_rope(wx_ctx* ctx, const float* pos, int64_t S, const float* inv_freq, int nf, void* cos_t,
+                  void* sin_t);
+
 /* ------------------------------------------------ conditioning (per generation) */
 /* Dense MfLinear (H3Common.swift:304-308, 361-366): w [k, n] bf16 stored
  * pre-transposed; y = bf16(bf16(x w) + bias). */

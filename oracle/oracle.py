@@ -437,3 +437,32 @@ def refine_text(text, cfg, condition_proj=None, blocks=(), final_norm=None, cp_l
     for b in blocks:
         h = refiner_block_forward(h, b, cfg)
     return rms_norm(h, final_norm, cfg["eps"]) if final_norm is not None else h
+
+
+# ---------------------------------------------------------------- RoPE and positions
+def axis_from_sqrt_area(dim: int, patch: int, sqrt_area: float) -> np.ndarray:
+    """axisFromSqrtArea (H3Layout.swift:188-194), float64."""
+    n = dim // patch
+    ratio = float(dim) / sqrt_area
+    step = ratio / n
+    start = (1.0 - ratio) / 2.0
+    return np.array([(i * step + start) * 32.0 for i in range(n)], dtype=np.float64)
+
+
+def video_t_grid(n: int, origin: float) -> np.ndarray:
+    """videoTGrid (H3Layout.swift:202-210) with videoTSpan = 5/3 * [1,4,4,4,4][k % 5]."""
+    out, acc = [], float(origin)
+    for i in range(n):
+        out.append(acc)
+        acc += (5.0 / 3.0) * (1, 4, 4, 4, 4)[i % 5]
+    return np.array(out, dtype=np.float64)
+
+
+def build_rope(pos: np.ndarray, inv_freq: np.ndarray):
+    """buildRope (H3Layout.swift:725-740): fp32 angles pos*inv, cos/sin evaluated in float64
+    and rounded to fp32, then to bf16."""
+    p = np.asarray(pos, dtype=np.float32)
+    inv = np.asarray(inv_freq, dtype=np.float32)
+    ang = (p[:, :, None] * inv[None, None, :]).astype(np.float32).reshape(p.shape[0], -1)
+    a64 = ang.astype(np.float64)
+    return f32_to_bf16(np.cos(a64).astype(np.float32)), f32_to_bf16(np.sin(a64).astype(np.float32))

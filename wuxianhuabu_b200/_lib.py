@@ -166,6 +166,11 @@ _SIGS = {
     "wx_bf16_to_f32": (_i32, [_vp, _vp, _i64, _vp]),
     "wx_f32_to_bf16": (_i32, [_vp, _vp, _i64, _vp]),
     "wx_euler_update": (_i32, [_vp, _vp, _vp, _i64, _f32]),
+    "wx_axis_from_sqrt_area": (_i32, [_u32, _u32, _f64, _vp, _i32]),
+    "wx_video_t_span": (_f64, [_i32]),
+    "wx_video_t_grid": (_i32, [_u32, _f64, _vp]),
+    "wx_write_frame_grid": (_i32, [_vp, _i64, _f64, _vp, _i32, _vp, _i32]),
+    "wx_build_rope": (_i32, [_vp, _vp, _i64, _vp, _i32, _vp, _vp]),
     "wx_linear_bf16": (_i32, [_vp, _vp, _i64, C.POINTER(DenseBf16), _vp]),
     "wx_time_embed": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _vp]),
     "wx_adaln_lut_coeffs": (_i32, [_vp, _vp, _i32, _vp, _i64, _i32, _vp]),

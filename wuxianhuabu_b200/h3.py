@@ -37,6 +37,7 @@ __all__ = [
     "EPI_NONE", "EPI_GELU", "EPI_GATE_RESID", "EPI_SWIGLU",
     "DenseLinear", "H3TimeEmbedder", "H3AdalnLUT", "H3AdalnW", "H3AdalnTables", "precompute_adaln",
     "H3TextRefiner", "rms_norm", "load_refiner_block", "load_text_refiner", "load_time_embedder", "load_adaln",
+    "axis_from_sqrt_area", "video_t_span", "video_t_grid", "write_frame_grid", "packed_positions", "build_rope",
 ]
 
 
@@ -572,6 +573,80 @@ class H3DiT:
         if attn_bcast is not None and refresh and sigma is not None:
             attn_bcast.cached_sigma = sigma
         return latents
+
+
+# ------------------------------------------------------------------- RoPE and positions
+def axis_from_sqrt_area(dim: int, patch: int, sqrt_area: float) -> list[float]:
+    """axisFromSqrtArea (H3Layout.swift:188-194)."""
+    lib = _lib.load()
+    n = lib.wx_axis_from_sqrt_area(dim, patch, float(sqrt_area), None, 0)
+    check(min(n, 0))
+    out = (C.c_double * max(n, 1))()
+    check(min(lib.wx_axis_from_sqrt_area(dim, patch, float(sqrt_area), out, n), 0))
+    return list(out)[:n]
+
+
+def video_t_span(k: int) -> float:
+    """videoTSpan (H3Layout.swift:197-200)."""
+    return float(_lib.load().wx_video_t_span(k))
+
+
+def video_t_grid(n: int, origin: float) -> list[float]:
+    """videoTGrid (H3Layout.swift:202-210)."""
+    out = (C.c_double * max(n, 1))()
+    check(_lib.load().wx_video_t_grid(n, float(origin), out))
+    return list(out)[:n]
+
+
+def write_frame_grid(pos: np.ndarray, row: int, t: float, h_axis: Sequence[float], w_axis: Sequence[float]) -> None:
+    """writeFrameGrid (H3Layout.swift:683-694) into pos [S, 3] float64 (in place)."""
+    if pos.dtype != np.float64 or not pos.flags.c_contiguous:
+        raise WxError(_lib.WX_ERR_INVALID, "positions must be a C-contiguous float64 [S, 3] array")
+    ha = (C.c_double * max(len(h_axis), 1))(*h_axis)
+    wa = (C.c_double * max(len(w_axis), 1))(*w_axis)
+    if row + len(h_axis) * len(w_axis) > pos.shape[0]:
+        raise WxError(_lib.WX_ERR_INVALID, "frame grid runs past the end of the positions")
+    check(_lib.load().wx_write_frame_grid(pos.ctypes.data, row, float(t), ha, len(h_axis), wa, len(w_axis)))
+
+
+def packed_positions(text_len: int, ref_images: Sequence[tuple], latent_t: int, latent_h: int,
+                     latent_w: int) -> np.ndarray:
+    """positionIds of PackedLayout (H3Layout.swift:336-650) for a layout of text, reference
+    images (ref2va image blocks) and the target video, without audio, keyframes or
+    continuation rows: text rows t = 0..L-1 (:409-411); each image block a frame grid at
+    the cursor, cursor += 1 (:524-537); the target video's frames at videoTGrid(latent_t,
+    cursor) (:638-643). ref_images: (latent_h, latent_w) per image. Returns [S, 3] float64."""
+    def grid(lh, lw):
+        area = math.sqrt(float(lh) * float(lw))
+        return axis_from_sqrt_area(lh, 2, area), axis_from_sqrt_area(lw, 2, area)
+    grids = [grid(h, w) for h, w in ref_images]
+    vh, vw = grid(latent_h, latent_w)
+    frame_rows = len(vh) * len(vw)
+    S = text_len + sum(len(a) * len(b) for a, b in grids) + latent_t * frame_rows
+    pos = np.zeros((S, 3), dtype=np.float64)
+    pos[:text_len, 0] = np.arange(text_len, dtype=np.float64)
+    row, cursor = text_len, float(text_len)
+    for ha, wa in grids:
+        write_frame_grid(pos, row, cursor, ha, wa)
+        row += len(ha) * len(wa)
+        cursor += 1.0
+    for f, tv in enumerate(video_t_grid(latent_t, cursor)):
+        write_frame_grid(pos, row + f * frame_rows, tv, vh, vw)
+    return pos
+
+
+def build_rope(positions: np.ndarray, inv_freq: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """buildRope (H3Layout.swift:725-740): positions [S, 3] (host, cast to fp32 as the reference
+    does) and inv_freq [nf] fp32 on the GPU -> cos, sin [S, 3*nf] bf16."""
+    if not inv_freq.is_cuda or inv_freq.dtype != torch.float32:
+        raise WxError(_lib.WX_ERR_INVALID, "inv_freq must be a CUDA fp32 tensor")
+    dev = inv_freq.device
+    pos = torch.from_numpy(np.ascontiguousarray(positions, dtype=np.float32)).to(dev)
+    S, nf = pos.shape[0], inv_freq.numel()
+    cos = torch.empty((S, 3 * nf), dtype=torch.bfloat16, device=dev)
+    sin = torch.empty_like(cos)
+    context(dev.index).call("wx_build_rope", _p(pos), S, _p(inv_freq.contiguous()), nf, _p(cos), _p(sin))
+    return cos, sin
 
 
 # ------------------------------------------------------------ conditioning (per generation)
