@@ -346,6 +346,12 @@ int wx_ctx_init_comm(wx_ctx* ctx, int nranks, int rank, const void* id128);
 int wx_ctx_comm_check(wx_ctx* ctx);
 /* aborts the communicator (pending collectives return); the context keeps working on one GPU */
 int wx_ctx_comm_abort(wx_ctx* ctx);
+/* exchange path of the sequence-parallel block: 1 = NVLink peer memory (the
+ * QK-norm/RoPE kernel and the attention kernels store straight into the other
+ * ranks' buffers, opened through CUDA IPC; WX_SP_P2P=0 turns it off), 0 = NCCL
+ * all-to-alls, -1 = not decided yet (decided collectively at the first refreshed
+ * block of a group) */
+int wx_ctx_sp_exchange(wx_ctx* ctx);
 int64_t wx_dit_block_sp_scratch_bytes(const wx_dit_config* cfg, int64_t S, int P);
 /* wx_dit_block_forward on this rank's rows of an S-row sequence (the context's
  * communicator decides P and the rank): h/rowmap/cos/sin/pab_slot are the

@@ -1,6 +1,8 @@
-"""Ulysses sequence parallelism on 2 GPUs: wx_dit_block_forward_sp over NCCL
-against the single-GPU block on the same inputs (dense, SOL and top-k
-attention; refresh and PAB reuse). Skipped on boxes with fewer than 2 GPUs."""
+"""Ulysses sequence parallelism on 2 GPUs: wx_dit_block_forward_sp against the
+single-GPU block on the same inputs (dense, SOL and top-k attention; refresh,
+refresh, PAB reuse in sequence), with the exchange over NVLink peer memory
+(default) and over NCCL all-to-alls (WX_SP_P2P=0). Skipped on boxes with fewer
+than 2 GPUs."""
 import datetime
 import os
 import socket
@@ -27,10 +29,11 @@ def _free_port() -> int:
     return p
 
 
-def _worker(rank, world, port, sparse_name, out_q):
+def _worker(rank, world, port, sparse_name, p2p, out_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    os.environ["WX_SP_P2P"] = p2p
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -41,8 +44,8 @@ def _worker(rank, world, port, sparse_name, out_q):
         from tests._util import cosine, f32, max_rel_err, to_np_bf16, to_torch_bf16
         from tests.test_gpu_block import gpu_block, make_block
         from wuxianhuabu_b200 import h3
-        hidden, heads, ffn, rot, eps, g = 256, 2, 512, 96, 1e-6, 40
-        S = 512
+        hidden, heads, ffn, rot, eps, g = 256, 4, 512, 96, 1e-6, 40
+        S = 1000  # 500 rows per rank: the rank boundary falls inside a 128-row query tile
         w, mods, h, cos, sin, rowmap = make_block(9, hidden, heads, ffn, 0, S, rot)
         sparse = {"dense": None, "sol": dict(tau=0.4), "topk": dict(block=128, topk_ratio=0.25, tail=False)}[sparse_name]
         spec = None if sparse is None else h3.H3SolAttnConfig(**sparse).spec(g)
@@ -50,12 +53,14 @@ def _worker(rank, world, port, sparse_name, out_q):
         md = [to_torch_bf16(m, dev) for m in mods]
         rm = torch.from_numpy(rowmap.view(np.int32)).to(dev)
         c, s = to_torch_bf16(cos, dev), to_torch_bf16(sin, dev)
+        schedule = [True, True, False]  # refresh, refresh, PAB reuse
         # single-GPU reference on this device (before the communicator exists)
         ref = to_torch_bf16(h, dev)
         slot_ref = torch.empty((S, hidden), dtype=torch.bfloat16, device=dev)
-        blk.block_forward(0, ref, md, rm, c, s, spec, pab_slot=slot_ref, refresh=True)
-        ref2 = ref.clone()
-        blk.block_forward(0, ref2, md, rm, c, s, spec, pab_slot=slot_ref, refresh=False)
+        refs = []
+        for refresh in schedule:
+            blk.block_forward(0, ref, md, rm, c, s, spec, pab_slot=slot_ref, refresh=refresh)
+            refs.append(ref.clone())
         torch.cuda.synchronize()
 
         def bcast(obj):
@@ -68,29 +73,30 @@ def _worker(rank, world, port, sparse_name, out_q):
         hl = to_torch_bf16(h, dev)[r0:r0 + rows].contiguous()
         slot = torch.empty((rows, hidden), dtype=torch.bfloat16, device=dev)
         blk2 = gpu_block(w, hidden, heads, ffn, 0, rot, eps)
-        blk2.block_forward(0, hl, md, rm[r0:r0 + rows].contiguous(), c[r0:r0 + rows].contiguous(),
-                           s[r0:r0 + rows].contiguous(), spec, pab_slot=slot, refresh=True, S_total=S)
-        hl2 = hl.clone()
-        blk2.block_forward(0, hl2, md, rm[r0:r0 + rows].contiguous(), c[r0:r0 + rows].contiguous(),
-                           s[r0:r0 + rows].contiguous(), spec, pab_slot=slot, refresh=False, S_total=S)
-        torch.cuda.synchronize()
+        res = []
+        for refresh, want in zip(schedule, refs):
+            blk2.block_forward(0, hl, md, rm[r0:r0 + rows].contiguous(), c[r0:r0 + rows].contiguous(),
+                               s[r0:r0 + rows].contiguous(), spec, pab_slot=slot, refresh=refresh, S_total=S)
+            torch.cuda.synchronize()
+            got, wnt = f32(to_np_bf16(hl)), f32(to_np_bf16(want[r0:r0 + rows]))
+            res += [max_rel_err(got, wnt), cosine(got, wnt)]
         h3.context(rank).check_device()
-        got, want = f32(to_np_bf16(hl)), f32(to_np_bf16(ref[r0:r0 + rows]))
-        got2, want2 = f32(to_np_bf16(hl2)), f32(to_np_bf16(ref2[r0:r0 + rows]))
-        out_q.put((rank, max_rel_err(got, want), cosine(got, want), max_rel_err(got2, want2), cosine(got2, want2)))
+        path = h3.context(rank).sp_exchange()
+        out_q.put((rank, path, *res))
     finally:
         dist.barrier()
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("p2p", ["1", "0"])
 @pytest.mark.parametrize("sparse_name", ["dense", "sol", "topk"])
-def test_ulysses_block_matches_single_gpu(sparse_name):
+def test_ulysses_block_matches_single_gpu(sparse_name, p2p):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, sparse_name, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, sparse_name, p2p, q)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -103,7 +109,9 @@ def test_ulysses_block_matches_single_gpu(sparse_name):
     while not q.empty():
         res.append(q.get())
     assert len(res) == 2
-    for rank, e1, c1, e2, c2 in res:
+    for rank, path, *errs in res:
+        # the exchange path asked for was taken (1 peer memory, 0 all-to-alls)
+        assert path == int(p2p), (rank, path)
         # same kernels on the same rows: only the attention split differs
-        assert e1 <= 2e-2 and c1 >= 0.999, (rank, e1, c1)
-        assert e2 <= 2e-2 and c2 >= 0.999, (rank, e2, c2)
+        for i in range(0, len(errs), 2):
+            assert errs[i] <= 2e-2 and errs[i + 1] >= 0.999, (rank, i // 2, errs[i], errs[i + 1])

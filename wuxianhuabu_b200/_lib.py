@@ -157,6 +157,7 @@ _SIGS = {
     "wx_ctx_init_comm": (_i32, [_vp, _i32, _i32, _vp]),
     "wx_ctx_comm_check": (_i32, [_vp]),
     "wx_ctx_comm_abort": (_i32, [_vp]),
+    "wx_ctx_sp_exchange": (_i32, [_vp]),
     "wx_dit_block_sp_scratch_bytes": (_i64, [C.POINTER(DitConfig), _i64, _i32]),
     "wx_dit_block_forward_sp": (_i32, [_vp, C.POINTER(DitConfig), C.POINTER(BlockWeights), C.POINTER(BlockMods),
                                        _vp, _vp, _i64, _vp, _vp, C.POINTER(SparseSpec), _vp, _i32, _vp]),

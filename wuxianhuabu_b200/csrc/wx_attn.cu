@@ -646,9 +646,14 @@ static int attn_pairs() {
   return v;
 }
 
+bool attn_peer_path_ok() {
+  return attn_kernel_variant() == 2 && attn_duo() && flash_pair_regs_ok(exp_poly_pairs());
+}
+
 static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, const AttnGeom& a,
                      const wx_sparse_spec* spec, float scale, const uint8_t* sel, const __nv_bfloat16* cm,
-                     const __nv_bfloat16* vsum, const float* lens, uint8_t* base, void* out, int64_t os) {
+                     const __nv_bfloat16* vsum, const float* lens, uint8_t* base, void* out, int64_t os,
+                     const SpPeerOut* po = nullptr) {
   Carve c;
   const size_t hnb = (size_t)a.H * a.nb;
   float* tT = reinterpret_cast<float*>(base + c.take(hnb * a.hd * 4));
@@ -707,7 +712,7 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
     if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
     attr = true;
   }
-  AttnParams p;
+  AttnParams p{};
   p.items = items;
   p.entries = entries;
   p.tailT = tail ? tT : nullptr;
@@ -719,6 +724,23 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = os;
   p.err = ctx->dev_err;
+  if (po) {
+    static_assert(kSpMaxPeers == kMaxPeers, "peer table sizes");
+    if (!attn_peer_path_ok() || po->P < 1 || po->P > kMaxPeers || po->rows <= 0)
+      return set_error(ctx, WX_ERR_UNSUPPORTED, "attention to peer memory needs the paired / duo kernels");
+    const int64_t n_rest = n_items - 2 * n_pairs;
+    for (int r = 0; r < kMaxPeers; ++r) {
+      p.out_peer[r] = r < po->P ? static_cast<__nv_bfloat16*>(po->out_peer[r]) : nullptr;
+      p.sig.flags[r] = r < po->P ? po->flags[r] : nullptr;
+    }
+    p.peer_rows = po->rows;
+    p.peer_col = po->col;
+    p.sig.counter = po->counter;
+    p.sig.total = (int)(n_pairs + (n_rest + 1) / 2);  // CTAs of the paired and the duo launch
+    p.sig.P = po->P;
+    p.sig.rank = po->rank;
+    p.sig.epoch = po->epoch;
+  }
 
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
   ProfScope prof(ctx, kProfAttn);
@@ -822,6 +844,12 @@ size_t attention_scratch_bytes(int64_t S, int H, int hd, const wx_sparse_spec* s
 // routing + flash with caller scratch (used by the block forward)
 int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
                            int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os, void* scratch) {
+  return attention_with_scratch_peer(ctx, q, k, v, rs, S, H, hd, spec, scale, out, os, scratch, nullptr);
+}
+
+int attention_with_scratch_peer(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S,
+                                int H, int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os,
+                                void* scratch, const SpPeerOut* po) {
   AttnGeom a;
   int st = geom_from(ctx, S, H, hd, spec, a);
   if (st) return st;
@@ -835,7 +863,7 @@ int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void
     if (st) return st;
     off = (route_bytes(a, spec->mode) + 255) & ~size_t(255);
   }
-  return run_flash(ctx, q, k, v, rs, a, spec, scale, sel, cm, vsum, lens, base + off, out, os);
+  return run_flash(ctx, q, k, v, rs, a, spec, scale, sel, cm, vsum, lens, base + off, out, os, po);
 }
 
 }  // namespace wx

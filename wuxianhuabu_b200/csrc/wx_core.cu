@@ -204,6 +204,8 @@ int wx_ctx_destroy(wx_ctx* ctx) {
   if (!ctx) return WX_OK;
   cudaSetDevice(ctx->device);
   cudaDeviceSynchronize();
+  sp_p2p_release(ctx);
+  if (ctx->p2p_counters) cudaFree(ctx->p2p_counters);
   sp_destroy_comm(ctx);
   for (auto& r : ctx->prof_recs) {
     cudaEventDestroy(r.a);

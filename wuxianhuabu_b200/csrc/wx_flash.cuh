@@ -35,7 +35,26 @@ struct AttnParams {
   __nv_bfloat16* out;
   int64_t out_stride;
   int* err;
+  // Sequence parallelism over peer memory (paired / duo kernels): query row s is
+  // written to rank s / peer_rows at out_peer[r] + (s - r*peer_rows)*out_stride +
+  // peer_col + head*128; out_peer[0] == nullptr writes to `out`. sig.counter !=
+  // nullptr: the last CTA of the call signals every rank (peer_signal_cta_done).
+  __nv_bfloat16* out_peer[kMaxPeers];
+  int64_t peer_rows;
+  int peer_col;
+  PeerSignal sig;
 };
+
+// destination of output row `row` (query row of the sequence) of head `head`
+__device__ __forceinline__ __nv_bfloat16* attn_out_row(const AttnParams& p, int64_t row, int head) {
+  if (p.out_peer[0] == nullptr) return p.out + row * p.out_stride + head * 128;
+  const int64_t owner = row / p.peer_rows;
+  __nv_bfloat16* base = p.out_peer[0];
+#pragma unroll
+  for (int r = 1; r < kMaxPeers; ++r)
+    if (owner == r) base = p.out_peer[r];
+  return base + (row - owner * p.peer_rows) * p.out_stride + p.peer_col + head * 128;
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;

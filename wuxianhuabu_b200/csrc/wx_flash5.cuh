@@ -405,7 +405,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
     }
     const float inv = lt > 0.f ? 1.0f / lt : 0.f;
     const bool row_ok = ok && present && r < it.q_rows;
-    __nv_bfloat16* orow = p.out + (int64_t)(it.q_start + r) * p.out_stride + it.head * 128;
+    __nv_bfloat16* orow = attn_out_row(p, (int64_t)(it.q_start + r), it.head);
 #pragma unroll 1
     for (int c = 0; c < 4 && present; ++c) {
       float o[32];
@@ -430,6 +430,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
     }
   }
 
+  if (p.sig.counter) peer_signal_cta_done(p.sig);  // rows written to other GPUs: tell them
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

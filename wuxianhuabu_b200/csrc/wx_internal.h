@@ -35,6 +35,15 @@ struct wx_ctx {
   // stream (forked and joined with the two events); created on first use
   cudaStream_t aux = nullptr;
   cudaEvent_t fork = nullptr, join = nullptr;
+  // sequence parallelism over NVLink peer memory (wx_sp.cu): this rank's exchange
+  // buffer (flags | attention rows | full-sequence q|k|v of its heads), exported by
+  // CUDA IPC and opened by every other rank; the peers' buffers; two CTA counters
+  int p2p_state = -1;  // -1 not decided, 0 off (NCCL all-to-alls), 1 on
+  void* p2p_buf = nullptr;
+  size_t p2p_bytes = 0;
+  void* p2p_peer[8] = {};
+  int* p2p_counters = nullptr;
+  uint32_t p2p_epoch = 0;
 };
 
 namespace wx {
@@ -75,6 +84,8 @@ int make_tmap_bf16_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t 
 
 // releases the NCCL communicator of a context (no-op without one)
 void sp_destroy_comm(wx_ctx* ctx);
+// releases the peer exchange buffers of a context (closes the peers' mappings first)
+void sp_p2p_release(wx_ctx* ctx);
 
 // checks the last launch(es) and counts `n` kernel launches on the context
 int launch_status(wx_ctx* ctx, const char* what, int n = 1);
@@ -110,6 +121,27 @@ int qlinear_lora_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda
                               const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw, void* wd, void* t,
                               void* swiglu_tmp);
 bool lora_pack_ok(const wx_lora_pack* l, const wx_qweight* w);
+
+// Attention output delivered straight into other ranks' memory (sequence
+// parallelism): query row s goes to rank s / rows at out_peer[r] + (s % rows) *
+// out_stride + col + head*128, and the last CTA stores `epoch` into flags[r][rank]
+// of every rank r.
+constexpr int kSpMaxPeers = 8;
+struct SpPeerOut {
+  void* out_peer[kSpMaxPeers];
+  int64_t rows;
+  int col;
+  int* counter;
+  uint32_t* flags[kSpMaxPeers];
+  int P, rank;
+  uint32_t epoch;
+};
+// true when the attention call takes the paired / duo kernels, the only ones that
+// write to peers
+bool attn_peer_path_ok();
+int attention_with_scratch_peer(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S,
+                                int H, int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os,
+                                void* scratch, const SpPeerOut* po);
 bool lora_packs_ok(const wx_dit_config* cfg, const wx_block_weights* w);
 
 }  // namespace wx

@@ -21,6 +21,7 @@ enum DevErr : int {
   kDevTimeoutSoftmax = 4,
   kDevTimeoutOther = 5,
   kDevBadArgs = 6,
+  kDevTimeoutPeer = 7,  // another rank's signal did not arrive (sequence parallelism)
 };
 
 static constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
@@ -262,6 +263,48 @@ __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 __device__ __forceinline__ float round_bf16(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// ------------------------------------------------------- peer (NVLink) signalling
+// A kernel that writes its results into other GPUs' memory (peer pointers opened
+// through CUDA IPC) tells each of them when all of its CTAs are done: every CTA
+// fences its stores at system scope and counts itself on a local counter; the
+// last CTA resets the counter and stores `epoch` into flags[r][rank] of every
+// rank r with release semantics at system scope. The receiving rank waits for
+// all flags with acquire loads (sp_wait_flags_kernel) before it reads.
+constexpr int kMaxPeers = 8;
+struct PeerSignal {
+  int* counter;                   // local; 0 between uses (nullptr = no signalling)
+  int total;                      // CTAs that count, over every kernel of the call
+  uint32_t* flags[kMaxPeers];     // flags[r] = this exchange's flag array [P] in rank r's memory
+  int P, rank;
+  uint32_t epoch;
+};
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Called by every thread of the CTA, after its last store (block-uniform).
+__device__ __forceinline__ void peer_signal_cta_done(const PeerSignal& s) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(s.counter, 1);
+    if (prev == s.total - 1) {
+      atomicExch(s.counter, 0);
+      __threadfence_system();
+#pragma unroll
+      for (int r = 0; r < kMaxPeers; ++r)
+        if (r < s.P) st_release_sys_u32(s.flags[r] + s.rank, s.epoch);
+    }
+  }
 }
 
 }  // namespace wx

@@ -99,65 +99,100 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 // warp keeps ~2.5 KB in flight instead of one 256-B row, and the rotation
 // partner (j +- rot/2) comes from lane +- rot/8 by shuffle.
 constexpr int kRopeHeads = 8;
+
+// where row (s, part, head h) of the result goes
+struct RopeLocalDst {  // the same packed layout, in place or into `out`
+  __nv_bfloat16* out;
+  int64_t out_stride, part_off;
+  __device__ __forceinline__ __nv_bfloat16* operator()(int64_t s, int part, int h) const {
+    return out + s * out_stride + part * part_off + (int64_t)h * 128;
+  }
+};
+struct RopePeerDst {  // sequence parallelism: the exchange buffer of the rank owning head h,
+                      // full-sequence row row0 + s, layout [S][3][Hl][128]
+  __nv_bfloat16* base[kMaxPeers];
+  int64_t row0;
+  int Hl;
+  __device__ __forceinline__ __nv_bfloat16* operator()(int64_t s, int part, int h) const {
+    const int r = h / Hl;
+    __nv_bfloat16* b = base[0];
+#pragma unroll
+    for (int i = 1; i < kMaxPeers; ++i)
+      if (r == i) b = base[i];
+    return b + ((row0 + s) * 3 + part) * (int64_t)Hl * 128 + (int64_t)(h - r * Hl) * 128;
+  }
+};
+
+// PEER: nparts = 3 and the third part (v) is copied unchanged; every row goes to the
+// owner of its head in another GPU's memory, and the last CTA signals the ranks.
+template <class Dst, bool PEER>
 __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
-    const __nv_bfloat16* x, int64_t x_stride, __nv_bfloat16* out,
-    int64_t out_stride, int64_t part_off, int nparts, int64_t S, int H, int n_groups,
+    const __nv_bfloat16* x, int64_t x_stride, Dst dst, int64_t part_off, int nparts, int64_t S, int H, int n_groups,
     const __nv_bfloat16* __restrict__ w0, const __nv_bfloat16* __restrict__ w1,
-    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int rot, float eps) {
+    const __nv_bfloat16* __restrict__ cos_t, const __nv_bfloat16* __restrict__ sin_t, int rot, float eps,
+    PeerSignal sig) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t task = (int64_t)blockIdx.x * 8 + warp;
-  if (task >= S * nparts * n_groups) return;
-  const int g = (int)(task % n_groups);
-  const int part = (int)((task / n_groups) % nparts);
-  const int64_t s = task / ((int64_t)n_groups * nparts);
-  const int h0 = g * kRopeHeads;
-  const int nh = min(kRopeHeads, H - h0);
-  const int64_t xoff = s * x_stride + part * part_off + (int64_t)h0 * 128 + lane * 4;
-  const int64_t ooff = s * out_stride + part * part_off + (int64_t)h0 * 128 + lane * 4;
-  uint2 raw[kRopeHeads];
+  if (task < S * nparts * n_groups) {
+    const int g = (int)(task % n_groups);
+    const int part = (int)((task / n_groups) % nparts);
+    const int64_t s = task / ((int64_t)n_groups * nparts);
+    const int h0 = g * kRopeHeads;
+    const int nh = min(kRopeHeads, H - h0);
+    const int64_t xoff = s * x_stride + part * part_off + (int64_t)h0 * 128 + lane * 4;
+    uint2 raw[kRopeHeads];
 #pragma unroll
-  for (int i = 0; i < kRopeHeads; ++i)
-    if (i < nh) raw[i] = *reinterpret_cast<const uint2*>(x + xoff + i * 128);  // may alias out (in place)
-  const int rh = rot >> 1;
-  const int j0 = lane * 4;
-  const bool rotated = j0 < rot;
-  const bool first = j0 < rh;
-  uint2 cr = make_uint2(0, 0), sr = make_uint2(0, 0);
-  if (rotated) {
-    const int64_t t = s * rh + (first ? j0 : j0 - rh);
-    cr = __ldg(reinterpret_cast<const uint2*>(cos_t + t));
-    sr = __ldg(reinterpret_cast<const uint2*>(sin_t + t));
-  }
-  const uint2 wr = __ldg(reinterpret_cast<const uint2*>((part == 0 ? w0 : w1) + j0));
-  const float wv[4] = {bf16_lo(wr.x), bf16_hi(wr.x), bf16_lo(wr.y), bf16_hi(wr.y)};
-  const float c[4] = {bf16_lo(cr.x), bf16_hi(cr.x), bf16_lo(cr.y), bf16_hi(cr.y)};
-  const float sn[4] = {bf16_lo(sr.x), bf16_hi(sr.x), bf16_lo(sr.y), bf16_hi(sr.y)};
-  const int partner = first ? lane + (rh >> 2) : lane - (rh >> 2);
-  const int src = rotated ? partner : lane;
+    for (int i = 0; i < kRopeHeads; ++i)
+      if (i < nh) raw[i] = *reinterpret_cast<const uint2*>(x + xoff + i * 128);  // may alias the output (in place)
+    if (PEER && part == 2) {
 #pragma unroll
-  for (int i = 0; i < kRopeHeads; ++i) {
-    if (i >= nh) break;
-    const float xv[4] = {bf16_lo(raw[i].x), bf16_hi(raw[i].x), bf16_lo(raw[i].y), bf16_hi(raw[i].y)};
-    float ss = 0.f;
+      for (int i = 0; i < kRopeHeads; ++i)
+        if (i < nh) *reinterpret_cast<uint2*>(dst(s, 2, h0 + i) + lane * 4) = raw[i];
+    } else {
+      const int rh = rot >> 1;
+      const int j0 = lane * 4;
+      const bool rotated = j0 < rot;
+      const bool first = j0 < rh;
+      uint2 cr = make_uint2(0, 0), sr = make_uint2(0, 0);
+      if (rotated) {
+        const int64_t t = s * rh + (first ? j0 : j0 - rh);
+        cr = __ldg(reinterpret_cast<const uint2*>(cos_t + t));
+        sr = __ldg(reinterpret_cast<const uint2*>(sin_t + t));
+      }
+      const uint2 wr = __ldg(reinterpret_cast<const uint2*>((part == 0 ? w0 : w1) + j0));
+      const float wv[4] = {bf16_lo(wr.x), bf16_hi(wr.x), bf16_lo(wr.y), bf16_hi(wr.y)};
+      const float c[4] = {bf16_lo(cr.x), bf16_hi(cr.x), bf16_lo(cr.y), bf16_hi(cr.y)};
+      const float sn[4] = {bf16_lo(sr.x), bf16_hi(sr.x), bf16_lo(sr.y), bf16_hi(sr.y)};
+      const int partner = first ? lane + (rh >> 2) : lane - (rh >> 2);
+      const int src = rotated ? partner : lane;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) ss += xv[e] * xv[e];
-    ss = warp_sum(ss);
-    const float rstd = rsqrtf(ss / 128.f + eps);
-    float nv[4], o[4];
+      for (int i = 0; i < kRopeHeads; ++i) {
+        if (i >= nh) break;
+        const float xv[4] = {bf16_lo(raw[i].x), bf16_hi(raw[i].x), bf16_lo(raw[i].y), bf16_hi(raw[i].y)};
+        float ss = 0.f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) nv[e] = round_bf16(xv[e] * rstd * wv[e]);
+        for (int e = 0; e < 4; ++e) ss += xv[e] * xv[e];
+        ss = warp_sum(ss);
+        const float rstd = rsqrtf(ss / 128.f + eps);
+        float nv[4], o[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float pv = __shfl_sync(0xffffffffu, nv[e], src);
-      if (!rotated)
-        o[e] = nv[e];
-      else if (first)
-        o[e] = nv[e] * c[e] - pv * sn[e];
-      else
-        o[e] = nv[e] * c[e] + pv * sn[e];
+        for (int e = 0; e < 4; ++e) nv[e] = round_bf16(xv[e] * rstd * wv[e]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float pv = __shfl_sync(0xffffffffu, nv[e], src);
+          if (!rotated)
+            o[e] = nv[e];
+          else if (first)
+            o[e] = nv[e] * c[e] - pv * sn[e];
+          else
+            o[e] = nv[e] * c[e] + pv * sn[e];
+        }
+        *reinterpret_cast<uint2*>(dst(s, part, h0 + i) + lane * 4) =
+            make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+      }
     }
-    *reinterpret_cast<uint2*>(out + ooff + i * 128) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
   }
+  if constexpr (PEER) peer_signal_cta_done(sig);
 }
 
 // ----------------------------------------------------------------- K4
@@ -406,8 +441,9 @@ int launch_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, void* out,
   if (vec_ok) {
     const int n_groups = (H + kRopeHeads - 1) / kRopeHeads;
     const int64_t tasks = S * nparts * n_groups;
-    qk_norm_rope_vec_kernel<<<(unsigned)((tasks + 7) / 8), 256, 0, ctx->stream>>>(
-        X, x_stride, O, out_stride, part_off, nparts, S, H, n_groups, W0, W1, C, Sn, rot, eps);
+    qk_norm_rope_vec_kernel<RopeLocalDst, false><<<(unsigned)((tasks + 7) / 8), 256, 0, ctx->stream>>>(
+        X, x_stride, RopeLocalDst{O, out_stride, part_off}, part_off, nparts, S, H, n_groups, W0, W1, C, Sn, rot,
+        eps, PeerSignal{});
     return launch_status(ctx, "qk_norm_rope");
   }
   if (hd == 128)
@@ -417,6 +453,34 @@ int launch_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, void* out,
     qk_norm_rope_kernel<64><<<grid, 256, 0, ctx->stream>>>(X, x_stride, O, out_stride, part_off, nparts, S,
                                                             H, W0, W1, C, Sn, rot, eps);
   return launch_status(ctx, "qk_norm_rope");
+}
+
+bool qkv_to_peers_ok(int hd, int rot) { return hd == 128 && (rot >> 1) % 4 == 0; }
+
+// Sequence parallelism: QK-RMSNorm + RoPE of this rank's rows of the packed qkv
+// ([rows, 3*H*128]) and the copy of v, each head's row written into the exchange
+// buffer of the rank that owns the head (peers[r], layout [S][3][Hl][128], rows
+// row0 + s); the last CTA signals every rank through `sig` (sig.total is set here).
+int launch_qkv_to_peers(wx_ctx* ctx, const void* qkv, int64_t rows, int64_t row0, int H, int Hl,
+                        void* const* peers, int P, const void* w0, const void* w1, const void* cos_t,
+                        const void* sin_t, int rot, float eps, PeerSignal sig) {
+  if (!qkv_to_peers_ok(128, rot) || P < 1 || P > kMaxPeers || Hl * P != H)
+    return set_error(ctx, WX_ERR_UNSUPPORTED, "qkv to peers: head_dim 128, rot/2 %% 4 == 0, H = P*Hl");
+  RopePeerDst d{};
+  for (int r = 0; r < kMaxPeers; ++r) d.base[r] = r < P ? static_cast<__nv_bfloat16*>(peers[r]) : nullptr;
+  d.row0 = row0;
+  d.Hl = Hl;
+  const int64_t inner = (int64_t)H * 128;
+  const int n_groups = (H + kRopeHeads - 1) / kRopeHeads;
+  const int64_t tasks = rows * 3 * n_groups;
+  const unsigned grid = (unsigned)std::max<int64_t>(1, (tasks + 7) / 8);
+  sig.total = (int)grid;
+  ProfScope prof(ctx, kProfRow);
+  qk_norm_rope_vec_kernel<RopePeerDst, true><<<grid, 256, 0, ctx->stream>>>(
+      static_cast<const __nv_bfloat16*>(qkv), 3 * inner, d, inner, 3, rows, H, n_groups,
+      static_cast<const __nv_bfloat16*>(w0), static_cast<const __nv_bfloat16*>(w1),
+      static_cast<const __nv_bfloat16*>(cos_t), static_cast<const __nv_bfloat16*>(sin_t), rot, eps, sig);
+  return launch_status(ctx, "qkv_to_peers");
 }
 
 int launch_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w,

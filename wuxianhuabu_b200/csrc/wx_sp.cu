@@ -53,6 +53,7 @@ struct NcclApi {
   ncclResult_t (*GroupStart)() = nullptr;
   ncclResult_t (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(ncclResult_t) = nullptr;
+  ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
   bool ok = false;
 };
 
@@ -74,6 +75,7 @@ static NcclApi& nccl() {
     api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(sym("ncclGroupStart"));
     api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(sym("ncclGroupEnd"));
     api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(sym("ncclGetErrorString"));
+    api.AllGather = reinterpret_cast<decltype(api.AllGather)>(sym("ncclAllGather"));  // optional (peer setup)
     api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.CommAbort && api.CommGetAsyncError &&
              api.Send && api.Recv && api.GroupStart && api.GroupEnd && api.GetErrorString;
   });
@@ -134,6 +136,171 @@ __global__ void sp_unpack_out_kernel(const __nv_bfloat16* __restrict__ recv, int
     const uint4 v = *reinterpret_cast<const uint4*>(recv + (r * rows + row) * Hl * hd + c * 8);
     *reinterpret_cast<uint4*>(att + row * (int64_t)P * Hl * hd + r * Hl * hd + c * 8) = v;
   }
+}
+
+// ------------------------------------------------------ exchange over peer memory
+// Instead of the two all-to-alls, each rank writes its rows of q|k|v (after
+// QK-norm + RoPE, in the same kernel) straight into the exchange buffer of the
+// rank that owns each head, and the attention kernels write each output row
+// straight into the out-projection operand of the rank that owns the row; NVLink
+// carries the stores, no staging copies, no collective launches. Each rank's
+// buffer: flags of exchange 1 [8] | flags of exchange 2 [8] | attention rows
+// [rows, H*128] | q|k|v of its heads for the whole sequence [S, 3*Hl*128].
+int launch_qkv_to_peers(wx_ctx* ctx, const void* qkv, int64_t rows, int64_t row0, int H, int Hl,
+                        void* const* peers, int P, const void* w0, const void* w1, const void* cos_t,
+                        const void* sin_t, int rot, float eps, PeerSignal sig);
+bool qkv_to_peers_ok(int hd, int rot);
+
+constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // 10 s
+
+// waits (bounded) until every rank r has stored `epoch` (or later) into flags[r]
+__global__ void sp_wait_flags_kernel(const uint32_t* flags, int P, uint32_t epoch, int* err) {
+  const int r = threadIdx.x;
+  if (r >= P) return;
+  const uint64_t t0 = globaltimer_ns();
+  while ((int32_t)(ld_acquire_sys_u32(flags + r) - epoch) < 0) {
+    if (globaltimer_ns() - t0 > kPeerWaitLimitNs) {
+      set_dev_error(err, kDevTimeoutPeer);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+struct P2PLayout {
+  size_t flags1 = 0, flags2 = 64, att = 256, qkv = 0, total = 0;
+};
+
+static size_t al(size_t b);
+
+static P2PLayout p2p_layout(int64_t S, int64_t rows, int64_t inner, int Hl, int hd) {
+  P2PLayout L;
+  L.qkv = L.att + al((size_t)rows * inner * 2);
+  L.total = L.qkv + al((size_t)S * 3 * Hl * hd * 2);
+  return L;
+}
+
+static bool sp_p2p_env() {
+  static int v = [] {
+    const char* e = getenv("WX_SP_P2P");
+    return e ? atoi(e) : 1;
+  }();
+  return v != 0;
+}
+
+void sp_p2p_release(wx_ctx* ctx) {
+  if (!ctx) return;
+  if (ctx->p2p_buf) {
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->aux) cudaStreamSynchronize(ctx->aux);
+    for (int r = 0; r < kSpMaxPeers; ++r)
+      if (ctx->p2p_peer[r] && ctx->p2p_peer[r] != ctx->p2p_buf) cudaIpcCloseMemHandle(ctx->p2p_peer[r]);
+    cudaFree(ctx->p2p_buf);
+  }
+  for (int r = 0; r < kSpMaxPeers; ++r) ctx->p2p_peer[r] = nullptr;
+  ctx->p2p_buf = nullptr;
+  ctx->p2p_bytes = 0;
+  ctx->p2p_epoch = 0;
+}
+
+// one record per rank in the all-gather: the IPC handle and whether the rank can take part
+struct P2PRecord {
+  cudaIpcMemHandle_t handle;
+  int32_t ok;
+  int32_t pad[15];
+};
+
+// all-gather of one record per rank over the context's communicator (blocking)
+static int p2p_all_gather(wx_ctx* ctx, const P2PRecord& mine, P2PRecord* all) {
+  const int P = ctx->sp_size;
+  void* dev = nullptr;
+  WX_CUDA_TRY(ctx, cudaMalloc(&dev, sizeof(P2PRecord) * (P + 1)));
+  auto* d = static_cast<uint8_t*>(dev);
+  cudaError_t e = cudaMemcpyAsync(d, &mine, sizeof(P2PRecord), cudaMemcpyHostToDevice, ctx->stream);
+  ncclResult_t nr = ncclSuccess;
+  if (e == cudaSuccess)
+    nr = nccl().AllGather(d, d + sizeof(P2PRecord), sizeof(P2PRecord), ncclUint8,
+                          static_cast<ncclComm_t>(ctx->comm), ctx->stream);
+  if (e == cudaSuccess && nr == ncclSuccess)
+    e = cudaMemcpyAsync(all, d + sizeof(P2PRecord), sizeof(P2PRecord) * P, cudaMemcpyDeviceToHost, ctx->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  cudaFree(dev);
+  if (nr != ncclSuccess) return set_error(ctx, WX_ERR_CUDA, "peer setup all-gather: %s", nccl().GetErrorString(nr));
+  if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "peer setup: %s", cudaGetErrorString(e));
+  return WX_OK;
+}
+
+// Collective (every rank calls it at the same point with the same size): makes
+// sure the exchange buffers of `bytes` exist and are opened by every rank.
+// Returns 1 when the peer path is on, 0 when the ranks use the all-to-alls.
+static int p2p_ensure(wx_ctx* ctx, size_t bytes, int hd, int rot, int* status) {
+  *status = WX_OK;
+  if (ctx->p2p_state == 0) return 0;
+  if (ctx->p2p_state == 1 && ctx->p2p_bytes >= bytes) return 1;
+  const int P = ctx->sp_size, rank = ctx->sp_rank;
+  sp_p2p_release(ctx);
+  P2PRecord mine{};
+  mine.ok = sp_p2p_env() && nccl().AllGather && P <= kSpMaxPeers && attn_peer_path_ok() && qkv_to_peers_ok(hd, rot);
+  if (mine.ok && !ctx->p2p_counters) {
+    if (cudaMalloc(&ctx->p2p_counters, 2 * sizeof(int)) != cudaSuccess ||
+        cudaMemset(ctx->p2p_counters, 0, 2 * sizeof(int)) != cudaSuccess)
+      mine.ok = 0;
+  }
+  if (mine.ok) {
+    if (cudaMalloc(&ctx->p2p_buf, bytes) != cudaSuccess) {
+      ctx->p2p_buf = nullptr;
+      mine.ok = 0;
+    } else if (cudaMemset(ctx->p2p_buf, 0, bytes) != cudaSuccess ||
+               cudaIpcGetMemHandle(&mine.handle, ctx->p2p_buf) != cudaSuccess) {
+      mine.ok = 0;
+    }
+    cudaGetLastError();
+  }
+  if (!nccl().AllGather) {  // cannot even agree: every rank sees the same library, so all fall back
+    ctx->p2p_state = 0;
+    sp_p2p_release(ctx);
+    return 0;
+  }
+  P2PRecord all[kSpMaxPeers + 1];
+  P2PRecord* recs = P <= kSpMaxPeers ? all : nullptr;
+  std::vector<P2PRecord> big;
+  if (!recs) {
+    big.resize(P);
+    recs = big.data();
+  }
+  if ((*status = p2p_all_gather(ctx, mine, recs))) return 0;
+  bool all_ok = true;
+  for (int r = 0; r < P; ++r) all_ok = all_ok && recs[r].ok;
+  P2PRecord opened{};
+  opened.ok = all_ok;
+  if (all_ok) {
+    for (int r = 0; r < P; ++r) {
+      if (r == rank) {
+        ctx->p2p_peer[r] = ctx->p2p_buf;
+        continue;
+      }
+      void* ptr = nullptr;
+      if (cudaIpcOpenMemHandle(&ptr, recs[r].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+        cudaGetLastError();
+        opened.ok = 0;
+        break;
+      }
+      ctx->p2p_peer[r] = ptr;
+    }
+  }
+  // every rank must agree that every rank opened every buffer
+  if ((*status = p2p_all_gather(ctx, opened, recs))) return 0;
+  bool open_all = all_ok;
+  for (int r = 0; r < P; ++r) open_all = open_all && recs[r].ok;
+  if (!open_all) {
+    sp_p2p_release(ctx);
+    ctx->p2p_state = 0;
+    return 0;
+  }
+  ctx->p2p_bytes = bytes;
+  ctx->p2p_epoch = 0;
+  ctx->p2p_state = 1;
+  return 1;
 }
 
 static unsigned grid_units(wx_ctx* ctx, int64_t total) {
@@ -231,6 +398,8 @@ int wx_ctx_init_comm(wx_ctx* ctx, int nranks, int rank, const void* id128) {
     api.CommDestroy(static_cast<ncclComm_t>(ctx->comm));
     ctx->comm = nullptr;
   }
+  sp_p2p_release(ctx);  // a new group decides the exchange path again
+  ctx->p2p_state = -1;
   ncclUniqueId id;
   memcpy(&id, id128, sizeof(id));
   ncclComm_t comm = nullptr;
@@ -252,10 +421,14 @@ int wx_ctx_comm_check(wx_ctx* ctx) {
   return WX_OK;
 }
 
+int wx_ctx_sp_exchange(wx_ctx* ctx) { return ctx ? ctx->p2p_state : WX_ERR_INVALID; }
+
 int wx_ctx_comm_abort(wx_ctx* ctx) {
   if (!ctx) return WX_ERR_INVALID;
   if (ctx->comm) nccl().CommAbort(static_cast<ncclComm_t>(ctx->comm));
   ctx->comm = nullptr;
+  sp_p2p_release(ctx);
+  ctx->p2p_state = -1;
   ctx->sp_size = 1;
   ctx->sp_rank = 0;
   return WX_OK;
@@ -307,6 +480,57 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
     if ((st = qlinear_lora_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
                                    3 * inner, nullptr, wd, lt, nullptr)))
       return st;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const P2PLayout PL = p2p_layout(S, rows, inner, Hl, hd);
+    const int peer = p2p_ensure(ctx, PL.total, hd, cfg->rot, &st);
+    if (st) return st;
+    if (peer) {
+      // exchange 1: QK-norm + RoPE (and v) of this rank's rows straight into the owners'
+      // buffers; exchange 2: attention rows straight into the owners' out-proj operand
+      const uint32_t ep = ++ctx->p2p_epoch;
+      const int rank = ctx->sp_rank;
+      void* qkv_dst[kSpMaxPeers] = {};
+      SpPeerOut po{};
+      PeerSignal sig1{};
+      for (int r = 0; r < P; ++r) {
+        uint8_t* b = static_cast<uint8_t*>(ctx->p2p_peer[r]);
+        qkv_dst[r] = b + PL.qkv;
+        po.out_peer[r] = b + PL.att;
+        po.flags[r] = reinterpret_cast<uint32_t*>(b + PL.flags2);
+        sig1.flags[r] = reinterpret_cast<uint32_t*>(b + PL.flags1);
+      }
+      sig1.counter = ctx->p2p_counters;
+      sig1.P = P;
+      sig1.rank = rank;
+      sig1.epoch = ep;
+      uint8_t* mine = static_cast<uint8_t*>(ctx->p2p_buf);
+      if ((st = launch_qkv_to_peers(ctx, qkv, rows, (int64_t)rank * rows, cfg->heads, Hl, qkv_dst, P, w->q_norm,
+                                    w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, sig1)))
+        return st;
+      sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(mine + PL.flags1), P, ep,
+                                                     ctx->dev_err);
+      if ((st = launch_status(ctx, "sp_wait_qkv"))) return st;
+      po.rows = rows;
+      po.col = rank * Hl * hd;
+      po.counter = ctx->p2p_counters + 1;
+      po.P = P;
+      po.rank = rank;
+      po.epoch = ep;
+      auto* full = reinterpret_cast<__nv_bfloat16*>(mine + PL.qkv);
+      void* att_mine = mine + PL.att;
+      const int64_t rs = 3 * (int64_t)Hl * hd;
+      if ((st = attention_with_scratch_peer(ctx, full, full + (int64_t)Hl * hd, full + 2 * (int64_t)Hl * hd, rs, S,
+                                            Hl, hd, spec, scale, att_mine, inner, base + L.attn, &po)))
+        return st;
+      sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(mine + PL.flags2), P, ep,
+                                                     ctx->dev_err);
+      if ((st = launch_status(ctx, "sp_wait_att"))) return st;
+      void* at_dst = pab_slot ? pab_slot : base + L.at;
+      if ((st = qlinear_lora_with_scratch(ctx, att_mine, rows, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID,
+                                          mods->gate_msa, h, rowmap, ha, cfg->hidden, at_dst, wd, lt, nullptr)))
+        return st;
+    }
+    if (!peer) {
     if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, rows, cfg->heads, hd, w->q_norm,
                                   w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
       return st;
@@ -317,7 +541,6 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
     if ((st = launch_status(ctx, "sp_pack_qkv"))) return st;
     if ((st = all_to_all(ctx, send, recv, (size_t)rows * 3 * Hl * hd * 2))) return st;
     // attention over the whole sequence for heads [rank*Hl, rank*Hl + Hl)
-    const float scale = 1.0f / sqrtf((float)hd);
     const int64_t rs = 3 * (int64_t)Hl * hd;
     if ((st = attention_with_scratch(ctx, recv, recv + (int64_t)Hl * hd, recv + 2 * (int64_t)Hl * hd, rs, S, Hl, hd,
                                      spec, scale, attf, (int64_t)Hl * hd, base + L.attn)))
@@ -331,6 +554,7 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
     if ((st = qlinear_lora_with_scratch(ctx, att, rows, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID, mods->gate_msa, h, rowmap, ha,
                                    cfg->hidden, at_dst, wd, lt, nullptr)))
       return st;
+    }
   } else {
     if ((st = launch_mod_gate(ctx, h, pab_slot, mods->gate_msa, rowmap, rows, cfg->hidden, ha))) return st;
   }

@@ -67,6 +67,11 @@ class Context:
     def check_device(self) -> None:
         check(self.lib.wx_ctx_check_device(self.h), self.h)
 
+    def sp_exchange(self) -> int:
+        """Sequence-parallel exchange path: 1 NVLink peer memory, 0 NCCL all-to-alls,
+        -1 not decided yet (no refreshed block has run on the group)."""
+        return int(self.lib.wx_ctx_sp_exchange(self.h))
+
     def call(self, name: str, *args) -> None:
         self.sync_stream()
         check(getattr(self.lib, name)(self.h, *args), self.h)
