@@ -314,7 +314,7 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
                          void* pab_slot, int refresh, void* scratch);
 
 /* ------------------------------------------- Ulysses sequence parallelism */
-/* No counterpart in the reference (single device; SURVEY of the reference: no
+/* No counterpart in the reference (it runs on a single device, with no
  * DP/TP/SP). Rank `rank` of P owns rows [row0, row0 + rows) of the packed
  * sequence (S/P each) for every row-local op, and heads [head0, head0 + heads)
  * (H/P each) for attention over the whole sequence. Before attention each rank
@@ -375,12 +375,20 @@ typedef struct wx_dit_model {
   const void* final_norm;      /* [hidden] bf16 */
   const float* out_w;          /* [hidden, patch_dim] fp32 final projection */
   const float* out_b;          /* [patch_dim] */
+  /* audio stream (H3DiT audioPatchW/B, audioOutW/B; H3Transformer.swift:1036-1041,
+   * 1176-1188); audio_dim 0 = no audio weights */
+  int32_t audio_dim;           /* latent features per audio row (32) */
+  const float* audio_embed_w;  /* [audio_dim, hidden] */
+  const float* audio_embed_b;  /* [hidden] */
+  const float* audio_out_w;    /* [hidden, audio_dim] */
+  const float* audio_out_b;    /* [audio_dim] */
 } wx_dit_model;
 
 /* One sampler step (the loop body of H3Pipeline.swift:1398-1445): packed rows
  * [0, text_rows) are text states, rows [text_rows, S) come from the patch embed
  * of `latents` ([S - text_rows, patch_dim] fp32: reference/cond rows, then the
- * video latent), rows [video_start, S) are denoised: final head, negated
+ * video latent; audio rows, when given, from the audio embed, see below),
+ * rows [video_start, S) are denoised: final head, negated
  * velocity, and latents[video rows] += -v * dsigma in place. Layers follow
  * sparse_mode_for_layer(policy); `spec` is used on the sparse layers. PAB:
  * pab_slots[bi] ([rows, hidden] each, or pab_slots NULL) are written when
@@ -405,6 +413,23 @@ typedef struct wx_dit_step_args {
   float dsigma;
   int32_t reserved;
   void* scratch;               /* wx_dit_step_scratch_bytes */
+  /* Audio rows (refAudio and audio segments of the PackedLayout): packed rows
+   * [audio_segs[2i], audio_segs[2i+1]) (host array, ascending, inside
+   * [text_rows, video_start)) take their embeddings from audio_latents
+   * ([sum of segment rows, audio_dim] fp32, segments in order) and every other
+   * row after the text from `latents` in order (so `latents` then holds
+   * S - text_rows - audio rows). Segment audio_target (-1 = none) is denoised:
+   * final head with audio_final_shift/scale (the audio t row of the final
+   * tables), then audio_latents += (aout * audio_vscale) * audio_dsigma
+   * (H3DiT.forward's -slope and the pipeline's dσa/slope, H3Pipeline.swift:1436-1443). */
+  const int64_t* audio_segs;
+  int32_t n_audio_segs;
+  int32_t audio_target;
+  float* audio_latents;
+  const void* audio_final_shift;
+  const void* audio_final_scale;
+  float audio_vscale;
+  float audio_dsigma;
 } wx_dit_step_args;
 int64_t wx_dit_step_scratch_bytes(wx_ctx* ctx, const wx_dit_model* m, int64_t S);
 int wx_dit_step(wx_ctx* ctx, const wx_dit_model* m, const wx_dit_step_args* a);

@@ -100,3 +100,56 @@ def test_step_pab_window_and_sparse_policy():
     v1 = (l1.cpu().numpy() - lat)[video_start - text:]
     v3 = (l3.cpu().numpy() - lat)[video_start - text:]
     assert cosine(v1, v3) > 0.99
+
+
+def test_step_with_audio_rows():
+    """Audio segments of the packed layout (refAudio, then the target audio; H3Transformer.swift
+    :1036-1062 embeds them with audioPatchW, :1176-1188 runs the audio head) inside a step:
+    cond video rows on both sides of them come from the video latents in order."""
+    import torch
+    from wuxianhuabu_b200 import h3
+    S, text, video_start, dsigma = 344, 40, 200, -0.05
+    segs = [(104, 114), (114, 134)]  # refAudio (never denoised), target audio
+    AD, vscale, da = 32, -1.25, 0.03
+    (blocks, cos, sin, rowmap, _lat, ew, eb, ow, ob, fn, fsh, fsc, ts) = _setup(2, S, text, seed=31)
+    n_audio = sum(e - s for s, e in segs)
+    lat = O.normal_f32((S - text - n_audio, PATCH), 31, 80)
+    alat = O.normal_f32((n_audio, AD), 31, 81)
+    aew, aeb = O.normal_f32((AD, HIDDEN), 31, 82, std=0.1), O.normal_f32((HIDDEN,), 31, 83, std=0.1)
+    aow, aob = O.normal_f32((HIDDEN, AD), 31, 84, std=0.05), O.normal_f32((AD,), 31, 85, std=0.05)
+    afsh, afsc = O.normal_bf16((HIDDEN,), 31, 86, std=0.1), O.normal_bf16((HIDDEN,), 31, 87, std=0.1)
+    # oracle: embed the runs in order, blocks, both heads
+    rows, vi, ai, p = [], 0, 0, text
+    for s0, s1 in segs + [(S, S)]:
+        if s0 > p:
+            rows.append(O.f32_to_bf16(O.dense_f32(lat[vi:vi + s0 - p], ew, eb)))
+            vi += s0 - p
+        if s1 > s0:
+            rows.append(O.f32_to_bf16(O.dense_f32(alat[ai:ai + s1 - s0], aew, aeb)))
+            ai += s1 - s0
+        p = s1
+    h = np.concatenate([ts] + rows, 0)
+    cfgd = dict(heads=HEADS, head_dim=128, eps=EPS, rot=ROT, mlp_kind=0)
+    for (w, mods, _h, _c, _s, _r) in blocks:
+        h, _ = O.block_forward(h, w, mods, rowmap, cos, sin, cfgd)
+    mv = O.norm_modscale(h[video_start:], fn, fsh[None], fsc[None], None, EPS)
+    ref_v = O.dense_f32(f32(mv), ow, ob)
+    ma = O.norm_modscale(h[segs[1][0]:segs[1][1]], fn, afsh[None], afsc[None], None, EPS)
+    ref_a = O.dense_f32(f32(ma), aow, aob)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    dit, _ = _gpu_model(blocks, ew, eb, ow, ob, fn)
+    dit = h3.H3DiT(dit.blocks, dit.mods, t(ew), t(eb), to_torch_bf16(fn), t(ow), t(ob), t(aew), t(aeb), t(aow), t(aob))
+    lat_d, alat_d = t(lat.copy()), t(alat.copy())
+    audio = h3.H3AudioRows(segs, alat_d, 1, to_torch_bf16(afsh), to_torch_bf16(afsc), vscale, da)
+    dit.step(S, text, video_start, to_torch_bf16(ts), lat_d, torch.from_numpy(rowmap.view(np.int32)).cuda(),
+             to_torch_bf16(cos), to_torch_bf16(sin), to_torch_bf16(fsh), to_torch_bf16(fsc), None, 0, None, True,
+             dsigma, audio=audio)
+    h3.context().check_device()
+    got, agot = lat_d.cpu().numpy(), alat_d.cpu().numpy()
+    nv = S - video_start
+    assert np.array_equal(got[:-nv], lat[:-nv])          # cond video rows untouched
+    assert np.array_equal(agot[:10], alat[:10])          # refAudio rows untouched
+    v_got = (got[-nv:] - lat[-nv:]) / -dsigma
+    assert_close(v_got, ref_v, rel=2e-2, cos=0.999, what="step velocity with audio rows")
+    a_got = (agot[10:] - alat[10:]) / np.float32(vscale * da)
+    assert_close(a_got, ref_a, rel=2e-2, cos=0.999, what="audio head")

@@ -84,7 +84,9 @@ class SpPlan(C.Structure):
 class DitModel(C.Structure):
     _fields_ = [("cfg", C.POINTER(DitConfig)), ("n_blocks", C.c_int32), ("patch_dim", C.c_int32),
                 ("blocks", C.POINTER(BlockWeights)), ("mods", C.POINTER(BlockMods)), ("embed_w", C.c_void_p),
-                ("embed_b", C.c_void_p), ("final_norm", C.c_void_p), ("out_w", C.c_void_p), ("out_b", C.c_void_p)]
+                ("embed_b", C.c_void_p), ("final_norm", C.c_void_p), ("out_w", C.c_void_p), ("out_b", C.c_void_p),
+                ("audio_dim", C.c_int32), ("audio_embed_w", C.c_void_p), ("audio_embed_b", C.c_void_p),
+                ("audio_out_w", C.c_void_p), ("audio_out_b", C.c_void_p)]
 
 
 class StepArgs(C.Structure):
@@ -92,7 +94,10 @@ class StepArgs(C.Structure):
                 ("latents", C.c_void_p), ("rowmap", C.c_void_p), ("cos_t", C.c_void_p), ("sin_t", C.c_void_p),
                 ("final_shift", C.c_void_p), ("final_scale", C.c_void_p), ("spec", C.POINTER(SparseSpec)),
                 ("policy", C.c_int32), ("refresh", C.c_int32), ("pab_slots", C.POINTER(C.c_void_p)),
-                ("dsigma", C.c_float), ("reserved", C.c_int32), ("scratch", C.c_void_p)]
+                ("dsigma", C.c_float), ("reserved", C.c_int32), ("scratch", C.c_void_p),
+                ("audio_segs", C.c_void_p), ("n_audio_segs", C.c_int32), ("audio_target", C.c_int32),
+                ("audio_latents", C.c_void_p), ("audio_final_shift", C.c_void_p), ("audio_final_scale", C.c_void_p),
+                ("audio_vscale", C.c_float), ("audio_dsigma", C.c_float)]
 
 
 class DenseBf16(C.Structure):

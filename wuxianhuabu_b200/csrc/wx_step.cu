@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <vector>
 
 #include "wx_internal.h"
 
@@ -17,9 +18,42 @@ namespace wx {
 int launch_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w, const void* shift,
                          const void* scale, const uint32_t* rowmap, float eps, void* out);
 
+// audio update of the pipeline: x += (aout * vscale) * dsigma (fp32, in that order)
+__global__ void scaled_update_kernel(float* __restrict__ x, const float* __restrict__ v, int64_t n, float vscale,
+                                     float dsigma) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    x[i] = x[i] + (v[i] * vscale) * dsigma;
+}
+
 struct StepLayout {
   size_t h, f32, h16, vel, blk, total;
 };
+
+// One run of packed rows [start, end) whose embeddings come from one latent array
+// starting at row `lat` of it.
+struct Piece {
+  int64_t start, end, lat;
+  bool audio;
+};
+
+// Splits [text, S) into runs of audio rows (the segments, in order) and video
+// rows (everything else after the text), with each run's first latent row.
+static std::vector<Piece> latent_pieces(int64_t text, int64_t S, const int64_t* segs, int nsegs) {
+  std::vector<Piece> out;
+  int64_t p = text, a_lat = 0, v_lat = 0;
+  for (int i = 0; i < nsegs; ++i) {
+    const int64_t s0 = segs[2 * i], s1 = segs[2 * i + 1];
+    if (s0 > p) {
+      out.push_back({p, s0, v_lat, false});
+      v_lat += s0 - p;
+    }
+    out.push_back({s0, s1, a_lat, true});
+    a_lat += s1 - s0;
+    p = s1;
+  }
+  if (S > p) out.push_back({p, S, v_lat, false});
+  return out;
+}
 
 static size_t al(size_t b) { return (b + 255) & ~size_t(255); }
 
@@ -32,7 +66,7 @@ static StepLayout step_layout(wx_ctx* ctx, const wx_dit_model* m, int64_t S) {
   L.h = off; off += al((size_t)rows * hid * 2);
   L.f32 = off; off += al((size_t)rows * hid * 4);
   L.h16 = off; off += al((size_t)rows * hid * 2);
-  L.vel = off; off += al((size_t)rows * m->patch_dim * 4);
+  L.vel = off; off += al((size_t)rows * std::max(m->patch_dim, std::max(m->audio_dim, 0)) * 4);
   const int64_t blk = P == 1 ? wx_dit_block_scratch_bytes(m->cfg, S) : wx_dit_block_sp_scratch_bytes(m->cfg, S, P);
   L.blk = off; off += al((size_t)std::max<int64_t>(blk, 0));
   L.total = off;
@@ -61,6 +95,16 @@ int wx_dit_step(wx_ctx* ctx, const wx_dit_model* m, const wx_dit_step_args* a) {
   WX_CHECK_ARG(ctx, a->refresh || a->pab_slots);
   const int P = ctx->sp_size;
   WX_CHECK_ARG(ctx, a->S % P == 0);
+  WX_CHECK_ARG(ctx, a->n_audio_segs >= 0 && (a->n_audio_segs == 0 || (a->audio_segs && a->audio_latents)));
+  WX_CHECK_ARG(ctx, a->n_audio_segs == 0 || (m->audio_dim > 0 && m->audio_embed_w && m->audio_embed_b));
+  WX_CHECK_ARG(ctx, a->audio_target >= -1 && a->audio_target < a->n_audio_segs);
+  WX_CHECK_ARG(ctx, a->audio_target < 0 || (m->audio_out_w && m->audio_out_b && a->audio_final_shift &&
+                                            a->audio_final_scale));
+  for (int i = 0; i < a->n_audio_segs; ++i) {
+    const int64_t s0 = a->audio_segs[2 * i], s1 = a->audio_segs[2 * i + 1];
+    const int64_t prev = i ? a->audio_segs[2 * i - 1] : a->text_rows;
+    WX_CHECK_ARG(ctx, s0 >= prev && s1 > s0 && s1 <= a->video_start);
+  }
   const wx_dit_config* cfg = m->cfg;
   const int64_t hid = cfg->hidden, pd = m->patch_dim, text = a->text_rows, S = a->S;
   const int64_t rows = S / P, row0 = (int64_t)ctx->sp_rank * rows, row1 = row0 + rows;
@@ -76,9 +120,18 @@ int wx_dit_step(wx_ctx* ctx, const wx_dit_model* m, const wx_dit_step_args* a) {
   if (t1 > row0)
     WX_CUDA_TRY(ctx, cudaMemcpyAsync(h, static_cast<const __nv_bfloat16*>(a->text_states) + row0 * hid,
                                      (size_t)(t1 - row0) * hid * 2, cudaMemcpyDeviceToDevice, ctx->stream));
-  const int64_t e0 = std::max(row0, text), ne = row1 - e0;
-  if (ne > 0) {
-    if ((st = wx_dense_f32(ctx, a->latents + (e0 - text) * pd, ne, pd, m->embed_w, hid, m->embed_b, f32))) return st;
+  const std::vector<Piece> pieces = latent_pieces(text, S, a->audio_segs, a->n_audio_segs);
+  for (const Piece& pc : pieces) {
+    const int64_t e0 = std::max(row0, pc.start), e1 = std::min(row1, pc.end), ne = e1 - e0;
+    if (ne <= 0) continue;
+    const int64_t lat = pc.lat + (e0 - pc.start);
+    if (pc.audio) {
+      const int64_t ad = m->audio_dim;
+      if ((st = wx_dense_f32(ctx, a->audio_latents + lat * ad, ne, ad, m->audio_embed_w, hid, m->audio_embed_b, f32)))
+        return st;
+    } else if ((st = wx_dense_f32(ctx, a->latents + lat * pd, ne, pd, m->embed_w, hid, m->embed_b, f32))) {
+      return st;
+    }
     if ((st = wx_f32_to_bf16(ctx, f32, ne * hid, h + (e0 - row0) * hid))) return st;
   }
   // blocks
@@ -96,15 +149,37 @@ int wx_dit_step(wx_ctx* ctx, const wx_dit_model* m, const wx_dit_step_args* a) {
                                           a->sin_t, spec, slot, refresh, base + L.blk);
     if (st) return st;
   }
-  // final head on the video rows + Euler update of their latents
+  // final head on the video rows + Euler update of their latents (video rows are the
+  // last run, so their latent rows are the last ones)
   const int64_t v0 = std::max(row0, a->video_start), nv = row1 - v0;
   if (nv > 0) {
+    const int64_t vlat = pieces.back().lat + (v0 - pieces.back().start);
     if ((st = launch_norm_modscale(ctx, h + (v0 - row0) * hid, nv, hid, m->final_norm, a->final_shift,
                                    a->final_scale, nullptr, cfg->eps, h16)))
       return st;
     if ((st = wx_bf16_to_f32(ctx, h16, nv * hid, f32))) return st;
     if ((st = wx_dense_f32(ctx, f32, nv, hid, m->out_w, pd, m->out_b, vel))) return st;
-    if ((st = wx_euler_update(ctx, a->latents + (v0 - text) * pd, vel, nv * pd, a->dsigma))) return st;
+    if ((st = wx_euler_update(ctx, a->latents + vlat * pd, vel, nv * pd, a->dsigma))) return st;
+  }
+  // final head on the target audio rows (finalHead with the audio t row) + their update
+  if (a->audio_target >= 0) {
+    const int64_t s0 = a->audio_segs[2 * a->audio_target], s1 = a->audio_segs[2 * a->audio_target + 1];
+    const int64_t b0 = std::max(row0, s0), b1 = std::min(row1, s1), nb = b1 - b0;
+    if (nb > 0) {
+      int64_t lat = 0;
+      for (const Piece& pc : pieces)
+        if (pc.audio && pc.start == s0) lat = pc.lat + (b0 - s0);
+      const int64_t ad = m->audio_dim;
+      if ((st = launch_norm_modscale(ctx, h + (b0 - row0) * hid, nb, hid, m->final_norm, a->audio_final_shift,
+                                     a->audio_final_scale, nullptr, cfg->eps, h16)))
+        return st;
+      if ((st = wx_bf16_to_f32(ctx, h16, nb * hid, f32))) return st;
+      if ((st = wx_dense_f32(ctx, f32, nb, hid, m->audio_out_w, ad, m->audio_out_b, vel))) return st;
+      const int64_t n = nb * ad;
+      scaled_update_kernel<<<(unsigned)std::min<int64_t>((n + 255) / 256, 65536), 256, 0, ctx->stream>>>(
+          a->audio_latents + lat * ad, vel, n, a->audio_vscale, a->audio_dsigma);
+      if ((st = launch_status(ctx, "audio_update"))) return st;
+    }
   }
   return WX_OK;
 }

@@ -38,6 +38,7 @@ __all__ = [
     "DenseLinear", "H3TimeEmbedder", "H3AdalnLUT", "H3AdalnW", "H3AdalnTables", "precompute_adaln",
     "H3TextRefiner", "rms_norm", "load_refiner_block", "load_text_refiner", "load_time_embedder", "load_adaln",
     "axis_from_sqrt_area", "video_t_span", "video_t_grid", "write_frame_grid", "packed_positions", "build_rope",
+    "H3DiT", "H3AudioRows",
 ]
 
 
@@ -531,28 +532,52 @@ class H3DiTBlocks:
         return h
 
 
+@dataclass
+class H3AudioRows:
+    """Audio rows of one sampler step: packed-row segments [start, end) (refAudio and the
+    target audio segment of the PackedLayout, ascending, before the video), their fp32 latents
+    [rows, audio_dim] in segment order, the index of the denoised segment (-1 none), this step's
+    audio row of the final AdaLN tables, and the update factors: out.audio = aout * vscale with
+    vscale = -slope (H3DiT.forward, H3Transformer.swift:1186-1188), audioX += out.audio * dsigma
+    with dsigma = dσa / slope (H3Pipeline.swift:1438-1442)."""
+    segs: Sequence[tuple]
+    latents: torch.Tensor
+    target: int
+    final_shift: Optional[torch.Tensor]
+    final_scale: Optional[torch.Tensor]
+    vscale: float
+    dsigma: float
+
+
 class H3DiT:
     """H3DiT (H3Transformer.swift:1022-1203) around the blocks: patch embed, final head,
-    and the sampler step of H3Pipeline.swift:1398-1445 as one native call (wx_dit_step)."""
+    and the sampler step of H3Pipeline.swift:1398-1445 as one native call (wx_dit_step);
+    optional audio patch embed / audio head (audioPatchW/B, audioOutW/B)."""
 
     def __init__(self, blocks: H3DiTBlocks, mods: Sequence[Sequence[torch.Tensor]], embed_w: torch.Tensor,
-                 embed_b: torch.Tensor, final_norm: torch.Tensor, out_w: torch.Tensor, out_b: torch.Tensor):
+                 embed_b: torch.Tensor, final_norm: torch.Tensor, out_w: torch.Tensor, out_b: torch.Tensor,
+                 audio_embed_w: Optional[torch.Tensor] = None, audio_embed_b: Optional[torch.Tensor] = None,
+                 audio_out_w: Optional[torch.Tensor] = None, audio_out_b: Optional[torch.Tensor] = None):
         self.blocks = blocks
         self.mods = [list(m) for m in mods]
         self._bw = (BlockWeights * len(blocks.blocks))(*blocks._wc)
         self._bm = (BlockMods * len(self.mods))(*[BlockMods(*[_p(t) for t in m]) for m in self.mods])
         self.embed_w, self.embed_b, self.final_norm, self.out_w, self.out_b = embed_w, embed_b, final_norm, out_w, out_b
+        self.audio = (audio_embed_w, audio_embed_b, audio_out_w, audio_out_b)
         self.patch_dim = embed_w.shape[0]
+        audio_dim = audio_embed_w.shape[0] if audio_embed_w is not None else 0
         self._m = _lib.DitModel(C.pointer(blocks._c), len(blocks.blocks), self.patch_dim, self._bw, self._bm,
-                                _p(embed_w), _p(embed_b), _p(final_norm), _p(out_w), _p(out_b))
+                                _p(embed_w), _p(embed_b), _p(final_norm), _p(out_w), _p(out_b), audio_dim,
+                                _p(audio_embed_w), _p(audio_embed_b), _p(audio_out_w), _p(audio_out_b))
         self._scratch: Optional[torch.Tensor] = None
 
     def step(self, S: int, text_rows: int, video_start: int, text_states: torch.Tensor, latents: torch.Tensor,
              rowmap: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, final_shift: torch.Tensor,
              final_scale: torch.Tensor, sparse_cfg: Optional[H3SolAttnConfig], policy: int,
              attn_bcast: Optional[H3AttnBroadcast], attn_refresh: bool, dsigma: float,
-             sigma: Optional[float] = None) -> torch.Tensor:
-        """One denoising step; latents [S - text_rows, patch] fp32 are updated in place."""
+             sigma: Optional[float] = None, audio: Optional[H3AudioRows] = None) -> torch.Tensor:
+        """One denoising step; latents [S - text_rows (- audio rows), patch] fp32 (and the audio
+        latents) are updated in place."""
         ctx = context(latents.device.index)
         lib = ctx.lib
         need = int(lib.wx_dit_step_scratch_bytes(ctx.h, C.byref(self._m), S))
@@ -574,6 +599,18 @@ class H3DiT:
                              _p(final_shift), _p(final_scale), C.pointer(spec) if spec is not None else None,
                              policy if sparse_cfg is not None else SparsePolicy.OFF, int(refresh), slots,
                              float(dsigma), 0, _p(self._scratch))
+        if audio is not None:
+            segs = (C.c_int64 * (2 * max(1, len(audio.segs))))(*[int(v) for sg in audio.segs for v in sg])
+            args.audio_segs = C.cast(segs, C.c_void_p)
+            args.n_audio_segs = len(audio.segs)
+            args.audio_target = audio.target
+            args.audio_latents = _p(audio.latents)
+            args.audio_final_shift = _p(audio.final_shift)
+            args.audio_final_scale = _p(audio.final_scale)
+            args.audio_vscale = float(audio.vscale)
+            args.audio_dsigma = float(audio.dsigma)
+        else:
+            args.audio_target = -1
         ctx.call("wx_dit_step", C.byref(self._m), C.byref(args))
         if attn_bcast is not None and refresh and sigma is not None:
             attn_bcast.cached_sigma = sigma
