@@ -10,7 +10,8 @@
 //   P_X overwrites the first 64 columns of S_X as packed bf16.
 //   Shared memory: Q_A, Q_B, K ring of 3, V ring of 2 (32 KB tiles, SW128).
 //   Warp 0: TMA producer. Warp 1 / warp 2: MMA issuer of slot A / B (one
-//   thread each: S_X(t), then after P_X(t) the PV_X(t), then S_X(t+1) — the
+//   thread each: S_X(t), then PV_X(t) in four pieces of 32 keys, each issued as
+//   soon as the softmax has stored that piece of P_X(t), then S_X(t+1) — the
 //   tensor pipe runs one thread's MMAs in issue order, so S_X(t+1) cannot
 //   overwrite P_X(t) before PV_X(t) has read it). Warp 3: idle.
 //   Warps 4-7 / 8-11: softmax + epilogue of slot A / B (thread r owns row r).
@@ -33,6 +34,13 @@ constexpr int kA5VStages = 2;
 #define WX_A5_TURN_CHUNK 2
 #endif
 constexpr int kA5TurnChunk = WX_A5_TURN_CHUNK;  // exponential chunks (of 4) after which the turn passes
+// P(t) is handed to the MMA issuer in kA5PVParts pieces (of the 4 chunks of 32 keys): the
+// PV(t) MMAs of a piece go out while the softmax still computes the next piece
+#ifndef WX_A5_PV_PARTS
+#define WX_A5_PV_PARTS 4
+#endif
+constexpr int kA5PVParts = WX_A5_PV_PARTS;
+static_assert(kA5PVParts == 1 || kA5PVParts == 2 || kA5PVParts == 4, "P pieces: 1, 2 or 4");
 constexpr int kA5BarOff = (2 + kA5KStages + kA5VStages) * kTileBytes;
 constexpr int kA5Smem = kA5BarOff + 512 + 1024;
 static_assert(kA5Threads == kA4Threads, "uses the register split of flash_attn4_kernel (kA4RegsLow/High)");
@@ -44,12 +52,13 @@ enum : int {
   kB5VFull = 7,   // [2]
   kB5VEmpty = 9,  // [2] count 2 (both slots' PV)
   kB5SFull = 11,  // [2] per slot
-  kB5PFull = 13,  // [2] per slot, count 4 (one per softmax warp)
-  kB5OFull = 15,  // [2] per slot
-  kB5Drain = 17,  // [2] per slot
-  kB5Turn = 19,   // [2] per slot, count 4: this slot's exponentials (all but the tail) are issued
-  kB5Count = 21
+  kB5PFull = 13,  // [2][kA5PVParts] per slot and piece of P, count 4 (one per softmax warp)
+  kB5OFull = 13 + 2 * kA5PVParts,  // [2] per slot
+  kB5Drain = kB5OFull + 2,         // [2] per slot
+  kB5Turn = kB5Drain + 2,          // [2] per slot, count 4: this slot's exponentials (all but the tail) are issued
+  kB5Count = kB5Turn + 2
 };
+static_assert(kB5Count <= 32, "barriers overlap the TMEM slot");
 
 template <int POLY, bool DUO>
 __global__ void __launch_bounds__(kA5Threads, 1)
@@ -82,7 +91,8 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       uint32_t c = 1;
       if (!DUO && (i == kB5KEmpty || i == kB5KEmpty + 1 || i == kB5KEmpty + 2 || i == kB5VEmpty || i == kB5VEmpty + 1))
         c = 2;
-      if (i == kB5PFull || i == kB5PFull + 1 || i == kB5Turn || i == kB5Turn + 1) c = 4;  // one per softmax warp
+      if ((i >= kB5PFull && i < kB5PFull + 2 * kA5PVParts) || i == kB5Turn || i == kB5Turn + 1)
+        c = 4;  // one per softmax warp
       mbar_init(bar(i), c);
     }
     *abort_flag = 0;
@@ -212,16 +222,27 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         // V(t) and K(t+1) are waited for before P(t): once the softmax hands over P(t),
         // PV(t) and S(t+1) go out back to back with no barrier wait between them
         if (!mbar_wait(bar(kB5VFull + vbar(t)), vpar(t), p.err, kDevTimeoutFull, abort_flag) ||
-            (t + 1 < nX && !k_ready(t + 1)) ||
-            !mbar_wait(bar(kB5PFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
+            (t + 1 < nX && !k_ready(t + 1))) {
           ok = false;
           break;
         }
-        tc_fence_after();
         const uint64_t dv = opaque64(smem_desc_sw128(sV(vbuf(t)), 16384, 1024));
+        constexpr int kk_per = 8 / kA5PVParts;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_bf16_ts(tO, tS + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
+        for (int part = 0; part < kA5PVParts && ok; ++part) {
+          if (!mbar_wait(bar(kB5PFull + X * kA5PVParts + part), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k2 = 0; k2 < kk_per; ++k2) {
+            const int kk = part * kk_per + k2;
+            umma_bf16_ts(tO, tS + kk * 8, dv + (uint64_t)(kk * (2048 >> 4)), idesc_o, (t > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        if (!ok) break;
         umma_commit(bar(kB5VEmpty + vbar(t)));
         if (t + 1 < nX) issue_s(t + 1);
       }
@@ -319,6 +340,21 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         alpha = ex2((m - m_new) * p.sl2);
         m = m_new;
       }
+      if constexpr (kA5PVParts > 1) {
+        if (any_need) {
+          // O_X is rescaled before any PV_X(t) MMA (they start with the first piece of P);
+          // PV_X(t-1) completed before S_X(t) (in-order tensor pipe), so O_X is stable
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+      }
       // The exponential phases of the two slots take turns (A(0), B(0), A(1),
       // B(1), ...): run together they would share the MUFU pipe while the tensor
       // pipe idles; in turns, each overlaps the other slot's TMEM loads, row max,
@@ -362,28 +398,41 @@ __global__ void __launch_bounds__(kA5Threads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(bar(kB5Turn + X));
         }
-      }
-      if (any_need) {
-        // PV_X(t-1) completed before S_X(t) (in-order tensor pipe): O_X is stable
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tO + c * 32, o);
+        if constexpr (kA5PVParts > 1) {
+          constexpr int per = 4 / kA5PVParts;
+          if ((c + 1) % per == 0) {  // this piece of P is in TMEM: its PV MMAs may start
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(kB5PFull + X * kA5PVParts + (c + 1) / per - 1));
+          }
         }
       }
-      tmem_wait_st();
+      if constexpr (kA5PVParts == 1) {
+        if (any_need) {
+          // PV_X(t-1) completed before S_X(t) (in-order tensor pipe): O_X is stable
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        tmem_wait_st();
+      }
       {
         const float2 a = __fadd2_rn(rs2[0], rs2[1]), c2 = __fadd2_rn(rs2[2], rs2[3]);
         const float2 u = __fadd2_rn(a, c2);
         l = l * alpha + (u.x + u.y);
       }
-      tc_fence_before();
-      __syncwarp();  // the warp's TMEM stores are complete: one arrival per warp (4, not 128 atomics)
-      if (lane == 0) mbar_arrive(bar(kB5PFull + X));
+      if constexpr (kA5PVParts == 1) {
+        tc_fence_before();
+        __syncwarp();  // the warp's TMEM stores are complete: one arrival per warp (4, not 128 atomics)
+        if (lane == 0) mbar_arrive(bar(kB5PFull + X));
+      }
     }
     if (ok && nX > 0) ok = mbar_wait(bar(kB5OFull + X), 0, p.err, kDevTimeoutSoftmax, abort_flag);
     tc_fence_after();
