@@ -31,7 +31,7 @@ constexpr int kA5Threads = 384;
 constexpr int kA5KStages = 3;
 constexpr int kA5VStages = 2;
 #ifndef WX_A5_TURN_CHUNK
-#define WX_A5_TURN_CHUNK 2
+#define WX_A5_TURN_CHUNK 3
 #endif
 constexpr int kA5TurnChunk = WX_A5_TURN_CHUNK;  // exponential chunks (of 4) after which the turn passes
 // P(t) is handed to the MMA issuer in kA5PVParts pieces (of the 4 chunks of 32 keys): the
@@ -359,8 +359,9 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       // B(1), ...): run together they would share the MUFU pipe while the tensor
       // pipe idles; in turns, each overlaps the other slot's TMEM loads, row max,
       // PV and next S.
-      // The turn passes when the other slot has issued all but its last chunk of
-      // exponentials, so the two phases overlap only in their tails.
+      // The turn passes when the other slot has stored its chunk kA5TurnChunk of P
+      // (by default the last: the phases do not overlap; with P handed over in
+      // pieces, passing it earlier measured slower).
       // (A slot whose partner has no tile at that index does not wait.)
       const bool turn = X == 0 ? (t == 0 || t - 1 >= nB ||
                                   mbar_wait(bar(kB5Turn + 1), ((uint32_t)t - 1) & 1, p.err, kDevTimeoutSoftmax,
