@@ -40,6 +40,13 @@ constexpr int kA5TurnChunk = WX_A5_TURN_CHUNK;  // exponential chunks (of 4) aft
 #define WX_A5_PV_PARTS 4
 #endif
 constexpr int kA5PVParts = WX_A5_PV_PARTS;
+// Paired (shared K/V) mode: S(t+1) in two halves of 64 keys. Keys 64..127 land in S
+// columns [64,128), which P(t) (bf16 in columns [0,64)) does not use, so that half
+// is issued as soon as the softmax has read S(t); only keys 0..63 wait for PV(t).
+#ifndef WX_A5_S_SPLIT
+#define WX_A5_S_SPLIT 0
+#endif
+constexpr bool kA5SSplit = WX_A5_S_SPLIT != 0;
 static_assert(kA5PVParts == 1 || kA5PVParts == 2 || kA5PVParts == 4, "P pieces: 1, 2 or 4");
 constexpr int kA5BarOff = (2 + kA5KStages + kA5VStages) * kTileBytes;
 constexpr int kA5Smem = kA5BarOff + 512 + 1024;
@@ -56,7 +63,8 @@ enum : int {
   kB5OFull = 13 + 2 * kA5PVParts,  // [2] per slot
   kB5Drain = kB5OFull + 2,         // [2] per slot
   kB5Turn = kB5Drain + 2,          // [2] per slot, count 4: this slot's exponentials (all but the tail) are issued
-  kB5Count = kB5Turn + 2
+  kB5SRead = kB5Turn + 2,          // [2] per slot, count 4: the softmax has read S(t) into registers
+  kB5Count = kB5SRead + 2
 };
 static_assert(kB5Count <= 32, "barriers overlap the TMEM slot");
 
@@ -91,7 +99,8 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       uint32_t c = 1;
       if (!DUO && (i == kB5KEmpty || i == kB5KEmpty + 1 || i == kB5KEmpty + 2 || i == kB5VEmpty || i == kB5VEmpty + 1))
         c = 2;
-      if ((i >= kB5PFull && i < kB5PFull + 2 * kA5PVParts) || i == kB5Turn || i == kB5Turn + 1)
+      if ((i >= kB5PFull && i < kB5PFull + 2 * kA5PVParts) || i == kB5Turn || i == kB5Turn + 1 ||
+          i == kB5SRead || i == kB5SRead + 1)
         c = 4;  // one per softmax warp
       mbar_init(bar(i), c);
     }
@@ -214,6 +223,19 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         umma_commit(bar(kB5SFull + X));
         umma_commit(bar(kB5KEmpty + kbar(t)));
       };
+      // one half of S(t) (keys 64*half .. 64*half+63 into S columns [64*half, 64*half+64))
+      constexpr uint32_t idesc_s64 = idesc_bf16_f32(128, 64, false, false);
+      auto issue_s_half = [&](int t, int half) {
+        tc_fence_after();
+        const uint64_t dk = opaque64(smem_desc_sw128(sK(kbuf(t)) + (uint32_t)half * 8192, 16, 1024));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+          umma_bf16(tS + (uint32_t)(half * 64), dq + off, dk + off, idesc_s64, kk > 0 ? 1u : 0u);
+        }
+        issued = true;
+      };
+      constexpr bool split = kA5SSplit && !DUO;
       auto k_ready = [&](int t) {
         return mbar_wait(bar(kB5KFull + kbar(t)), kpar(t), p.err, kDevTimeoutFull, abort_flag);
       };
@@ -225,6 +247,14 @@ __global__ void __launch_bounds__(kA5Threads, 1)
             (t + 1 < nX && !k_ready(t + 1))) {
           ok = false;
           break;
+        }
+        if (split && t + 1 < nX) {
+          // keys 64..127 of S(t+1) as soon as the softmax has read S(t)
+          if (!mbar_wait(bar(kB5SRead + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
+            ok = false;
+            break;
+          }
+          issue_s_half(t + 1, 1);
         }
         const uint64_t dv = opaque64(smem_desc_sw128(sV(vbuf(t)), 16384, 1024));
         constexpr int kk_per = 8 / kA5PVParts;
@@ -244,7 +274,15 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         }
         if (!ok) break;
         umma_commit(bar(kB5VEmpty + vbar(t)));
-        if (t + 1 < nX) issue_s(t + 1);
+        if (t + 1 < nX) {
+          if (split) {
+            issue_s_half(t + 1, 0);
+            umma_commit(bar(kB5SFull + X));
+            umma_commit(bar(kB5KEmpty + kbar(t + 1)));
+          } else {
+            issue_s(t + 1);
+          }
+        }
       }
       if (ok) umma_commit(bar(kB5OFull + X));
       if (issued) {  // every MMA of this thread completes before TMEM is released
@@ -312,6 +350,11 @@ __global__ void __launch_bounds__(kA5Threads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<float(*)[32]>(v + c * 32));
       tmem_wait_ld();
+      if constexpr (kA5SSplit && !DUO) {  // S(t) is in registers: the next S may overwrite keys 64..127
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(kB5SRead + X));
+      }
       const int lim0 = ((cur.z >> (8 + qh)) & 1) ? (cur.z & 0xFF) : 0;
       const int lim1 = ((cur.w >> (8 + qh)) & 1) ? (cur.w & 0xFF) : 0;
       if (__any_sync(0xffffffffu, lim0 != 64 || lim1 != 64)) {
