@@ -113,6 +113,41 @@ def test_qlinear_swiglu(torch_mod):
     assert_close(f32(got), f32(ref), rel=1e-2, cos=0.9999, what="swiglu")
 
 
+@pytest.mark.parametrize("epi", ["none", "gelu", "gate_resid", "lora"])
+def test_qlinear_many_tiles_vs_oracle(torch_mod, epi):
+    """A shape with several waves of 128x256 tiles of the persistent kernel and a ragged
+    last M tile, each epilogue (and a LoRA extension) against the oracle."""
+    torch = torch_mod
+    from wuxianhuabu_b200 import h3
+    m, k, n = 4000, 1024, 12288
+    x = O.normal_bf16((m, k), 35, 1)
+    wq, sc, bi = O.quantize(O.normal_f32((n, k), 35, 2, std=0.03))
+    bias = O.normal_bf16((n,), 35, 3, std=0.1)
+    lin = _mf(torch, wq, sc, bi, k, bias)
+    kw, tkw = {}, {}
+    if epi == "gate_resid":
+        g = json.load(open(GOLD / "modrun.json"))
+        rowmap = np.array((g["map"] * (m // 16 + 1))[:m], dtype=np.uint32)
+        gate = O.normal_bf16((6, n), 35, 4)
+        resid = O.normal_bf16((m, n), 35, 5)
+        kw = dict(epilogue=O.EPI_GATE_RESID, gate=gate, resid=resid, rowmap=rowmap)
+        tkw = dict(epilogue=h3.EPI_GATE_RESID, gate=to_torch_bf16(gate), resid=to_torch_bf16(resid),
+                   rowmap=torch.from_numpy(rowmap.view(np.int32)).cuda())
+    elif epi == "gelu":
+        kw, tkw = dict(epilogue=O.EPI_GELU), dict(epilogue=h3.EPI_GELU)
+    if epi == "lora":
+        ad = [(O.normal_bf16((k, 32), 35, 6, std=0.05), O.normal_bf16((32, n), 35, 7, std=0.05), 0.7)]
+        lin.set_lora([h3.LoraRef(to_torch_bf16(a), to_torch_bf16(b), sc_) for a, b, sc_ in ad])
+        ref = O.qlinear_lora(x, wq, sc, bi, ad, bias=bias)
+        rel = 2e-2  # one fp32 accumulator against the reference's bf16 intermediates
+    else:
+        ref = O.qlinear(x, wq, sc, bi, bias=bias, **kw)
+        rel = 1e-2
+    got = to_np_bf16(lin(to_torch_bf16(x), **tkw))
+    h3.context().check_device()
+    assert_close(f32(got), f32(ref), rel=rel, cos=0.9999, what=f"many tiles {epi}")
+
+
 @pytest.mark.parametrize("m,k,n", [(4096, 3072, 3072), (1000, 12288, 3072), (2000, 3072, 12288)])
 def test_qlinear_large_vs_torch_fp32(torch_mod, m, k, n):
     """Large shapes against a plain PyTorch fp32 matmul of the GPU-dequantized weight."""

@@ -83,6 +83,62 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
   return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
 }
 
+// Epilogue of 32 accumulator values of output row m, columns n0..n0+31: bf16(acc)
+// (+ bias, rounded again), then GELU, or gate + residual (mr = the row's mod row), or
+// nothing; bf16 stores (and the raw pre-gate values when y_raw is set).
+__device__ __forceinline__ void gemm_epilogue32(const GemmParams& p, float (&v)[32], int64_t m, int64_t mr,
+                                                int64_t n0) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = round_bf16(v[i]);
+  if (p.bias) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      uint4 bv = *reinterpret_cast<const uint4*>(p.bias + n0 + i);
+      const uint32_t bu[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[i + 2 * q] = round_bf16(v[i + 2 * q] + bf16_lo(bu[q]));
+        v[i + 2 * q + 1] = round_bf16(v[i + 2 * q + 1] + bf16_hi(bu[q]));
+      }
+    }
+  }
+  __nv_bfloat16* yrow = p.y + m * p.ldy + n0;
+  if (p.epi == WX_EPI_GATE_RESID) {
+    const __nv_bfloat16* rrow = p.resid + m * p.ldy + n0;
+    const __nv_bfloat16* grow = p.gate + mr * (int64_t)p.N + n0;
+    if (p.y_raw) {
+      __nv_bfloat16* raw = p.y_raw + m * p.ldy + n0;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8)
+        *reinterpret_cast<uint4*>(raw + i) =
+            make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                       pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+      uint4 rv = *reinterpret_cast<const uint4*>(rrow + i);
+      uint4 gv = *reinterpret_cast<const uint4*>(grow + i);
+      const uint32_t ru[4] = {rv.x, rv.y, rv.z, rv.w}, gu[4] = {gv.x, gv.y, gv.z, gv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        o[q] = pack_bf16x2(bf16_lo(ru[q]) + v[i + 2 * q] * bf16_lo(gu[q]),
+                           bf16_hi(ru[q]) + v[i + 2 * q + 1] * bf16_hi(gu[q]));
+      *reinterpret_cast<uint4*>(yrow + i) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  } else {
+    if (p.epi == WX_EPI_GELU) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 8)
+      *reinterpret_cast<uint4*>(yrow + i) =
+          make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
+                     pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -220,56 +276,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_wait_ld();
         if (!row_ok) continue;
         const int64_t n0 = (int64_t)nb * BN + c * 32;
-        // t = bf16(acc) (+ bias, rounded again)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] = round_bf16(v[i]);
-        if (p.bias) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 bv = *reinterpret_cast<const uint4*>(p.bias + n0 + i);
-            const uint32_t bu[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              v[i + 2 * q] = round_bf16(v[i + 2 * q] + bf16_lo(bu[q]));
-              v[i + 2 * q + 1] = round_bf16(v[i + 2 * q + 1] + bf16_hi(bu[q]));
-            }
-          }
-        }
-        __nv_bfloat16* yrow = p.y + m * p.ldy + n0;
-        if (p.epi == WX_EPI_GATE_RESID) {
-          const __nv_bfloat16* rrow = p.resid + m * p.ldy + n0;
-          const __nv_bfloat16* grow = p.gate + mr * (int64_t)p.N + n0;
-          if (p.y_raw) {
-            __nv_bfloat16* raw = p.y_raw + m * p.ldy + n0;
-#pragma unroll
-            for (int i = 0; i < 32; i += 8)
-              *reinterpret_cast<uint4*>(raw + i) =
-                  make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
-                             pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
-          }
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 rv = *reinterpret_cast<const uint4*>(rrow + i);
-            uint4 gv = *reinterpret_cast<const uint4*>(grow + i);
-            const uint32_t ru[4] = {rv.x, rv.y, rv.z, rv.w}, gu[4] = {gv.x, gv.y, gv.z, gv.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              o[q] = pack_bf16x2(bf16_lo(ru[q]) + v[i + 2 * q] * bf16_lo(gu[q]),
-                                 bf16_hi(ru[q]) + v[i + 2 * q + 1] * bf16_hi(gu[q]));
-            *reinterpret_cast<uint4*>(yrow + i) = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        } else {
-          if (p.epi == WX_EPI_GELU) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = gelu_tanh_f(v[i]);
-          }
-#pragma unroll
-          for (int i = 0; i < 32; i += 8)
-            *reinterpret_cast<uint4*>(yrow + i) =
-                make_uint4(pack_bf16x2(v[i], v[i + 1]), pack_bf16x2(v[i + 2], v[i + 3]),
-                           pack_bf16x2(v[i + 4], v[i + 5]), pack_bf16x2(v[i + 6], v[i + 7]));
-        }
+        gemm_epilogue32(p, v, m, mr, n0);
       }
       tc_fence_before();
       mbar_arrive(acce_bar(acc));
