@@ -292,7 +292,7 @@ class Runner:
 
 
 # ------------------------------------------------------------------ CPU baseline
-def cpu_sample(c: dict, rows: int = 1024, att_rows: int = 384, seed: int = 99) -> dict:
+def cpu_sample(c: dict, rows: int = 2048, att_rows: int = 640, seed: int = 99) -> dict:
     """Bounded sample of the step on the host cores with the oracle (the reference
     algorithm restated in C): the four 6-bit linears on `rows` rows, the row kernels,
     and one head's attention for `att_rows` strip rows (dense) and `att_rows` video
