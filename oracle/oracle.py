@@ -39,6 +39,7 @@ _SIGS = {
                                          _vp, _i32, _i64, _i64, _vp, _i64]),
     "wxo_dense_f32": (_i32, [_vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "wxo_num_threads": (_i32, []),
+    "wxo_set_num_threads": (_i32, [_i32]),
 }
 
 _lib = None
@@ -266,6 +267,11 @@ def dense_f32(x, w, b=None):
 
 def num_threads() -> int:
     return lib().wxo_num_threads()
+
+
+def set_num_threads(n: int = 0) -> int:
+    """OpenMP threads of later oracle calls, overriding OMP_NUM_THREADS (n <= 0: all processors)."""
+    return lib().wxo_set_num_threads(int(n))
 
 
 # ---------------------------------------------------------------- block composition

@@ -23,6 +23,19 @@ int wxo_num_threads(void) {
 #endif
 }
 
+/* OpenMP threads of every later oracle call, whatever OMP_NUM_THREADS says (a launcher such
+ * as torchrun sets it to 1); n <= 0 selects every processor the runtime reports */
+int wxo_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n <= 0) n = omp_get_num_procs();
+  omp_set_num_threads(n);
+  return omp_get_max_threads();
+#else
+  (void)n;
+  return 1;
+#endif
+}
+
 /* ------------------------------------------------------------------ bf16 */
 float wxo_bf2f(uint16_t h) {
   uint32_t u = ((uint32_t)h) << 16;
@@ -161,6 +174,37 @@ static inline float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
 }
 
+/* t[r][c] = sum over i = 0, 1, ..., k-1 of (double)xf[r][i] * (double)wf[c][i], in that
+ * order, for a 4 x 4 block of outputs at once: the sixteen accumulators are independent,
+ * so the adds of one output do not wait on one another's latency, and every output still
+ * takes exactly the sequence acc = acc + x*w of the one-output loop. Rows/columns past the
+ * edge repeat the last valid one and are not stored. */
+__attribute__((target_clones("avx2", "default"))) static void dot_block4(const float* xf, int64_t m, const float* wf, int64_t n, int64_t k, int64_t r0, int64_t c0,
+                       double* out /* [4][4] */) {
+  const float* xr[4];
+  const float* wr[4];
+  for (int j = 0; j < 4; ++j) {
+    const int64_t r = r0 + j < m ? r0 + j : m - 1;
+    const int64_t c = c0 + j < n ? c0 + j : n - 1;
+    xr[j] = xf + r * k;
+    wr[j] = wf + c * k;
+  }
+  double a00 = 0, a01 = 0, a02 = 0, a03 = 0, a10 = 0, a11 = 0, a12 = 0, a13 = 0;
+  double a20 = 0, a21 = 0, a22 = 0, a23 = 0, a30 = 0, a31 = 0, a32 = 0, a33 = 0;
+  for (int64_t i = 0; i < k; ++i) {
+    const double x0 = xr[0][i], x1 = xr[1][i], x2 = xr[2][i], x3 = xr[3][i];
+    const double w0 = wr[0][i], w1 = wr[1][i], w2 = wr[2][i], w3 = wr[3][i];
+    a00 += x0 * w0; a01 += x0 * w1; a02 += x0 * w2; a03 += x0 * w3;
+    a10 += x1 * w0; a11 += x1 * w1; a12 += x1 * w2; a13 += x1 * w3;
+    a20 += x2 * w0; a21 += x2 * w1; a22 += x2 * w2; a23 += x2 * w3;
+    a30 += x3 * w0; a31 += x3 * w1; a32 += x3 * w2; a33 += x3 * w3;
+  }
+  out[0] = a00; out[1] = a01; out[2] = a02; out[3] = a03;
+  out[4] = a10; out[5] = a11; out[6] = a12; out[7] = a13;
+  out[8] = a20; out[9] = a21; out[10] = a22; out[11] = a23;
+  out[12] = a30; out[13] = a31; out[14] = a32; out[15] = a33;
+}
+
 int wxo_qlinear(const uint16_t* x, int64_t m, int64_t k,
                 const uint32_t* wq, const uint16_t* scales, const uint16_t* biases,
                 int64_t n, int group, int bits, const uint16_t* bias, int epilogue,
@@ -169,50 +213,58 @@ int wxo_qlinear(const uint16_t* x, int64_t m, int64_t k,
   if (!quant_geometry_ok(k, group, bits) || m < 0 || n <= 0) return -1;
   if (epilogue == WXO_EPI_SWIGLU && (n & 1)) return -1;
   if (epilogue == WXO_EPI_GATE_RESID && (!gate || !resid)) return -1;
+  if (m == 0) return 0;
   uint16_t* wd = (uint16_t*)malloc((size_t)n * k * 2);
   float* wf = (float*)malloc((size_t)n * k * 4);
-  if (!wd || !wf) { free(wd); free(wf); return -2; }
+  float* xf = (float*)malloc((size_t)m * k * 4);
+  float* t = (float*)malloc((size_t)m * n * 4);
+  if (!wd || !wf || !xf || !t) { free(wd); free(wf); free(xf); free(t); return -2; }
   wxo_dequantize_affine(wq, scales, biases, n, k, group, bits, wd);
   wxo_bf16_to_f32(wd, wf, n * k);
   free(wd);
-  const int64_t F = n / 2;
-#pragma omp parallel
-  {
-    float* xr = (float*)malloc((size_t)k * 4);
-    float* t = (float*)malloc((size_t)n * 4);
-#pragma omp for schedule(dynamic, 4)
-    for (int64_t r = 0; r < m; ++r) {
-      for (int64_t i = 0; i < k; ++i) xr[i] = bf(x[r * k + i]);
-      for (int64_t c = 0; c < n; ++c) {
-        const float* wr = wf + c * k;
-        double acc = 0.0;
-        for (int64_t i = 0; i < k; ++i) acc += (double)xr[i] * (double)wr[i];
-        float tv = rbf((float)acc);
-        if (bias) tv = rbf(tv + bf(bias[c]));
-        t[c] = tv;
+  wxo_bf16_to_f32(x, xf, m * k);
+  /* t = bf16(acc), then bf16(t + bias): 32 x 32 output tiles per task, 4 x 4 blocks inside */
+  const int64_t mt = (m + 31) / 32, nt = (n + 31) / 32;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int64_t tile = 0; tile < mt * nt; ++tile) {
+    const int64_t rt = (tile / nt) * 32, ct = (tile % nt) * 32;
+    double blk[16];
+    for (int64_t r0 = rt; r0 < rt + 32 && r0 < m; r0 += 4)
+      for (int64_t c0 = ct; c0 < ct + 32 && c0 < n; c0 += 4) {
+        dot_block4(xf, m, wf, n, k, r0, c0, blk);
+        for (int a = 0; a < 4 && r0 + a < m; ++a)
+          for (int b = 0; b < 4 && c0 + b < n; ++b) {
+            float tv = rbf((float)blk[a * 4 + b]);
+            if (bias) tv = rbf(tv + bf(bias[c0 + b]));
+            t[(r0 + a) * n + c0 + b] = tv;
+          }
       }
-      const uint32_t mr = rowmap ? rowmap[r] : 0u;
-      if (epilogue == WXO_EPI_SWIGLU) {
-        for (int64_t j = 0; j < F; ++j) {
-          float gt = t[j], up = t[F + j];
-          float silu = gt / (1.0f + expf(-gt));
-          y[r * F + j] = wxo_f2bf(silu * up);
-        }
-      } else {
-        for (int64_t c = 0; c < n; ++c) {
-          float o;
-          if (epilogue == WXO_EPI_GELU) o = gelu_tanh(t[c]);
-          else if (epilogue == WXO_EPI_GATE_RESID) o = bf(resid[r * n + c]) + t[c] * bf(gate[(int64_t)mr * n + c]);
-          else o = t[c];
-          y[r * n + c] = wxo_f2bf(o);
-          if (y_raw) y_raw[r * n + c] = wxo_f2bf(t[c]);
-        }
-      }
-    }
-    free(xr);
-    free(t);
   }
   free(wf);
+  free(xf);
+  const int64_t F = n / 2;
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < m; ++r) {
+    const float* tr = t + r * n;
+    const uint32_t mr = rowmap ? rowmap[r] : 0u;
+    if (epilogue == WXO_EPI_SWIGLU) {
+      for (int64_t j = 0; j < F; ++j) {
+        float gt = tr[j], up = tr[F + j];
+        float silu = gt / (1.0f + expf(-gt));
+        y[r * F + j] = wxo_f2bf(silu * up);
+      }
+    } else {
+      for (int64_t c = 0; c < n; ++c) {
+        float o;
+        if (epilogue == WXO_EPI_GELU) o = gelu_tanh(tr[c]);
+        else if (epilogue == WXO_EPI_GATE_RESID) o = bf(resid[r * n + c]) + tr[c] * bf(gate[(int64_t)mr * n + c]);
+        else o = tr[c];
+        y[r * n + c] = wxo_f2bf(o);
+        if (y_raw) y_raw[r * n + c] = wxo_f2bf(tr[c]);
+      }
+    }
+  }
+  free(t);
   return 0;
 }
 
@@ -306,6 +358,26 @@ static void block_stats(const uint16_t* src, int64_t row_stride, int64_t S, int 
     }
 }
 
+/* acc[t] = fma-chain over d = 0, 1, ... of qr[d] * kr[t*hd + d] for the next (up to) four
+ * key blocks: four independent chains, each in the one-block order */
+static inline void score_chains4(const float* qr, const float* kr, int avail, int hd, float* acc) {
+  const float* k0 = kr;
+  const float* k1 = avail > 1 ? kr + hd : kr;
+  const float* k2 = avail > 2 ? kr + 2 * hd : kr;
+  const float* k3 = avail > 3 ? kr + 3 * hd : kr;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  for (int d = 0; d < hd; ++d) {
+    a0 = fmaf(qr[d], k0[d], a0);
+    a1 = fmaf(qr[d], k1[d], a1);
+    a2 = fmaf(qr[d], k2[d], a2);
+    a3 = fmaf(qr[d], k3[d], a3);
+  }
+  acc[0] = a0;
+  acc[1] = a1;
+  acc[2] = a2;
+  acc[3] = a3;
+}
+
 static int route_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64_t row_stride,
                         int64_t S, int H, int hd, int64_t g, int block, int* nb_out,
                         float** qc, float** kc, uint16_t* vsum, float* lens) {
@@ -361,10 +433,10 @@ int wxo_sol_route(const uint16_t* q, const uint16_t* k, const uint16_t* v, int64
       for (int d = 0; d < hd; ++d) var += (qr[d] * qr[d]) * kvar[(int64_t)h * hd + d];
       const float th = tau * sqrtf(var * (scale * scale) + 1e-6f);
       thr[(int64_t)h * nb + i] = th;
+      float accs[4];
       for (int j = 0; j < nb; ++j) {
-        const float* kr = kc + ((int64_t)h * nb + j) * hd;
-        float acc = 0.f;
-        for (int d = 0; d < hd; ++d) acc = fmaf(qr[d], kr[d], acc);
+        if ((j & 3) == 0) score_chains4(qr, kc + ((int64_t)h * nb + j) * hd, nb - j, hd, accs);
+        const float acc = accs[j & 3];
         uint16_t c = wxo_f2bf(acc * scale);
         const int64_t idx = ((int64_t)h * nb + i) * nb + j;
         cm[idx] = c;
@@ -407,10 +479,10 @@ int wxo_topk_route(const uint16_t* q, const uint16_t* k, const uint16_t* v, int6
     for (int i = 0; i < nb; ++i) {
       const float* qr = qc + ((int64_t)h * nb + i) * hd;
       float* sr = scores + ((int64_t)h * nb + i) * nb;
+      float accs[4];
       for (int j = 0; j < nb; ++j) {
-        const float* kr = kc + ((int64_t)h * nb + j) * hd;
-        float acc = 0.f;
-        for (int d = 0; d < hd; ++d) acc = fmaf(qr[d], kr[d], acc);
+        if ((j & 3) == 0) score_chains4(qr, kc + ((int64_t)h * nb + j) * hd, nb - j, hd, accs);
+        const float acc = accs[j & 3];
         sr[j] = acc * scale;
         cm[((int64_t)h * nb + i) * nb + j] = wxo_f2bf(sr[j]);
       }
@@ -436,25 +508,59 @@ int wxo_topk_route(const uint16_t* q, const uint16_t* k, const uint16_t* v, int6
 }
 
 /* ------------------------------------------------------------- attention */
+/* Online softmax of up to ATT_G query rows that see the same keys in the same order
+ * (strip rows, or the rows of one video query block). Every row takes exactly the
+ * one-row sequence of operations: s = sum_d q[d]*k[d] in ascending d (fp32), s *= scale,
+ * m2 = max(m, s), a = exp(m - m2), p = exp(s - m2), acc = acc*a + p*v, l = l*a + p.
+ * The rows are only interleaved (independent chains), which changes no result. */
+#define ATT_G 8
 typedef struct {
-  float m, l;
-  float acc[256];
-} soft_state;
+  float m[ATT_G], l[ATT_G];
+  float acc[ATT_G][256];
+} soft_group;
 
-static inline void feed_rows(soft_state* st, const float* qv, const uint16_t* k, const uint16_t* v,
-                             int64_t row_stride, int h, int hd, int64_t r0, int64_t r1, float scale) {
+__attribute__((target_clones("avx2", "default"))) static void feed_rows_g(soft_group* st, const float (*qv)[256], const uint16_t* k, const uint16_t* v,
+                        int64_t row_stride, int h, int hd, int64_t r0, int64_t r1, float scale) {
+  float kf[256], vf[256];
   for (int64_t r = r0; r < r1; ++r) {
     const uint16_t* kr = k + r * row_stride + (int64_t)h * hd;
     const uint16_t* vr = v + r * row_stride + (int64_t)h * hd;
-    float s = 0.f;
-    for (int d = 0; d < hd; ++d) s += qv[d] * bf(kr[d]);
-    s *= scale;
-    const float m2 = s > st->m ? s : st->m;
-    const float a = expf(st->m - m2);
-    const float p = expf(s - m2);
-    for (int d = 0; d < hd; ++d) st->acc[d] = st->acc[d] * a + p * bf(vr[d]);
-    st->l = st->l * a + p;
-    st->m = m2;
+    for (int d = 0; d < hd; ++d) {
+      kf[d] = bf(kr[d]);
+      vf[d] = bf(vr[d]);
+    }
+    float s[ATT_G];
+    for (int j = 0; j < ATT_G; ++j) s[j] = 0.f;
+    for (int d = 0; d < hd; ++d)
+      for (int j = 0; j < ATT_G; ++j) s[j] += qv[j][d] * kf[d];
+    for (int j = 0; j < ATT_G; ++j) {
+      const float sj = s[j] * scale;
+      const float m2 = sj > st->m[j] ? sj : st->m[j];
+      const float a = expf(st->m[j] - m2);
+      const float p = expf(sj - m2);
+      float* acc = st->acc[j];
+      for (int d = 0; d < hd; ++d) acc[d] = acc[d] * a + p * vf[d];
+      st->l[j] = st->l[j] * a + p;
+      st->m[j] = m2;
+    }
+  }
+}
+
+/* the SOL tail term of one unselected block for every row of the group */
+static void feed_tail_g(soft_group* st, float sc, float len, const uint16_t* vs, int hd) {
+  for (int j = 0; j < ATT_G; ++j) {
+    const float m2 = sc > st->m[j] ? sc : st->m[j];
+    const float a = expf(st->m[j] - m2);
+    const float p = expf(sc - m2);
+    float* acc = st->acc[j];
+    if (len > 0.f) {
+      for (int d = 0; d < hd; ++d) acc[d] = acc[d] * a + p * bf(vs[d]);
+      st->l[j] = st->l[j] * a + p * len;
+    } else {
+      for (int d = 0; d < hd; ++d) acc[d] *= a;
+      st->l[j] *= a;
+    }
+    st->m[j] = m2;
   }
 }
 
@@ -475,48 +581,61 @@ int wxo_sparse_attention_rows(const uint16_t* q, const uint16_t* k, const uint16
   if (sel && (S <= g || block <= 0)) return -1;
   const int64_t L = S - g;
   const int nb = sel ? (int)((L + block - 1) / block) : 0;
-#pragma omp parallel for collapse(2) schedule(dynamic, 8)
+  /* groups of <= ATT_G consecutive rows with the same keys: strip rows (all of S), or
+   * the rows of one video query block */
+  int64_t ngroups = 0;
+  int64_t* gstart = (int64_t*)malloc((size_t)(row1 - row0 + 1) * sizeof(int64_t));
+  if (!gstart) return -2;
+  for (int64_t s = row0; s < row1;) {
+    int64_t end;
+    if (!sel) end = row1;
+    else if (s < g) end = g;
+    else end = g + ((s - g) / block + 1) * block;
+    if (end > row1) end = row1;
+    if (end > s + ATT_G) end = s + ATT_G;
+    gstart[ngroups++] = s;
+    s = end;
+  }
+  gstart[ngroups] = row1;
+#pragma omp parallel for collapse(2) schedule(dynamic, 2)
   for (int h = 0; h < H; ++h)
-    for (int64_t s = row0; s < row1; ++s) {
-      soft_state st;
-      st.m = -INFINITY;
-      st.l = 0.f;
-      for (int d = 0; d < hd; ++d) st.acc[d] = 0.f;
-      float qv[256];
-      for (int d = 0; d < hd; ++d) qv[d] = bf(q[s * row_stride + (int64_t)h * hd + d]);
-      if (!sel || s < g) {
-        feed_rows(&st, qv, k, v, row_stride, h, hd, 0, S, scale);
+    for (int64_t gi = 0; gi < ngroups; ++gi) {
+      const int64_t s0 = gstart[gi], s1 = gstart[gi + 1];
+      soft_group* st = (soft_group*)malloc(sizeof(soft_group));
+      float(*qv)[256] = (float(*)[256])malloc(sizeof(float) * ATT_G * 256);
+      for (int j = 0; j < ATT_G; ++j) {
+        const int64_t s = s0 + j < s1 ? s0 + j : s1 - 1; /* padding rows repeat the last row */
+        st->m[j] = -INFINITY;
+        st->l[j] = 0.f;
+        for (int d = 0; d < hd; ++d) st->acc[j][d] = 0.f;
+        for (int d = 0; d < hd; ++d) qv[j][d] = bf(q[s * row_stride + (int64_t)h * hd + d]);
+      }
+      if (!sel || s0 < g) {
+        feed_rows_g(st, (const float(*)[256])qv, k, v, row_stride, h, hd, 0, S, scale);
       } else {
-        feed_rows(&st, qv, k, v, row_stride, h, hd, 0, g, scale);
-        const int qb = (int)((s - g) / block);
+        feed_rows_g(st, (const float(*)[256])qv, k, v, row_stride, h, hd, 0, g, scale);
+        const int qb = (int)((s0 - g) / block);
         for (int j = 0; j < nb; ++j) {
           const int64_t idx = ((int64_t)h * nb + qb) * nb + j;
           if (sel[idx]) {
             int64_t r0 = g + (int64_t)j * block, r1 = r0 + block;
             if (r1 > S) r1 = S;
-            feed_rows(&st, qv, k, v, row_stride, h, hd, r0, r1, scale);
+            feed_rows_g(st, (const float(*)[256])qv, k, v, row_stride, h, hd, r0, r1, scale);
           } else if (tail) {
-            const float sc = bf(cm[idx]);
-            const float m2 = sc > st.m ? sc : st.m;
-            const float a = expf(st.m - m2);
-            const float p = expf(sc - m2);
-            const float len = lens[j];
-            const uint16_t* vs = vsum + ((int64_t)h * nb + j) * hd;
-            if (len > 0.f) {
-              for (int d = 0; d < hd; ++d) st.acc[d] = st.acc[d] * a + p * bf(vs[d]);
-              st.l = st.l * a + p * len;
-            } else {
-              for (int d = 0; d < hd; ++d) st.acc[d] *= a;
-              st.l *= a;
-            }
-            st.m = m2;
+            feed_tail_g(st, bf(cm[idx]), lens[j], vsum + ((int64_t)h * nb + j) * hd, hd);
           }
         }
       }
-      const float inv = 1.0f / st.l;
-      uint16_t* orow = out + s * out_stride + (int64_t)h * hd;
-      for (int d = 0; d < hd; ++d) orow[d] = wxo_f2bf(st.acc[d] * inv);
+      for (int64_t s = s0; s < s1; ++s) {
+        const int j = (int)(s - s0);
+        const float inv = 1.0f / st->l[j];
+        uint16_t* orow = out + s * out_stride + (int64_t)h * hd;
+        for (int d = 0; d < hd; ++d) orow[d] = wxo_f2bf(st->acc[j][d] * inv);
+      }
+      free(st);
+      free(qv);
     }
+  free(gstart);
   return 0;
 }
 

@@ -135,6 +135,8 @@ int wxo_dense_f32(const float* x, int64_t m, int64_t k, const float* w, int64_t 
                   const float* b, float* y);
 
 int wxo_num_threads(void);
+/* OpenMP threads of later calls (n <= 0: every processor); returns the count now in force */
+int wxo_set_num_threads(int n);
 
 #ifdef __cplusplus
 }
