@@ -60,7 +60,7 @@ PAB_MAX_STALE = 0.06    # lifts the reference default 0.04 so step 2 is reused (
 EPS = 1e-6
 ROT = 96                # 3 axes x 16 inverse frequencies x 2
 # DRAM bytes (read + write) of one attention call of the config-5 step, weighted over its
-# 6 dense + 42 top-k layers, from one ncu capture (profiles/traffic_attention_c5.md)
+# 6 dense + 42 top-k layers, from one ncu capture of the attention kernels
 ATTN_TRAFFIC_C5 = (6 * 10.1699e9 + 42 * 12.8100e9) / 48
 
 
@@ -601,8 +601,7 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     ach_attn = attn_flops / (attn_ms / 1e3) / 1e12 if attn_ms > 0 else 0.0
     ach_gemm = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
     if attn_ms >= gemm_ms:
-        # DRAM bytes per attention call from one ncu capture of this workload
-        # (profiles/traffic_attention_c5.md); a rank holds 1/world of the heads
+        # DRAM bytes per attention call from one ncu capture; a rank holds 1/world of the heads
         traffic = ATTN_TRAFFIC_C5 / world if c["name"] == "c5" else None
         roof = dict(kernel="flash_attn_pair_kernel <paired> + <duo> (tcgen05 sparse/dense flash attention)", bound="tensor",
                     achieved=ach_attn, peak=peak_t, unit="TFLOP/s", frac=ach_attn / peak_t,
