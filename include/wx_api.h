@@ -202,13 +202,23 @@ int wx_qlinear_lora(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx
  * weight lives in a 64 MiB static device array inside libwx, created on every
  * GPU that loads the library and held until exit, so w->n * w->k may be at
  * most 33,554,432; larger weights, and WX_EPI_SWIGLU, are rejected
- * (WX_ERR_INVALID / WX_ERR_UNSUPPORTED). The first call on a device looks up
- * the array's address (cudaGetSymbolAddress); make that first call before any
- * stream capture. All calls share the array: calls that overlap on the GPU
- * race. Other arguments and results are those of wx_qlinear. */
+ * (WX_ERR_INVALID / WX_ERR_UNSUPPORTED). With CUDA's lazy module loading (the
+ * default) the array is reserved on a device at the first call there, and that
+ * call also looks up its address (cudaGetSymbolAddress): make the first call on
+ * each device during set-up, before any stream capture. All calls share the
+ * array: calls that overlap on the GPU race. Other arguments and results are
+ * those of wx_qlinear; a failure's message is in wx_qlinear_noalloc_last_error. */
 int wx_qlinear_noalloc(void* stream, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
                        int epilogue, const void* gate, const void* resid, const uint32_t* rowmap,
                        void* y, int64_t ldy, void* y_raw);
+/* No counterpart in the reference. Device-side status of the wx_qlinear_noalloc
+ * calls on the current device: synchronises `stream`, reads the error word their
+ * kernels write when a bounded wait expires, clears it, and returns WX_ERR_DEVICE
+ * if it was set (WX_OK otherwise). Allocates nothing. */
+int wx_qlinear_noalloc_check(void* stream);
+/* No counterpart in the reference. Message of the last failed wx_qlinear_noalloc
+ * or wx_qlinear_noalloc_check call on this thread. */
+const char* wx_qlinear_noalloc_last_error(void);
 
 /* ------------------------------------------------------ checkpoints */
 /* Safetensors container (H3Weights, H3Common.swift:180-261): the file is mapped

@@ -127,6 +127,8 @@ _SIGS = {
     "wx_qlinear_lora": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), C.POINTER(LoraPack), _i32, _vp, _vp, _vp,
                                _vp, _i64, _vp]),
     "wx_qlinear_noalloc": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
+    "wx_qlinear_noalloc_check": (_i32, [_vp]),
+    "wx_qlinear_noalloc_last_error": (C.c_char_p, []),
     "wx_st_open": (_i32, [C.c_char_p, C.POINTER(_vp)]),
     "wx_st_close": (_i32, [_vp]),
     "wx_st_last_error": (C.c_char_p, []),

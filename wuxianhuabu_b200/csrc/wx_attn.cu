@@ -580,8 +580,8 @@ static int run_routing(wx_ctx* ctx, const void* q, const void* k, const void* v,
     int keep = (int)std::min<double>(want, a.nb - 1);
     if (keep < 0) keep = 0;
     const size_t smem = (size_t)a.nb * 4;
-    if (smem > 48 * 1024)
-      cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > 48 * 1024 && (st = ensure_smem_attr(ctx, (const void*)topk_select_kernel, (int)smem, "topk_select")))
+      return st;
     topk_select_kernel<<<dim3(a.nb, a.H), 256, smem, ctx->stream>>>(scores, a.nb, keep, sel);
     st = launch_status(ctx, "topk_select");
     if (st) return st;
@@ -697,20 +697,24 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   if ((st = make_tmap_bf16_2d(ctx, &tq, q, (uint64_t)a.S, (uint64_t)cols, (uint64_t)rs, 64, 64))) return st;
   if ((st = make_tmap_bf16_2d(ctx, &tk, k, (uint64_t)a.S, (uint64_t)cols, (uint64_t)rs, 64, 64))) return st;
   if ((st = make_tmap_bf16_2d(ctx, &tv, v, (uint64_t)a.S, (uint64_t)cols, (uint64_t)rs, 64, 64))) return st;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaSuccess;
-    for (auto fn : {flash_attn_kernel<0>, flash_attn_kernel<1>, flash_attn_kernel<2>})
-      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
-    for (auto fn : {flash_attn2_kernel<0>, flash_attn2_kernel<1>, flash_attn2_kernel<2>})
-      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA2Smem);
-    for (auto fn : {flash_attn4_kernel<0>, flash_attn4_kernel<1>, flash_attn4_kernel<2>})
-      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA4Smem);
-    for (auto fn : {flash_attn_pair_kernel<0, false>, flash_attn_pair_kernel<1, false>, flash_attn_pair_kernel<2, false>,
-                    flash_attn_pair_kernel<0, true>, flash_attn_pair_kernel<1, true>, flash_attn_pair_kernel<2, true>})
-      if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kA5Smem);
-    if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "attn smem attribute: %s", cudaGetErrorString(e));
-    attr = true;
+  {
+    struct KS {
+      const void* fn;
+      int bytes;
+    };
+    const KS ks[] = {{(const void*)flash_attn_kernel<0>, kAttnSmem}, {(const void*)flash_attn_kernel<1>, kAttnSmem},
+                     {(const void*)flash_attn_kernel<2>, kAttnSmem}, {(const void*)flash_attn2_kernel<0>, kA2Smem},
+                     {(const void*)flash_attn2_kernel<1>, kA2Smem}, {(const void*)flash_attn2_kernel<2>, kA2Smem},
+                     {(const void*)flash_attn4_kernel<0>, kA4Smem}, {(const void*)flash_attn4_kernel<1>, kA4Smem},
+                     {(const void*)flash_attn4_kernel<2>, kA4Smem},
+                     {(const void*)flash_attn_pair_kernel<0, false>, kA5Smem},
+                     {(const void*)flash_attn_pair_kernel<1, false>, kA5Smem},
+                     {(const void*)flash_attn_pair_kernel<2, false>, kA5Smem},
+                     {(const void*)flash_attn_pair_kernel<0, true>, kA5Smem},
+                     {(const void*)flash_attn_pair_kernel<1, true>, kA5Smem},
+                     {(const void*)flash_attn_pair_kernel<2, true>, kA5Smem}};
+    for (const KS& k2 : ks)
+      if ((st = ensure_smem_attr(ctx, k2.fn, k2.bytes, "flash attention"))) return st;
   }
   AttnParams p{};
   p.items = items;

@@ -9,6 +9,8 @@
 
 #include <algorithm>
 #include <mutex>
+#include <map>
+#include <utility>
 
 #include "wx_internal.h"
 #include "wx_ptx.cuh"
@@ -88,6 +90,24 @@ int launch_status(wx_ctx* ctx, const char* what, int n) {
   ctx->launches += n;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return WX_OK;
+}
+
+int ensure_smem_attr(wx_ctx* ctx, const void* fn, int bytes, const char* what) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> limit set so far
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "%s: cudaGetDevice: %s", what, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair(fn, dev);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return WX_OK;  // the limit only ever grows
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return set_error(ctx, WX_ERR_CUDA, "%s shared-memory attribute (%d bytes, device %d): %s", what, bytes, dev,
+                     cudaGetErrorString(e));
+  done[key] = bytes;
   return WX_OK;
 }
 

@@ -295,13 +295,8 @@ template <int BN>
 static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
                           const CUtensorMap& tb2, GemmParams& p) {
   using L = GemmSmem<BN>;
-  static bool attr_done = false;
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         L::kBytes);
-    if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "gemm smem attribute: %s", cudaGetErrorString(e));
-    attr_done = true;
-  }
+  int st = ensure_smem_attr(ctx, (const void*)gemm_bf16_tc_kernel<BN>, L::kBytes, "gemm_bf16_tc");
+  if (st) return st;
   p.tiles_m = (p.M + kGemmBM - 1) / kGemmBM;
   p.tiles_n = p.N / BN;
   p.num_tiles = p.tiles_m * p.tiles_n;

@@ -275,14 +275,10 @@ bool fused_eligible(const wx_qweight* w, int64_t M, int epilogue) {
 int qlinear_fused(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const wx_qweight* w, int epilogue,
                   const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw,
                   void* scratch) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_q6_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem);
-    if (e != cudaSuccess) return set_error(ctx, WX_ERR_CUDA, "fused gemm smem attribute: %s", cudaGetErrorString(e));
-    attr = true;
-  }
+  int st = ensure_smem_attr(ctx, (const void*)gemm_q6_fused_kernel, kFSmem, "gemm_q6_fused");
+  if (st) return st;
   CUtensorMap ta;
-  int st = make_tmap_bf16_2d(ctx, &ta, x, (uint64_t)M, (uint64_t)w->k, (uint64_t)lda, kFBK, 128);
+  st = make_tmap_bf16_2d(ctx, &ta, x, (uint64_t)M, (uint64_t)w->k, (uint64_t)lda, kFBK, 128);
   if (st) return st;
   float* part = static_cast<float*>(scratch);
   const int n_tiles = (int)(w->n / kFBN);

@@ -90,6 +90,12 @@ void sp_p2p_release(wx_ctx* ctx);
 // checks the last launch(es) and counts `n` kernel launches on the context
 int launch_status(wx_ctx* ctx, const char* what, int n = 1);
 
+// Raises kernel `fn`'s dynamic shared-memory limit to at least `bytes` on the CURRENT
+// device (the limit only grows; set once per kernel and device): cudaFuncSetAttribute acts
+// on one device only, so a process that drives several GPUs needs it on each.
+// Thread-safe. WX_OK or a status set on ctx.
+int ensure_smem_attr(wx_ctx* ctx, const void* fn, int bytes, const char* what);
+
 enum ProfKind { kProfGemm = 0, kProfAttn = 1, kProfRoute = 2, kProfRow = 3, kProfDequant = 4, kProfOther = 5,
                 kProfKinds = 6 };
 
