@@ -292,70 +292,88 @@ class Runner:
 
 
 # ------------------------------------------------------------------ CPU baseline
-def cpu_sample(c: dict, rows: int = 2048, att_rows: int = 640, seed: int = 99) -> dict:
+class CpuSample:
     """Bounded sample of the step on the host cores with the oracle (the reference
-    algorithm restated in C): the four 6-bit linears on `rows` rows, the row kernels,
-    and one head's attention for `att_rows` strip rows (dense) and `att_rows` video
-    rows (strip + top-k kept blocks). Extrapolated to s/step over the PAB window."""
-    from oracle import oracle as O
-    hdn, inner, ffn, S, g, H = c["hidden"], c["inner"], c["ffn"], c["S"], c["g"], c["heads"]
-    t0 = time.perf_counter()
-    lin = {}
-    for i, (name, n, k) in enumerate([("qkv", 3 * inner, hdn), ("out", hdn, inner), ("fc1", ffn, hdn),
-                                      ("fc2", hdn, ffn)]):
-        lin[name] = O.quantize(O.normal_f32((n, k), seed, i, std=0.02))
-    x = O.normal_bf16((rows, hdn), seed, 10)
-    xi = O.normal_bf16((rows, inner), seed, 11)
-    xf = O.normal_bf16((rows, ffn), seed, 12)
-    q = O.normal_bf16((S, 1, 128), seed, 13)
-    k = O.normal_bf16((S, 1, 128), seed, 14)
-    v = O.normal_bf16((S, 1, 128), seed, 15)
-    prep = time.perf_counter() - t0
+    algorithm restated in C, OpenMP on every host thread): the four 6-bit linears on
+    `rows` rows, the row kernels, and one head's routing and attention for `att_rows`
+    strip rows (dense over all S keys) and `att_rows` video rows (strip + top-k kept
+    blocks). Inputs and quantized weights are prepared once; run() times one sample and
+    extrapolates it linearly in rows / heads / layers to s/step over the PAB window."""
 
-    def tm(fn):
-        a = time.perf_counter()
-        fn()
-        return time.perf_counter() - a
+    def __init__(self, c: dict, plan: list, rows: int = 1024, att_rows: int = 384, seed: int = 99):
+        from oracle import oracle as O
+        O.build()
+        self.threads = O.set_num_threads(0)  # every host thread, whatever OMP_NUM_THREADS says
+        self.O, self.c, self.plan, self.rows, self.att_rows = O, c, list(plan), rows, att_rows
+        hdn, inner, ffn, S = c["hidden"], c["inner"], c["ffn"], c["S"]
+        t0 = time.perf_counter()
+        self.lin = {}
+        for i, (name, n, k) in enumerate([("qkv", 3 * inner, hdn), ("out", hdn, inner), ("fc1", ffn, hdn),
+                                          ("fc2", hdn, ffn)]):
+            self.lin[name] = O.quantize(O.normal_f32((n, k), seed, i, std=0.02))
+        self.x = O.normal_bf16((rows, hdn), seed, 10)
+        self.xi = O.normal_bf16((rows, inner), seed, 11)
+        self.xf = O.normal_bf16((rows, ffn), seed, 12)
+        self.q = O.normal_bf16((S, 1, 128), seed, 13)
+        self.k = O.normal_bf16((S, 1, 128), seed, 14)
+        self.v = O.normal_bf16((S, 1, 128), seed, 15)
+        self.w1 = O.normal_bf16((hdn,), seed, 16)
+        self.mods = O.normal_bf16((4, hdn), seed, 17)
+        self.prep_s = time.perf_counter() - t0
+        self.sample = (f"oracle (C, OpenMP, {self.threads} threads) on {rows} rows through the 4 six-bit linears + "
+                       f"row kernels and 1 of {c['heads']} heads' routing and attention for {att_rows} strip + "
+                       f"{att_rows} video query rows at S={S}; extrapolated linearly in rows/heads/layers over the "
+                       f"PAB window {self.plan}")
 
-    # each oracle qlinear call expands its whole weight once (a per-layer cost) and then
-    # does per-row work: split the two so the extrapolation scales only the row part
-    t_dq = {n: tm(lambda n=n, k=k: O.dequantize(*lin[n], k)) for n, k in
-            (("qkv", hdn), ("out", inner), ("fc1", hdn), ("fc2", ffn))}
-    t_qkv = tm(lambda: O.qlinear(x, *lin["qkv"])) - t_dq["qkv"]
-    t_out = tm(lambda: O.qlinear(xi, *lin["out"])) - t_dq["out"]
-    t_fc1 = tm(lambda: O.qlinear(x, *lin["fc1"], epilogue=O.EPI_GELU)) - t_dq["fc1"]
-    t_fc2 = tm(lambda: O.qlinear(xf, *lin["fc2"])) - t_dq["fc2"]
-    w1 = O.normal_bf16((hdn,), seed, 16)
-    mods = O.normal_bf16((4, hdn), seed, 17)
-    rm = np.zeros(rows, np.uint32)
-    t_norm = tm(lambda: O.norm_modscale(x, w1, mods, mods, rm, EPS))
-    scale = float(1 / np.sqrt(128))
-    t_route = tm(lambda: O.topk_route(q, k, v, g, scale, TOPK_DENSITY))
-    route = O.topk_route(q, k, v, g, scale, TOPK_DENSITY)
-    route.update(g=g, block=128)
-    t_strip = tm(lambda: O.attention_rows(q, k, v, g, scale, 0, att_rows, route=route))
-    t_video = tm(lambda: O.attention_rows(q, k, v, g, scale, g, g + att_rows, route=route))
-    # extrapolation to the full step
-    per_row = lambda t: t / rows
-    gemm_attn_rows = per_row(t_qkv) + per_row(t_out) * (inner / inner)
-    gemm_mlp_rows = per_row(t_fc1) + per_row(t_fc2)
-    rowops = per_row(t_norm) * 4  # norm1, norm2, q/k rope (~norm cost), gate
-    attn_sparse = H * (t_strip / att_rows * g + t_video / att_rows * (S - g)) + H * t_route
-    attn_dense = H * (t_strip / att_rows * S)
-    L = c["layers"]
-    n_dense = sum(1 for lyr in range(L) if _is_dense(lyr, L))
-    dq_attn = t_dq["qkv"] + t_dq["out"]
-    dq_mlp = t_dq["fc1"] + t_dq["fc2"]
-    refresh_step = (L * (S * (gemm_attn_rows + gemm_mlp_rows + rowops) + dq_attn + dq_mlp)
-                    + n_dense * attn_dense + (L - n_dense) * attn_sparse)
-    reuse_step = L * (S * (gemm_mlp_rows + rowops * 0.5) + dq_mlp)
-    plan = [True, True, False, True]
-    s_per_step = sum(refresh_step if r else reuse_step for r in plan) / len(plan)
-    sampled = t_qkv + t_out + t_fc1 + t_fc2 + sum(t_dq.values()) * 2 + t_norm + t_route + t_strip + t_video
-    return dict(value=s_per_step, sampled_s=sampled, prep_s=prep,
-                sample=(f"oracle (C, OpenMP) on {rows} rows through the 4 six-bit linears + row kernels and 1 of {H} "
-                        f"heads' attention for {att_rows} strip + {att_rows} video query rows at S={S}; "
-                        f"extrapolated linearly in rows/heads/layers over the PAB window {plan}"))
+    def run(self) -> dict:
+        O, c, rows, att_rows = self.O, self.c, self.rows, self.att_rows
+        hdn, inner, ffn, S, g, H = c["hidden"], c["inner"], c["ffn"], c["S"], c["g"], c["heads"]
+        lin = self.lin
+
+        def tm(fn):
+            a = time.perf_counter()
+            fn()
+            return time.perf_counter() - a
+
+        # each oracle qlinear call expands its whole weight once (a per-layer cost) and then
+        # does per-row work: split the two so the extrapolation scales only the row part
+        t_dq = {n: tm(lambda n=n, k=k: O.dequantize(*lin[n], k)) for n, k in
+                (("qkv", hdn), ("out", inner), ("fc1", hdn), ("fc2", ffn))}
+        t_qkv = max(0.0, tm(lambda: O.qlinear(self.x, *lin["qkv"])) - t_dq["qkv"])
+        t_out = max(0.0, tm(lambda: O.qlinear(self.xi, *lin["out"])) - t_dq["out"])
+        t_fc1 = max(0.0, tm(lambda: O.qlinear(self.x, *lin["fc1"], epilogue=O.EPI_GELU)) - t_dq["fc1"])
+        t_fc2 = max(0.0, tm(lambda: O.qlinear(self.xf, *lin["fc2"])) - t_dq["fc2"])
+        rm = np.zeros(rows, np.uint32)
+        t_norm = tm(lambda: O.norm_modscale(self.x, self.w1, self.mods, self.mods, rm, EPS))
+        scale = float(1 / np.sqrt(128))
+        route = {}
+        t_route = tm(lambda: route.update(O.topk_route(self.q, self.k, self.v, g, scale, TOPK_DENSITY)))
+        route.update(g=g, block=128)
+        t_strip = tm(lambda: O.attention_rows(self.q, self.k, self.v, g, scale, 0, att_rows, route=route))
+        t_video = tm(lambda: O.attention_rows(self.q, self.k, self.v, g, scale, g, g + att_rows, route=route))
+        per_row = lambda t: t / rows
+        gemm_attn_rows = per_row(t_qkv) + per_row(t_out)
+        gemm_mlp_rows = per_row(t_fc1) + per_row(t_fc2)
+        rowops = per_row(t_norm) * 4  # norm1, norm2, q/k rope (~norm cost), gate
+        attn_sparse = H * (t_strip / att_rows * g + t_video / att_rows * (S - g)) + H * t_route
+        attn_dense = H * (t_strip / att_rows * S)
+        L = c["layers"]
+        n_dense = sum(1 for lyr in range(L) if _is_dense(lyr, L))
+        dq_attn = t_dq["qkv"] + t_dq["out"]
+        dq_mlp = t_dq["fc1"] + t_dq["fc2"]
+        refresh_step = (L * (S * (gemm_attn_rows + gemm_mlp_rows + rowops) + dq_attn + dq_mlp)
+                        + n_dense * attn_dense + (L - n_dense) * attn_sparse)
+        reuse_step = L * (S * (gemm_mlp_rows + rowops * 0.5) + dq_mlp)
+        s_per_step = sum(refresh_step if r else reuse_step for r in self.plan) / len(self.plan)
+        sampled = t_qkv + t_out + t_fc1 + t_fc2 + sum(t_dq.values()) * 2 + t_norm + t_route + t_strip + t_video
+        return dict(value=s_per_step, sampled_s=sampled)
+
+
+def window_plan() -> list:
+    """The PAB refresh plan of the 4-step window (attnBroadcastPlan over sigmaSchedule(4, 12),
+    k = 2, maxStale 0.06): host logic of libwx, no GPU needed."""
+    from wuxianhuabu_b200 import h3
+    return list(h3.attn_broadcast_plan(h3.sigma_schedule(WINDOW, SHIFT), PAB_K, PAB_MAX_STALE))
 
 
 # ------------------------------------------------------------------ kernel-level configs
@@ -396,8 +414,8 @@ def run_c3(args, seq: int, dense: bool = False) -> dict:
     flash_ms = ms[1] / max(1, cnt[1])
     ach = flops / (flash_ms / 1e3) / 1e12
     pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
-    kernel = ("flash_attn_pair_kernel<0, false> (paired query tiles, shared K/V)" if dense else
-              "flash_attn_pair_kernel<0, true> (duo: two routed query tiles per CTA)")
+    kernel = ("flash_attn_pair_kernel<false, 128> (paired query tiles, shared K/V)" if dense else
+              "flash_attn_pair_kernel<true, 128> (duo: two routed query tiles per CTA)")
     what = "dense attention" if dense else "SOL top-k 25% attention"
     return dict(metric=f"{'dense' if dense else 'sparse'} attention ms/call (c3)", value=per_call, unit="ms/call",
                 config=dict(workload=f"c3: {what}, S={seq}, 24x128 heads", S=seq), higher_is_better=False,
@@ -405,6 +423,143 @@ def run_c3(args, seq: int, dense: bool = False) -> dict:
                               frac=ach / pk, avg_launch_ms=flash_ms, flops_per_launch=flops,
                               peak_kind=f"{kind} burst bf16"),
                 routing_ms=ms[2] / max(1, args.steps))
+
+
+def _rope_grid16(O, S: int):
+    """cos/sin [S, 32] of the config-1 latent grid (t, h, w each 0..15; 8/12/12 frequency
+    pairs of theta 10000 per axis), formed as buildRope does (H3Layout.swift:725-740)."""
+    t, hh, ww = np.meshgrid(np.arange(16), np.arange(16), np.arange(16), indexing="ij")
+    pos = np.stack([t.ravel(), hh.ravel(), ww.ravel()], 1).astype(np.float32)[:S]
+    ang = []
+    for axis, nf in enumerate((8, 12, 12)):
+        inv = (1.0 / 10000.0 ** (np.arange(nf, dtype=np.float64) * 2 / (2 * nf))).astype(np.float32)
+        ang.append((pos[:, axis:axis + 1] * inv[None, :]).astype(np.float32))
+    a = np.concatenate(ang, 1).astype(np.float64)
+    return O.f32_to_bf16(np.cos(a).astype(np.float32)), O.f32_to_bf16(np.sin(a).astype(np.float32))
+
+
+def run_c1(args) -> dict:
+    """one DiT block (hidden 1024, 16 heads of 64, FFN 4096 GELU,
+    S = 4096 = 16 x 16 x 16 latent grid, QK-RMSNorm eps 1e-6, 3-D RoPE over 8/12/12 frequency
+    pairs, dense attention, 6-bit group-64 weights ~ N(0, 0.02), activations ~ N(0, 1)) on one
+    GPU, beside the oracle's whole block on every host thread (timed whole, not extrapolated).
+    The same quantized weights and inputs go to both sides; the line also carries the GPU
+    block's max rel err and cosine against the oracle's output."""
+    import ctypes
+    import torch
+    from oracle import oracle as O
+    from wuxianhuabu_b200 import h3
+    O.build()
+    S, hdn, H, hd, ffn, rot, eps, seed = 4096, 1024, 16, 64, 4096, 64, 1e-6, 1234
+    inner = H * hd
+    w = {}
+    for i, (name, n, k) in enumerate([("qkv", 3 * inner, hdn), ("out", hdn, inner), ("fc1", ffn, hdn),
+                                      ("fc2", hdn, ffn)]):
+        wq, sc, bi = O.quantize(O.normal_f32((n, k), seed, 10 + i, std=0.02))
+        w[name] = (wq, sc, bi, O.normal_bf16((n,), seed, 20 + i, std=0.02))
+    for j, name in enumerate(("q_norm", "k_norm")):
+        w[name] = O.normal_bf16((hd,), seed, 30 + j, mean=1.0, std=0.02)
+    for j, name in enumerate(("norm1", "norm2")):
+        w[name] = O.normal_bf16((hdn,), seed, 32 + j, mean=1.0, std=0.02)
+    mods = [O.normal_bf16((3, hdn), seed, 40 + j, std=0.05) for j in range(6)]
+    h0 = O.normal_bf16((S, hdn), seed, 50)
+    rowmap = np.zeros(S, np.uint32)  # one modulation row (a single video segment at one t)
+    cos, sin = _rope_grid16(O, S)
+
+    dev = torch.device("cuda", 0)
+    bf = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16).to(dev)
+
+    def lin(t, k):
+        wq, sc, bi, b = t
+        return h3.MfLinear(torch.from_numpy(wq.view(np.int32)).to(dev), bf(sc), bf(bi), k, bf(b))
+    bw = h3.H3BlockWeights(lin(w["qkv"], hdn), lin(w["out"], inner), lin(w["fc1"], hdn), lin(w["fc2"], ffn),
+                           bf(w["q_norm"]), bf(w["k_norm"]), bf(w["norm1"]), bf(w["norm2"]))
+    cfg = h3.H3DiTConfig(hidden=hdn, heads=H, head_dim=hd, ffn=ffn, mlp_kind=h3.MLP_GELU, rot=rot, eps=eps, layers=1)
+    blk = h3.H3DiTBlocks(cfg, [bw])
+    md = [bf(m) for m in mods]
+    rm = torch.from_numpy(rowmap.view(np.int32)).to(dev)
+    ct, st = bf(cos), bf(sin)
+    h_init = bf(h0)
+    h = h_init.clone()
+    blk.block_forward(0, h, md, rm, ct, st, None)  # parity run on the oracle's inputs
+    got = h.cpu().view(torch.int16).numpy().view(np.uint16)
+    ctx = h3.context(0)
+    ctx.check_device()
+    for _ in range(max(3, args.warmup)):
+        h.copy_(h_init)
+        blk.block_forward(0, h, md, rm, ct, st, None)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    clocks = ClockSampler(0)
+    clocks.start()
+    ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
+    n0 = ctx.lib.wx_ctx_launch_count(ctx.h)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(1, args.steps)
+    e0.record(stream)
+    for _ in range(steps):
+        h.copy_(h_init)  # every step starts from the same input (an 8 MB device copy)
+        blk.block_forward(0, h, md, rm, ct, st, None)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    n1 = ctx.lib.wx_ctx_launch_count(ctx.h)
+    clk = clocks.stop()
+    ms = (ctypes.c_double * 6)()
+    cnt = (ctypes.c_int64 * 6)()
+    ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 6)
+    ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
+    ctx.check_device()
+    ms_block = e0.elapsed_time(e1) / steps
+    # end to end through the public API with host buffers: pinned H2D of h, the block, D2H of h
+    host_in = torch.from_numpy(h0.view(np.int16).copy()).view(torch.bfloat16).pin_memory()
+    host_out = torch.empty_like(host_in).pin_memory()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(steps):
+        h.copy_(host_in, non_blocking=True)
+        blk.block_forward(0, h, md, rm, ct, st, None)
+        host_out.copy_(h, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1) / steps
+    gemm_fl = 2.0 * S * (hdn * 3 * inner + inner * hdn + hdn * ffn + ffn * hdn)
+    attn_fl = 4.0 * S * S * hd * H
+    peaks, kind = load_peaks()
+    pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    attn_ms, gemm_ms = ms[1] / steps, ms[0] / steps
+    roof = dict(kernel="flash_attn_pair_kernel<false, 64> (dense, paired query tiles)", bound="tensor",
+                achieved=attn_fl / (attn_ms / 1e3) / 1e12 if attn_ms > 0 else 0.0, peak=pk, unit="TFLOP/s",
+                avg_launch_ms=attn_ms, flops_per_launch=attn_fl, traffic=None, peak_kind=f"{kind} burst bf16")
+    roof["frac"] = roof["achieved"] / pk
+    # the oracle's whole block on every host thread (best of 3)
+    threads = O.set_num_threads(0)
+    cfgd = dict(heads=H, head_dim=hd, eps=eps, rot=rot, mlp_kind=0)
+    cpu_t, ref = [], None
+    for _ in range(3):
+        t0 = time.perf_counter()
+        ref, _at = O.block_forward(h0, w, mods, rowmap, cos, sin, cfgd)
+        cpu_t.append(time.perf_counter() - t0)
+    gf, rf = O.bf16_to_f32(got).astype(np.float64), O.bf16_to_f32(ref).astype(np.float64)
+    rel = float(np.abs(gf - rf).max() / np.abs(rf).max())
+    cosv = float((gf.ravel() @ rf.ravel()) / (np.linalg.norm(gf) * np.linalg.norm(rf)))
+    return dict(metric="DiT block ms/block (c1)", value=ms_block, unit="ms/block", n_gpus=1, steps=steps,
+                warmup=max(3, args.warmup), ms_per_step=ms_block, higher_is_better=False, scaling="weak",
+                vs_baseline=None, dtype="bf16", data="synthetic",
+                config=dict(workload="c1: one DiT block, S=4096 (16x16x16), hidden 1024, 16x64 heads, FFN 4096 GELU, "
+                                     "dense attention, 6-bit g64", S=S, hidden=hdn, heads=H, head_dim=hd, ffn=ffn,
+                            l2="inputs smaller than L2; each step restarts from the same h (device copy inside the "
+                               "timed region)"),
+                roofline=roof,
+                qgemm=dict(tflops=gemm_fl / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0, ms=gemm_ms,
+                           flops=gemm_fl),
+                kernel_ms={k: dict(ms=float(ms[i]) / steps, launches=int(cnt[i]) // steps) for i, k in
+                           enumerate(["qgemm", "attention", "routing", "row_kernels", "dequant", "other"])},
+                gpu_launches=int(n1 - n0), clocks=clk,
+                e2e=dict(value=e2e_ms, unit="ms/block", h2d_bytes_per_step=S * hdn * 2, d2h_bytes_per_step=S * hdn * 2),
+                parity=dict(max_rel_err=rel, cosine=cosv, bound="max rel err <= 2e-2, cosine >= 0.999"),
+                cpu_baseline=dict(value=min(cpu_t) * 1e3, unit="ms/block", cores=threads, kind="port",
+                                  sample="the whole block (oracle, C, OpenMP), best of 3, same weights and inputs"))
 
 
 def run_c2(args) -> dict:
@@ -456,17 +611,21 @@ def main():
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
-    ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c3", "c3full", "c3dense", "c2"])
+    ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c1", "c3", "c3full", "c3dense", "c2"])
     ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
-    if args.config in ("c3", "c3full", "c3dense", "c2"):
+    if args.config in ("c1", "c3", "c3full", "c3dense", "c2"):
         import torch
         torch.cuda.set_device(0)
-        r = (run_c2(args) if args.config == "c2" else
-             run_c3(args, 111600 if args.config == "c3full" else 28520, dense=args.config == "c3dense"))
+        if args.config == "c1":
+            r = run_c1(args)
+        elif args.config == "c2":
+            r = run_c2(args)
+        else:
+            r = run_c3(args, 111600 if args.config == "c3full" else 28520, dense=args.config == "c3dense")
         print(json.dumps(r))
         return
     c = geometry(args.config)
@@ -480,21 +639,27 @@ def main():
                     pab=dict(k=PAB_K, max_stale=PAB_MAX_STALE, window=WINDOW), global_batch=1, seq_len=c["S"],
                     parallelism=f"ulysses{world}" if world > 1 else "single", l2="inputs larger than L2 (h 0.78 GB, weights 4.4 GB)")
 
+    plan = window_plan()
+    positions = [i % WINDOW for i in range(args.warmup, args.warmup + args.steps)]
+    n_refresh = sum(1 for pos in positions if plan[pos])
+    base_cfg.update(refresh_steps=n_refresh, reuse_steps=args.steps - n_refresh)
+
     if args.impl == "reference":
         if rank != 0:
             return
-        from oracle import oracle as O
-        O.build()
-        vals = []
+        cs = CpuSample(c, plan)
+        vals, sampled = [], []
         for i in range(args.warmup + args.steps):
-            r = cpu_sample(c)
+            r = cs.run()
             if i >= args.warmup:
                 vals.append(r["value"])
+                sampled.append(r["sampled_s"])
         v = float(np.mean(vals))
         line = dict(metric=METRIC, value=v, unit="s/step", n_gpus=args.gpus, steps=args.steps, warmup=args.warmup,
                     ms_per_step=v * 1e3, higher_is_better=False, scaling="strong", vs_baseline=None, dtype="bf16",
                     data="synthetic", config=base_cfg, impl="reference",
-                    cpu_baseline=dict(value=v, unit="s/step", cores=O.num_threads(), kind="port", sample=r["sample"]),
+                    cpu_baseline=dict(value=v, unit="s/step", cores=cs.threads, kind="port", sample=cs.sample,
+                                      sampled_s_per_step=float(np.mean(sampled))),
                     e2e=dict(value=v, unit="s/step", h2d_bytes_per_step=0, d2h_bytes_per_step=0),
                     note="reference = the oracle's C restatement of the reference's MLX/Metal algorithm; "
                          "Swift/MLX/Metal cannot run on this box")
@@ -613,8 +778,7 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
                     frac=ach_gemm / peak_t, traffic=None, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True)
     line = dict(metric=METRIC, value=s_per_step, unit="s/step", n_gpus=world, steps=args.steps, warmup=args.warmup,
                 ms_per_step=s_per_step * 1e3, higher_is_better=False, scaling="strong", vs_baseline=None,
-                dtype="bf16", data="synthetic", config=dict(base_cfg, refresh_steps=n_refresh,
-                                                            reuse_steps=args.steps - n_refresh),
+                dtype="bf16", data="synthetic", config=dict(base_cfg),
                 roofline=roof,
                 qgemm=dict(tflops=ach_gemm, frac=ach_gemm / peak_t, ms=gemm_ms, launches=prof["qgemm"]["launches"],
                            flops=gemm_flops, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True),
@@ -640,11 +804,10 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
         line["e2e"] = dict(value=e2e, unit="s/step", h2d_bytes_per_step=nbytes, d2h_bytes_per_step=nbytes,
                            finite=finite)
     if not args.no_cpu_baseline and rank == 0 and world == 1:
-        from oracle import oracle as O
-        O.build()
-        r = cpu_sample(c)
-        line["cpu_baseline"] = dict(value=r["value"], unit="s/step", cores=O.num_threads(), kind="port",
-                                    sample=r["sample"], sampled_s=r["sampled_s"])
+        cs = CpuSample(c, run.plan)
+        r = cs.run()
+        line["cpu_baseline"] = dict(value=r["value"], unit="s/step", cores=cs.threads, kind="port",
+                                    sample=cs.sample, sampled_s=r["sampled_s"])
     return line
 
 

@@ -275,12 +275,15 @@ def set_num_threads(n: int = 0) -> int:
 
 
 # ---------------------------------------------------------------- block composition
-def block_forward(h, w, mods, rowmap, cos, sin, cfg, route_fn=None, at_cached=None, refresh=True):
+def block_forward(h, w, mods, rowmap, cos, sin, cfg, route_fn=None, at_cached=None, refresh=True,
+                  qkv_override=None):
     """One H3 DiT block (H3Transformer.swift:1078-1159) composed from the oracle ops.
 
     w: dict of quantized triples qkv/out/fc1/fc2 (wq, sc, bi, bias) and norms, optionally
     w["lora"][name] = [(a, b, scale), ...] (loraDelta, H3Common.swift:424-433); mods: 6 tables;
-    route_fn(q, k, v) -> route dict or None for dense. Returns (h_new, at)."""
+    route_fn(q, k, v) -> route dict or None for dense. qkv_override: the qkv projection's
+    output [S, 3*inner] to use instead of computing it (a test that checks the projection on
+    its own can feed the block the checked tensor). Returns (h_new, at)."""
     S, hidden = h.shape
     H, hd = cfg["heads"], cfg["head_dim"]
     inner = H * hd
@@ -293,8 +296,11 @@ def block_forward(h, w, mods, rowmap, cos, sin, cfg, route_fn=None, at_cached=No
         return qlinear(x, *w[name][:3], bias=w[name][3], **kw)
 
     if refresh or at_cached is None:
-        m1 = norm_modscale(h, w["norm1"], mods[0], mods[1], rowmap, eps)
-        qkv = lin("qkv", m1)
+        if qkv_override is None:
+            m1 = norm_modscale(h, w["norm1"], mods[0], mods[1], rowmap, eps)
+            qkv = lin("qkv", m1)
+        else:
+            qkv = np.ascontiguousarray(qkv_override, dtype=np.uint16)
         q = qkv[:, :inner].reshape(S, H, hd)
         k = qkv[:, inner:2 * inner].reshape(S, H, hd)
         v = np.ascontiguousarray(qkv[:, 2 * inner:].reshape(S, H, hd))

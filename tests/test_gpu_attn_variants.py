@@ -1,6 +1,8 @@
-"""The non-default flash-attention kernels (selected by WX_ATTN_KERNEL, read once
-per process) against the CPU oracle: each variant runs in its own child process
-on dense, SOL and top-k cases with strip rows and ragged tails."""
+"""The documented fallbacks of the flash-attention path (switches read once per
+process) against the CPU oracle: routed tiles in flash_attn2_kernel
+(WX_ATTN_DUO=0) and unpaired strip / dense tiles (WX_ATTN_PAIRS=0). Each runs in
+its own child process on dense, SOL and top-k cases with strip rows and ragged
+tails."""
 import os
 import subprocess
 import sys
@@ -43,9 +45,9 @@ print("ok")
 '''
 
 
-@pytest.mark.parametrize("variant,poly", [("1", "0"), ("4", "0"), ("4", "1"), ("2", "1")])
-def test_flash_variant_matches_oracle(variant, poly):
-    env = dict(os.environ, WX_ATTN_KERNEL=variant, WX_EXP_POLY_PAIRS=poly)
+@pytest.mark.parametrize("duo,pairs", [("0", "1"), ("1", "0"), ("0", "0")])
+def test_flash_fallback_matches_oracle(duo, pairs):
+    env = dict(os.environ, WX_ATTN_DUO=duo, WX_ATTN_PAIRS=pairs)
     r = subprocess.run([sys.executable, "-c", CHILD, str(ROOT)], env=env, capture_output=True, text=True,
                        timeout=600, cwd=str(ROOT))
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-2000:]

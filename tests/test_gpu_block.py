@@ -14,8 +14,7 @@ pytestmark = pytest.mark.gpu
 GOLD = Path(__file__).resolve().parent / "golden"
 
 
-def make_block(seed, hidden, heads, ffn, mlp_kind, S, rot=96):
-    hd = 128
+def make_block(seed, hidden, heads, ffn, mlp_kind, S, rot=96, hd=128):
     inner = heads * hd
     fc1_n = 2 * ffn if mlp_kind == 1 else ffn
     w = {}
@@ -36,7 +35,7 @@ def make_block(seed, hidden, heads, ffn, mlp_kind, S, rot=96):
     return w, mods, h, cos, sin, rowmap
 
 
-def gpu_block(w, hidden, heads, ffn, mlp_kind, rot, eps):
+def gpu_block(w, hidden, heads, ffn, mlp_kind, rot, eps, hd=128):
     import torch
     from wuxianhuabu_b200 import h3
 
@@ -44,13 +43,80 @@ def gpu_block(w, hidden, heads, ffn, mlp_kind, rot, eps):
         wq, sc, bi, b = t
         return h3.MfLinear(torch.from_numpy(wq.view(np.int32)).cuda(), to_torch_bf16(sc), to_torch_bf16(bi), k,
                            to_torch_bf16(b))
-    inner = heads * 128
+    inner = heads * hd
     bw = h3.H3BlockWeights(lin(w["qkv"], hidden), lin(w["out"], inner), lin(w["fc1"], hidden), lin(w["fc2"], ffn),
                            to_torch_bf16(w["q_norm"]), to_torch_bf16(w["k_norm"]), to_torch_bf16(w["norm1"]),
                            to_torch_bf16(w["norm2"]))
-    cfg = h3.H3DiTConfig(hidden=hidden, heads=heads, head_dim=128, ffn=ffn, mlp_kind=mlp_kind, rot=rot, eps=eps,
+    cfg = h3.H3DiTConfig(hidden=hidden, heads=heads, head_dim=hd, ffn=ffn, mlp_kind=mlp_kind, rot=rot, eps=eps,
                          layers=1)
     return h3.H3DiTBlocks(cfg, [bw])
+
+
+def oracle_route(q, k, v, g, scale, sparse):
+    """The oracle router of a sparse spec dict (topk_ratio -> top-k over 128-blocks, else SOL tau
+    over 64-blocks with the tail term), as the oracle block composition takes it."""
+    if sparse.get("topk_ratio"):
+        r = O.topk_route(q, k, v, g, scale, sparse["topk_ratio"])
+        r.update(g=g, block=128, tail=bool(sparse.get("tail", False)))
+    else:
+        sink = sparse.get("sink_blocks") or range(0, 0)
+        r = O.sol_route(q, k, v, g, scale, sparse["tau"], sink=(sink.start, sink.stop))
+        r.update(g=g, block=64, tail=bool(sparse.get("tail", True)))
+    return r
+
+
+def gpu_block_qkv(blk, bi, h, mods, rowmap):
+    """The GPU block's qkv projection of h (norm1 + modulation, then the qkv linear with its
+    LoRA adapters when attached: the kernels wx_dit_block_forward runs), before the per-head
+    norm; [S, 3*inner] bf16 on the device."""
+    from wuxianhuabu_b200 import h3
+    w = blk.blocks[bi]
+    m1 = h3.H3FusedKernels.fused_norm_modscale(h, w.norm1, mods[0], mods[1], rowmap, blk.cfg.eps)
+    return w.qkv(m1)
+
+
+def gpu_block_routing(blk, bi, h, mods, rowmap, cos, sin, sparse, g):
+    """The block-selection decisions the GPU block will take on h: its own q/k/v (norm1 +
+    modulation, the qkv projection, per-head RMSNorm + RoPE in place, the same kernels as
+    wx_dit_block_forward) routed on the GPU. The oracle router on the same q/k/v must give the
+    same tables bit for bit (asserted). Returns the selection [H, nb, nb] (host uint8)."""
+    import torch
+    from wuxianhuabu_b200 import h3
+    cfg = blk.cfg
+    w = blk.blocks[bi]
+    S = h.shape[0]
+    H, hd = cfg.heads, cfg.head_dim
+    inner = H * hd
+    qkv = gpu_block_qkv(blk, bi, h, mods, rowmap)
+    h3.context().call("wx_qk_norm_rope_qkv", qkv.data_ptr(), S, H, hd, w.q_norm.data_ptr(), w.k_norm.data_ptr(),
+                      cos.data_ptr(), sin.data_ptr(), cfg.rot, float(cfg.eps))
+    q, k, v = (qkv[:, i * inner:(i + 1) * inner].view(S, H, hd) for i in range(3))
+    scale = float(1 / np.sqrt(np.float32(hd)))
+    hcfg = h3.H3SolAttnConfig(**sparse)
+    got = h3.H3SolAttn.route(q, k, v, g, scale, hcfg)
+    qn, kn, vn = (np.ascontiguousarray(to_np_bf16(t.contiguous())) for t in (q, k, v))
+    ref = oracle_route(qn, kn, vn, g, scale, sparse)
+    torch.cuda.synchronize()
+    assert np.array_equal(got["sel"].cpu().numpy(), ref["sel"]), "GPU and oracle routers disagree on the same q/k"
+    assert np.array_equal(to_np_bf16(got["cm"]), ref["cm"])
+    assert np.array_equal(to_np_bf16(got["vsum"]), ref["vsum"])
+    assert np.array_equal(got["lens"].cpu().numpy(), ref["lens"])
+    if "thr" in got:
+        assert np.array_equal(got["thr"].cpu().numpy().view(np.uint32), ref["thr"].view(np.uint32))
+    else:
+        assert np.array_equal(got["scores"].cpu().numpy().view(np.uint32), ref["scores"].view(np.uint32))
+    return ref["sel"]
+
+
+def route_with_selection(sel, g, scale, sparse):
+    """An oracle route_fn that routes the oracle's own q/k/v (tail statistics) but takes the
+    block selection the GPU block takes, so that a near-tie in the block scores cannot pick
+    different blocks on the two sides."""
+    def fn(q, k, v):
+        r = oracle_route(q, k, v, g, scale, sparse)
+        r["sel"] = sel
+        return r
+    return fn
 
 
 CASES = [
@@ -72,30 +138,22 @@ def test_block_vs_oracle(name, mlp_kind, sparse):
     w, mods, h, cos, sin, rowmap = make_block(7, hidden, heads, ffn, mlp_kind, S, rot)
     cfgd = dict(heads=heads, head_dim=128, eps=eps, rot=rot, mlp_kind=mlp_kind)
     scale = float(1 / np.sqrt(np.float32(128)))
-
-    def route_fn(q, k, v):
-        if sparse is None:
-            return None
-        if sparse.get("topk_ratio"):
-            r = O.topk_route(q, k, v, g, scale, sparse["topk_ratio"])
-            r.update(g=g, block=128, tail=False)
-        else:
-            r = O.sol_route(q, k, v, g, scale, sparse["tau"])
-            r.update(g=g, block=64, tail=True)
-        return r
-
-    ref, ref_at = O.block_forward(h, w, mods, rowmap, cos, sin, cfgd, route_fn=route_fn)
     blk = gpu_block(w, hidden, heads, ffn, mlp_kind, rot, eps)
+    md = [to_torch_bf16(m) for m in mods]
+    rm = torch.from_numpy(rowmap.view(np.int32)).cuda()
+    ct, st = to_torch_bf16(cos), to_torch_bf16(sin)
+    route_fn = None
+    if sparse is not None:
+        sel = gpu_block_routing(blk, 0, to_torch_bf16(h), md, rm, ct, st, sparse, g)
+        route_fn = route_with_selection(sel, g, scale, sparse)
+    ref, ref_at = O.block_forward(h, w, mods, rowmap, cos, sin, cfgd, route_fn=route_fn)
     ht = to_torch_bf16(h)
     spec = None if sparse is None else h3.H3SolAttnConfig(**sparse).spec(g)
     slot = torch.empty((S, hidden), dtype=torch.bfloat16, device="cuda")
-    blk.block_forward(0, ht, [to_torch_bf16(m) for m in mods], torch.from_numpy(rowmap.view(np.int32)).cuda(),
-                      to_torch_bf16(cos), to_torch_bf16(sin), spec, pab_slot=slot, refresh=True)
+    blk.block_forward(0, ht, md, rm, ct, st, spec, pab_slot=slot, refresh=True)
     h3.context().check_device()
-    # routing decisions can flip at bf16 ties for tau=0.4: require the cosine bound there
-    rel = 2e-2 if name != "sol" else 5e-2
-    assert_close(f32(to_np_bf16(slot)), f32(ref_at), rel=rel, cos=0.999, what=f"{name} at")
-    assert_close(f32(to_np_bf16(ht)), f32(ref), rel=rel, cos=0.999, what=f"{name} h")
+    assert_close(f32(to_np_bf16(slot)), f32(ref_at), rel=2e-2, cos=0.999, what=f"{name} at")
+    assert_close(f32(to_np_bf16(ht)), f32(ref), rel=2e-2, cos=0.999, what=f"{name} h")
 
 
 def test_pab_reuse_equals_refresh_with_same_inputs():

@@ -105,7 +105,13 @@ def test_zero_scale_lora_is_bit_identical_to_base():
 
 
 def test_block_with_lora_vs_oracle():
+    """A block with two adapters on each of its four linears. The qkv projection with its
+    adapters is checked on its own first (GPU vs oracle at the linear tolerance); the oracle
+    block is then fed that same projection, so that the projection's rounding differences
+    (one fp32 accumulator here, the reference's bf16 intermediates in loraDelta) are not
+    amplified by the softmax into the block comparison, which keeps the north-star bound."""
     import torch
+    from tests.test_gpu_block import gpu_block_qkv
     from wuxianhuabu_b200 import h3
     hidden, heads, ffn, rot, eps = 256, 2, 512, 96, 1e-6
     S = 344
@@ -114,18 +120,20 @@ def test_block_with_lora_vs_oracle():
     dims = {"qkv": (hidden, 3 * inner), "out": (inner, hidden), "fc1": (hidden, ffn), "fc2": (ffn, hidden)}
     w["lora"] = {name: _adapters(30 + i, k, n, [16, 8], [0.7, 1.3]) for i, (name, (k, n)) in enumerate(dims.items())}
     cfgd = dict(heads=heads, head_dim=128, eps=eps, rot=rot, mlp_kind=0)
-    ref, ref_at = O.block_forward(h, w, mods, rowmap, cos, sin, cfgd)
     blk = gpu_block(w, hidden, heads, ffn, 0, rot, eps)
     for name, lin in zip(dims, blk.blocks[0].linears()):
         lin.set_lora(_refs(w["lora"][name]))
     blk = h3.H3DiTBlocks(blk.cfg, blk.blocks)  # re-read the packs and the LoRA rank
+    md = [to_torch_bf16(m) for m in mods]
+    rm = torch.from_numpy(rowmap.view(np.int32)).cuda()
+    qkv_gpu = to_np_bf16(gpu_block_qkv(blk, 0, to_torch_bf16(h), md, rm))
+    m1 = O.norm_modscale(h, w["norm1"], mods[0], mods[1], rowmap, eps)
+    qkv_ref = O.qlinear_lora(m1, *w["qkv"][:3], w["lora"]["qkv"], bias=w["qkv"][3])
+    assert_close(f32(qkv_gpu), f32(qkv_ref), rel=1e-2, cos=0.9999, what="qkv projection with adapters")
+    ref, ref_at = O.block_forward(h, w, mods, rowmap, cos, sin, cfgd, qkv_override=qkv_gpu)
     ht = to_torch_bf16(h)
     slot = torch.empty((S, hidden), dtype=torch.bfloat16, device="cuda")
-    blk.block_forward(0, ht, [to_torch_bf16(m) for m in mods], torch.from_numpy(rowmap.view(np.int32)).cuda(),
-                      to_torch_bf16(cos), to_torch_bf16(sin), None, pab_slot=slot, refresh=True)
+    blk.block_forward(0, ht, md, rm, to_torch_bf16(cos), to_torch_bf16(sin), None, pab_slot=slot, refresh=True)
     h3.context().check_device()
-    # the qkv adapters' bf16 rounding differences (one fp32 accumulator here, four roundings
-    # in the reference) pass through the softmax, which amplifies them in a few rows:
-    # the cosine bar stays 0.999, the max-element bar is 5e-2
-    assert_close(f32(to_np_bf16(slot)), f32(ref_at), rel=5e-2, cos=0.999, what="lora block at")
-    assert_close(f32(to_np_bf16(ht)), f32(ref), rel=5e-2, cos=0.999, what="lora block h")
+    assert_close(f32(to_np_bf16(slot)), f32(ref_at), rel=2e-2, cos=0.999, what="lora block at")
+    assert_close(f32(to_np_bf16(ht)), f32(ref), rel=2e-2, cos=0.999, what="lora block h")

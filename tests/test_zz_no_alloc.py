@@ -50,7 +50,7 @@ def test_qlinear_noalloc_matches_oracle_and_qlinear_on_two_calls():
     lib = _lib.load()
     stream = torch.cuda.current_stream().cuda_stream
     shapes = [(300, 1024, 3072, h3.EPI_NONE), (257, 3072, 1024, h3.EPI_GATE_RESID)]
-    cases, refs = [], []
+    cases, refs, keep = [], [], []  # keep: the linears whose device memory the QWeight structs point at
     for call, (m, k, n, epi) in enumerate(shapes):
         lin, (wq, sc, bi, bias) = _linear(60 + call, n, k)
         xn = O.normal_bf16((m, k), 70 + call, 1)
@@ -68,6 +68,7 @@ def test_qlinear_noalloc_matches_oracle_and_qlinear_on_two_calls():
                            want_raw=gate is not None)
         out = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda")
         raw = torch.full((m, n), float("nan"), dtype=torch.bfloat16, device="cuda") if gate is not None else None
+        keep.append(lin)
         cases.append((x, lin.qweight(), epi, gate, resid, rowmap, out, raw))
         refs.append((via_ctx, raw_q, oracle))
     # set-up call: with lazy module loading this reserves the static array on the device

@@ -10,10 +10,11 @@
 //      one (max score C, weight sum L, value vector T) triple
 //   4. kept-list builder: per (head, 128-row q tile) a list of 128-key tiles,
 //      each made of two 64-key halves with per-(q-half, key-half) masks
-//   5. flash kernel (tcgen05): one CTA per (head, q tile); S = Q K^T and
-//      O += P V on the tensor cores with S double-buffered and O resident in
+//   5. flash kernels (tcgen05): strip / dense query tiles in pairs that share
+//      each K/V tile, routed video tiles two independent items per CTA (same
+//      schedule); S = Q K^T and O += P V on the tensor cores with P and O in
 //      TMEM; online softmax in registers with lazy rescaling; tail term and
-//      normalisation in the epilogue.
+//      normalisation in the epilogue. head_dim 128 or 64.
 // The routing arithmetic uses a fixed fp32 operation order (explicit _rn
 // intrinsics) so that its decisions are bit-identical to the CPU oracle.
 #include <cuda.h>
@@ -450,35 +451,9 @@ __global__ void items_kernel(int H, int nst, int nvt, int64_t S, int64_t g, int 
 // ------------------------------------------------------------ 5. flash kernel
 #include "wx_flash.cuh"
 #include "wx_flash2.cuh"
-#include "wx_flash4.cuh"
 #include "wx_flash5.cuh"
 
 // ------------------------------------------------------------- host driver
-// Share of the softmax exponentials taken by the FMA-pipe polynomial (tuning knob
-// WX_EXP_POLY_PAIRS = 0, 1 or 2, read once): pairs out of every 4 in flash_attn2 /
-// flash_attn4, out of every 8 in the paired and duo kernels.
-static int exp_poly_pairs() {
-  static int v = [] {
-    const char* e = getenv("WX_EXP_POLY_PAIRS");
-    int x = e ? atoi(e) : 0;
-    return x < 0 ? 0 : (x > 2 ? 2 : x);
-  }();
-  return v;
-}
-
-// Flash kernel variant (tuning knob WX_ATTN_KERNEL, read once): 1 = one CTA per SM
-// with double-buffered S/P (flash_attn_kernel), 2 = two CTAs per SM with P in
-// TMEM (flash_attn2_kernel, the default), 4 = persistent, softmax split over two
-// warpgroups, two MMA issuers (flash_attn4_kernel).
-static int attn_kernel_variant() {
-  static int v = [] {
-    const char* e = getenv("WX_ATTN_KERNEL");
-    const int x = e ? atoi(e) : 2;
-    return (x == 1 || x == 4) ? x : 2;
-  }();
-  return v;
-}
-
 struct AttnGeom {
   int64_t S, g;
   int H, hd, block, nb, nvt, nst, qpb;
@@ -595,40 +570,20 @@ static int run_routing(wx_ctx* ctx, const void* q, const void* k, const void* v,
   return WX_OK;
 }
 
-// The register split of flash_attn4_kernel (setmaxnreg) must fit the register
-// file the launch reserves: check the compiled per-thread count once.
-static bool flash4_regs_ok(int poly) {
-  static int ok[3] = {-1, -1, -1};
-  const int i = poly < 0 ? 0 : (poly > 2 ? 2 : poly);
-  if (ok[i] < 0) {
+// The register split of the paired / duo kernels (setmaxnreg) must fit the register
+// file the launch reserves: check the compiled per-thread count once per instantiation.
+template <bool DUO, int HD>
+static bool flash_pair_regs_ok() {
+  static const int ok = [] {
     cudaFuncAttributes fa{};
-    const void* fn = i == 0 ? (const void*)flash_attn4_kernel<0>
-                            : (i == 1 ? (const void*)flash_attn4_kernel<1> : (const void*)flash_attn4_kernel<2>);
-    ok[i] = cudaFuncGetAttributes(&fa, fn) == cudaSuccess &&
-            fa.numRegs * kA4Threads >= kA4RegsLow * 128 + kA4RegsHigh * 256;
-    if (!ok[i])
-      fprintf(stderr, "wx: flash_attn4 register split does not fit %d registers/thread; using flash_attn2\n",
-              fa.numRegs);
-  }
-  return ok[i] == 1;
+    return cudaFuncGetAttributes(&fa, (const void*)flash_attn_pair_kernel<DUO, HD>) == cudaSuccess &&
+           fa.numRegs * kA5Threads >= kRegsLow * 128 + kRegsHigh * 256;
+  }();
+  return ok != 0;
 }
 
-static bool flash_pair_regs_ok(int poly) {
-  static int ok[3] = {-1, -1, -1};
-  const int i = poly < 0 ? 0 : (poly > 2 ? 2 : poly);
-  if (ok[i] < 0) {
-    cudaFuncAttributes fa{};
-    // the DUO instantiations share the register split and compile to the same budget
-    const void* fn = i == 0 ? (const void*)flash_attn_pair_kernel<0, false>
-                            : (i == 1 ? (const void*)flash_attn_pair_kernel<1, false>
-                                      : (const void*)flash_attn_pair_kernel<2, false>);
-    ok[i] = cudaFuncGetAttributes(&fa, fn) == cudaSuccess &&
-            fa.numRegs * kA5Threads >= kA4RegsLow * 128 + kA4RegsHigh * 256;
-  }
-  return ok[i] == 1;
-}
-
-// Two routed items per CTA (flash_attn_pair_kernel<.., true>; WX_ATTN_DUO, read once; 0 = off).
+// Two routed items per CTA (flash_attn_pair_kernel<true, HD>; WX_ATTN_DUO, read once; 0 =
+// routed items in flash_attn2_kernel instead, head_dim 128 only).
 static int attn_duo() {
   static int v = [] {
     const char* e = getenv("WX_ATTN_DUO");
@@ -646,9 +601,7 @@ static int attn_pairs() {
   return v;
 }
 
-bool attn_peer_path_ok() {
-  return attn_kernel_variant() == 2 && attn_duo() && flash_pair_regs_ok(exp_poly_pairs());
-}
+bool attn_peer_path_ok() { return attn_duo() && flash_pair_regs_ok<false, 128>() && flash_pair_regs_ok<true, 128>(); }
 
 static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, const AttnGeom& a,
                      const wx_sparse_spec* spec, float scale, const uint8_t* sel, const __nv_bfloat16* cm,
@@ -702,17 +655,11 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
       const void* fn;
       int bytes;
     };
-    const KS ks[] = {{(const void*)flash_attn_kernel<0>, kAttnSmem}, {(const void*)flash_attn_kernel<1>, kAttnSmem},
-                     {(const void*)flash_attn_kernel<2>, kAttnSmem}, {(const void*)flash_attn2_kernel<0>, kA2Smem},
-                     {(const void*)flash_attn2_kernel<1>, kA2Smem}, {(const void*)flash_attn2_kernel<2>, kA2Smem},
-                     {(const void*)flash_attn4_kernel<0>, kA4Smem}, {(const void*)flash_attn4_kernel<1>, kA4Smem},
-                     {(const void*)flash_attn4_kernel<2>, kA4Smem},
-                     {(const void*)flash_attn_pair_kernel<0, false>, kA5Smem},
-                     {(const void*)flash_attn_pair_kernel<1, false>, kA5Smem},
-                     {(const void*)flash_attn_pair_kernel<2, false>, kA5Smem},
-                     {(const void*)flash_attn_pair_kernel<0, true>, kA5Smem},
-                     {(const void*)flash_attn_pair_kernel<1, true>, kA5Smem},
-                     {(const void*)flash_attn_pair_kernel<2, true>, kA5Smem}};
+    const KS ks[] = {{(const void*)flash_attn2_kernel, kA2Smem},
+                     {(const void*)flash_attn_pair_kernel<false, 128>, A5Geom<128>::kSmem},
+                     {(const void*)flash_attn_pair_kernel<true, 128>, A5Geom<128>::kSmem},
+                     {(const void*)flash_attn_pair_kernel<false, 64>, A5Geom<64>::kSmem},
+                     {(const void*)flash_attn_pair_kernel<true, 64>, A5Geom<64>::kSmem}};
     for (const KS& k2 : ks)
       if ((st = ensure_smem_attr(ctx, k2.fn, k2.bytes, "flash attention"))) return st;
   }
@@ -748,12 +695,16 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
 
   if (n_items > INT32_MAX) return set_error(ctx, WX_ERR_UNSUPPORTED, "too many attention work items");
   ProfScope prof(ctx, kProfAttn);
-  const int poly = exp_poly_pairs();
+  const bool hd64 = a.hd == 64;
   // The paired (strip / dense) items are few and long, the routed ones many and short:
   // the routed kernel runs on a side stream so that its CTAs fill the SMs left idle by
   // the last, partial wave of paired CTAs.
-  const int64_t n_rest_all = n_items - 2 * n_pairs;
-  const bool side = n_pairs > 0 && n_rest_all > 0 && attn_kernel_variant() == 2 && attn_duo();
+  const int64_t n_rest = n_items - 2 * n_pairs;
+  const bool duo = attn_duo() && (hd64 ? flash_pair_regs_ok<true, 64>() : flash_pair_regs_ok<true, 128>());
+  if (n_rest > 0 && !duo && (hd64 || po))
+    return set_error(ctx, WX_ERR_UNSUPPORTED, "%s needs the two-item attention kernel (WX_ATTN_DUO=0 or its register "
+                     "split does not fit)", hd64 ? "head_dim 64" : "attention to peer memory");
+  const bool side = n_pairs > 0 && n_rest > 0 && duo;
   if (side) {
     if (!ctx->aux) {
       cudaError_t e = cudaStreamCreateWithFlags(&ctx->aux, cudaStreamNonBlocking);
@@ -765,32 +716,29 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
     cudaStreamWaitEvent(ctx->aux, ctx->fork, 0);
   }
   if (n_pairs > 0) {
-    if (!flash_pair_regs_ok(poly)) return set_error(ctx, WX_ERR_CUDA, "flash_attn_pair: register split does not fit");
+    const bool regs = hd64 ? flash_pair_regs_ok<false, 64>() : flash_pair_regs_ok<false, 128>();
+    if (!regs) return set_error(ctx, WX_ERR_CUDA, "flash_attn_pair: register split does not fit");
     const int np2 = (int)(2 * n_pairs);
-    if (poly == 0)
-      flash_attn_pair_kernel<0, false><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, np2);
-    else if (poly == 2)
-      flash_attn_pair_kernel<2, false><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, np2);
+    if (hd64)
+      flash_attn_pair_kernel<false, 64><<<(unsigned)n_pairs, kA5Threads, A5Geom<64>::kSmem, ctx->stream>>>(
+          tq, tk, tv, p, np2);
     else
-      flash_attn_pair_kernel<1, false><<<(unsigned)n_pairs, kA5Threads, kA5Smem, ctx->stream>>>(tq, tk, tv, p, np2);
+      flash_attn_pair_kernel<false, 128><<<(unsigned)n_pairs, kA5Threads, A5Geom<128>::kSmem, ctx->stream>>>(
+          tq, tk, tv, p, np2);
     if ((st = launch_status(ctx, "flash_attn_pair"))) return st;
   }
   // the remaining (unpaired) items
-  WorkItem* const items_all = items;
-  const int64_t n_rest = n_items - 2 * n_pairs;
   p.items = items + 2 * n_pairs;
   if (n_rest == 0) return WX_OK;
-  if (attn_kernel_variant() == 2 && attn_duo() && flash_pair_regs_ok(poly)) {
+  if (duo) {
     // two independent (routed) items per CTA, their exponential phases taking turns
     const unsigned grid = (unsigned)((n_rest + 1) / 2);
     const int nr = (int)n_rest;
     cudaStream_t sm = side ? ctx->aux : ctx->stream;
-    if (poly == 0)
-      flash_attn_pair_kernel<0, true><<<grid, kA5Threads, kA5Smem, sm>>>(tq, tk, tv, p, nr);
-    else if (poly == 2)
-      flash_attn_pair_kernel<2, true><<<grid, kA5Threads, kA5Smem, sm>>>(tq, tk, tv, p, nr);
+    if (hd64)
+      flash_attn_pair_kernel<true, 64><<<grid, kA5Threads, A5Geom<64>::kSmem, sm>>>(tq, tk, tv, p, nr);
     else
-      flash_attn_pair_kernel<1, true><<<grid, kA5Threads, kA5Smem, sm>>>(tq, tk, tv, p, nr);
+      flash_attn_pair_kernel<true, 128><<<grid, kA5Threads, A5Geom<128>::kSmem, sm>>>(tq, tk, tv, p, nr);
     st = launch_status(ctx, "flash_attn_duo");
     if (side) {  // join: the context stream continues after both kernels
       cudaEventRecord(ctx->join, ctx->aux);
@@ -798,41 +746,16 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
     }
     return st;
   }
-  if (attn_kernel_variant() == 4 && flash4_regs_ok(poly)) {
-    // persistent: one CTA per SM, items fetched dynamically, softmax split over two warpgroups
-    const unsigned grid = (unsigned)std::min<int64_t>(ctx->num_sms, n_rest);
-    int* counter = reinterpret_cast<int*>(items_all + n_items);
-    const int ni = (int)n_rest;
-    if (poly == 0)
-      flash_attn4_kernel<0><<<grid, kA4Threads, kA4Smem, ctx->stream>>>(tq, tk, tv, p, ni, counter);
-    else if (poly == 2)
-      flash_attn4_kernel<2><<<grid, kA4Threads, kA4Smem, ctx->stream>>>(tq, tk, tv, p, ni, counter);
-    else
-      flash_attn4_kernel<1><<<grid, kA4Threads, kA4Smem, ctx->stream>>>(tq, tk, tv, p, ni, counter);
-    return launch_status(ctx, "flash_attn4");
-  }
-  if (attn_kernel_variant() == 2) {
-    if (poly == 0)
-      flash_attn2_kernel<0><<<(unsigned)n_rest, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
-    else if (poly == 2)
-      flash_attn2_kernel<2><<<(unsigned)n_rest, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
-    else
-      flash_attn2_kernel<1><<<(unsigned)n_rest, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
-    return launch_status(ctx, "flash_attn2");
-  }
-  if (poly == 0)
-    flash_attn_kernel<0><<<(unsigned)n_rest, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
-  else if (poly == 2)
-    flash_attn_kernel<2><<<(unsigned)n_rest, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
-  else
-    flash_attn_kernel<1><<<(unsigned)n_rest, kAttnThreads, kAttnSmem, ctx->stream>>>(tq, tk, tv, p);
-  return launch_status(ctx, "flash_attn");
+  // fallback for the routed items (head_dim 128): one item per CTA, two CTAs per SM
+  flash_attn2_kernel<<<(unsigned)n_rest, kAttnThreads, kA2Smem, ctx->stream>>>(tq, tk, tv, p);
+  return launch_status(ctx, "flash_attn2");
 }
 
 static int check_attn_args(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
                            int hd, const void* out, int64_t os) {
   WX_CHECK_ARG(ctx, ctx && q && k && v && out && S > 0 && H > 0);
-  if (hd != 128) return set_error(ctx, WX_ERR_UNSUPPORTED, "attention head_dim must be 128 (got %d)", hd);
+  if (hd != 128 && hd != 64)
+    return set_error(ctx, WX_ERR_UNSUPPORTED, "attention head_dim must be 128 or 64 (got %d)", hd);
   WX_CHECK_ARG(ctx, rs >= (int64_t)H * hd && os >= (int64_t)H * hd && rs % 8 == 0 && os % 8 == 0);
   WX_CHECK_ARG(ctx, aligned16(q) && aligned16(k) && aligned16(v) && aligned16(out));
   WX_CHECK_ARG(ctx, S < (int64_t)1 << 30);
@@ -893,7 +816,7 @@ static int route_api(wx_ctx* ctx, const void* q, const void* k, const void* v, i
                      void* cm, void* vsum, float* lens) {
   WX_CHECK_ARG(ctx, ctx && q && k && v && spec && sel && cm && vsum && lens && S > 0 && H > 0);
   WX_CHECK_ARG(ctx, spec->mode == want_mode);
-  if (hd != 128) return set_error(ctx, WX_ERR_UNSUPPORTED, "routing head_dim must be 128");
+  if (hd != 128 && hd != 64) return set_error(ctx, WX_ERR_UNSUPPORTED, "routing head_dim must be 128 or 64");
   AttnGeom a;
   int st = geom_from(ctx, S, H, hd, spec, a);
   if (st) return st;

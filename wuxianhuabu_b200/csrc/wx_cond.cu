@@ -350,7 +350,8 @@ int64_t wx_refiner_scratch_bytes(const wx_dit_config* cfg, int64_t L) {
 int wx_refiner_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_weights* w, void* h, int64_t L,
                              void* scratch) {
   WX_CHECK_ARG(ctx, ctx && cfg && h && scratch && L > 0);
-  WX_CHECK_ARG(ctx, cfg->head_dim == 128 && cfg->heads > 0 && cfg->hidden > 0 && cfg->ffn > 0);
+  WX_CHECK_ARG(ctx, (cfg->head_dim == 128 || cfg->head_dim == 64) && cfg->heads > 0 && cfg->hidden > 0 &&
+                        cfg->ffn > 0);
   int st = check_refiner_block(ctx, cfg, w);
   if (st) return st;
   const RefinerLayout R = refiner_layout(cfg, L);
@@ -376,7 +377,8 @@ int wx_refine_text(wx_ctx* ctx, const wx_dit_config* cfg, const wx_qweight* cond
                         condition_proj->n == cfg->hidden);
   WX_CHECK_ARG(ctx, !condition_lora || lora_pack_ok(condition_lora, condition_proj));
   WX_CHECK_ARG(ctx, !condition_lora || condition_lora->R <= cfg->lora_rank);
-  WX_CHECK_ARG(ctx, cfg->head_dim == 128 && cfg->heads > 0 && cfg->hidden > 0 && cfg->ffn > 0);
+  WX_CHECK_ARG(ctx, (cfg->head_dim == 128 || cfg->head_dim == 64) && cfg->heads > 0 && cfg->hidden > 0 &&
+                        cfg->ffn > 0);
   int st;
   for (int b = 0; b < n_blocks; ++b)
     if ((st = check_refiner_block(ctx, cfg, &blocks[b]))) return st;

@@ -92,7 +92,8 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
                          const wx_block_mods* mods, const uint32_t* rowmap, void* h, int64_t S, const void* cos_t,
                          const void* sin_t, const wx_sparse_spec* spec, void* pab_slot, int refresh, void* scratch) {
   WX_CHECK_ARG(ctx, ctx && cfg && w && mods && h && scratch && S > 0);
-  WX_CHECK_ARG(ctx, cfg->head_dim == 128 && cfg->heads > 0 && cfg->hidden > 0 && cfg->ffn > 0);
+  WX_CHECK_ARG(ctx, (cfg->head_dim == 128 || cfg->head_dim == 64) && cfg->heads > 0 && cfg->hidden > 0 &&
+                        cfg->ffn > 0);
   const int64_t inner = (int64_t)cfg->heads * cfg->head_dim;
   const int64_t fc1_n = cfg->mlp_kind == WX_MLP_SWIGLU ? 2 * cfg->ffn : cfg->ffn;
   WX_CHECK_ARG(ctx, qweight_ok(&w->qkv) && w->qkv.k == cfg->hidden && w->qkv.n == 3 * inner);

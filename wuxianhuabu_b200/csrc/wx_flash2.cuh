@@ -1,5 +1,7 @@
-// wx_flash2.cuh — flash-attention kernel sized for TWO CTAs per SM (included by
-// wx_attn.cu after wx_flash.cuh, whose helpers it shares).
+// wx_flash2.cuh — flash-attention kernel sized for TWO CTAs per SM, head_dim 128
+// (included by wx_attn.cu after wx_flash.cuh, whose helpers it shares). It runs
+// the routed (video) query tiles when the two-item kernel of wx_flash5.cuh is
+// switched off (WX_ATTN_DUO=0) or its register split does not fit.
 //
 // The softmax of one (head, 128-row q tile) and the tensor-core work of another
 // overlap because two CTAs share each SM, instead of two q tiles sharing one
@@ -13,12 +15,12 @@
 // A from TMEM). tcgen05.mma instructions of one thread run in issue order, so
 // S_{j+1} (issued after PV_j) cannot overwrite P_j before PV_j has read it, and
 // PV_{j-1} is complete whenever S_j is. K_{j+1} streams in once S_j is done, V_{j+1}
-// once PV_j is done. Warp roles as in flash_attn_kernel.
+// once PV_j is done. Warp 0: TMA producer; warp 1: MMA issuer (one thread) and
+// TMEM owner; warps 2-5: softmax and epilogue, thread r owning query row r.
 #pragma once
 
 constexpr int kA2Smem = 3 * kTileBytes + 256 + 1024;
 
-template <int POLY>
 __global__ void __launch_bounds__(kAttnThreads, 2)
     flash_attn2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, AttnParams p) {
@@ -73,7 +75,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       mbar_arrive_expect_tx(q_full, kTileBytes);
       for (int ch = 0; ch < 2; ++ch)
         for (int rh = 0; rh < 2; ++rh)
-          tma_load_2d(sQ + ch * 16384 + rh * 8192, &tmQ, q_full, hcol + ch * 64, it.q_start + rh * 64);
+          tma_load_2d(sQ + ch * kChunkBytes + rh * kHalfBytes, &tmQ, q_full, hcol + ch * 64, it.q_start + rh * 64);
       int4 e = kv_entry(it, p.entries, 0);
       for (int j = 0; j < n_kv; ++j) {
         const int4 cur = e;
@@ -81,14 +83,14 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         if (!mbar_wait(k_empty, (j & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(k_full, kTileBytes);
         for (int ch = 0; ch < 2; ++ch) {
-          tma_load_2d(sK + ch * 16384, &tmK, k_full, hcol + ch * 64, cur.x);
-          tma_load_2d(sK + ch * 16384 + 8192, &tmK, k_full, hcol + ch * 64, cur.y);
+          tma_load_2d(sK + ch * kChunkBytes, &tmK, k_full, hcol + ch * 64, cur.x);
+          tma_load_2d(sK + ch * kChunkBytes + kHalfBytes, &tmK, k_full, hcol + ch * 64, cur.y);
         }
         if (!mbar_wait(v_empty, (j & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(v_full, kTileBytes);
         for (int ch = 0; ch < 2; ++ch) {
-          tma_load_2d(sV + ch * 16384, &tmV, v_full, hcol + ch * 64, cur.x);
-          tma_load_2d(sV + ch * 16384 + 8192, &tmV, v_full, hcol + ch * 64, cur.y);
+          tma_load_2d(sV + ch * kChunkBytes, &tmV, v_full, hcol + ch * 64, cur.x);
+          tma_load_2d(sV + ch * kChunkBytes + kHalfBytes, &tmV, v_full, hcol + ch * 64, cur.y);
         }
       }
     }
@@ -206,12 +208,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 a = __ffma2_rn(make_float2(t[2 * i], t[2 * i + 1]), sl2x2, nmu2);
-          float2 pv;
-          if ((i & 3) < POLY) {
-            pv = ex2_poly2(a);
-          } else {
-            pv = make_float2(ex2(a.x), ex2(a.y));
-          }
+          const float2 pv = make_float2(ex2(a.x), ex2(a.y));
           rs2[i & 3] = __fadd2_rn(rs2[i & 3], pv);
           pk[i] = pack_bf16x2(pv.x, pv.y);
         }

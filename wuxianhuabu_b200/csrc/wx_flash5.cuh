@@ -1,14 +1,16 @@
 // wx_flash5.cuh — flash-attention kernel for PAIRS of query tiles that walk the
 // same key tiles (strip rows and dense layers: every key of the sequence), so
 // each K/V tile is loaded once for 256 query rows (included by wx_attn.cu after
-// wx_flash.cuh and wx_flash4.cuh, whose helpers it shares).
+// wx_flash.cuh, whose helpers it shares). Head dimension HD = 128 (the H3 and
+// benchmark geometries) or 64 (benchmark config 1).
 //
 // One CTA per pair (head, q tiles A and B). Per key tile t the tensor pipe runs
-// S_X = Q_X K^T and O_X += P_X V for X in {A, B} (2048 cycles); the shared K/V
-// tile (64 KB) halves the load traffic per FLOP of the single-tile kernels.
-//   TMEM (512 columns): S/P_A [0,128), S/P_B [128,256), O_A [256,384), O_B [384,512);
-//   P_X overwrites the first 64 columns of S_X as packed bf16.
-//   Shared memory: Q_A, Q_B, K ring of 3, V ring of 2 (32 KB tiles, SW128).
+// S_X = Q_X K^T and O_X += P_X V for X in {A, B} (2048 cycles at HD 128); the
+// shared K/V tile halves the load traffic per FLOP of a single-tile kernel.
+//   TMEM (512 columns): S/P_A [0,128), S/P_B [128,256), O_A [256,256+HD),
+//   O_B [384,384+HD); P_X overwrites the first 64 columns of S_X as packed bf16.
+//   Shared memory: Q_A, Q_B, K ring of 3, V ring of 2 (128 x HD bf16 tiles, SW128,
+//   in 64-column chunks).
 //   Warp 0: TMA producer. Warp 1 / warp 2: MMA issuer of slot A / B (one
 //   thread each: S_X(t), then PV_X(t) in four pieces of 32 keys, each issued as
 //   soon as the softmax has stored that piece of P_X(t), then S_X(t+1) — the
@@ -27,7 +29,6 @@
 // epilogue adds the SOL tail term.
 #pragma once
 
-constexpr int kA5Threads = 384;
 constexpr int kA5KStages = 3;
 constexpr int kA5VStages = 2;
 #ifndef WX_A5_TURN_CHUNK
@@ -48,9 +49,15 @@ constexpr int kA5PVParts = WX_A5_PV_PARTS;
 #endif
 constexpr bool kA5SSplit = WX_A5_S_SPLIT != 0;
 static_assert(kA5PVParts == 1 || kA5PVParts == 2 || kA5PVParts == 4, "P pieces: 1, 2 or 4");
-constexpr int kA5BarOff = (2 + kA5KStages + kA5VStages) * kTileBytes;
-constexpr int kA5Smem = kA5BarOff + 512 + 1024;
-static_assert(kA5Threads == kA4Threads, "uses the register split of flash_attn4_kernel (kA4RegsLow/High)");
+// shared-memory plan of the kernel for head dimension HD
+template <int HD>
+struct A5Geom {
+  static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+  static constexpr int kTile = 128 * HD * 2;  // one 128-row Q, K or V tile
+  static constexpr int kChunks = HD / 64;     // 64-column SW128 chunks per tile
+  static constexpr int kBarOff = (2 + kA5KStages + kA5VStages) * kTile;
+  static constexpr int kSmem = kBarOff + 512 + 1024;
+};
 
 enum : int {
   kB5QFull = 0,
@@ -68,18 +75,20 @@ enum : int {
 };
 static_assert(kB5Count <= 32, "barriers overlap the TMEM slot");
 
-template <int POLY, bool DUO>
+template <bool DUO, int HD>
 __global__ void __launch_bounds__(kA5Threads, 1)
     flash_attn_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, AttnParams p, int n_items) {
+  using G = A5Geom<HD>;
+  constexpr int kTile = G::kTile;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  auto sQ = [&](int X) { return sbase + (uint32_t)X * kTileBytes; };
+  auto sQ = [&](int X) { return sbase + (uint32_t)X * kTile; };
   // shared K ring / V ring, or (DUO) K_X at tile 2 + 2X and V_X at tile 3 + 2X
-  auto sK = [&](int s) { return sbase + (uint32_t)(2 + s) * kTileBytes; };
-  auto sV = [&](int s) { return sbase + (uint32_t)((DUO ? 3 : 2 + kA5KStages) + s) * kTileBytes; };
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kA5BarOff);
+  auto sK = [&](int s) { return sbase + (uint32_t)(2 + s) * kTile; };
+  auto sV = [&](int s) { return sbase + (uint32_t)((DUO ? 3 : 2 + kA5KStages) + s) * kTile; };
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + G::kBarOff);
   auto bar = [&](int i) { return smem_u32(bars + i); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 32);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -92,7 +101,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
   const int nA = item_tiles(itA);
   const int nB = has_b ? item_tiles(p.items[2 * blockIdx.x + 1]) : 0;
   const int n_kv = DUO ? (nA > nB ? nA : nB) : nA;  // tiles of the longer slot
-  const int hcol = itA.head * 128;
+  const int hcol = itA.head * HD;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kB5Count; ++i) {
@@ -117,7 +126,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
-    reg_dealloc4();
+    reg_dealloc_low();
     if (lane == 0 && n_kv > 0) {
       // ------------------------------------------------------------ producer
       prefetch_tmap(&tmQ);
@@ -126,19 +135,19 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       bool ok = true;
       uint32_t nk = 0, nv = 0, nk_b = 0;  // loads issued (DUO: K of slot A, K of slot B)
       const int nslots = (DUO && !has_b) ? 1 : 2;
-      mbar_arrive_expect_tx(bar(kB5QFull), nslots * kTileBytes);
+      mbar_arrive_expect_tx(bar(kB5QFull), nslots * kTile);
       for (int X = 0; X < nslots; ++X) {
         const WorkItem w = p.items[2 * blockIdx.x + X];
-        for (int ch = 0; ch < 2; ++ch)
+        for (int ch = 0; ch < G::kChunks; ++ch)
           for (int rh = 0; rh < 2; ++rh)
-            tma_load_2d(sQ(X) + ch * 16384 + rh * 8192, &tmQ, bar(kB5QFull), w.head * 128 + ch * 64,
+            tma_load_2d(sQ(X) + ch * kChunkBytes + rh * kHalfBytes, &tmQ, bar(kB5QFull), w.head * HD + ch * 64,
                         w.q_start + rh * 64);
       }
       auto tile_load = [&](const CUtensorMap* tm, uint32_t dst, uint32_t full, int hc, int4 e) {
-        mbar_arrive_expect_tx(full, kTileBytes);
-        for (int ch = 0; ch < 2; ++ch) {
-          tma_load_2d(dst + ch * 16384, tm, full, hc + ch * 64, e.x);
-          tma_load_2d(dst + ch * 16384 + 8192, tm, full, hc + ch * 64, e.y);
+        mbar_arrive_expect_tx(full, kTile);
+        for (int ch = 0; ch < G::kChunks; ++ch) {
+          tma_load_2d(dst + ch * kChunkBytes, tm, full, hc + ch * 64, e.x);
+          tma_load_2d(dst + ch * kChunkBytes + kHalfBytes, tm, full, hc + ch * 64, e.y);
         }
       };
       if constexpr (!DUO) {
@@ -172,7 +181,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
               ok = false;
               break;
             }
-            tile_load(&tmK, sK(2 * X), bar(kB5KFull + X), w.head * 128, kv_entry(w, p.entries, t));
+            tile_load(&tmK, sK(2 * X), bar(kB5KFull + X), w.head * HD, kv_entry(w, p.entries, t));
             (X == 0 ? nk : nk_b) = (uint32_t)t + 1;
           }
         }
@@ -191,13 +200,13 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       }
     }
   } else if (warp == 1 || warp == 2) {
-    reg_dealloc4();
+    reg_dealloc_low();
     const int X = warp - 1;
     const int nX = X == 0 ? nA : nB;
     if (lane == 0 && nX > 0) {
       // ------------------------------------------------------------ MMA issuer of slot X
       constexpr uint32_t idesc_s = idesc_bf16_f32(128, 128, false, false);
-      constexpr uint32_t idesc_o = idesc_bf16_f32(128, 128, false, true);  // A = P from TMEM, B = V MN-major
+      constexpr uint32_t idesc_o = idesc_bf16_f32(128, HD, false, true);  // A = P from TMEM, B = V MN-major
       const uint32_t tS = tmem + (uint32_t)(X * 128);
       const uint32_t tO = tmem + 256 + (uint32_t)(X * 128);
       bool ok = mbar_wait(bar(kB5QFull), 0, p.err, kDevTimeoutFull, abort_flag);
@@ -215,8 +224,8 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         tc_fence_after();
         const uint64_t dk = opaque64(smem_desc_sw128(sK(kbuf(t)), 16, 1024));
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
           umma_bf16(tS, dq + off, dk + off, idesc_s, kk > 0 ? 1u : 0u);
         }
         issued = true;
@@ -227,10 +236,10 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       constexpr uint32_t idesc_s64 = idesc_bf16_f32(128, 64, false, false);
       auto issue_s_half = [&](int t, int half) {
         tc_fence_after();
-        const uint64_t dk = opaque64(smem_desc_sw128(sK(kbuf(t)) + (uint32_t)half * 8192, 16, 1024));
+        const uint64_t dk = opaque64(smem_desc_sw128(sK(kbuf(t)) + (uint32_t)half * kHalfBytes, 16, 1024));
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = ((kk >> 2) * kChunkBytes + (kk & 3) * 32) >> 4;
           umma_bf16(tS + (uint32_t)(half * 64), dq + off, dk + off, idesc_s64, kk > 0 ? 1u : 0u);
         }
         issued = true;
@@ -256,7 +265,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
           }
           issue_s_half(t + 1, 1);
         }
-        const uint64_t dv = opaque64(smem_desc_sw128(sV(vbuf(t)), 16384, 1024));
+        const uint64_t dv = opaque64(smem_desc_sw128(sV(vbuf(t)), kChunkBytes, 1024));
         constexpr int kk_per = 8 / kA5PVParts;
 #pragma unroll
         for (int part = 0; part < kA5PVParts && ok; ++part) {
@@ -291,7 +300,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       }
     }
   } else if (warp == 3) {
-    reg_dealloc4();
+    reg_dealloc_low();
     if (DUO && lane == 0 && n_kv > 0) {
       // ------------------------------------------------------------ V producer (DUO)
       // one V buffer per slot: V_X(t) waits for PV_X(t-1)
@@ -308,10 +317,10 @@ __global__ void __launch_bounds__(kA5Threads, 1)
           }
           const int4 e = kv_entry(w, p.entries, t);
           const uint32_t full = bar(kB5VFull + X), dst = sV(2 * X);
-          mbar_arrive_expect_tx(full, kTileBytes);
-          for (int ch = 0; ch < 2; ++ch) {
-            tma_load_2d(dst + ch * 16384, &tmV, full, w.head * 128 + ch * 64, e.x);
-            tma_load_2d(dst + ch * 16384 + 8192, &tmV, full, w.head * 128 + ch * 64, e.y);
+          mbar_arrive_expect_tx(full, kTile);
+          for (int ch = 0; ch < G::kChunks; ++ch) {
+            tma_load_2d(dst + ch * kChunkBytes, &tmV, full, w.head * HD + ch * 64, e.x);
+            tma_load_2d(dst + ch * kChunkBytes + kHalfBytes, &tmV, full, w.head * HD + ch * 64, e.y);
           }
           (X == 0 ? nv_a : nv_b) = (uint32_t)t + 1;
         }
@@ -322,7 +331,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       }
     }
   } else {
-    reg_alloc4();
+    reg_alloc_high();
     // ------------------------------------------------ softmax + epilogue of slot X
     const int X = (warp - 4) >> 2;
     const bool present = X == 0 || has_b;
@@ -388,7 +397,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
           // O_X is rescaled before any PV_X(t) MMA (they start with the first piece of P);
           // PV_X(t-1) completed before S_X(t) (in-order tensor pipe), so O_X is stable
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < HD / 32; ++c) {
             float o[32];
             tmem_ld32(tO + c * 32, o);
             tmem_wait_ld();
@@ -428,12 +437,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const float2 a = __ffma2_rn(make_float2(v[32 * c + 2 * i], v[32 * c + 2 * i + 1]), sl2x2, nmu2);
-          float2 pv;
-          if ((i & 7) < POLY) {  // POLY pairs of every 8 on the FMA pipe
-            pv = ex2_poly2(a);
-          } else {
-            pv = make_float2(ex2(a.x), ex2(a.y));
-          }
+          const float2 pv = make_float2(ex2(a.x), ex2(a.y));
           rs2[i & 3] = __fadd2_rn(rs2[i & 3], pv);
           pk[i] = pack_bf16x2(pv.x, pv.y);
         }
@@ -456,7 +460,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         if (any_need) {
           // PV_X(t-1) completed before S_X(t) (in-order tensor pipe): O_X is stable
 #pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < HD / 32; ++c) {
             float o[32];
             tmem_ld32(tO + c * 32, o);
             tmem_wait_ld();
@@ -493,14 +497,14 @@ __global__ void __launch_bounds__(kA5Threads, 1)
         a1 = (m == -INFINITY) ? 0.f : ex2(ms - M2);
         a2 = ex2(C2 - M2);
         lt = l * a1 + p.tailL[o] * a2;
-        T = p.tailT + o * 128;
+        T = p.tailT + o * HD;
       }
     }
     const float inv = lt > 0.f ? 1.0f / lt : 0.f;
     const bool row_ok = ok && present && r < it.q_rows;
-    __nv_bfloat16* orow = attn_out_row(p, (int64_t)(it.q_start + r), it.head);
+    __nv_bfloat16* orow = attn_out_row<HD>(p, (int64_t)(it.q_start + r), it.head);
 #pragma unroll 1
-    for (int c = 0; c < 4 && present; ++c) {
+    for (int c = 0; c < HD / 32 && present; ++c) {
       float o[32];
       if (nX > 0) {
         tmem_ld32(tO + c * 32, o);
