@@ -504,9 +504,9 @@ def run_c1(args) -> dict:
     torch.cuda.synchronize()
     n1 = ctx.lib.wx_ctx_launch_count(ctx.h)
     clk = clocks.stop()
-    ms = (ctypes.c_double * 6)()
-    cnt = (ctypes.c_int64 * 6)()
-    ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 6)
+    ms = (ctypes.c_double * 10)()
+    cnt = (ctypes.c_int64 * 10)()
+    ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
     ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
     ctx.check_device()
     ms_block = e0.elapsed_time(e1) / steps
@@ -554,7 +554,8 @@ def run_c1(args) -> dict:
                 qgemm=dict(tflops=gemm_fl / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0, ms=gemm_ms,
                            flops=gemm_fl),
                 kernel_ms={k: dict(ms=float(ms[i]) / steps, launches=int(cnt[i]) // steps) for i, k in
-                           enumerate(["qgemm", "attention", "routing", "row_kernels", "dequant", "other"])},
+                           enumerate(["qgemm", "attention", "routing", "row_kernels", "dequant", "other",
+                                      "qk_norm_rope", "norm_modscale"])},
                 gpu_launches=int(n1 - n0), clocks=clk,
                 e2e=dict(value=e2e_ms, unit="ms/block", h2d_bytes_per_step=S * hdn * 2, d2h_bytes_per_step=S * hdn * 2),
                 parity=dict(max_rel_err=rel, cosine=cosv, bound="max rel err <= 2e-2, cosine >= 0.999"),
@@ -709,6 +710,46 @@ def _sum_over_ranks(x: float, dist) -> float:
     return float(t.item())
 
 
+def memory_bound_kernels(c: dict, prof: dict, world: int, peaks: dict, peaks_kind: str) -> dict:
+    """Achieved bandwidth of the HBM-bound kernels of the step (per launch, this rank's rows),
+    from the CUDA-event times libwx recorded around each launch and the algorithmic bytes:
+      QK-RMSNorm + RoPE of q and k: read + write of 2 x rows x inner bf16, + cos/sin rows;
+      RMSNorm + modulation: read + write of rows x hidden bf16 (+ the u32 row map);
+      the fused sequence-parallel exchange (QK-norm/RoPE + v copy stored into the owners'
+      buffers): reads rows x 3 x inner bf16 and stores the same, (P-1)/P of it over NVLink.
+    HBM peak: MEASURED_PEAKS hbm_gbs; NVLink: the pool's measured peer copy of 770 GB/s per
+    direction per GPU (900 nominal)."""
+    rows = c["S"] // world
+    inner, hidden = c["inner"], c["hidden"]
+    hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+    nvlink = 770.0
+
+    def rate(kind, nbytes, peak):
+        ms_, n = prof[kind]["ms"], prof[kind]["launches"]
+        if n == 0 or ms_ <= 0:
+            return None
+        t = ms_ / n / 1e3
+        return dict(gbs=nbytes / t / 1e9, frac=nbytes / t / 1e9 / peak, avg_launch_ms=t * 1e3,
+                    bytes_per_launch=nbytes, launches=n)
+    rope_b = 2 * (2 * rows * inner * 2) + 2 * rows * (ROT // 2) * 2
+    norm_b = 2 * rows * hidden * 2 + rows * 4
+    out = dict(row_kernels=dict(qk_norm_rope=rate("qk_norm_rope", rope_b, hbm),
+                                norm_modscale=rate("norm_modscale", norm_b, hbm),
+                                peak=hbm, peak_kind=f"{peaks_kind} HBM GB/s (copy)"))
+    if world > 1:
+        xb = rows * 3 * inner * 2
+        ex = rate("qkv_to_peers", xb * (world - 1) / world, nvlink)
+        if ex is not None:
+            ex["what"] = "bytes this rank stores into the other ranks' buffers per launch (q|k|v rows of their heads)"
+        pw = prof["peer_wait"]
+        out["exchange"] = dict(qkv_to_peers=ex, nvlink_peak_gbs=nvlink,
+                               nvlink_peak_kind="measured peer copy per direction (pool figure)",
+                               peer_wait_ms=pw["ms"], peer_wait_launches=pw["launches"],
+                               attention_out_peer_bytes_per_launch=(c["S"] * (c["heads"] // world) * 128 * 2
+                                                                    * (world - 1) / world))
+    return out
+
+
 def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     import ctypes
     import torch
@@ -744,9 +785,9 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     sync_all()
     n1 = lib.wx_ctx_launch_count(ctx.h)
     clk = clocks.stop()
-    ms = (ctypes.c_double * 6)()
-    cnt = (ctypes.c_int64 * 6)()
-    lib.wx_ctx_profile_read(ctx.h, ms, cnt, 6)
+    ms = (ctypes.c_double * 10)()
+    cnt = (ctypes.c_int64 * 10)()
+    lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
     lib.wx_ctx_profile_enable(ctx.h, 0)
     ctx.check_device()
     total_ms = _max_over_ranks(e0.elapsed_time(e1), dist)
@@ -757,7 +798,8 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     # work done by this rank: 1/world of every GEMM row and of every attention head
     gemm_flops = sum(f["gemm"] for f in fl) / world
     attn_flops = sum(f["attn"] for f in fl) / world
-    kinds = ["qgemm", "attention", "routing", "row_kernels", "dequant", "collectives"]
+    kinds = ["qgemm", "attention", "routing", "row_kernels", "dequant", "collectives", "qk_norm_rope",
+             "norm_modscale", "qkv_to_peers", "peer_wait"]
     prof = {k: dict(ms=float(ms[i]), launches=int(cnt[i])) for i, k in enumerate(kinds)}
     attn_ms = prof["attention"]["ms"]
     gemm_ms = prof["qgemm"]["ms"]
@@ -783,6 +825,7 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
                 qgemm=dict(tflops=ach_gemm, frac=ach_gemm / peak_t, ms=gemm_ms, launches=prof["qgemm"]["launches"],
                            flops=gemm_flops, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True),
                 kernel_ms=prof, gpu_launches=int(_sum_over_ranks(n1 - n0, dist)), clocks=clk)
+    line.update(memory_bound_kernels(c, prof, world, peaks, peaks_kind))
     # e2e through the public API with host buffers (pinned H2D of each rank's latent rows,
     # D2H of the updated rows)
     if not args.no_e2e:

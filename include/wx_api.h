@@ -158,10 +158,14 @@ size_t wx_ctx_workspace_bytes(wx_ctx* ctx);
 int64_t wx_ctx_launch_count(wx_ctx* ctx);
 int wx_version(void);
 /* Device timing by kernel class (0 qGEMM, 1 flash attention, 2 routing + list
- * build, 3 row kernels, 4 weight dequant, 5 other): while enabled, CUDA events
- * bracket each launch on the context stream. enable(…, 0/1) clears the record;
- * read() synchronises, returns the summed milliseconds and launch counts of the
- * first nkinds classes since the last enable/read, and clears the record. */
+ * build, 3 other row kernels (gated residual, RMSNorm, conversions), 4 weight
+ * dequant, 5 other (NCCL all-to-alls, pack/unpack), 6 QK-RMSNorm + RoPE,
+ * 7 RMSNorm + modulation, 8 QK-RMSNorm + RoPE storing into other ranks' memory
+ * (the fused sequence-parallel exchange), 9 waits for other ranks' signals):
+ * while enabled, CUDA events bracket each launch on the context stream.
+ * enable(…, 0/1) clears the record; read() synchronises, returns the summed
+ * milliseconds and launch counts of the first nkinds classes since the last
+ * enable/read, and clears the record. */
 int wx_ctx_profile_enable(wx_ctx* ctx, int enable);
 int wx_ctx_profile_read(wx_ctx* ctx, double* ms, int64_t* launches, int nkinds);
 
@@ -362,6 +366,21 @@ int wx_ctx_comm_abort(wx_ctx* ctx);
  * all-to-alls, -1 = not decided yet (decided collectively at the first refreshed
  * block of a group) */
 int wx_ctx_sp_exchange(wx_ctx* ctx);
+/* No counterpart in the reference (it has no multi-GPU path). Limit of every wait for
+ * another GPU's signal (the exchange flags of wx_dit_block_forward_sp, and
+ * wx_ctx_wait_flags): a waiting kernel that sees no signal within `seconds` records
+ * a device error (wx_ctx_check_device then returns WX_ERR_DEVICE) and returns, so a
+ * rank that never signals turns into an error on the others instead of a hang; the
+ * context stays usable. Default 10 s; 0 < seconds <= 600. */
+int wx_ctx_set_peer_wait_limit(wx_ctx* ctx, double seconds);
+/* No counterpart in the reference. Cross-GPU signalling on the context stream, the
+ * mechanism of the peer-memory exchange: signal stores `epoch` into flags[0..n) with
+ * release semantics at system scope once this stream's earlier writes are visible
+ * (flags may be another GPU's memory opened in this process); wait holds the stream
+ * until every flags[i] has reached `epoch` (acquire, wrap-around order), bounded by
+ * the peer wait limit. flags 4-byte aligned, n > 0. */
+int wx_ctx_signal_flags(wx_ctx* ctx, uint32_t* flags, int n, uint32_t epoch);
+int wx_ctx_wait_flags(wx_ctx* ctx, const uint32_t* flags, int n, uint32_t epoch);
 int64_t wx_dit_block_sp_scratch_bytes(const wx_dit_config* cfg, int64_t S, int P);
 /* wx_dit_block_forward on this rank's rows of an S-row sequence (the context's
  * communicator decides P and the rank): h/rowmap/cos/sin/pab_slot are the
@@ -443,6 +462,25 @@ typedef struct wx_dit_step_args {
 } wx_dit_step_args;
 int64_t wx_dit_step_scratch_bytes(wx_ctx* ctx, const wx_dit_model* m, int64_t S);
 int wx_dit_step(wx_ctx* ctx, const wx_dit_model* m, const wx_dit_step_args* a);
+
+/* Classifier-free guidance of the SelfLift sampler step (SelfLiftH3-(h3专属).swift:826-845):
+ * the forward runs on the positive condition (a->text_states, with the PAB slots and
+ * a->refresh as in wx_dit_step) and, when text_states_neg is given, again on the negative
+ * condition with attention computed fresh and no PAB slot read or written; the video output
+ * is v = v_neg + cfg_scale * (v_pos - v_neg) in fp32 (audio takes the positive branch).
+ * update = 1 applies the Euler update of wx_dit_step with that output; update = 0 leaves the
+ * latents as they are. velocity_out, when not NULL, receives the video output
+ * ([this rank's video rows, patch_dim] fp32, the forward's negated velocity, the `out.video`
+ * the sampler adds times dsigma). text_states_neg NULL: a single forward (a velocity-out
+ * mode of wx_dit_step). Scratch: wx_dit_step_guided_scratch_bytes bytes in a->scratch. */
+typedef struct wx_dit_guidance {
+  const void* text_states_neg; /* [text_rows, hidden] bf16, padded to the positive's text_rows; NULL = no CFG */
+  float cfg_scale;
+  int32_t update;              /* 1: Euler update of the latents; 0: none */
+  float* velocity_out;         /* NULL or [video rows of this rank, patch_dim] fp32 */
+} wx_dit_guidance;
+int64_t wx_dit_step_guided_scratch_bytes(wx_ctx* ctx, const wx_dit_model* m, int64_t S);
+int wx_dit_step_guided(wx_ctx* ctx, const wx_dit_model* m, const wx_dit_step_args* a, const wx_dit_guidance* g);
 
 /* fp32 dense linear y = x*w + b (H3TensorOps.denseLinear: patch embed and final
  * head islands, H3Transformer.swift:1036-1039, 1192-1203); w [k, n] fp32. */

@@ -245,7 +245,7 @@ def test_invalid_arguments_return_errors(torch_mod):
                       torch.zeros((8, 1), dtype=torch.bfloat16, device="cuda"), 100)
     with pytest.raises(_lib.WxError):
         lin(x)  # K not a multiple of the group / word geometry
-    q = torch.zeros((10, 2, 64), dtype=torch.bfloat16, device="cuda")
+    q = torch.zeros((10, 2, 96), dtype=torch.bfloat16, device="cuda")
     with pytest.raises(_lib.WxError):
-        h3.H3SolAttn.forward(q, q, q, 0, 0.125, None)  # head_dim 64 is not supported by the flash kernel
+        h3.H3SolAttn.forward(q, q, q, 0, 0.125, None)  # the flash kernels take head_dim 128 or 64 only
     h3.context().check_device()

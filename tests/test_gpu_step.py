@@ -153,3 +153,62 @@ def test_step_with_audio_rows():
     assert_close(v_got, ref_v, rel=2e-2, cos=0.999, what="step velocity with audio rows")
     a_got = (agot[10:] - alat[10:]) / np.float32(vscale * da)
     assert_close(a_got, ref_a, rel=2e-2, cos=0.999, what="audio head")
+
+
+def test_step_cfg_guidance():
+    """The SelfLift CFG step (SelfLiftH3-(h3专属).swift:826-845) through wx_dit_step_guided:
+    each branch's video output matches the oracle composition of the step; the guided output is
+    exactly v_neg + cfg*(v_pos - v_neg) of the two single-branch outputs; the negative branch
+    neither reads nor writes the PAB slots; update=1 without CFG equals wx_dit_step."""
+    import torch
+    from wuxianhuabu_b200 import h3
+    S, text, video_start, dsigma, cfg = 344, 40, 104, -0.05, 4.0
+    (blocks, cos, sin, rowmap, lat, ew, eb, ow, ob, fn, fsh, fsc, ts) = _setup(3, S, text, seed=41)
+    ts_neg = O.normal_bf16((text, HIDDEN), 41, 99)
+    dit, _ = _gpu_model(blocks, ew, eb, ow, ob, fn)
+    common = dict(rowmap=torch.from_numpy(rowmap.view(np.int32)).cuda(), cos=to_torch_bf16(cos),
+                  sin=to_torch_bf16(sin), final_shift=to_torch_bf16(fsh), final_scale=to_torch_bf16(fsc))
+    pos_t, neg_t = to_torch_bf16(ts), to_torch_bf16(ts_neg)
+    nv = S - video_start
+    lat_d = torch.from_numpy(lat.copy()).cuda()
+
+    def run(text_states, **kw):
+        v = torch.full((nv, PATCH), float("nan"), dtype=torch.float32, device="cuda")
+        dit.step(S, text, video_start, text_states, lat_d, sparse_cfg=None, policy=0, attn_refresh=True,
+                 dsigma=dsigma, update=False, velocity_out=v, **dict(dict(attn_bcast=None), **kw), **common)
+        return v
+
+    vp = run(pos_t)
+    vn = run(neg_t)
+    vc = run(pos_t, text_states_neg=neg_t, cfg_scale=cfg)
+    h3.context().check_device()
+    assert torch.equal(lat_d, torch.from_numpy(lat).cuda()), "update=0 must leave the latents untouched"
+    vp_, vn_, vc_ = (t.cpu().numpy() for t in (vp, vn, vc))
+    assert np.array_equal(vc_, vn_ + (vp_ - vn_) * np.float32(cfg)), "guided output is not the CFG combination"
+    # each branch against the oracle composition (its velocity is minus the video output)
+    _, ref_pos = _oracle_step(blocks, cos, sin, rowmap, lat, ew, eb, ow, ob, fn, fsh, fsc, ts, text, video_start,
+                              dsigma)
+    _, ref_neg = _oracle_step(blocks, cos, sin, rowmap, lat, ew, eb, ow, ob, fn, fsh, fsc, ts_neg, text,
+                              video_start, dsigma)
+    assert_close(-vp_, ref_pos, rel=2e-2, cos=0.999, what="positive branch")
+    assert_close(-vn_, ref_neg, rel=2e-2, cos=0.999, what="negative branch")
+    # PAB: a guided refresh writes the positive branch's attention outputs only, so a
+    # positive-only reuse step on the same state reproduces the positive output exactly
+    pab = h3.H3AttnBroadcast(3)
+    vc2 = run(pos_t, text_states_neg=neg_t, cfg_scale=cfg, attn_bcast=pab)
+    v_reuse = torch.full((nv, PATCH), float("nan"), dtype=torch.float32, device="cuda")
+    dit.step(S, text, video_start, pos_t, lat_d, sparse_cfg=None, policy=0, attn_bcast=pab, attn_refresh=False,
+             dsigma=dsigma, update=False, velocity_out=v_reuse, **common)
+    torch.cuda.synchronize()
+    assert torch.equal(vc2, vc)
+    assert torch.equal(v_reuse, vp)
+    # update=1 without guidance is wx_dit_step
+    l1, l2 = torch.from_numpy(lat.copy()).cuda(), torch.from_numpy(lat.copy()).cuda()
+    dit.step(S, text, video_start, pos_t, l1, sparse_cfg=None, policy=0, attn_bcast=None, attn_refresh=True,
+             dsigma=dsigma, **common)
+    vo = torch.empty((nv, PATCH), dtype=torch.float32, device="cuda")
+    dit.step(S, text, video_start, pos_t, l2, sparse_cfg=None, policy=0, attn_bcast=None, attn_refresh=True,
+             dsigma=dsigma, velocity_out=vo, **common)
+    h3.context().check_device()
+    assert torch.equal(l1, l2)
+    assert torch.equal(vo, vp)

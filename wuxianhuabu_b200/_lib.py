@@ -100,6 +100,11 @@ class StepArgs(C.Structure):
                 ("audio_vscale", C.c_float), ("audio_dsigma", C.c_float)]
 
 
+class Guidance(C.Structure):
+    _fields_ = [("text_states_neg", C.c_void_p), ("cfg_scale", C.c_float), ("update", C.c_int32),
+                ("velocity_out", C.c_void_p)]
+
+
 class DenseBf16(C.Structure):
     _fields_ = [("w", C.c_void_p), ("bias", C.c_void_p), ("k", C.c_int64), ("n", C.c_int64)]
 
@@ -165,11 +170,16 @@ _SIGS = {
     "wx_ctx_comm_check": (_i32, [_vp]),
     "wx_ctx_comm_abort": (_i32, [_vp]),
     "wx_ctx_sp_exchange": (_i32, [_vp]),
+    "wx_ctx_set_peer_wait_limit": (_i32, [_vp, C.c_double]),
+    "wx_ctx_signal_flags": (_i32, [_vp, _vp, _i32, C.c_uint32]),
+    "wx_ctx_wait_flags": (_i32, [_vp, _vp, _i32, C.c_uint32]),
     "wx_dit_block_sp_scratch_bytes": (_i64, [C.POINTER(DitConfig), _i64, _i32]),
     "wx_dit_block_forward_sp": (_i32, [_vp, C.POINTER(DitConfig), C.POINTER(BlockWeights), C.POINTER(BlockMods),
                                        _vp, _vp, _i64, _vp, _vp, C.POINTER(SparseSpec), _vp, _i32, _vp]),
     "wx_dit_step_scratch_bytes": (_i64, [_vp, C.POINTER(DitModel), _i64]),
     "wx_dit_step": (_i32, [_vp, C.POINTER(DitModel), C.POINTER(StepArgs)]),
+    "wx_dit_step_guided_scratch_bytes": (_i64, [_vp, C.POINTER(DitModel), _i64]),
+    "wx_dit_step_guided": (_i32, [_vp, C.POINTER(DitModel), C.POINTER(StepArgs), C.POINTER(Guidance)]),
     "wx_dense_f32": (_i32, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp]),
     "wx_bf16_to_f32": (_i32, [_vp, _vp, _i64, _vp]),
     "wx_f32_to_bf16": (_i32, [_vp, _vp, _i64, _vp]),

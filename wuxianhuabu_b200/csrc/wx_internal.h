@@ -44,6 +44,8 @@ struct wx_ctx {
   void* p2p_peer[8] = {};
   int* p2p_counters = nullptr;
   uint32_t p2p_epoch = 0;
+  // limit of the cross-GPU flag waits (sequence-parallel exchange, wx_ctx_wait_flags)
+  uint64_t peer_wait_ns = 10000000000ull;
 };
 
 namespace wx {
@@ -97,7 +99,7 @@ int launch_status(wx_ctx* ctx, const char* what, int n = 1);
 int ensure_smem_attr(wx_ctx* ctx, const void* fn, int bytes, const char* what);
 
 enum ProfKind { kProfGemm = 0, kProfAttn = 1, kProfRoute = 2, kProfRow = 3, kProfDequant = 4, kProfOther = 5,
-                kProfKinds = 6 };
+                kProfNormRope = 6, kProfNormMod = 7, kProfExchange = 8, kProfPeerWait = 9, kProfKinds = 10 };
 
 // Records CUDA events around the launches of one kernel class on the
 // context stream while profiling is enabled (no-op otherwise).

@@ -426,7 +426,7 @@ int launch_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, void* out,
   const int64_t rows = S * nparts * H;
   if (rows == 0) return WX_OK;
   const unsigned grid = (unsigned)((rows + 7) / 8);
-  ProfScope prof(ctx, kProfRow);
+  ProfScope prof(ctx, kProfNormRope);
   auto X = static_cast<const __nv_bfloat16*>(x);
   auto O = static_cast<__nv_bfloat16*>(out);
   auto W0 = static_cast<const __nv_bfloat16*>(w0);
@@ -475,7 +475,7 @@ int launch_qkv_to_peers(wx_ctx* ctx, const void* qkv, int64_t rows, int64_t row0
   const int64_t tasks = rows * 3 * n_groups;
   const unsigned grid = (unsigned)std::max<int64_t>(1, (tasks + 7) / 8);
   sig.total = (int)grid;
-  ProfScope prof(ctx, kProfRow);
+  ProfScope prof(ctx, kProfExchange);
   qk_norm_rope_vec_kernel<RopePeerDst, true><<<grid, 256, 0, ctx->stream>>>(
       static_cast<const __nv_bfloat16*>(qkv), 3 * inner, d, inner, 3, rows, H, n_groups,
       static_cast<const __nv_bfloat16*>(w0), static_cast<const __nv_bfloat16*>(w1),
@@ -486,7 +486,7 @@ int launch_qkv_to_peers(wx_ctx* ctx, const void* qkv, int64_t rows, int64_t row0
 int launch_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w,
                          const void* shift, const void* scale, const uint32_t* rowmap, float eps, void* out) {
   if (S == 0) return WX_OK;
-  ProfScope prof(ctx, kProfRow);
+  ProfScope prof(ctx, kProfNormMod);
   auto kern = shift ? norm_modscale_kernel<true> : norm_modscale_kernel<false>;
   kern<<<(unsigned)((S + 7) / 8), 256, 0, ctx->stream>>>(
       static_cast<const __nv_bfloat16*>(x), S, (int)hidden, static_cast<const __nv_bfloat16*>(w),

@@ -151,20 +151,26 @@ int launch_qkv_to_peers(wx_ctx* ctx, const void* qkv, int64_t rows, int64_t row0
                         const void* sin_t, int rot, float eps, PeerSignal sig);
 bool qkv_to_peers_ok(int hd, int rot);
 
-constexpr uint64_t kPeerWaitLimitNs = 10000000000ull;  // 10 s
-
-// waits (bounded) until every rank r has stored `epoch` (or later) into flags[r]
-__global__ void sp_wait_flags_kernel(const uint32_t* flags, int P, uint32_t epoch, int* err) {
-  const int r = threadIdx.x;
-  if (r >= P) return;
+// waits (bounded by limit_ns) until every flags[r], r < n, holds `epoch` or later
+// (wrap-around order); one warp, each lane polling flags lane, lane + 32, ...
+__global__ void sp_wait_flags_kernel(const uint32_t* flags, int n, uint32_t epoch, int* err, uint64_t limit_ns) {
   const uint64_t t0 = globaltimer_ns();
-  while ((int32_t)(ld_acquire_sys_u32(flags + r) - epoch) < 0) {
-    if (globaltimer_ns() - t0 > kPeerWaitLimitNs) {
-      set_dev_error(err, kDevTimeoutPeer);
-      return;
+  for (int r = threadIdx.x; r < n; r += blockDim.x) {
+    while ((int32_t)(ld_acquire_sys_u32(flags + r) - epoch) < 0) {
+      if (globaltimer_ns() - t0 > limit_ns) {
+        set_dev_error(err, kDevTimeoutPeer);
+        return;
+      }
+      __nanosleep(200);
     }
-    __nanosleep(200);
   }
+}
+
+// stores `epoch` into flags[r], r < n, with release semantics at system scope, after
+// every earlier write of this stream is visible (stream order + system fence)
+__global__ void sp_signal_flags_kernel(uint32_t* flags, int n, uint32_t epoch) {
+  __threadfence_system();
+  for (int r = threadIdx.x; r < n; r += blockDim.x) st_release_sys_u32(flags + r, epoch);
 }
 
 struct P2PLayout {
@@ -423,6 +429,25 @@ int wx_ctx_comm_check(wx_ctx* ctx) {
 
 int wx_ctx_sp_exchange(wx_ctx* ctx) { return ctx ? ctx->p2p_state : WX_ERR_INVALID; }
 
+int wx_ctx_set_peer_wait_limit(wx_ctx* ctx, double seconds) {
+  WX_CHECK_ARG(ctx, ctx && seconds > 0.0 && seconds <= 600.0);
+  ctx->peer_wait_ns = (uint64_t)(seconds * 1e9);
+  return WX_OK;
+}
+
+int wx_ctx_signal_flags(wx_ctx* ctx, uint32_t* flags, int n, uint32_t epoch) {
+  WX_CHECK_ARG(ctx, ctx && flags && n > 0 && ((uintptr_t)flags & 3) == 0);
+  sp_signal_flags_kernel<<<1, 32, 0, ctx->stream>>>(flags, n, epoch);
+  return launch_status(ctx, "signal_flags");
+}
+
+int wx_ctx_wait_flags(wx_ctx* ctx, const uint32_t* flags, int n, uint32_t epoch) {
+  WX_CHECK_ARG(ctx, ctx && flags && n > 0 && ((uintptr_t)flags & 3) == 0);
+  ProfScope prof(ctx, kProfPeerWait);
+  sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(flags, n, epoch, ctx->dev_err, ctx->peer_wait_ns);
+  return launch_status(ctx, "wait_flags");
+}
+
 int wx_ctx_comm_abort(wx_ctx* ctx) {
   if (!ctx) return WX_ERR_INVALID;
   if (ctx->comm) nccl().CommAbort(static_cast<ncclComm_t>(ctx->comm));
@@ -507,8 +532,11 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
       if ((st = launch_qkv_to_peers(ctx, qkv, rows, (int64_t)rank * rows, cfg->heads, Hl, qkv_dst, P, w->q_norm,
                                     w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, sig1)))
         return st;
-      sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(mine + PL.flags1), P, ep,
-                                                     ctx->dev_err);
+      {
+        ProfScope wprof(ctx, kProfPeerWait);
+        sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(mine + PL.flags1), P, ep,
+                                                       ctx->dev_err, ctx->peer_wait_ns);
+      }
       if ((st = launch_status(ctx, "sp_wait_qkv"))) return st;
       po.rows = rows;
       po.col = rank * Hl * hd;
@@ -522,8 +550,11 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
       if ((st = attention_with_scratch_peer(ctx, full, full + (int64_t)Hl * hd, full + 2 * (int64_t)Hl * hd, rs, S,
                                             Hl, hd, spec, scale, att_mine, inner, base + L.attn, &po)))
         return st;
-      sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(mine + PL.flags2), P, ep,
-                                                     ctx->dev_err);
+      {
+        ProfScope wprof(ctx, kProfPeerWait);
+        sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(mine + PL.flags2), P, ep,
+                                                       ctx->dev_err, ctx->peer_wait_ns);
+      }
       if ((st = launch_status(ctx, "sp_wait_att"))) return st;
       void* at_dst = pab_slot ? pab_slot : base + L.at;
       if ((st = qlinear_lora_with_scratch(ctx, att_mine, rows, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID,

@@ -575,12 +575,21 @@ class H3DiT:
              rowmap: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, final_shift: torch.Tensor,
              final_scale: torch.Tensor, sparse_cfg: Optional[H3SolAttnConfig], policy: int,
              attn_bcast: Optional[H3AttnBroadcast], attn_refresh: bool, dsigma: float,
-             sigma: Optional[float] = None, audio: Optional[H3AudioRows] = None) -> torch.Tensor:
+             sigma: Optional[float] = None, audio: Optional[H3AudioRows] = None,
+             text_states_neg: Optional[torch.Tensor] = None, cfg_scale: float = 0.0, update: bool = True,
+             velocity_out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """One denoising step; latents [S - text_rows (- audio rows), patch] fp32 (and the audio
-        latents) are updated in place."""
+        latents) are updated in place. With text_states_neg (and cfg_scale > 0) the step is the
+        SelfLift CFG step (SelfLiftH3-(h3专属).swift:826-845): a second forward on the negative
+        condition without the PAB cache and v = v_neg + cfg·(v_pos − v_neg). update=False leaves
+        the latents untouched; velocity_out receives the video output (the negated velocity)."""
         ctx = context(latents.device.index)
         lib = ctx.lib
-        need = int(lib.wx_dit_step_scratch_bytes(ctx.h, C.byref(self._m), S))
+        guided = (text_states_neg is not None and cfg_scale > 0) or not update or velocity_out is not None
+        if guided:
+            need = int(lib.wx_dit_step_guided_scratch_bytes(ctx.h, C.byref(self._m), S))
+        else:
+            need = int(lib.wx_dit_step_scratch_bytes(ctx.h, C.byref(self._m), S))
         if need <= 0:
             raise WxError(_lib.WX_ERR_INVALID, f"no step plan for S={S}")
         if self._scratch is None or self._scratch.numel() < need:
@@ -611,7 +620,12 @@ class H3DiT:
             args.audio_dsigma = float(audio.dsigma)
         else:
             args.audio_target = -1
-        ctx.call("wx_dit_step", C.byref(self._m), C.byref(args))
+        if guided:
+            g = _lib.Guidance(_p(text_states_neg) if cfg_scale > 0 else None, float(cfg_scale), int(bool(update)),
+                              _p(velocity_out))
+            ctx.call("wx_dit_step_guided", C.byref(self._m), C.byref(args), C.byref(g))
+        else:
+            ctx.call("wx_dit_step", C.byref(self._m), C.byref(args))
         if attn_bcast is not None and refresh and sigma is not None:
             attn_bcast.cached_sigma = sigma
         return latents
