@@ -54,8 +54,11 @@ def test_dequant_reference_4bit_fixture(torch_mod):
 
 
 SHAPES = [(1, 128, 192), (77, 256, 384), (128, 512, 512), (300, 1024, 3072), (256, 3072, 256),
-          # small M takes the fused path (weights expanded in shared memory, split-K):
-          (256, 3072, 3072), (257, 1024, 1024), (512, 1024, 3072), (600, 512, 256)]
+          # M <= 512 and N % 128 == 0 take the fused path (weights expanded in shared memory,
+          # K split over a thread-block cluster): one row, a few rows, K blocks not divisible
+          # by the split count, K = 12288 (the fc2 shape), two token tiles
+          (256, 3072, 3072), (257, 1024, 1024), (512, 1024, 3072), (600, 512, 256),
+          (1, 256, 128), (8, 3072, 9216), (100, 704, 640), (33, 12288, 3072), (256, 12288, 3072)]
 
 
 @pytest.mark.parametrize("m,k,n", SHAPES)
@@ -68,6 +71,17 @@ def test_qlinear_none(torch_mod, m, k, n, with_bias):
     ref = O.qlinear(x, wq, sc, bi, bias=bias)
     got = to_np_bf16(_mf(torch_mod, wq, sc, bi, k, bias)(to_torch_bf16(x)))
     assert_close(f32(got), f32(ref), rel=1e-2, cos=0.9999, what=f"qlinear {m}x{k}x{n}")
+
+
+def test_qlinear_fused_is_deterministic(torch_mod):
+    """The split-K sums of the small-M path are reduced in a fixed order: bit-identical runs."""
+    m, k, n = 256, 3072, 3072
+    x = to_torch_bf16(O.normal_bf16((m, k), 35, 1))
+    wq, sc, bi = O.quantize(O.normal_f32((n, k), 35, 2, std=0.02))
+    lin = _mf(torch_mod, wq, sc, bi, k)
+    a = lin(x).clone()
+    b = lin(x)
+    assert torch_mod.equal(a, b)
 
 
 def test_qlinear_gelu(torch_mod):

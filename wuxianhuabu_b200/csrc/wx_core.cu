@@ -86,6 +86,25 @@ int make_tmap_bf16_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t 
   return WX_OK;
 }
 
+int make_tmap_u32_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                     uint32_t box_cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(ctx, WX_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (!aligned16(base) || (ld * 4) % 16 != 0 || (box_cols * 4) % 16 != 0)
+    return set_error(ctx, WX_ERR_INVALID, "TMA operand needs 16-byte aligned base, row pitch and box width");
+  cuuint64_t gdim[2] = {cols, rows};
+  cuuint64_t gstride[1] = {ld * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), gdim, gstride, box, estride,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(ctx, WX_ERR_CUDA, "cuTensorMapEncodeTiled (u32) failed (%d): rows=%llu cols=%llu ld=%llu", (int)r,
+                     (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)ld);
+  return WX_OK;
+}
+
 int launch_status(wx_ctx* ctx, const char* what, int n) {
   ctx->launches += n;
   cudaError_t e = cudaGetLastError();

@@ -69,13 +69,6 @@ __device__ __forceinline__ int4 kv_entry(const WorkItem& it, const int4* entries
 
 __device__ __forceinline__ int item_tiles(const WorkItem& it) { return it.n_implicit + it.list_len; }
 
-// bounded wait used only while draining after an abort (no error recorded)
-__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
-  const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity))
-    if (globaltimer_ns() - t0 > kWaitLimitNs) return;
-}
-
 // a value the compiler must recompute where it is used (keeps MMA descriptors
 // out of registers between uses instead of hoisting all of them)
 __device__ __forceinline__ uint64_t opaque64(uint64_t v) {

@@ -1,20 +1,25 @@
-// wx_gemm_fused.cu — 6-bit quantized linear for small M (weight-bandwidth bound):
-// the packed weights are unpacked and dequantised in shared memory and fed to
-// tcgen05.mma without an expanded copy in global memory.
+// wx_gemm_fused.cu — 6-bit quantized linear for small M (M <= 512: AdaLN tables,
+// condition_proj, the text refiner, the small-M points of the GEMM sweep): the packed
+// weights are expanded in shared memory and fed to tcgen05.mma, with no bf16 copy of
+// the weight in global memory and no second launch.
 //
-// Tiling: a CTA owns a 64-column slice of N, up to 2 x 128 rows of M and a
-// K range (split-K over CTAs so that small-M problems still fill 148 SMs).
-// Per 64-wide K block (= one quantization group):
-//   warp 0      TMA-loads the activation tiles (128x64 bf16, SW128) of every M tile
-//   warps 6..7  each thread loads its weight row's 12 words + scale/bias, expands
-//               the 64 values with fp32 q*scale+bias -> bf16 (bit-identical to
-//               the reference dequant) and stores them in the SW128 K-major
-//               layout the MMA reads; fence.proxy.async; arrive
-//   warp 1      issues tcgen05.mma (M=128, N=64, K=16) per M tile into TMEM
-// after the last K block warps 2..5 store the fp32 partial tile of this K split;
-// a second kernel sums the splits in a fixed order (deterministic) and applies
-// the epilogue (bf16 rounding, bias, GELU or gate + residual) exactly as the main
-// GEMM does.
+// Operand roles are swapped: D^T[n, m] = W[n, :] . X[m, :], so 128 weight rows are the
+// MMA's M and the tokens (up to 256 per CTA) its N; one CTA owns 128 output columns, a
+// tile of up to 256 rows and a K range. Per 64-wide K block (one quantization group):
+//   warp 0      TMA: the activation tile X [Mt x 64] bf16 (SW128) and the packed
+//               weight words [128 rows x 12 u32] of the block
+//   warps 2..5  thread t expands weight row n0+t: 64 six-bit values -> fp32
+//               q*scale+bias (one rounding, as the reference's dequant) -> bf16,
+//               stored in the SW128 K-major layout the MMA reads; scales and biases
+//               come from a 4-deep register ring of plain loads
+//   warp 1      four tcgen05.mma (M=128, N=Mt, K=16) into TMEM [128 lanes x Mt]
+// K is split over the CTAs of a thread-block cluster (up to 8) so that small-M
+// problems fill the SMs. After the last MMA each CTA copies its fp32 partial tile to
+// its own shared memory (transposed, [Mt][128]); after a cluster barrier CTA r sums
+// columns [r*Mt/s, (r+1)*Mt/s) of every CTA's partial through distributed shared
+// memory, in split order 0, 1, ... (deterministic), and applies the epilogue of the
+// main GEMM (bf16 rounding, bias, GELU or gate + residual); a second cluster barrier
+// keeps every partial alive until all CTAs have read it.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -28,77 +33,100 @@ namespace wx {
 
 bool qweight_ok(const wx_qweight* w);
 
-constexpr int kFBN = 64;            // columns per CTA
-constexpr int kFMaxSplits = 4;      // K splits (bounded: the partials live in scratch)
-constexpr int kFBK = 64;            // K per stage (one quantization group)
-constexpr int kFStages = 4;
-constexpr int kFMaxMT = 2;          // M tiles per CTA
-constexpr int kFThreads = 256;      // 8 warps: TMA, MMA, 4 epilogue, 2 dequant (one thread per weight row)
-constexpr int kFABytes = 128 * kFBK * 2;   // one activation tile
-constexpr int kFBBytes = kFBN * kFBK * 2;  // the expanded weight tile
-constexpr int kFStageBytes = kFMaxMT * kFABytes + kFBBytes;
-constexpr int kFBarOffset = kFStages * kFStageBytes;
-constexpr int kFSmem = kFBarOffset + 256 + 1024;
+constexpr int kQRows = 128;          // weight rows (output columns) per CTA
+constexpr int kQBK = 64;             // K per stage (one quantization group)
+constexpr int kQWords = 12;          // packed words of 64 six-bit values
+constexpr int kQStages = 4;
+constexpr int kQMaxMt = 256;         // tokens per CTA (the MMA's N)
+constexpr int kQMaxSplits = 8;       // K splits = cluster size (portable limit)
+constexpr int kQThreads = 192;       // warp 0 TMA, warp 1 MMA, warps 2..5 dequant + epilogue
+constexpr int kQXBytes = kQMaxMt * kQBK * 2;     // activation tile (32 KB)
+constexpr int kQWBytes = kQRows * kQBK * 2;      // expanded weight tile (16 KB)
+constexpr int kQPBytes = kQRows * kQWords * 4;   // packed weight words (6 KB)
+constexpr int kQStageBytes = kQXBytes + kQWBytes + kQPBytes;
+constexpr int kQBarOff = kQStages * kQStageBytes;
+constexpr int kQSmem = kQBarOff + 256 + 1024;
+static_assert(kQStageBytes % 1024 == 0, "SW128 tiles need 1024-byte aligned stages");
+static_assert(kQMaxMt * kQRows * 4 <= kQBarOff, "the partial tile reuses the stage buffers");
 
-struct FusedParams {
-  int M, N, K, mt;            // mt = M tiles this CTA computes (rows m_base .. m_base + 128*mt)
-  int kb_per_split;
-  const uint32_t* wq;
+struct Q6Params {
+  int M, N, K;
+  int Mt;            // tokens per CTA tile (multiple of 16, <= 256)
+  int kb_per_split;  // K blocks per split
+  int splits;        // = cluster size
   const __nv_bfloat16* scales;
   const __nv_bfloat16* biases;
-  int64_t words_per_row;
-  int groups_per_row;
-  float* part;                // [splits][M][N] fp32 partial sums
+  int groups;        // K / 64
+  const __nv_bfloat16* bias;
+  int epi;
+  const __nv_bfloat16* gate;
+  const __nv_bfloat16* resid;
+  const uint32_t* rowmap;
+  __nv_bfloat16* y;
+  int64_t ldy;
+  __nv_bfloat16* y_raw;
   int* err;
 };
 
-// 6-bit value i (0..15) of a 3-word bundle
-__device__ __forceinline__ uint32_t q6(uint32_t w0, uint32_t w1, uint32_t w2, int i) {
+// 6-bit value i (0..15) of a 3-word bundle, OR-ed into the mantissa of 2^23 (so that
+// float(result) - 2^23 = q exactly)
+__device__ __forceinline__ uint32_t q6_bits(uint32_t w0, uint32_t w1, uint32_t w2, int i) {
+  uint32_t q;
   switch (i) {
-    case 0: return w0 & 63u;
-    case 1: return (w0 >> 6) & 63u;
-    case 2: return (w0 >> 12) & 63u;
-    case 3: return (w0 >> 18) & 63u;
-    case 4: return (w0 >> 24) & 63u;
-    case 5: return __funnelshift_r(w0, w1, 30) & 63u;
-    case 6: return (w1 >> 4) & 63u;
-    case 7: return (w1 >> 10) & 63u;
-    case 8: return (w1 >> 16) & 63u;
-    case 9: return (w1 >> 22) & 63u;
-    case 10: return __funnelshift_r(w1, w2, 28) & 63u;
-    case 11: return (w2 >> 2) & 63u;
-    case 12: return (w2 >> 8) & 63u;
-    case 13: return (w2 >> 14) & 63u;
-    case 14: return (w2 >> 20) & 63u;
-    default: return w2 >> 26;
+    case 0: q = w0; break;
+    case 1: q = w0 >> 6; break;
+    case 2: q = w0 >> 12; break;
+    case 3: q = w0 >> 18; break;
+    case 4: q = w0 >> 24; break;
+    case 5: q = __funnelshift_r(w0, w1, 30); break;
+    case 6: q = w1 >> 4; break;
+    case 7: q = w1 >> 10; break;
+    case 8: q = w1 >> 16; break;
+    case 9: q = w1 >> 22; break;
+    case 10: q = __funnelshift_r(w1, w2, 28); break;
+    case 11: q = w2 >> 2; break;
+    case 12: q = w2 >> 8; break;
+    case 13: q = w2 >> 14; break;
+    case 14: q = w2 >> 20; break;
+    default: q = w2 >> 26; break;
   }
+  return (q & 63u) | 0x4B000000u;
 }
 
-// float(q) exactly, by placing q in the low mantissa bits of 2^23
-__device__ __forceinline__ float q_to_f(uint32_t q) { return __uint_as_float(0x4B000000u | q) - 8388608.0f; }
+__device__ __forceinline__ float gelu_tanh_q(float x) {
+  const float c = 0.7978845608028654f;
+  return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
+}
 
-__global__ void __launch_bounds__(kFThreads, 1)
-    gemm_q6_fused_kernel(const __grid_constant__ CUtensorMap tmA, FusedParams p) {
+__global__ void __launch_bounds__(kQThreads, 1)
+    gemm_q6_fused_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                         Q6Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFBarOffset);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kFStages + 1);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kQBarOff);
+  auto full_bar = [&](int s) { return smem_u32(bars + s); };               // X + packed words landed
+  auto wfull_bar = [&](int s) { return smem_u32(bars + kQStages + s); };   // weight tile expanded
+  auto empty_bar = [&](int s) { return smem_u32(bars + 2 * kQStages + s); };  // MMAs of the stage done
+  const uint32_t done_bar = smem_u32(bars + 3 * kQStages);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kQStages + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  auto full_bar = [&](int s) { return smem_u32(bars + s); };
-  auto empty_bar = [&](int s) { return smem_u32(bars + kFStages + s); };
-  const uint32_t done_bar = smem_u32(bars + 2 * kFStages);
+  auto sX = [&](int s) { return smem_u32(smem + s * kQStageBytes); };
+  auto sW = [&](int s) { return smem_u32(smem + s * kQStageBytes + kQXBytes); };
+  auto sP = [&](int s) { return smem_u32(smem + s * kQStageBytes + kQXBytes + kQWBytes); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * kFBN;
-  const int m_base = blockIdx.z * kFMaxMT * 128;
-  const int kb0 = blockIdx.y * p.kb_per_split;
-  const int kb1 = min(kb0 + p.kb_per_split, p.K / kFBK);
-  const int nkb = kb1 - kb0;
-  const int mt = p.mt;
+  const int n0 = blockIdx.x * kQRows;
+  const int split = (int)cluster_ctarank();
+  const int m0 = blockIdx.z * p.Mt;
+  const int kb0 = split * p.kb_per_split;
+  const int kb1 = min(kb0 + p.kb_per_split, p.groups);
+  const int nkb = max(0, kb1 - kb0);
+  const uint32_t tcols = p.Mt <= 32 ? 32u : (p.Mt <= 64 ? 64u : (p.Mt <= 128 ? 128u : 256u));
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kFStages; ++s) {
-      mbar_init(full_bar(s), 1 + kFBN);  // A producer (with tx bytes) + one dequant thread per weight row
+    for (int s = 0; s < kQStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(wfull_bar(s), 4);  // one arrival per dequant warp
       mbar_init(empty_bar(s), 1);
     }
     mbar_init(done_bar, 1);
@@ -106,216 +134,258 @@ __global__ void __launch_bounds__(kFThreads, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kFMaxMT * kFBN);
+    tmem_alloc(smem_u32(tmem_slot), tcols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  bool acc_ok = false;  // (epilogue warps) the accumulator holds this split's sum
 
   if (warp == 0) {
-    if (lane == 0) {
-      prefetch_tmap(&tmA);
+    if (lane == 0 && nkb > 0) {
+      prefetch_tmap(&tmX);
+      prefetch_tmap(&tmW);
+      const uint32_t bytes = (uint32_t)p.Mt * kQBK * 2 + kQPBytes;
+      int issued = 0;
       for (int i = 0; i < nkb; ++i) {
-        const int s = i % kFStages;
-        if (!mbar_wait(empty_bar(s), ((i / kFStages) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
-        mbar_arrive_expect_tx(full_bar(s), mt * kFABytes);
-        const uint32_t sa = smem_u32(smem + s * kFStageBytes);
-        for (int t = 0; t < mt; ++t)
-          tma_load_2d(sa + t * kFABytes, &tmA, full_bar(s), (kb0 + i) * kFBK, m_base + t * 128);
+        const int s = i % kQStages;
+        if (!mbar_wait(empty_bar(s), ((i / kQStages) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
+        mbar_arrive_expect_tx(full_bar(s), bytes);
+        tma_load_2d(sX(s), &tmX, full_bar(s), (kb0 + i) * kQBK, m0);
+        tma_load_2d(sP(s), &tmW, full_bar(s), (kb0 + i) * kQWords, n0);
+        issued = i + 1;
       }
+      if (issued < nkb)  // aborted: let the copies in flight land before the buffers are reused
+        for (int j = max(0, issued - kQStages); j < issued; ++j) mbar_drain(full_bar(j % kQStages), (j / kQStages) & 1);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(128, kFBN, false, false);
+    if (lane == 0 && nkb > 0) {
+      const uint32_t idesc = idesc_bf16_f32(128, p.Mt, false, false);
       bool ok = true;
       for (int i = 0; i < nkb && ok; ++i) {
-        const int s = i % kFStages;
-        if (!mbar_wait(full_bar(s), (i / kFStages) & 1, p.err, kDevTimeoutFull, abort_flag)) {
+        const int s = i % kQStages;
+        const uint32_t par = (i / kQStages) & 1;
+        if (!mbar_wait(full_bar(s), par, p.err, kDevTimeoutFull, abort_flag) ||
+            !mbar_wait(wfull_bar(s), par, p.err, kDevTimeoutFull, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * kFStageBytes);
-        const uint32_t sb = sa + kFMaxMT * kFABytes;
-        for (int t = 0; t < mt; ++t) {
 #pragma unroll
-          for (int kk = 0; kk < kFBK / 16; ++kk)
-            umma_bf16(tmem + t * kFBN, smem_desc_sw128(sa + t * kFABytes + kk * 32, 16, 1024),
-                      smem_desc_sw128(sb + kk * 32, 16, 1024), idesc, (i | kk) != 0 ? 1u : 0u);
-        }
+        for (int kk = 0; kk < kQBK / 16; ++kk)
+          umma_bf16(tmem, smem_desc_sw128(sW(s) + kk * 32, 16, 1024), smem_desc_sw128(sX(s) + kk * 32, 16, 1024),
+                    idesc, (i | kk) != 0 ? 1u : 0u);
         umma_commit(empty_bar(s));
       }
       if (ok) umma_commit(done_bar);
     }
-  } else if (warp >= 6) {
-    // dequant producers: thread t expands weight row n0 + t
-    const int t = threadIdx.x - 6 * 32;
-    const int64_t n = n0 + t;
-    const uint32_t* wrow = p.wq + n * p.words_per_row;
-    const __nv_bfloat16* srow = p.scales + n * p.groups_per_row;
-    const __nv_bfloat16* brow = p.biases + n * p.groups_per_row;
-    // three K blocks of packed words in flight (register ring, statically indexed)
-    constexpr int kDepth = 3;
-    uint4 ra[kDepth], rb[kDepth], rc[kDepth];
-    float rs[kDepth], rbi[kDepth];
-    auto fetch = [&](int slot, int kb) {
-      const uint4* src = reinterpret_cast<const uint4*>(wrow + (int64_t)kb * 12);
-      ra[slot] = __ldg(src);
-      rb[slot] = __ldg(src + 1);
-      rc[slot] = __ldg(src + 2);
-      rs[slot] = __bfloat162float(srow[kb]);
-      rbi[slot] = __bfloat162float(brow[kb]);
-    };
-#pragma unroll
-    for (int d = 0; d < kDepth; ++d)
-      if (d < nkb) fetch(d, kb0 + d);
-    bool ok = true;
-    auto expand = [&](int i, int slot) {
-      const int s = i % kFStages;
-      const uint32_t w[12] = {ra[slot].x, ra[slot].y, ra[slot].z, ra[slot].w, rb[slot].x, rb[slot].y,
-                              rb[slot].z, rb[slot].w, rc[slot].x, rc[slot].y, rc[slot].z, rc[slot].w};
-      const float2 s2 = make_float2(rs[slot], rs[slot]), b2 = make_float2(rbi[slot], rbi[slot]);
-      if (i + kDepth < nkb) fetch(slot, kb0 + i + kDepth);
-      if (!mbar_wait(empty_bar(s), ((i / kFStages) & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) {
-        ok = false;
-        return;
-      }
-      const uint32_t rowaddr = smem_u32(smem + s * kFStageBytes + kFMaxMT * kFABytes) + t * 128;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {  // 8 values per 16-byte chunk; 16 values per 3 words
-        const int bundle = ch >> 1, half = ch & 1;
-        const uint32_t w0 = w[bundle * 3], w1 = w[bundle * 3 + 1], w2 = w[bundle * 3 + 2];
-        uint32_t packed[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i0 = half * 8 + 2 * e;
-          const float2 q = make_float2(q_to_f(q6(w0, w1, w2, i0)), q_to_f(q6(w0, w1, w2, i0 + 1)));
-          const float2 v = __ffma2_rn(q, s2, b2);  // one rounding, as fp32 q*s + b (q*s exact)
-          packed[e] = pack_bf16x2(v.x, v.y);
-        }
-        const uint32_t addr = rowaddr + ((ch ^ (t & 7)) << 4);
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[0]), "r"(packed[1]),
-                     "r"(packed[2]), "r"(packed[3])
-                     : "memory");
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(full_bar(s));
-    };
-    for (int i = 0; i < nkb && ok; i += kDepth) {
-#pragma unroll
-      for (int d = 0; d < kDepth; ++d)
-        if (ok && i + d < nkb) expand(i + d, d);
-    }
   } else {
-    // warps 2..5: store this split's fp32 partial tile
-    const int quarter = warp & 3;
-    const bool ok = nkb > 0 && mbar_wait(done_bar, 0, p.err, kDevTimeoutAcc, abort_flag);
-    tc_fence_after();
-    for (int tt = 0; tt < mt; ++tt) {
-      const int64_t m = m_base + tt * 128 + quarter * 32 + lane;
-#pragma unroll 1
-      for (int cc = 0; cc < kFBN / 32; ++cc) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + tt * kFBN + cc * 32, v);
-        tmem_wait_ld();
-        if (!ok || m >= p.M) continue;
-        float* dst = p.part + ((int64_t)blockIdx.y * p.M + m) * p.N + n0 + cc * 32;
+    // ---------------------------------------------------------------- dequant
+    const int t = threadIdx.x - 64;  // weight row n0 + t (0..127)
+    const int64_t n = n0 + t;
+    const __nv_bfloat16* srow = p.scales + n * p.groups;
+    const __nv_bfloat16* brow = p.biases + n * p.groups;
+    constexpr int kDepth = 4;  // scale/bias of the next K blocks in flight
+    float rs[kDepth], rb[kDepth];
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    for (int d = 0; d < kDepth; ++d) {
+      rs[d] = d < nkb ? __bfloat162float(srow[kb0 + d]) : 0.f;
+      rb[d] = d < nkb ? __bfloat162float(brow[kb0 + d]) : 0.f;
+    }
+    bool ok = true;
+    for (int i0 = 0; i0 < nkb && ok; i0 += kDepth) {
+#pragma unroll
+      for (int d = 0; d < kDepth; ++d) {
+        const int i = i0 + d;
+        if (!ok || i >= nkb) break;
+        const int s = i % kQStages;
+        if (!mbar_wait(full_bar(s), (i / kQStages) & 1, p.err, kDevTimeoutFull, abort_flag)) {
+          ok = false;
+          break;
+        }
+        uint32_t w[12];
+        const uint32_t pa = sP(s) + t * (kQWords * 4);
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(w[4 * q]), "=r"(w[4 * q + 1]), "=r"(w[4 * q + 2]), "=r"(w[4 * q + 3])
+                       : "r"(pa + q * 16));
+        const float2 s2 = make_float2(rs[d], rs[d]), b2 = make_float2(rb[d], rb[d]);
+        if (i + kDepth < nkb) {  // refill this ring slot for block i + kDepth
+          rs[d] = __bfloat162float(srow[kb0 + i + kDepth]);
+          rb[d] = __bfloat162float(brow[kb0 + i + kDepth]);
+        }
+        const uint32_t rowaddr = sW(s) + t * 128;
+        const float2 magic = make_float2(-8388608.0f, -8388608.0f);
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {  // 8 values per 16-byte chunk; 16 values per 3 words
+          const int bundle = ch >> 1, half = ch & 1;
+          const uint32_t w0 = w[bundle * 3], w1 = w[bundle * 3 + 1], w2 = w[bundle * 3 + 2];
+          uint32_t packed[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i0v = half * 8 + 2 * e;
+            float2 q = make_float2(__uint_as_float(q6_bits(w0, w1, w2, i0v)),
+                                   __uint_as_float(q6_bits(w0, w1, w2, i0v + 1)));
+            q = __fadd2_rn(q, magic);                 // exact: the integer q in [0, 63]
+            const float2 v = __ffma2_rn(q, s2, b2);   // one rounding, as fp32 q*s + b (q*s exact)
+            packed[e] = pack_bf16x2(v.x, v.y);
+          }
+          const uint32_t addr = rowaddr + ((ch ^ (t & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[0]), "r"(packed[1]),
+                       "r"(packed[2]), "r"(packed[3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(wfull_bar(s));
       }
+    }
+    // ------------------------------------------------ partial tile -> shared memory
+    acc_ok = ok && nkb > 0 && mbar_wait(done_bar, 0, p.err, kDevTimeoutAcc, abort_flag);
+    tc_fence_after();
+    // (every MMA has completed, so the stage buffers are free for the transposed partial)
+    float* part = reinterpret_cast<float*>(smem);  // [Mt][128]
+    const int q4 = warp & 3;                       // TMEM lane quarter of this warp
+    const int r = q4 * 32 + lane;
+    for (int c0 = 0; c0 < p.Mt; c0 += 32) {
+      float v[32];
+      if (acc_ok) {
+        tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + c0, v);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (c0 + i < p.Mt) part[(c0 + i) * kQRows + r] = v[i];
     }
   }
+  __syncwarp();
+  cluster_sync_all();  // every CTA's partial is in its shared memory
+  if (warp >= 2) {
+    // ------------------------------------- reduction over the cluster + epilogue
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const int64_t n = n0 + r;
+    const int per = (p.Mt + p.splits - 1) / p.splits;
+    const int c_lo = split * per, c_hi = min(p.Mt, c_lo + per);
+    const uint32_t base = smem_u32(smem) + (uint32_t)r * 4;
+    uint32_t peer[kQMaxSplits];
+#pragma unroll
+    for (int j = 0; j < kQMaxSplits; ++j) peer[j] = j < p.splits ? mapa_shared(base, (uint32_t)j) : 0u;
+    const float bv = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
+    for (int c = c_lo; c < c_hi; ++c) {
+      const int64_t m = m0 + c;
+      if (m >= p.M) break;
+      const uint32_t off = (uint32_t)c * kQRows * 4;
+      float acc = ld_shared_cluster_f32(peer[0] + off);
+#pragma unroll
+      for (int j = 1; j < kQMaxSplits; ++j)
+        if (j < p.splits) acc += ld_shared_cluster_f32(peer[j] + off);
+      float tv = round_bf16(acc);
+      if (p.bias) tv = round_bf16(tv + bv);
+      float o = tv;
+      if (p.epi == WX_EPI_GATE_RESID) {
+        const int64_t mr = p.rowmap ? (int64_t)p.rowmap[m] : 0;
+        if (p.y_raw) p.y_raw[m * p.ldy + n] = __float2bfloat16_rn(tv);
+        o = __bfloat162float(p.resid[m * p.ldy + n]) + tv * __bfloat162float(p.gate[mr * (int64_t)p.N + n]);
+      } else if (p.epi == WX_EPI_GELU) {
+        o = gelu_tanh_q(tv);
+      }
+      p.y[m * p.ldy + n] = __float2bfloat16_rn(o);
+    }
+  }
+  __syncwarp();
+  cluster_sync_all();  // no CTA leaves while another still reads its partial
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, kFMaxMT * kFBN);
+    tmem_dealloc(tmem, tcols);
   }
 }
 
-// epilogue of the split-K path: same rounding sequence as the main GEMM epilogue
-__global__ void fused_epilogue_kernel(const float* __restrict__ part, int splits, int64_t M, int N,
-                                      const __nv_bfloat16* __restrict__ bias, int epi,
-                                      const __nv_bfloat16* __restrict__ gate, const __nv_bfloat16* __restrict__ resid,
-                                      const uint32_t* __restrict__ rowmap, __nv_bfloat16* __restrict__ y, int64_t ldy,
-                                      __nv_bfloat16* __restrict__ y_raw) {
-  const int64_t total = M * N;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / N;
-    const int n = (int)(i % N);
-    float a = part[i];
-    for (int sp = 1; sp < splits; ++sp) a += part[(int64_t)sp * total + i];
-    float t = round_bf16(a);
-    if (bias) t = round_bf16(t + __bfloat162float(bias[n]));
-    float o = t;
-    if (epi == WX_EPI_GELU) {
-      const float cst = 0.7978845608028654f;
-      o = 0.5f * t * (1.0f + tanhf(cst * (t + 0.044715f * t * t * t)));
-    } else if (epi == WX_EPI_GATE_RESID) {
-      const int64_t mr = rowmap ? (int64_t)rowmap[m] : 0;
-      o = __bfloat162float(resid[m * ldy + n]) + t * __bfloat162float(gate[mr * N + n]);
-      if (y_raw) y_raw[m * ldy + n] = __float2bfloat16_rn(t);
-    }
-    y[m * ldy + n] = __float2bfloat16_rn(o);
-  }
-}
+size_t fused_scratch_bytes(int64_t, int64_t) { return 0; }
 
-size_t fused_scratch_bytes(int64_t M, int64_t N) { return ((size_t)kFMaxSplits * M * N * 4 + 255) & ~size_t(255); }
-
-// eligible: 6-bit, group 64, N % 128 == 0, small M (handled in blocks of 256 rows)
+// eligible: 6-bit, group 64, N % 128 == 0, M <= 512 (tiles of <= 256 rows), not SwiGLU
 bool fused_eligible(const wx_qweight* w, int64_t M, int epilogue) {
-  // beyond one wave of N tiles (148 x 64 columns) every CTA streams all of K and
-  // the two-pass GEMM measured faster (M=256, N=12288: 111 vs 130 us)
-  return w->bits == 6 && w->group == kFBK && w->n % kFBN == 0 && w->k % kFBK == 0 && M > 0 && M <= 512 &&
-         w->n <= 148 * kFBN && epilogue != WX_EPI_SWIGLU && (w->k * 6 / 32) % 4 == 0;
+  return w->bits == 6 && w->group == kQBK && w->n % kQRows == 0 && w->k % kQBK == 0 && M > 0 && M <= 512 &&
+         epilogue != WX_EPI_SWIGLU && w->n <= INT32_MAX && w->k <= INT32_MAX;
 }
 
 int qlinear_fused(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const wx_qweight* w, int epilogue,
                   const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw,
-                  void* scratch) {
-  int st = ensure_smem_attr(ctx, (const void*)gemm_q6_fused_kernel, kFSmem, "gemm_q6_fused");
+                  void* /*scratch*/) {
+  int st = ensure_smem_attr(ctx, (const void*)gemm_q6_fused_kernel, kQSmem, "gemm_q6_fused");
   if (st) return st;
-  CUtensorMap ta;
-  st = make_tmap_bf16_2d(ctx, &ta, x, (uint64_t)M, (uint64_t)w->k, (uint64_t)lda, kFBK, 128);
-  if (st) return st;
-  float* part = static_cast<float*>(scratch);
-  const int n_tiles = (int)(w->n / kFBN);
-  const int m_groups = (int)((M + kFMaxMT * 128 - 1) / (kFMaxMT * 128));
-  const int kbs = (int)(w->k / kFBK);
-  int splits = std::max(1, ctx->num_sms / std::max(1, n_tiles * m_groups));
-  splits = std::min(std::min(splits, kFMaxSplits), std::max(1, kbs / 4));  // >= 4 K blocks per CTA
+  if (!aligned16(x) || lda % 8 != 0)
+    return set_error(ctx, WX_ERR_INVALID, "fused qlinear: x needs 16-byte aligned rows");
+  // token tiles of Mt rows (balanced, a multiple of 16, at most 256)
+  const int zt = (int)((M + kQMaxMt - 1) / kQMaxMt);
+  const int Mt = (int)((((M + zt - 1) / zt) + 15) / 16 * 16);
+  const int n_tiles = (int)(w->n / kQRows);
+  const int kbs = (int)(w->k / kQBK);
+  // K splits (= cluster size, <= 8): the fewest waves of CTAs times K blocks per CTA, plus
+  // a small cost per split for the cluster reduction
+  int splits = 1;
+  double best = 1e30;
+  for (int s = 1; s <= kQMaxSplits && s <= kbs; ++s) {
+    const int64_t ctas = (int64_t)n_tiles * zt * s;
+    const double waves = (double)((ctas + ctx->num_sms - 1) / ctx->num_sms);
+    const double cost = waves * ((kbs + s - 1) / s + 3) + 0.25 * s;
+    if (cost < best - 1e-9) {
+      best = cost;
+      splits = s;
+    }
+  }
   const int kb_per = (kbs + splits - 1) / splits;
-  splits = (kbs + kb_per - 1) / kb_per;
-  FusedParams p{};
+  CUtensorMap tx, tw;
+  if ((st = make_tmap_bf16_2d(ctx, &tx, x, (uint64_t)M, (uint64_t)w->k, (uint64_t)lda, kQBK, (uint32_t)Mt))) return st;
+  const int64_t words = w->k * 6 / 32;
+  if ((st = make_tmap_u32_2d(ctx, &tw, w->wq, (uint64_t)w->n, (uint64_t)words, (uint64_t)words, kQWords, kQRows)))
+    return st;
+  Q6Params p{};
   p.M = (int)M;
   p.N = (int)w->n;
   p.K = (int)w->k;
-  p.mt = (int)std::min<int64_t>(kFMaxMT, (M + 127) / 128);
+  p.Mt = Mt;
   p.kb_per_split = kb_per;
-  p.wq = w->wq;
+  p.splits = splits;
   p.scales = static_cast<const __nv_bfloat16*>(w->scales);
   p.biases = static_cast<const __nv_bfloat16*>(w->biases);
-  p.words_per_row = w->k * 6 / 32;
-  p.groups_per_row = (int)(w->k / kFBK);
-  p.part = part;
+  p.groups = kbs;
+  p.bias = static_cast<const __nv_bfloat16*>(w->bias);
+  p.epi = epilogue;
+  p.gate = static_cast<const __nv_bfloat16*>(gate);
+  p.resid = static_cast<const __nv_bfloat16*>(resid);
+  p.rowmap = rowmap;
+  p.y = static_cast<__nv_bfloat16*>(y);
+  p.ldy = ldy;
+  p.y_raw = static_cast<__nv_bfloat16*>(y_raw);
   p.err = ctx->dev_err;
-  {
-    ProfScope prof(ctx, kProfGemm);
-    // rows past M in the last group read zero-filled activation tiles and are not stored
-    dim3 grid(n_tiles, splits, m_groups);
-    gemm_q6_fused_kernel<<<grid, kFThreads, kFSmem, ctx->stream>>>(ta, p);
-    if ((st = launch_status(ctx, "gemm_q6_fused"))) return st;
-    const int64_t total = M * w->n;
-    const unsigned g = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, ctx->num_sms * 8));
-    fused_epilogue_kernel<<<g, 256, 0, ctx->stream>>>(part, splits, M, (int)w->n, static_cast<const __nv_bfloat16*>(w->bias),
-                                                      epilogue, static_cast<const __nv_bfloat16*>(gate),
-                                                      static_cast<const __nv_bfloat16*>(resid), rowmap,
-                                                      static_cast<__nv_bfloat16*>(y), ldy,
-                                                      static_cast<__nv_bfloat16*>(y_raw));
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)n_tiles, (unsigned)splits, (unsigned)zt);
+  cfg.blockDim = dim3(kQThreads, 1, 1);
+  cfg.dynamicSmemBytes = kQSmem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)splits;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ProfScope prof(ctx, kProfGemm);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_q6_fused_kernel, tx, tw, p);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(ctx, WX_ERR_CUDA, "gemm_q6_fused launch (cluster of %d): %s", splits, cudaGetErrorString(e));
   }
-  return launch_status(ctx, "fused_epilogue");
+  return launch_status(ctx, "gemm_q6_fused");
 }
 
 }  // namespace wx

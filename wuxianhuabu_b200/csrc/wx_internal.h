@@ -84,6 +84,11 @@ struct Carve {
 int make_tmap_bf16_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t rows,
                       uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows);
 
+// 2-D uint32 tensor map (no swizzle): `rows` x `cols` words, row pitch `ld` words,
+// box `box_cols` x `box_rows`, zero fill out of bounds.
+int make_tmap_u32_2d(wx_ctx* ctx, CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                     uint32_t box_cols, uint32_t box_rows);
+
 // releases the NCCL communicator of a context (no-op without one)
 void sp_destroy_comm(wx_ctx* ctx);
 // releases the peer exchange buffers of a context (closes the peers' mappings first)
@@ -110,14 +115,9 @@ struct ProfScope {
   ~ProfScope();
 };
 
-// Scratch of one quantized linear: the expanded bf16 weight of the two-pass
-// GEMM, or (small M, at most 512 rows) the fp32 partials of up to 4 K splits
-// of the shared-memory dequant path.
-inline size_t qlinear_ws_need(int64_t m, int64_t n, int64_t k) {
-  const size_t two_pass = (size_t)n * k * 2;
-  const size_t fused = m <= 512 ? (size_t)4 * m * n * 4 : 0;
-  return two_pass > fused ? two_pass : fused;
-}
+// Scratch of one quantized linear: the expanded bf16 weight of the two-pass GEMM
+// (the small-M path, at most 512 rows, expands in shared memory and needs none).
+inline size_t qlinear_ws_need(int64_t /*m*/, int64_t n, int64_t k) { return (size_t)n * k * 2; }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
