@@ -8,13 +8,14 @@
 // tile of up to 256 rows and a K range. Per 64-wide K block (one quantization group):
 //   warp 0      TMA: the activation tile X [Mt x 64] bf16 (SW128) and the packed
 //               weight words [128 rows x 12 u32] of the block
-//   warps 2..5  thread t expands weight row n0+t: 64 six-bit values -> fp32
-//               q*scale+bias (one rounding, as the reference's dequant) -> bf16,
-//               stored in the SW128 K-major layout the MMA reads; scales and biases
-//               come from a 4-deep register ring of plain loads
+//   warps 2..9  two threads per weight row (row n0 + t/2, half t%2): 32 six-bit
+//               values each -> fp32 q*scale+bias (one rounding, as the reference's
+//               dequant) -> bf16, stored in the SW128 K-major layout the MMA reads;
+//               scales and biases come from a 4-deep register ring of plain loads
 //   warp 1      four tcgen05.mma (M=128, N=Mt, K=16) into TMEM [128 lanes x Mt]
 // K is split over the CTAs of a thread-block cluster (up to 8) so that small-M
-// problems fill the SMs. After the last MMA each CTA copies its fp32 partial tile to
+// problems fill the SMs; the split count is chosen so that every cluster of the
+// launch is resident at once (cudaOccupancyMaxActiveClusters). After the last MMA each CTA copies its fp32 partial tile to
 // its own shared memory (transposed, [Mt][128]); after a cluster barrier CTA r sums
 // columns [r*Mt/s, (r+1)*Mt/s) of every CTA's partial through distributed shared
 // memory, in split order 0, 1, ... (deterministic), and applies the epilogue of the
@@ -25,6 +26,9 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "wx_internal.h"
 #include "wx_ptx.cuh"
@@ -39,7 +43,8 @@ constexpr int kQWords = 12;          // packed words of 64 six-bit values
 constexpr int kQStages = 4;
 constexpr int kQMaxMt = 256;         // tokens per CTA (the MMA's N)
 constexpr int kQMaxSplits = 8;       // K splits = cluster size (portable limit)
-constexpr int kQThreads = 192;       // warp 0 TMA, warp 1 MMA, warps 2..5 dequant + epilogue
+constexpr int kQThreads = 320;       // warp 0 TMA, warp 1 MMA, warps 2..9 dequant + epilogue
+constexpr int kQDequantWarps = 8;
 constexpr int kQXBytes = kQMaxMt * kQBK * 2;     // activation tile (32 KB)
 constexpr int kQWBytes = kQRows * kQBK * 2;      // expanded weight tile (16 KB)
 constexpr int kQPBytes = kQRows * kQWords * 4;   // packed weight words (6 KB)
@@ -126,7 +131,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kQStages; ++s) {
       mbar_init(full_bar(s), 1);
-      mbar_init(wfull_bar(s), 4);  // one arrival per dequant warp
+      mbar_init(wfull_bar(s), kQDequantWarps);  // one arrival per dequant warp
       mbar_init(empty_bar(s), 1);
     }
     mbar_init(done_bar, 1);
@@ -183,8 +188,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- dequant
-    const int t = threadIdx.x - 64;  // weight row n0 + t (0..127)
-    const int64_t n = n0 + t;
+    const int t = threadIdx.x - 64;  // 0..255
+    const int row = t >> 1, hf = t & 1;  // weight row n0 + row, values [32 hf, 32 hf + 32) of the block
+    const int64_t n = n0 + row;
     const __nv_bfloat16* srow = p.scales + n * p.groups;
     const __nv_bfloat16* brow = p.biases + n * p.groups;
     constexpr int kDepth = 4;  // scale/bias of the next K blocks in flight
@@ -205,23 +211,22 @@ __global__ void __launch_bounds__(kQThreads, 1)
           ok = false;
           break;
         }
-        uint32_t w[12];
-        const uint32_t pa = sP(s) + t * (kQWords * 4);
+        uint32_t w[6];  // two 3-word bundles = 32 values
+        const uint32_t pa = sP(s) + row * (kQWords * 4) + hf * 24;
 #pragma unroll
         for (int q = 0; q < 3; ++q)
-          asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(w[4 * q]), "=r"(w[4 * q + 1]), "=r"(w[4 * q + 2]), "=r"(w[4 * q + 3])
-                       : "r"(pa + q * 16));
+          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[2 * q]), "=r"(w[2 * q + 1]) : "r"(pa + q * 8));
         const float2 s2 = make_float2(rs[d], rs[d]), b2 = make_float2(rb[d], rb[d]);
         if (i + kDepth < nkb) {  // refill this ring slot for block i + kDepth
           rs[d] = __bfloat162float(srow[kb0 + i + kDepth]);
           rb[d] = __bfloat162float(brow[kb0 + i + kDepth]);
         }
-        const uint32_t rowaddr = sW(s) + t * 128;
+        const uint32_t rowaddr = sW(s) + row * 128;
         const float2 magic = make_float2(-8388608.0f, -8388608.0f);
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {  // 8 values per 16-byte chunk; 16 values per 3 words
-          const int bundle = ch >> 1, half = ch & 1;
+        for (int c4 = 0; c4 < 4; ++c4) {  // 8 values per 16-byte chunk; 16 values per 3 words
+          const int ch = hf * 4 + c4;
+          const int bundle = c4 >> 1, half = c4 & 1;
           const uint32_t w0 = w[bundle * 3], w1 = w[bundle * 3 + 1], w2 = w[bundle * 3 + 2];
           uint32_t packed[4];
 #pragma unroll
@@ -233,7 +238,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
             const float2 v = __ffma2_rn(q, s2, b2);   // one rounding, as fp32 q*s + b (q*s exact)
             packed[e] = pack_bf16x2(v.x, v.y);
           }
-          const uint32_t addr = rowaddr + ((ch ^ (t & 7)) << 4);
+          const uint32_t addr = rowaddr + ((ch ^ (row & 7)) << 4);
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(packed[0]), "r"(packed[1]),
                        "r"(packed[2]), "r"(packed[3])
                        : "memory");
@@ -249,8 +254,9 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // (every MMA has completed, so the stage buffers are free for the transposed partial)
     float* part = reinterpret_cast<float*>(smem);  // [Mt][128]
     const int q4 = warp & 3;                       // TMEM lane quarter of this warp
+    const int cg = (warp - 2) >> 2;                // column group: 32-column chunks cg, cg + 2, ...
     const int r = q4 * 32 + lane;
-    for (int c0 = 0; c0 < p.Mt; c0 += 32) {
+    for (int c0 = cg * 32; c0 < p.Mt; c0 += 64) {
       float v[32];
       if (acc_ok) {
         tmem_ld32(tmem + ((uint32_t)(q4 * 32) << 16) + c0, v);
@@ -269,6 +275,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (warp >= 2) {
     // ------------------------------------- reduction over the cluster + epilogue
     const int q4 = warp & 3;
+    const int cg = (warp - 2) >> 2;  // even / odd columns of the slice
     const int r = q4 * 32 + lane;
     const int64_t n = n0 + r;
     const int per = (p.Mt + p.splits - 1) / p.splits;
@@ -278,7 +285,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
 #pragma unroll
     for (int j = 0; j < kQMaxSplits; ++j) peer[j] = j < p.splits ? mapa_shared(base, (uint32_t)j) : 0u;
     const float bv = p.bias ? __bfloat162float(p.bias[n]) : 0.f;
-    for (int c = c_lo; c < c_hi; ++c) {
+    for (int c = c_lo + cg; c < c_hi; c += 2) {
       const int64_t m = m0 + c;
       if (m >= p.M) break;
       const uint32_t off = (uint32_t)c * kQRows * 4;
@@ -317,6 +324,35 @@ bool fused_eligible(const wx_qweight* w, int64_t M, int epilogue) {
          epilogue != WX_EPI_SWIGLU && w->n <= INT32_MAX && w->k <= INT32_MAX;
 }
 
+// clusters of `size` CTAs of the kernel the current device holds at once (cached per device)
+static int max_active_clusters(int size) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find({dev, size});
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1, (unsigned)size, 1);
+  cfg.blockDim = dim3(kQThreads, 1, 1);
+  cfg.dynamicSmemBytes = kQSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)size;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_q6_fused_kernel, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[{dev, size}] = n;
+  return n;
+}
+
 int qlinear_fused(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const wx_qweight* w, int epilogue,
                   const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw,
                   void* /*scratch*/) {
@@ -329,13 +365,16 @@ int qlinear_fused(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const wx_q
   const int Mt = (int)((((M + zt - 1) / zt) + 15) / 16 * 16);
   const int n_tiles = (int)(w->n / kQRows);
   const int kbs = (int)(w->k / kQBK);
-  // K splits (= cluster size, <= 8): the fewest waves of CTAs times K blocks per CTA, plus
-  // a small cost per split for the cluster reduction
+  // K splits (= cluster size, <= 8): the fewest waves of clusters (at most the number of
+  // clusters of that size the device holds at once) times K blocks per CTA, plus a small
+  // cost per split for the cluster reduction
+  const int64_t clusters = (int64_t)n_tiles * zt;
   int splits = 1;
   double best = 1e30;
   for (int s = 1; s <= kQMaxSplits && s <= kbs; ++s) {
-    const int64_t ctas = (int64_t)n_tiles * zt * s;
-    const double waves = (double)((ctas + ctx->num_sms - 1) / ctx->num_sms);
+    const int active = max_active_clusters(s);
+    if (active <= 0) continue;
+    const double waves = (double)((clusters + active - 1) / active);
     const double cost = waves * ((kbs + s - 1) / s + 3) + 0.25 * s;
     if (cost < best - 1e-9) {
       best = cost;
