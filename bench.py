@@ -377,10 +377,12 @@ def window_plan() -> list:
 
 
 # ------------------------------------------------------------------ kernel-level configs
-def run_c3(args, seq: int, dense: bool = False) -> dict:
+def run_c3(args, seq: int, dense: bool = False, g: int = 0) -> dict:
     """standalone block-sparse attention (24 x 128 heads,
     128-row blocks, diagonal + top-k 25 %, g = 0, no tail), routing included.
-    dense=True: the dense attention of the dense layers and strip rows at the same size."""
+    dense=True: the dense attention of the dense layers and strip rows at the same size.
+    g > 0: the attention call of the config-5 step's layers (strip rows [0, g) exact over all
+    keys, video rows routed), standalone; used for the DRAM-traffic capture of the roofline."""
     import torch
     from wuxianhuabu_b200 import h3
     dev = torch.device("cuda", 0)
@@ -392,23 +394,23 @@ def run_c3(args, seq: int, dense: bool = False) -> dict:
     scale = float(1 / math.sqrt(128))
     ctx = h3.context(0)
     for _ in range(args.warmup):
-        h3.H3SolAttn.forward(q, k, v, 0, scale, cfg, out=out)
+        h3.H3SolAttn.forward(q, k, v, g, scale, cfg, out=out)
     torch.cuda.synchronize()
     import ctypes
     ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        h3.H3SolAttn.forward(q, k, v, 0, scale, cfg, out=out)
+        h3.H3SolAttn.forward(q, k, v, g, scale, cfg, out=out)
     e1.record()
     torch.cuda.synchronize()
     ms = (ctypes.c_double * 6)()
     cnt = (ctypes.c_int64 * 6)()
     ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 6)
     ctx.check_device()
-    nb = (seq + 127) // 128
+    nb = (seq - g + 127) // 128
     keep = min(math.ceil(TOPK_DENSITY * nb), nb - 1) + 1
-    flops = 4.0 * 128 * H * seq * (seq if dense else min(keep * 128, seq))
+    flops = 4.0 * 128 * H * (seq * seq if dense else g * seq + (seq - g) * (g + min(keep * 128, seq - g)))
     peaks, kind = load_peaks()
     per_call = e0.elapsed_time(e1) / args.steps
     flash_ms = ms[1] / max(1, cnt[1])
@@ -417,8 +419,10 @@ def run_c3(args, seq: int, dense: bool = False) -> dict:
     kernel = ("flash_attn_pair_kernel<false, 128> (paired query tiles, shared K/V)" if dense else
               "flash_attn_pair_kernel<true, 128> (duo: two routed query tiles per CTA)")
     what = "dense attention" if dense else "SOL top-k 25% attention"
-    return dict(metric=f"{'dense' if dense else 'sparse'} attention ms/call (c3)", value=per_call, unit="ms/call",
-                config=dict(workload=f"c3: {what}, S={seq}, 24x128 heads", S=seq), higher_is_better=False,
+    name = "c3" if g == 0 else "c5 layer geometry"
+    return dict(metric=f"{'dense' if dense else 'sparse'} attention ms/call ({name})", value=per_call, unit="ms/call",
+                config=dict(workload=f"{name}: {what}, S={seq}, strip rows {g}, 24x128 heads", S=seq, g=g),
+                higher_is_better=False,
                 roofline=dict(kernel=kernel, bound="tensor", achieved=ach, peak=pk, unit="TFLOP/s",
                               frac=ach / pk, avg_launch_ms=flash_ms, flops_per_launch=flops,
                               peak_kind=f"{kind} burst bf16"),
@@ -569,8 +573,10 @@ def run_c2(args) -> dict:
     from wuxianhuabu_b200 import h3
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(1234 + 1)
+    import ctypes
     peaks, kind = load_peaks()
     pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
+    hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
     res = []
     shapes = [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]
     ms_list = (256, 4096, 28520, 111600)
@@ -589,6 +595,8 @@ def run_c2(args) -> dict:
             for _ in range(max(1, args.warmup)):
                 lin(x, out=y)
             torch.cuda.synchronize()
+            ctx = h3.context(0)
+            ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             reps = max(1, args.steps)
@@ -596,13 +604,24 @@ def run_c2(args) -> dict:
                 lin(x, out=y)
             e1.record()
             torch.cuda.synchronize()
-            t = e0.elapsed_time(e1) / reps / 1e3
+            ms = (ctypes.c_double * 10)()
+            cnt = (ctypes.c_int64 * 10)()
+            ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
+            ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
+            t_call = e0.elapsed_time(e1) / reps / 1e3
+            # the kernels' own time: CUDA events libwx records around each launch (the GEMM,
+            # plus the weight expansion of the two-pass path), free of host gaps between calls
+            t = (ms[0] + ms[4]) / reps / 1e3
             fl = 2.0 * M * N * K
             byts = 2 * M * K + 0.75 * N * K + 4 * N * (K // 64) + 2 * M * N
             res.append(dict(M=M, K=K, N=N, ms=t * 1e3, tflops=fl / t / 1e12, frac=fl / t / 1e12 / pk,
-                            gbs=byts / t / 1e9, lora_rank=args.lora))
+                            gbs=byts / t / 1e9, gbs_frac=byts / t / 1e9 / hbm, ms_per_call=t_call * 1e3,
+                            path="fused" if (M <= 512 and N % 128 == 0 and args.lora == 0) else "two-pass",
+                            lora_rank=args.lora))
             del x, y
-    return dict(metric="6-bit qGEMM sweep (c2)", unit="TFLOP/s", peak=pk, peak_kind=f"{kind} burst bf16", sweep=res)
+    return dict(metric="6-bit qGEMM sweep (c2)", unit="TFLOP/s", peak=pk, peak_kind=f"{kind} burst bf16", hbm_peak=hbm,
+                sweep=res, timing="ms = the kernels' CUDA-event time per call (libwx records events around each "
+                                  "launch); ms_per_call = events around the loop of calls (host gaps included)")
 
 
 # ------------------------------------------------------------------ main
@@ -612,19 +631,22 @@ def main():
     ap.add_argument("--steps", type=int, default=4)
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
-    ap.add_argument("--config", default="c5", choices=list(CONFIGS) + ["c1", "c3", "c3full", "c3dense", "c2"])
+    ap.add_argument("--config", default="c5",
+                    choices=list(CONFIGS) + ["c1", "c3", "c3full", "c3dense", "c2", "c5attn", "c5attn_dense"])
     ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
-    if args.config in ("c1", "c3", "c3full", "c3dense", "c2"):
+    if args.config in ("c1", "c3", "c3full", "c3dense", "c2", "c5attn", "c5attn_dense"):
         import torch
         torch.cuda.set_device(0)
         if args.config == "c1":
             r = run_c1(args)
         elif args.config == "c2":
             r = run_c2(args)
+        elif args.config.startswith("c5attn"):  # the config-5 step's attention call, standalone
+            r = run_c3(args, 126512, dense=args.config == "c5attn_dense", g=14912)
         else:
             r = run_c3(args, 111600 if args.config == "c3full" else 28520, dense=args.config == "c3dense")
         print(json.dumps(r))

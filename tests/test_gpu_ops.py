@@ -73,15 +73,17 @@ def test_qlinear_none(torch_mod, m, k, n, with_bias):
     assert_close(f32(got), f32(ref), rel=1e-2, cos=0.9999, what=f"qlinear {m}x{k}x{n}")
 
 
-def test_qlinear_fused_is_deterministic(torch_mod):
-    """The split-K sums of the small-M path are reduced in a fixed order: bit-identical runs."""
-    m, k, n = 256, 3072, 3072
+@pytest.mark.parametrize("m,k,n", [(256, 3072, 3072), (33, 12288, 3072), (256, 12288, 3072)])
+def test_qlinear_fused_is_deterministic(torch_mod, m, k, n):
+    """The split-K sums of the small-M path are reduced in a fixed order, and no stage of its
+    shared-memory rings is reused before every reader is done with it: bit-identical runs,
+    also with many K blocks per CTA (the rings wrap many times)."""
     x = to_torch_bf16(O.normal_bf16((m, k), 35, 1))
     wq, sc, bi = O.quantize(O.normal_f32((n, k), 35, 2, std=0.02))
     lin = _mf(torch_mod, wq, sc, bi, k)
     a = lin(x).clone()
-    b = lin(x)
-    assert torch_mod.equal(a, b)
+    for _ in range(3):
+        assert torch_mod.equal(a, lin(x))
 
 
 def test_qlinear_gelu(torch_mod):

@@ -194,11 +194,13 @@ __global__ void __launch_bounds__(kQThreads, 1)
     const __nv_bfloat16* srow = p.scales + n * p.groups;
     const __nv_bfloat16* brow = p.biases + n * p.groups;
     constexpr int kDepth = 4;  // scale/bias of the next K blocks in flight
-    float rs[kDepth], rb[kDepth];
+    const unsigned short* srow16 = reinterpret_cast<const unsigned short*>(srow);
+    const unsigned short* brow16 = reinterpret_cast<const unsigned short*>(brow);
+    unsigned short rs[kDepth], rb[kDepth];
 #pragma unroll
     for (int d = 0; d < kDepth; ++d) {
-      rs[d] = d < nkb ? __bfloat162float(srow[kb0 + d]) : 0.f;
-      rb[d] = d < nkb ? __bfloat162float(brow[kb0 + d]) : 0.f;
+      rs[d] = d < nkb ? __ldg(srow16 + kb0 + d) : (unsigned short)0;
+      rb[d] = d < nkb ? __ldg(brow16 + kb0 + d) : (unsigned short)0;
     }
     bool ok = true;
     for (int i0 = 0; i0 < nkb && ok; i0 += kDepth) {
@@ -216,10 +218,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
 #pragma unroll
         for (int q = 0; q < 3; ++q)
           asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(w[2 * q]), "=r"(w[2 * q + 1]) : "r"(pa + q * 8));
-        const float2 s2 = make_float2(rs[d], rs[d]), b2 = make_float2(rb[d], rb[d]);
-        if (i + kDepth < nkb) {  // refill this ring slot for block i + kDepth
-          rs[d] = __bfloat162float(srow[kb0 + i + kDepth]);
-          rb[d] = __bfloat162float(brow[kb0 + i + kDepth]);
+        const float sv = __uint_as_float((uint32_t)rs[d] << 16), bvv = __uint_as_float((uint32_t)rb[d] << 16);
+        const float2 s2 = make_float2(sv, sv), b2 = make_float2(bvv, bvv);
+        if (i + kDepth < nkb) {
+          rs[d] = __ldg(srow16 + kb0 + i + kDepth);
+          rb[d] = __ldg(brow16 + kb0 + i + kDepth);
         }
         const uint32_t rowaddr = sW(s) + row * 128;
         const float2 magic = make_float2(-8388608.0f, -8388608.0f);

@@ -293,9 +293,11 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t ran
   return r;
 }
 
+// (no memory clobber: the cluster barrier before the reads orders them, and several
+// loads may then be in flight at once)
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
 
