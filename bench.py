@@ -60,8 +60,9 @@ PAB_MAX_STALE = 0.06    # lifts the reference default 0.04 so step 2 is reused (
 EPS = 1e-6
 ROT = 96                # 3 axes x 16 inverse frequencies x 2
 # DRAM bytes (read + write) of one attention call of the config-5 step, weighted over its
-# 6 dense + 42 top-k layers, from one ncu capture of the attention kernels
-ATTN_TRAFFIC_C5 = (6 * 10.1699e9 + 42 * 12.8100e9) / 48
+# 6 dense + 42 top-k layers, from one ncu capture of the attention kernels on a config-5 layer's
+# attention call run standalone (bench.py --config c5attn / c5attn_dense)
+ATTN_TRAFFIC_C5 = (6 * 1.1935e+10 + 42 * 1.0894e+10) / 48
 
 
 def geometry(name: str) -> dict:
@@ -386,9 +387,9 @@ def run_c3(args, seq: int, dense: bool = False, g: int = 0) -> dict:
     import torch
     from wuxianhuabu_b200 import h3
     dev = torch.device("cuda", 0)
-    g = torch.Generator(device=dev).manual_seed(1234 + 2)
+    gen = torch.Generator(device=dev).manual_seed(1234 + 2)
     H = 24
-    q, k, v = [torch.randn((seq, H, 128), device=dev, generator=g).to(torch.bfloat16) for _ in range(3)]
+    q, k, v = [torch.randn((seq, H, 128), device=dev, generator=gen).to(torch.bfloat16) for _ in range(3)]
     out = torch.empty_like(q)
     cfg = None if dense else h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False)
     scale = float(1 / math.sqrt(128))
