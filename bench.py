@@ -65,6 +65,19 @@ ROT = 96                # 3 axes x 16 inverse frequencies x 2
 ATTN_TRAFFIC_C5 = (6 * 1.1935e+10 + 42 * 1.0894e+10) / 48
 
 
+def phase_summary(trace: list, steps: int) -> dict:
+    """Per-layer phase trace of the timed region (this rank): milliseconds per step of each
+    block phase summed over the layers, and the mean block time per attention mode."""
+    phases = ("norm1", "qkv", "rope", "attn", "out", "mlp")
+    out = dict(ms_per_step={p: sum(r[p + "_ms"] for r in trace) / steps for p in phases},
+               blocks=len(trace), source="wx_ctx_trace (CUDA events at the block's phase boundaries)")
+    for mode in ("dense", "sparse", "reuse"):
+        sel = [r["total_ms"] for r in trace if r["mode"] == mode]
+        if sel:
+            out[f"{mode}_block_ms"] = dict(mean=sum(sel) / len(sel), count=len(sel))
+    return out
+
+
 def geometry(name: str) -> dict:
     c = dict(CONFIGS[name])
     t, hh, ww = c["grid"]
@@ -383,7 +396,10 @@ def run_c3(args, seq: int, dense: bool = False, g: int = 0) -> dict:
     128-row blocks, diagonal + top-k 25 %, g = 0, no tail), routing included.
     dense=True: the dense attention of the dense layers and strip rows at the same size.
     g > 0: the attention call of the config-5 step's layers (strip rows [0, g) exact over all
-    keys, video rows routed), standalone; used for the DRAM-traffic capture of the roofline."""
+    keys, video rows routed), standalone; used for the DRAM-traffic capture of the roofline.
+    args.router == "sol": the reference's production router instead of top-k (H3SolAttnConfig
+    defaults, SOL:79-98: tau 1.3 over 64-row blocks, pooled tail term); its selection depends on
+    the data, so the FLOPs are counted from the selection the router made."""
     import torch
     from wuxianhuabu_b200 import h3
     dev = torch.device("cuda", 0)
@@ -391,7 +407,9 @@ def run_c3(args, seq: int, dense: bool = False, g: int = 0) -> dict:
     H = 24
     q, k, v = [torch.randn((seq, H, 128), device=dev, generator=gen).to(torch.bfloat16) for _ in range(3)]
     out = torch.empty_like(q)
-    cfg = None if dense else h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False)
+    sol = args.router == "sol" and not dense
+    cfg = (None if dense else h3.H3SolAttnConfig(tau=1.3, tail=True) if sol
+           else h3.H3SolAttnConfig(block=128, topk_ratio=TOPK_DENSITY, tail=False))
     scale = float(1 / math.sqrt(128))
     ctx = h3.context(0)
     for _ in range(args.warmup):
@@ -412,6 +430,14 @@ def run_c3(args, seq: int, dense: bool = False, g: int = 0) -> dict:
     nb = (seq - g + 127) // 128
     keep = min(math.ceil(TOPK_DENSITY * nb), nb - 1) + 1
     flops = 4.0 * 128 * H * (seq * seq if dense else g * seq + (seq - g) * (g + min(keep * 128, seq - g)))
+    density = None
+    if sol:  # kept key rows of every (head, video query block) from the router's own selection
+        r = h3.H3SolAttn.route(q, k, v, g, scale, cfg)
+        lens = r["lens"].double()
+        kept = (r["sel"].double() * lens[None, None, :]).sum(-1)  # [H, nb] video key rows kept
+        flops = 4.0 * 128 * (H * g * seq + float((lens[None, :] * (g + kept)).sum()))
+        density = float(r["sel"].double().mean())
+        del r
     peaks, kind = load_peaks()
     per_call = e0.elapsed_time(e1) / args.steps
     flash_ms = ms[1] / max(1, cnt[1])
@@ -419,10 +445,15 @@ def run_c3(args, seq: int, dense: bool = False, g: int = 0) -> dict:
     pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
     kernel = ("flash_attn_pair_kernel<false, 128> (paired query tiles, shared K/V)" if dense else
               "flash_attn_pair_kernel<true, 128> (duo: two routed query tiles per CTA)")
-    what = "dense attention" if dense else "SOL top-k 25% attention"
+    what = ("dense attention" if dense else "SOL tau 1.3 attention (64-row blocks, tail)" if sol
+            else "SOL top-k 25% attention")
     name = "c3" if g == 0 else "c5 layer geometry"
+    conf = dict(workload=f"{name}: {what}, S={seq}, strip rows {g}, 24x128 heads", S=seq, g=g,
+                router="dense" if dense else "sol" if sol else "topk")
+    if density is not None:
+        conf.update(kept_block_fraction=density, data="q, k, v ~ N(0, 1) (no attention structure)")
     return dict(metric=f"{'dense' if dense else 'sparse'} attention ms/call ({name})", value=per_call, unit="ms/call",
-                config=dict(workload=f"{name}: {what}, S={seq}, strip rows {g}, 24x128 heads", S=seq, g=g),
+                config=conf,
                 higher_is_better=False,
                 roofline=dict(kernel=kernel, bound="tensor", achieved=ach, peak=pk, unit="TFLOP/s",
                               frac=ach / pk, avg_launch_ms=flash_ms, flops_per_launch=flops,
@@ -634,6 +665,8 @@ def main():
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
     ap.add_argument("--config", default="c5",
                     choices=list(CONFIGS) + ["c1", "c3", "c3full", "c3dense", "c2", "c5attn", "c5attn_dense"])
+    ap.add_argument("--router", default="topk", choices=["topk", "sol"],
+                    help="c3 / c3full / c5attn: top-k 25%% over 128-row blocks, or SOL tau 1.3 over 64-row blocks")
     ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -798,6 +831,7 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     clocks.start()
     stream = torch.cuda.current_stream()
     lib.wx_ctx_profile_enable(ctx.h, 1)
+    ctx.trace(True)
     n0 = lib.wx_ctx_launch_count(ctx.h)
     sync_all()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -812,6 +846,8 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     cnt = (ctypes.c_int64 * 10)()
     lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
     lib.wx_ctx_profile_enable(ctx.h, 0)
+    trace = ctx.trace_read(max_records=64 * 48 * max(1, args.steps))
+    ctx.trace(False)
     ctx.check_device()
     total_ms = _max_over_ranks(e0.elapsed_time(e1), dist)
     s_per_step = total_ms / 1e3 / args.steps
@@ -849,6 +885,7 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
                            flops=gemm_flops, peak_kind=f"{peaks_kind} sustained bf16", per_gpu=True),
                 kernel_ms=prof, gpu_launches=int(_sum_over_ranks(n1 - n0, dist)), clocks=clk)
     line.update(memory_bound_kernels(c, prof, world, peaks, peaks_kind))
+    line["phases"] = phase_summary(trace, args.steps)
     # e2e through the public API with host buffers (pinned H2D of each rank's latent rows,
     # D2H of the updated rows)
     if not args.no_e2e:

@@ -169,6 +169,35 @@ int wx_version(void);
 int wx_ctx_profile_enable(wx_ctx* ctx, int enable);
 int wx_ctx_profile_read(wx_ctx* ctx, double* ms, int64_t* launches, int nkinds);
 
+/* Per-layer phase trace: the NA_H3PROF timers of the attention forward
+ * (model/minimax h3/H3Transformer.swift:445-450, 575-597: qkv, ropeN, attn, out,
+ * tot per layer), extended to the whole block. While enabled, every block
+ * forward (wx_dit_block_forward, _sp, and the blocks of the step functions)
+ * records CUDA events on the context stream at its phase boundaries and opens
+ * NVTX ranges "wx.block" and "wx.<phase>" on the calling thread (visible to any
+ * NVTX-aware tool; free without one). enable(…, 0/1) clears the record and the
+ * layer counter. read() synchronises and writes up to max_records records of
+ * WX_TRACE_FIELDS doubles:
+ *   [0] layer (block forwards counted from 0 since enable/read)
+ *   [1] mode (WX_TRACE_DENSE, WX_TRACE_SPARSE, WX_TRACE_REUSE)
+ *   [2 + p] milliseconds of phase p (wx_trace_phase), 0 when the phase did not run
+ *   [2 + WX_TRACE_PHASES] milliseconds of the whole block
+ * sets *count to the number written and clears the record (records beyond
+ * max_records are dropped). */
+enum wx_trace_phase {
+  WX_TRACE_NORM1 = 0, /* RMSNorm + modulation before attention */
+  WX_TRACE_QKV = 1,   /* fused q|k|v projection */
+  WX_TRACE_ROPE = 2,  /* QK-RMSNorm + RoPE (+ the sequence-parallel exchange and its waits) */
+  WX_TRACE_ATTN = 3,  /* routing + flash attention (+ the return exchange) */
+  WX_TRACE_OUT = 4,   /* out projection + gated residual (PAB reuse: the cached gated residual) */
+  WX_TRACE_MLP = 5,   /* RMSNorm + modulation, fc1 + activation, fc2 + gated residual */
+  WX_TRACE_PHASES = 6
+};
+enum { WX_TRACE_DENSE = 0, WX_TRACE_SPARSE = 1, WX_TRACE_REUSE = 2 };
+#define WX_TRACE_FIELDS 9
+int wx_ctx_trace_enable(wx_ctx* ctx, int enable);
+int wx_ctx_trace_read(wx_ctx* ctx, double* records, int max_records, int* count);
+
 /* ---------------------------------------------------- quantized linear */
 /* Affine group quantization of fp32 w [n, k] (the offline step of
  * model/minimax h3/tools/quantize_h3_g64.py:92-99, done on the GPU). */
@@ -288,7 +317,7 @@ int wx_topk_route(wx_ctx* ctx, const void* q, const void* k, const void* v, int6
                   uint8_t* sel, float* scores, void* cm, void* vsum, float* lens);
 /* H3SolAttn.forward (SOL:388-532) / scaledDotProductAttention for dense layers:
  * routing + tcgen05 flash attention; out rows at out + s*out_stride + h*head_dim.
- * head_dim must be 128; q/k/v rows 16-byte aligned. */
+ * head_dim 128 or 64; q/k/v rows 16-byte aligned. */
 int wx_sparse_attention(wx_ctx* ctx, const void* q, const void* k, const void* v,
                         int64_t row_stride, int64_t S, int H, int head_dim,
                         const wx_sparse_spec* spec, float scale, void* out, int64_t out_stride);

@@ -123,6 +123,8 @@ _SIGS = {
     "wx_ctx_launch_count": (_i64, [_vp]),
     "wx_ctx_profile_enable": (_i32, [_vp, _i32]),
     "wx_ctx_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
+    "wx_ctx_trace_enable": (_i32, [_vp, _i32]),
+    "wx_ctx_trace_read": (_i32, [_vp, _vp, _i32, C.POINTER(_i32)]),
     "wx_quantize_affine": (_i32, [_vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "wx_dequantize_affine": (_i32, [_vp, C.POINTER(QWeight), _vp]),
     "wx_qlinear": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),

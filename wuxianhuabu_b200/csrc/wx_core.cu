@@ -12,6 +12,8 @@
 #include <map>
 #include <utility>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "wx_internal.h"
 #include "wx_ptx.cuh"
 
@@ -153,6 +155,58 @@ ProfScope::~ProfScope() {
   if (idx >= 0) cudaEventRecord(c->prof_recs[idx].b, c->stream);
 }
 
+static const char* const kTraceNames[WX_TRACE_PHASES] = {"wx.norm1", "wx.qkv", "wx.rope", "wx.attn", "wx.out",
+                                                         "wx.mlp"};
+
+LayerTrace::LayerTrace(wx_ctx* ctx, int mode) : c(ctx) {
+  if (!c || !c->trace) return;
+  wx_ctx::TraceRec r{};
+  r.layer = c->trace_layer++;
+  r.mode = mode;
+  r.n = 1;
+  r.mark[0] = pool_event(c);
+  cudaEventRecord(r.mark[0], c->stream);
+  c->trace_recs.push_back(r);
+  idx = (int)c->trace_recs.size() - 1;
+  nvtxRangePushA("wx.block");
+}
+
+void LayerTrace::begin(int phase) {
+  if (idx < 0 || phase < 0 || phase >= WX_TRACE_PHASES) return;
+  wx_ctx::TraceRec& r = c->trace_recs[idx];
+  if (open > 0 && r.n <= WX_TRACE_PHASES) {  // end the open phase here
+    r.mark[r.n] = pool_event(c);
+    r.phase_of[r.n] = open - 1;
+    cudaEventRecord(r.mark[r.n], c->stream);
+    ++r.n;
+    nvtxRangePop();
+  }
+  open = phase + 1;
+  nvtxRangePushA(kTraceNames[phase]);
+}
+
+static void trace_release(wx_ctx* ctx) {
+  for (auto& r : ctx->trace_recs)
+    for (int i = 0; i < r.n; ++i) ctx->prof_pool.push_back(r.mark[i]);
+  ctx->trace_recs.clear();
+  ctx->trace_layer = 0;
+}
+
+LayerTrace::~LayerTrace() {
+  if (idx < 0) return;
+  wx_ctx::TraceRec& r = c->trace_recs[idx];
+  if (open > 0) {
+    if (r.n <= WX_TRACE_PHASES) {
+      r.mark[r.n] = pool_event(c);
+      r.phase_of[r.n] = open - 1;
+      cudaEventRecord(r.mark[r.n], c->stream);
+      ++r.n;
+    }
+    nvtxRangePop();
+  }
+  nvtxRangePop();
+}
+
 // ------------------------------------------------------------ fp32 islands
 __global__ void dense_f32_kernel(const float* __restrict__ x, int64_t m, int64_t k,
                                  const float* __restrict__ w, int64_t n, const float* __restrict__ b,
@@ -250,6 +304,7 @@ int wx_ctx_destroy(wx_ctx* ctx) {
     cudaEventDestroy(r.a);
     cudaEventDestroy(r.b);
   }
+  trace_release(ctx);
   for (auto e : ctx->prof_pool) cudaEventDestroy(e);
   if (ctx->aux) cudaStreamDestroy(ctx->aux);
   if (ctx->fork) cudaEventDestroy(ctx->fork);
@@ -300,6 +355,38 @@ int wx_ctx_profile_read(wx_ctx* ctx, double* ms, int64_t* launches, int nkinds) 
     ctx->prof_pool.push_back(r.b);
   }
   ctx->prof_recs.clear();
+  return WX_OK;
+}
+
+int wx_ctx_trace_enable(wx_ctx* ctx, int enable) {
+  if (!ctx) return WX_ERR_INVALID;
+  trace_release(ctx);
+  ctx->trace = enable != 0;
+  return WX_OK;
+}
+
+int wx_ctx_trace_read(wx_ctx* ctx, double* records, int max_records, int* count) {
+  if (!ctx || !count || max_records < 0 || (max_records > 0 && !records)) return WX_ERR_INVALID;
+  *count = 0;
+  WX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  int k = 0;
+  for (auto& r : ctx->trace_recs) {
+    if (k >= max_records) break;
+    double* o = records + (size_t)k * WX_TRACE_FIELDS;
+    for (int f = 0; f < WX_TRACE_FIELDS; ++f) o[f] = 0.0;
+    o[0] = r.layer;
+    o[1] = r.mode;
+    for (int i = 1; i < r.n; ++i) {
+      float t = 0.f;
+      if (cudaEventElapsedTime(&t, r.mark[i - 1], r.mark[i]) == cudaSuccess) o[2 + r.phase_of[i]] += t;
+    }
+    float tot = 0.f;
+    if (r.n > 1 && cudaEventElapsedTime(&tot, r.mark[0], r.mark[r.n - 1]) == cudaSuccess)
+      o[2 + WX_TRACE_PHASES] = tot;
+    ++k;
+  }
+  *count = k;
+  trace_release(ctx);
   return WX_OK;
 }
 

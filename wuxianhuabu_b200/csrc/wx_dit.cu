@@ -117,35 +117,45 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
   void* sw = base + L.sw;
   void* lt = base + L.lt;
   int st;
-  if (refresh || !pab_slot) {
+  const bool full = refresh || !pab_slot;
+  LayerTrace tr(ctx, !full ? WX_TRACE_REUSE : (spec && spec->mode != WX_SPARSE_DENSE) ? WX_TRACE_SPARSE
+                                                                                       : WX_TRACE_DENSE);
+  if (full) {
     // m1 = norm1(h) * (scaleMSA + 1) + shiftMSA
+    tr.begin(WX_TRACE_NORM1);
     if ((st = launch_norm_modscale(ctx, h, S, cfg->hidden, w->norm1, mods->shift_msa, mods->scale_msa, rowmap,
                                    cfg->eps, m)))
       return st;
     // qkv = qkv_proj(m1)
+    tr.begin(WX_TRACE_QKV);
     if ((st = qlinear_lora_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
                                    3 * inner, nullptr, wd, lt, nullptr)))
       return st;
     // per-head RMSNorm + RoPE of q and k, in place
+    tr.begin(WX_TRACE_ROPE);
     if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, S, cfg->heads, cfg->head_dim,
                                   w->q_norm, w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
       return st;
     // attention over the packed sequence
     const uint8_t* qb = static_cast<const uint8_t*>(qkv);
     const float scale = 1.0f / sqrtf((float)cfg->head_dim);
+    tr.begin(WX_TRACE_ATTN);
     if ((st = attention_with_scratch(ctx, qb, qb + inner * 2, qb + 2 * inner * 2, 3 * inner, S, cfg->heads,
                                      cfg->head_dim, spec, scale, att, inner, base + L.attn)))
       return st;
     // at = out_proj(att) (-> PAB slot); hAttn = h + at * gateMSA
     void* at_dst = pab_slot ? pab_slot : base + L.at;
+    tr.begin(WX_TRACE_OUT);
     if ((st = qlinear_lora_with_scratch(ctx, att, S, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID, mods->gate_msa, h, rowmap, ha,
                                    cfg->hidden, at_dst, wd, lt, nullptr)))
       return st;
   } else {
     // PAB reuse: at = cache[bi]; hAttn = h + at * gateMSA (current step's gate)
+    tr.begin(WX_TRACE_OUT);
     if ((st = launch_mod_gate(ctx, h, pab_slot, mods->gate_msa, rowmap, S, cfg->hidden, ha))) return st;
   }
   // m2 = norm2(hAttn) * (scaleMLP + 1) + shiftMLP
+  tr.begin(WX_TRACE_MLP);
   if ((st = launch_norm_modscale(ctx, ha, S, cfg->hidden, w->norm2, mods->shift_mlp, mods->scale_mlp, rowmap,
                                  cfg->eps, m)))
     return st;

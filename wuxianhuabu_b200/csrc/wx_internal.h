@@ -31,6 +31,16 @@ struct wx_ctx {
   };
   std::vector<ProfRec> prof_recs;
   std::vector<cudaEvent_t> prof_pool;
+  // per-layer phase trace (wx_ctx_trace_enable / _read): one record per block
+  // forward, mark[0] its start and mark[i] (i >= 1) the end of phase phase_of[i]
+  bool trace = false;
+  int trace_layer = 0;
+  struct TraceRec {
+    int layer, mode, n;
+    cudaEvent_t mark[WX_TRACE_PHASES + 1];
+    int phase_of[WX_TRACE_PHASES + 1];
+  };
+  std::vector<TraceRec> trace_recs;
   // side stream for independent kernels that run concurrently with the context
   // stream (forked and joined with the two events); created on first use
   cudaStream_t aux = nullptr;
@@ -113,6 +123,20 @@ struct ProfScope {
   int idx = -1;
   ProfScope(wx_ctx* ctx, int kind);
   ~ProfScope();
+};
+
+// Phase trace of one block forward (the reference's NA_H3PROF per-layer timers):
+// the constructor marks the block's start, begin(p) ends the open phase and opens
+// phase p (a wx_trace_phase), the destructor ends the last one. While tracing is
+// enabled each mark is a CUDA event on the context stream and the block and each
+// phase are NVTX ranges ("wx.block", "wx.<phase>"); otherwise nothing is recorded.
+struct LayerTrace {
+  wx_ctx* c;
+  int idx = -1;
+  int open = 0;
+  LayerTrace(wx_ctx* ctx, int mode);
+  void begin(int phase);
+  ~LayerTrace();
 };
 
 // Scratch of one quantized linear: the expanded bf16 weight of the two-pass GEMM

@@ -492,16 +492,21 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
   void* wd = base + L.wd;
   void* lt = base + L.lt;
   int st;
-  if (refresh || !pab_slot) {
+  const bool full_fwd = refresh || !pab_slot;
+  LayerTrace tr(ctx, !full_fwd ? WX_TRACE_REUSE
+                               : (spec && spec->mode != WX_SPARSE_DENSE) ? WX_TRACE_SPARSE : WX_TRACE_DENSE);
+  if (full_fwd) {
     void* qkv = base + L.qkv;
     auto* send = reinterpret_cast<__nv_bfloat16*>(base + L.send);
     auto* recv = reinterpret_cast<__nv_bfloat16*>(base + L.recv);
     auto* attf = reinterpret_cast<__nv_bfloat16*>(base + L.attf);
     auto* ret = reinterpret_cast<__nv_bfloat16*>(base + L.ret);
     auto* att = reinterpret_cast<__nv_bfloat16*>(base + L.att);
+    tr.begin(WX_TRACE_NORM1);
     if ((st = launch_norm_modscale(ctx, h, rows, cfg->hidden, w->norm1, mods->shift_msa, mods->scale_msa, rowmap,
                                    cfg->eps, m)))
       return st;
+    tr.begin(WX_TRACE_QKV);
     if ((st = qlinear_lora_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
                                    3 * inner, nullptr, wd, lt, nullptr)))
       return st;
@@ -529,6 +534,7 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
       sig1.rank = rank;
       sig1.epoch = ep;
       uint8_t* mine = static_cast<uint8_t*>(ctx->p2p_buf);
+      tr.begin(WX_TRACE_ROPE);
       if ((st = launch_qkv_to_peers(ctx, qkv, rows, (int64_t)rank * rows, cfg->heads, Hl, qkv_dst, P, w->q_norm,
                                     w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, sig1)))
         return st;
@@ -547,6 +553,7 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
       auto* full = reinterpret_cast<__nv_bfloat16*>(mine + PL.qkv);
       void* att_mine = mine + PL.att;
       const int64_t rs = 3 * (int64_t)Hl * hd;
+      tr.begin(WX_TRACE_ATTN);
       if ((st = attention_with_scratch_peer(ctx, full, full + (int64_t)Hl * hd, full + 2 * (int64_t)Hl * hd, rs, S,
                                             Hl, hd, spec, scale, att_mine, inner, base + L.attn, &po)))
         return st;
@@ -557,38 +564,44 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
       }
       if ((st = launch_status(ctx, "sp_wait_att"))) return st;
       void* at_dst = pab_slot ? pab_slot : base + L.at;
+      tr.begin(WX_TRACE_OUT);
       if ((st = qlinear_lora_with_scratch(ctx, att_mine, rows, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID,
                                           mods->gate_msa, h, rowmap, ha, cfg->hidden, at_dst, wd, lt, nullptr)))
         return st;
     }
     if (!peer) {
-    if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, rows, cfg->heads, hd, w->q_norm,
-                                  w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
-      return st;
-    // q|k|v of this rank's rows, grouped by destination head block
-    const int64_t pack_units = (int64_t)P * rows * 3 * Hl * hd / 8;
-    sp_pack_qkv_kernel<<<grid_units(ctx, pack_units), 256, 0, ctx->stream>>>(
-        static_cast<const __nv_bfloat16*>(qkv), rows, P, cfg->heads, Hl, hd, send);
-    if ((st = launch_status(ctx, "sp_pack_qkv"))) return st;
-    if ((st = all_to_all(ctx, send, recv, (size_t)rows * 3 * Hl * hd * 2))) return st;
-    // attention over the whole sequence for heads [rank*Hl, rank*Hl + Hl)
-    const int64_t rs = 3 * (int64_t)Hl * hd;
-    if ((st = attention_with_scratch(ctx, recv, recv + (int64_t)Hl * hd, recv + 2 * (int64_t)Hl * hd, rs, S, Hl, hd,
-                                     spec, scale, attf, (int64_t)Hl * hd, base + L.attn)))
-      return st;
-    // rows of rank r go back to r; gather this rank's rows of every head
-    if ((st = all_to_all(ctx, attf, ret, (size_t)rows * Hl * hd * 2))) return st;
-    const int64_t un_units = (int64_t)P * rows * Hl * hd / 8;
-    sp_unpack_out_kernel<<<grid_units(ctx, un_units), 256, 0, ctx->stream>>>(ret, rows, P, Hl, hd, att);
-    if ((st = launch_status(ctx, "sp_unpack_out"))) return st;
-    void* at_dst = pab_slot ? pab_slot : base + L.at;
-    if ((st = qlinear_lora_with_scratch(ctx, att, rows, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID, mods->gate_msa, h, rowmap, ha,
-                                   cfg->hidden, at_dst, wd, lt, nullptr)))
-      return st;
+      tr.begin(WX_TRACE_ROPE);
+      if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, rows, cfg->heads, hd, w->q_norm,
+                                    w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
+        return st;
+      // q|k|v of this rank's rows, grouped by destination head block
+      const int64_t pack_units = (int64_t)P * rows * 3 * Hl * hd / 8;
+      sp_pack_qkv_kernel<<<grid_units(ctx, pack_units), 256, 0, ctx->stream>>>(
+          static_cast<const __nv_bfloat16*>(qkv), rows, P, cfg->heads, Hl, hd, send);
+      if ((st = launch_status(ctx, "sp_pack_qkv"))) return st;
+      if ((st = all_to_all(ctx, send, recv, (size_t)rows * 3 * Hl * hd * 2))) return st;
+      // attention over the whole sequence for heads [rank*Hl, rank*Hl + Hl)
+      const int64_t rs = 3 * (int64_t)Hl * hd;
+      tr.begin(WX_TRACE_ATTN);
+      if ((st = attention_with_scratch(ctx, recv, recv + (int64_t)Hl * hd, recv + 2 * (int64_t)Hl * hd, rs, S, Hl,
+                                       hd, spec, scale, attf, (int64_t)Hl * hd, base + L.attn)))
+        return st;
+      // rows of rank r go back to r; gather this rank's rows of every head
+      if ((st = all_to_all(ctx, attf, ret, (size_t)rows * Hl * hd * 2))) return st;
+      const int64_t un_units = (int64_t)P * rows * Hl * hd / 8;
+      sp_unpack_out_kernel<<<grid_units(ctx, un_units), 256, 0, ctx->stream>>>(ret, rows, P, Hl, hd, att);
+      if ((st = launch_status(ctx, "sp_unpack_out"))) return st;
+      void* at_dst = pab_slot ? pab_slot : base + L.at;
+      tr.begin(WX_TRACE_OUT);
+      if ((st = qlinear_lora_with_scratch(ctx, att, rows, inner, &w->out, w->lora[1], WX_EPI_GATE_RESID,
+                                          mods->gate_msa, h, rowmap, ha, cfg->hidden, at_dst, wd, lt, nullptr)))
+        return st;
     }
   } else {
+    tr.begin(WX_TRACE_OUT);
     if ((st = launch_mod_gate(ctx, h, pab_slot, mods->gate_msa, rowmap, rows, cfg->hidden, ha))) return st;
   }
+  tr.begin(WX_TRACE_MLP);
   if ((st = launch_norm_modscale(ctx, ha, rows, cfg->hidden, w->norm2, mods->shift_mlp, mods->scale_mlp, rowmap,
                                  cfg->eps, m)))
     return st;

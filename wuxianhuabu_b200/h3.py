@@ -18,6 +18,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Optional, Sequence
 
@@ -76,6 +77,41 @@ class Context:
     def call(self, name: str, *args) -> None:
         self.sync_stream()
         check(getattr(self.lib, name)(self.h, *args), self.h)
+
+    TRACE_PHASES = ("norm1", "qkv", "rope", "attn", "out", "mlp")
+    TRACE_MODES = ("dense", "sparse", "reuse")
+
+    def trace(self, enable: bool = True) -> None:
+        """Start (or stop) the per-layer phase trace; clears what was recorded."""
+        check(self.lib.wx_ctx_trace_enable(self.h, int(enable)), self.h)
+
+    def trace_read(self, max_records: int = 4096) -> list:
+        """Records since trace()/the last read, one per block forward: dicts with the layer
+        (block forwards counted from 0), mode, the milliseconds of each phase and the total."""
+        import ctypes
+        nf = 9
+        buf = (ctypes.c_double * (nf * max_records))()
+        n = ctypes.c_int(0)
+        check(self.lib.wx_ctx_trace_read(self.h, buf, max_records, ctypes.byref(n)), self.h)
+        out = []
+        for i in range(n.value):
+            r = buf[i * nf:(i + 1) * nf]
+            d = dict(layer=int(r[0]), mode=self.TRACE_MODES[int(r[1])], total_ms=r[8])
+            d.update({p + "_ms": r[2 + j] for j, p in enumerate(self.TRACE_PHASES)})
+            out.append(d)
+        return out
+
+    @staticmethod
+    def format_trace(records: list) -> str:
+        """The records as the reference's per-layer profile lines
+        (H3Transformer.swift:587-588: qkv, ropeN, attn(mode), out, tot), with norm1 and mlp added."""
+        lines = []
+        for r in records:
+            mode = {"dense": "dense", "sparse": "sol", "reuse": "pab"}[r["mode"]]
+            lines.append("[PROF] L%02d norm1=%.2fms qkv=%.2fms ropeN=%.2fms attn(%s)=%.2fms out=%.2fms mlp=%.2fms "
+                         "tot=%.2fms" % (r["layer"] + 1, r["norm1_ms"], r["qkv_ms"], r["rope_ms"], mode,
+                                         r["attn_ms"], r["out_ms"], r["mlp_ms"], r["total_ms"]))
+        return "\n".join(lines)
 
     def close(self) -> None:
         if self.h:
@@ -620,12 +656,19 @@ class H3DiT:
             args.audio_dsigma = float(audio.dsigma)
         else:
             args.audio_target = -1
+        # WX_H3PROF set: per-layer phase lines after the step, as the reference's NA_H3PROF prints them
+        prof = bool(os.environ.get("WX_H3PROF"))
+        if prof:
+            ctx.trace(True)
         if guided:
             g = _lib.Guidance(_p(text_states_neg) if cfg_scale > 0 else None, float(cfg_scale), int(bool(update)),
                               _p(velocity_out))
             ctx.call("wx_dit_step_guided", C.byref(self._m), C.byref(args), C.byref(g))
         else:
             ctx.call("wx_dit_step", C.byref(self._m), C.byref(args))
+        if prof:
+            print(Context.format_trace(ctx.trace_read()), flush=True)
+            ctx.trace(False)
         if attn_bcast is not None and refresh and sigma is not None:
             attn_bcast.cached_sigma = sigma
         return latents
