@@ -42,7 +42,7 @@ def gpu_block(w, hidden, heads, ffn, mlp_kind, rot, eps, hd=128):
     def lin(t, k):
         wq, sc, bi, b = t
         return h3.MfLinear(torch.from_numpy(wq.view(np.int32)).cuda(), to_torch_bf16(sc), to_torch_bf16(bi), k,
-                           to_torch_bf16(b))
+                           to_torch_bf16(b) if b is not None else None)
     inner = heads * hd
     bw = h3.H3BlockWeights(lin(w["qkv"], hidden), lin(w["out"], inner), lin(w["fc1"], hidden), lin(w["fc2"], ffn),
                            to_torch_bf16(w["q_norm"]), to_torch_bf16(w["k_norm"]), to_torch_bf16(w["norm1"]),

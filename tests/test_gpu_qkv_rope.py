@@ -1,0 +1,75 @@
+"""The q|k|v projection with QK-RMSNorm + RoPE fused into the GEMM's epilogue
+(gemm_bf16_tc_kernel<BN, true>) against the separate path (GEMM, then qk_norm_rope_vec_kernel),
+which WX_QKV_ROPE_FUSED=0 selects in a child process (both children with WX_QGEMM_TWO_PASS=1,
+so that every projection runs the same GEMM).
+
+The two paths round at the same points and form the sum of squares in the same order, so whole
+DiT blocks (dense, top-k and SOL attention, ragged last row tile, 2 and 3 heads so that both the
+256- and the 128-column tiles run, with and without a bias on the projection, a PAB slot) must
+come out bit-identical. The oracle comparison of the fused path is in test_gpu_block /
+test_gpu_parity_full (they run the default path)."""
+import os
+import subprocess
+import sys
+import tempfile
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parent.parent
+
+CHILD = r'''
+import sys
+import numpy as np
+sys.path.insert(0, sys.argv[1])
+import torch
+from oracle import oracle as O
+from tests._util import to_np_bf16, to_torch_bf16
+from tests.test_gpu_block import gpu_block, make_block
+from wuxianhuabu_b200 import h3
+outs = {}
+for (S, heads, bias, mode, g) in [(300, 2, False, "dense", 0), (1000, 3, True, "topk", 200),
+                                  (1000, 2, False, "sol", 130), (2048, 2, True, "dense", 0)]:
+    hidden, ffn, rot, eps = 256, 512, 96, 1e-6
+    w, mods, h, cos, sin, rowmap = make_block(50 + S + heads, hidden, heads, ffn, 0, S, rot)
+    wq, sc, bi, b = w["qkv"]
+    w["qkv"] = (wq, sc, bi, O.normal_bf16((3 * heads * 128,), 9, S, std=0.5) if bias else None)
+    blk = gpu_block(w, hidden, heads, ffn, 0, rot, eps)
+    spec = None
+    if mode == "topk":
+        spec = h3.H3SolAttnConfig(block=128, topk_ratio=0.25, tail=False).spec(g)
+    elif mode == "sol":
+        spec = h3.H3SolAttnConfig(tau=0.4, tail=True).spec(g)
+    x = to_torch_bf16(h)
+    slot = torch.empty((S, hidden), dtype=torch.bfloat16, device="cuda")
+    blk.block_forward(0, x, [to_torch_bf16(m) for m in mods], torch.from_numpy(rowmap.view(np.int32)).cuda(),
+                      to_torch_bf16(cos), to_torch_bf16(sin), spec, pab_slot=slot, refresh=True)
+    h3.context().check_device()
+    key = f"{S}_{heads}_{int(bias)}_{mode}"
+    outs[key + "_h"] = to_np_bf16(x).view(np.uint16)
+    outs[key + "_at"] = to_np_bf16(slot).view(np.uint16)
+np.savez(sys.argv[2], **outs)
+print("ok")
+'''
+
+
+def _run(fused: str, path: str):
+    # both runs on the two-pass GEMM (the separate path would otherwise take the small-M
+    # kernel at S = 300, whose split-K sums round differently)
+    env = dict(os.environ, WX_QKV_ROPE_FUSED=fused, WX_QGEMM_TWO_PASS="1")
+    r = subprocess.run([sys.executable, "-c", CHILD, str(ROOT), path], env=env, capture_output=True, text=True,
+                       timeout=600, cwd=str(ROOT))
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-2000:]
+    return np.load(path)
+
+
+def test_fused_qkv_rope_epilogue_is_bit_identical_to_the_separate_kernel():
+    with tempfile.TemporaryDirectory() as d:
+        a = _run("1", os.path.join(d, "fused.npz"))
+        b = _run("0", os.path.join(d, "separate.npz"))
+        assert sorted(a.files) == sorted(b.files)
+        for k in a.files:
+            diff = int(np.count_nonzero(a[k] != b[k]))
+            assert diff == 0, f"{k}: {diff} of {a[k].size} elements differ"

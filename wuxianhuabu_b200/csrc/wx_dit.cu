@@ -25,6 +25,13 @@ int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, con
                          const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
                          void* y_raw, void* wd, void* swiglu_tmp);
 bool qweight_ok(const wx_qweight* w);
+struct QkvPeerOut;
+bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
+                      const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t);
+int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                          const wx_lora_pack* lora, void* y, int64_t ldy, const void* q_norm, const void* k_norm,
+                          const void* cos_t, const void* sin_t, int rot, float eps, void* wd, void* t,
+                          const QkvPeerOut* peers);
 size_t attention_scratch_bytes(int64_t S, int H, int hd, const wx_sparse_spec* spec);
 int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
                            int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os, void* scratch);
@@ -126,16 +133,23 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
     if ((st = launch_norm_modscale(ctx, h, S, cfg->hidden, w->norm1, mods->shift_msa, mods->scale_msa, rowmap,
                                    cfg->eps, m)))
       return st;
-    // qkv = qkv_proj(m1)
+    // qkv = qkv_proj(m1); per-head RMSNorm + RoPE of q and k (in the GEMM's epilogue
+    // where the geometry allows, else as a separate kernel, in place)
     tr.begin(WX_TRACE_QKV);
-    if ((st = qlinear_lora_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
-                                   3 * inner, nullptr, wd, lt, nullptr)))
-      return st;
-    // per-head RMSNorm + RoPE of q and k, in place
-    tr.begin(WX_TRACE_ROPE);
-    if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, S, cfg->heads, cfg->head_dim,
-                                  w->q_norm, w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
-      return st;
+    if (qkv_rope_fusable(&w->qkv, S, w->lora[0] != nullptr, false, cfg->head_dim, cfg->rot, w->q_norm, w->k_norm,
+                         cos_t, sin_t)) {
+      if ((st = qkv_rope_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], qkv, 3 * inner, w->q_norm,
+                                      w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, wd, lt, nullptr)))
+        return st;
+    } else {
+      if ((st = qlinear_lora_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr,
+                                          nullptr, nullptr, qkv, 3 * inner, nullptr, wd, lt, nullptr)))
+        return st;
+      tr.begin(WX_TRACE_ROPE);
+      if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, S, cfg->heads, cfg->head_dim,
+                                    w->q_norm, w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
+        return st;
+    }
     // attention over the packed sequence
     const uint8_t* qb = static_cast<const uint8_t*>(qkv);
     const float scale = 1.0f / sqrtf((float)cfg->head_dim);

@@ -44,6 +44,33 @@ constexpr int kGemmStages = 4;
 constexpr int kGemmThreads = 192;
 constexpr int kGroupM = 16;
 
+// q|k|v projection epilogue with QK-RMSNorm + RoPE fused (gemm_bf16_tc_kernel<BN, true>):
+// columns [0, inner) are q heads, [inner, 2 inner) k heads, [2 inner, 3 inner) v heads,
+// head_dim 128. base[0] == nullptr: the result goes in place into y; otherwise head h of
+// row m goes to the exchange buffer of rank h / Hl (layout [S][3][Hl][128], row row0 + m)
+// and the last CTA raises sig (sequence parallelism over peer memory).
+struct QkRopeEpi {
+  const __nv_bfloat16* w0;  // q_norm [128]
+  const __nv_bfloat16* w1;  // k_norm [128]
+  const __nv_bfloat16* cos_t;
+  const __nv_bfloat16* sin_t;  // [M, rot/2]
+  int rot;
+  float eps;
+  int inner;
+  __nv_bfloat16* base[kMaxPeers];
+  int64_t row0;
+  int Hl;
+  PeerSignal sig;
+};
+
+static bool qkv_rope_fused_enabled() {  // WX_QKV_ROPE_FUSED=0: separate kernels (A/B), read once
+  static bool v = [] {
+    const char* e = getenv("WX_QKV_ROPE_FUSED");
+    return !(e && atoi(e) == 0);
+  }();
+  return v;
+}
+
 struct GemmParams {
   int M, N, K;
   int K2;  // extra K columns read through the second operand pair (LoRA: t [M,K2], bt [N,K2]); 0 = none
@@ -57,15 +84,21 @@ struct GemmParams {
   const uint32_t* rowmap;
   __nv_bfloat16* y_raw;
   int* err;
+  QkRopeEpi qk;
 };
 
-template <int BN>
+// QKR adds a 32-row x 256-byte staging buffer per epilogue warp (the rows of one
+// head, re-read in 512-byte coalesced pieces for the stores)
+template <int BN, bool QKR = false>
 struct GemmSmem {
   static constexpr int kABytes = kGemmBM * kGemmBK * 2;
   static constexpr int kBBytes = BN * kGemmBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = kGemmStages * kStageBytes;
+  static constexpr int kOutOffset = kGemmStages * kStageBytes;
+  static constexpr int kOutBytes = QKR ? 4 * 32 * 256 : 0;
+  static constexpr int kBarOffset = kOutOffset + kOutBytes;
   static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
+  static_assert(kBytes <= 227 * 1024, "GEMM shared memory exceeds the per-CTA limit");
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& mb, int& nb) {
@@ -139,12 +172,112 @@ __device__ __forceinline__ void gemm_epilogue32(const GemmParams& p, float (&v)[
   }
 }
 
-template <int BN>
+// 16-byte chunk c (of 16) of staging row r: XOR-swizzled so that the row-per-thread
+// writes and the row-pair reads of the copy-out are both free of bank conflicts
+__device__ __forceinline__ uint4* stage_chunk(uint8_t* buf, int r, int c) {
+  return reinterpret_cast<uint4*>(buf + r * 256 + ((c ^ (r & 15)) << 4));
+}
+
+// One 128-column head of output row m for the q|k|v projection (one thread per row,
+// v = the fp32 accumulators): the GEMM's bf16 result (+ bias, rounded again); for q and
+// k heads then nv = bf16(x * rstd * w) and the split-half rotation of pairs (j, j + rot/2)
+// of h3_fused_rmsnorm_rope (网络算子-融合-RMSNormRoPE-通用.swift:41-94); v heads pass
+// through. The result goes as bf16 into the thread's staging row `lane`. The sum of
+// squares is formed in the order of qk_norm_rope_vec_kernel (partials over 4 consecutive
+// elements, combined as its xor butterfly combines lanes) and the rotation with the same
+// explicit roundings, so the fused and the separate path give identical bits.
+__device__ __forceinline__ void qk_rope_head(const GemmParams& p, float (&v)[4][32], int64_t m, int64_t n0,
+                                             int part, uint8_t* buf, int lane) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[c][i] = round_bf16(v[c][i]);
+  if (p.bias) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + n0 + c * 32 + i));
+        const uint32_t bu[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[c][i + 2 * q] = round_bf16(v[c][i + 2 * q] + bf16_lo(bu[q]));
+          v[c][i + 2 * q + 1] = round_bf16(v[c][i + 2 * q + 1] + bf16_hi(bu[q]));
+        }
+      }
+  }
+  if (part < 2) {
+    float t[32];
+#pragma unroll
+    for (int l = 0; l < 32; ++l) {
+      const int c = l >> 3, i = (l & 7) * 4;
+      float a = __fmaf_rn(v[c][i], v[c][i], 0.f);
+      a = __fmaf_rn(v[c][i + 1], v[c][i + 1], a);
+      a = __fmaf_rn(v[c][i + 2], v[c][i + 2], a);
+      t[l] = __fmaf_rn(v[c][i + 3], v[c][i + 3], a);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int l = 0; l < o; ++l) t[l] = __fadd_rn(t[l], t[l + o]);
+    const float rstd = rsqrtf(t[0] / 128.f + p.qk.eps);
+    const __nv_bfloat16* w = part == 0 ? p.qk.w0 : p.qk.w1;
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + c * 32 + i));
+        const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[c][i + 2 * q] = round_bf16(v[c][i + 2 * q] * rstd * bf16_lo(wu[q]));
+          v[c][i + 2 * q + 1] = round_bf16(v[c][i + 2 * q + 1] * rstd * bf16_hi(wu[q]));
+        }
+      }
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int i = 0; i < 32; i += 8)
+      *stage_chunk(buf, lane, c * 4 + i / 8) =
+          make_uint4(pack_bf16x2(v[c][i], v[c][i + 1]), pack_bf16x2(v[c][i + 2], v[c][i + 3]),
+                     pack_bf16x2(v[c][i + 4], v[c][i + 5]), pack_bf16x2(v[c][i + 6], v[c][i + 7]));
+  if (part < 2 && p.qk.rot > 0) {
+    const int rc = p.qk.rot >> 4;  // chunks of 8 in rot/2
+    const int64_t rh = p.qk.rot >> 1;
+    const __nv_bfloat16* cr = p.qk.cos_t + m * rh;
+    const __nv_bfloat16* sr = p.qk.sin_t + m * rh;
+#pragma unroll 1
+    for (int ch = 0; ch < rc; ++ch) {
+      uint4* pa = stage_chunk(buf, lane, ch);
+      uint4* pb = stage_chunk(buf, lane, ch + rc);
+      const uint4 av = *pa, bv = *pb;
+      const uint4 cv = __ldg(reinterpret_cast<const uint4*>(cr + ch * 8));
+      const uint4 sv = __ldg(reinterpret_cast<const uint4*>(sr + ch * 8));
+      const uint32_t au[4] = {av.x, av.y, av.z, av.w}, bu[4] = {bv.x, bv.y, bv.z, bv.w};
+      const uint32_t cu[4] = {cv.x, cv.y, cv.z, cv.w}, su[4] = {sv.x, sv.y, sv.z, sv.w};
+      uint32_t oa[4], ob[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float a0 = bf16_lo(au[q]), a1 = bf16_hi(au[q]), b0 = bf16_lo(bu[q]), b1 = bf16_hi(bu[q]);
+        const float c0 = bf16_lo(cu[q]), c1 = bf16_hi(cu[q]), s0 = bf16_lo(su[q]), s1 = bf16_hi(su[q]);
+        oa[q] = pack_bf16x2(__fsub_rn(__fmul_rn(a0, c0), __fmul_rn(b0, s0)),
+                            __fsub_rn(__fmul_rn(a1, c1), __fmul_rn(b1, s1)));
+        ob[q] = pack_bf16x2(__fadd_rn(__fmul_rn(b0, c0), __fmul_rn(a0, s0)),
+                            __fadd_rn(__fmul_rn(b1, c1), __fmul_rn(a1, s1)));
+      }
+      *pa = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+      *pb = make_uint4(ob[0], ob[1], ob[2], ob[3]);
+    }
+  }
+}
+
+template <int BN, bool QKR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                         GemmParams p) {
-  using L = GemmSmem<BN>;
+  using L = GemmSmem<BN, QKR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
@@ -255,6 +388,59 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) umma_commit(accf_bar(acc));
       }
     }
+  } else if constexpr (QKR) {
+    // epilogue of the q|k|v projection: QK-RMSNorm + RoPE per head, rows staged in
+    // shared memory and stored in 512-byte pieces (in place, or into the owners' buffers)
+    const int quarter = warp & 3;
+    uint8_t* buf = smem + L::kOutOffset + quarter * 32 * 256;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(accf_bar(acc), acc_phase, p.err, kDevTimeoutAcc, abort_flag)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_coords(tile, p.tiles_m, p.tiles_n, mb, nb);
+      const int64_t row_base = (int64_t)mb * kGemmBM + quarter * 32;
+      const int64_t m = row_base + lane;
+#pragma unroll 1
+      for (int hh = 0; hh < BN / 128; ++hh) {
+        float v[4][32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + hh * 128 + c * 32, v[c]);
+        tmem_wait_ld();
+        const int64_t n0 = (int64_t)nb * BN + hh * 128;
+        const int part = (int)(n0 / p.qk.inner);
+        const int head = (int)((n0 - (int64_t)part * p.qk.inner) >> 7);
+        if (m < p.M) qk_rope_head(p, v, m, n0, part, buf, lane);
+        __syncwarp();
+        __nv_bfloat16* dst;
+        int64_t dst_stride;
+        if (p.qk.base[0] == nullptr) {
+          dst = p.y + row_base * p.ldy + n0;
+          dst_stride = p.ldy;
+        } else {
+          const int owner = head / p.qk.Hl;
+          __nv_bfloat16* b = p.qk.base[0];
+#pragma unroll
+          for (int r = 1; r < kMaxPeers; ++r)
+            if (owner == r) b = p.qk.base[r];
+          dst_stride = 3 * (int64_t)p.qk.Hl * 128;
+          dst = b + (p.qk.row0 + row_base) * dst_stride + (int64_t)part * p.qk.Hl * 128 +
+                (int64_t)(head - owner * p.qk.Hl) * 128;
+        }
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+          const int r = 2 * i + (lane >> 4), ch = lane & 15;
+          const uint4 val = *stage_chunk(buf, r, ch);
+          if (row_base + r < p.M) *reinterpret_cast<uint4*>(dst + r * dst_stride + ch * 8) = val;
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(acce_bar(acc));
+    }
   } else {
     const int quarter = warp & 3;
     const int row_in_tile = quarter * 32 + lane;
@@ -289,20 +475,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }
+  if constexpr (QKR) {
+    if (p.qk.sig.counter) peer_signal_cta_done(p.qk.sig);  // after every store of this CTA
+  }
 }
 
-template <int BN>
+template <int BN, bool QKR = false>
 static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
                           const CUtensorMap& tb2, GemmParams& p) {
-  using L = GemmSmem<BN>;
-  int st = ensure_smem_attr(ctx, (const void*)gemm_bf16_tc_kernel<BN>, L::kBytes, "gemm_bf16_tc");
+  using L = GemmSmem<BN, QKR>;
+  int st = ensure_smem_attr(ctx, (const void*)gemm_bf16_tc_kernel<BN, QKR>, L::kBytes,
+                            QKR ? "gemm_bf16_tc (qk-norm/rope epilogue)" : "gemm_bf16_tc");
   if (st) return st;
   p.tiles_m = (p.M + kGemmBM - 1) / kGemmBM;
   p.tiles_n = p.N / BN;
   p.num_tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(p.num_tiles, ctx->num_sms);
+  if (QKR) p.qk.sig.total = grid;  // every CTA of the launch counts once
   ProfScope prof(ctx, kProfGemm);
-  gemm_bf16_tc_kernel<BN><<<grid, kGemmThreads, L::kBytes, ctx->stream>>>(ta, tb, ta2, tb2, p);
+  gemm_bf16_tc_kernel<BN, QKR><<<grid, kGemmThreads, L::kBytes, ctx->stream>>>(ta, tb, ta2, tb2, p);
   return launch_status(ctx, "gemm_bf16_tc");
 }
 
@@ -310,8 +501,9 @@ static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap&
 // Wd [N,K] (pitch K), T [M,k2] (pitch k2), Bt [N,k2] (pitch k2)
 int gemm_bf16_ext(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd, int64_t N, int64_t K,
                   const void* t, const void* bt, int64_t k2, const void* bias, int epi, const void* gate,
-                  const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw) {
-  if (M == 0) return WX_OK;
+                  const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw,
+                  const QkRopeEpi* qk = nullptr) {
+  if (M == 0) return WX_OK;  // (the q|k|v epilogue is only used with M > 0)
   if (K % kGemmBK != 0 || k2 % kGemmBK != 0 || N % 64 != 0 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX ||
       k2 > INT32_MAX)
     return set_error(ctx, WX_ERR_UNSUPPORTED, "gemm needs K %% 64 == 0 and N %% 64 == 0 (M=%lld N=%lld K=%lld)",
@@ -346,6 +538,13 @@ int gemm_bf16_ext(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void
   p.rowmap = rowmap;
   p.y_raw = static_cast<__nv_bfloat16*>(y_raw);
   p.err = ctx->dev_err;
+  if (qk) {
+    if (epi != WX_EPI_NONE || BN < 128 || qk->inner % 128 != 0 || N != 3 * (int64_t)qk->inner)
+      return set_error(ctx, WX_ERR_UNSUPPORTED, "qk-norm/rope epilogue: q|k|v of 128-wide heads, N %% 128 == 0");
+    p.qk = *qk;
+    if (BN == 256) return launch_gemm_bn<256, true>(ctx, ta, tb, ta2, tb2, p);
+    return launch_gemm_bn<128, true>(ctx, ta, tb, ta2, tb2, p);
+  }
   if (BN == 256) return launch_gemm_bn<256>(ctx, ta, tb, ta2, tb2, p);
   if (BN == 128) return launch_gemm_bn<128>(ctx, ta, tb, ta2, tb2, p);
   return launch_gemm_bn<64>(ctx, ta, tb, ta2, tb2, p);
@@ -357,10 +556,6 @@ int gemm_bf16(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd
   return gemm_bf16_ext(ctx, x, M, lda, wd, N, K, nullptr, nullptr, 0, bias, epi, gate, resid, rowmap, y, ldy,
                        y_raw);
 }
-
-int gemm_bf16_ext(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void* wd, int64_t N, int64_t K,
-                  const void* t, const void* bt, int64_t k2, const void* bias, int epi, const void* gate,
-                  const void* resid, const uint32_t* rowmap, void* y, int64_t ldy, void* y_raw);
 
 bool lora_pack_ok(const wx_lora_pack* l, const wx_qweight* w) {
   return l && l->at && l->bt && l->R > 0 && l->R % 64 == 0 && l->n == w->n && l->k == w->k && aligned16(l->at) &&
@@ -394,6 +589,53 @@ int qlinear_lora_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda
   }
   return gemm_bf16_ext(ctx, x, m, lda, wd, w->n, w->k, t, bt, R, w->bias, epilogue, gate, resid, rowmap, y, ldy,
                        y_raw);
+}
+
+// The fused epilogue runs on the two-pass GEMM; where the small-M kernel would serve the
+// projection (M <= 512, no LoRA) the separate path is kept, except for the peer-memory
+// exchange (peer = true), which the fused epilogue replaces whatever M is.
+bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
+                      const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t) {
+  if (!qkv_rope_fused_enabled() || head_dim != 128 || rot < 0 || rot > 128 || rot % 16 != 0 || !aligned16(q_norm) ||
+      !aligned16(k_norm) || (rot != 0 && (!aligned16(cos_t) || !aligned16(sin_t))))
+    return false;
+  const bool small_m = !has_lora && fused_eligible(w, m, WX_EPI_NONE) && !force_two_pass();
+  return peer || !small_m;
+}
+
+// The q|k|v projection with QK-RMSNorm + RoPE in the GEMM's epilogue: dequant into `wd`,
+// (LoRA: t = x at^T), then one GEMM whose epilogue normalises and rotates q and k per
+// head. peers == nullptr: the result goes in place into y (pitch ldy); otherwise into
+// the owners' exchange buffers, and the launch's last CTA raises peers->sig.
+int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                          const wx_lora_pack* lora, void* y, int64_t ldy, const void* q_norm, const void* k_norm,
+                          const void* cos_t, const void* sin_t, int rot, float eps, void* wd, void* t,
+                          const QkvPeerOut* peers) {
+  if (w->n % 3 != 0 || (w->n / 3) % 128 != 0 || m <= 0 ||
+      !qkv_rope_fusable(w, m, lora != nullptr, true, 128, rot, q_norm, k_norm, cos_t, sin_t))
+    return set_error(ctx, WX_ERR_UNSUPPORTED, "qkv rope epilogue: n = 3 * heads * 128, rot %% 16 == 0");
+  int st = launch_dequant(ctx, w, wd);
+  if (st) return st;
+  const int64_t R = lora ? lora->R : 0;
+  if (R > 0 && (st = gemm_bf16(ctx, x, m, lda, lora->at, R, w->k, nullptr, WX_EPI_NONE, nullptr, nullptr, nullptr,
+                               t, R, nullptr)))
+    return st;
+  QkRopeEpi e{};
+  e.w0 = static_cast<const __nv_bfloat16*>(q_norm);
+  e.w1 = static_cast<const __nv_bfloat16*>(k_norm);
+  e.cos_t = static_cast<const __nv_bfloat16*>(cos_t);
+  e.sin_t = static_cast<const __nv_bfloat16*>(sin_t);
+  e.rot = rot;
+  e.eps = eps;
+  e.inner = (int)(w->n / 3);
+  if (peers) {
+    for (int r = 0; r < kMaxPeers; ++r) e.base[r] = static_cast<__nv_bfloat16*>(peers->base[r]);
+    e.row0 = peers->row0;
+    e.Hl = peers->Hl;
+    e.sig = peers->sig;
+  }
+  return gemm_bf16_ext(ctx, x, m, lda, wd, w->n, w->k, t, R > 0 ? lora->bt : nullptr, R, w->bias, WX_EPI_NONE,
+                       nullptr, nullptr, nullptr, y, ldy, nullptr, &e);
 }
 
 int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,

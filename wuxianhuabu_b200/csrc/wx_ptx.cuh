@@ -317,6 +317,16 @@ struct PeerSignal {
   uint32_t epoch;
 };
 
+// Destination of the q|k|v projection's fused QK-norm/RoPE epilogue under sequence
+// parallelism: head h of local row m goes to base[h / Hl] (layout [S][3][Hl][128], row
+// row0 + m); sig is raised by the launch's last CTA.
+struct QkvPeerOut {
+  void* base[kMaxPeers];
+  int64_t row0;
+  int Hl;
+  PeerSignal sig;
+};
+
 __device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }

@@ -26,6 +26,9 @@ __device__ __forceinline__ float warp_sum(float v) {
 // (s, h) row. nv = bf16(x*rstd*w); split-half rotation of pairs (j, j+rh)
 // for j < rh; dims >= rot pass through. Rows are located by (s, part, h):
 // x + s*x_stride + part*part_off + h*hd, output likewise with out_stride.
+// The rotation's products are rounded separately (no contraction into FMAs) and
+// the sum of squares uses explicit FMAs, so the q|k|v GEMM's fused epilogue
+// (wx_gemm.cu) reproduces these bits.
 template <int HD>
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     const __nv_bfloat16* __restrict__ x, int64_t x_stride, __nv_bfloat16* __restrict__ out,
@@ -56,7 +59,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   }
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < E; ++i) ss += xv[i] * xv[i];
+  for (int i = 0; i < E; ++i) ss = __fmaf_rn(xv[i], xv[i], ss);
   ss = warp_sum(ss);
   const float rstd = rsqrtf(ss / (float)HD + eps);
 #pragma unroll
@@ -74,11 +77,11 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     if (j < rh) {
       const float c = __bfloat162float(cos_t[s * rh + j]);
       const float sn = __bfloat162float(sin_t[s * rh + j]);
-      o[i] = nv * c - nv_s[warp][j + rh] * sn;
+      o[i] = __fsub_rn(__fmul_rn(nv, c), __fmul_rn(nv_s[warp][j + rh], sn));
     } else if (j < rot) {
       const float c = __bfloat162float(cos_t[s * rh + j - rh]);
       const float sn = __bfloat162float(sin_t[s * rh + j - rh]);
-      o[i] = nv * c + nv_s[warp][j - rh] * sn;
+      o[i] = __fadd_rn(__fmul_rn(nv, c), __fmul_rn(nv_s[warp][j - rh], sn));
     } else {
       o[i] = nv;
     }
@@ -171,7 +174,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
         const float xv[4] = {bf16_lo(raw[i].x), bf16_hi(raw[i].x), bf16_lo(raw[i].y), bf16_hi(raw[i].y)};
         float ss = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) ss += xv[e] * xv[e];
+        for (int e = 0; e < 4; ++e) ss = __fmaf_rn(xv[e], xv[e], ss);
         ss = warp_sum(ss);
         const float rstd = rsqrtf(ss / 128.f + eps);
         float nv[4], o[4];
@@ -183,9 +186,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_vec_kernel(
           if (!rotated)
             o[e] = nv[e];
           else if (first)
-            o[e] = nv[e] * c[e] - pv * sn[e];
+            o[e] = __fsub_rn(__fmul_rn(nv[e], c[e]), __fmul_rn(pv, sn[e]));
           else
-            o[e] = nv[e] * c[e] + pv * sn[e];
+            o[e] = __fadd_rn(__fmul_rn(nv[e], c[e]), __fmul_rn(pv, sn[e]));
         }
         *reinterpret_cast<uint2*>(dst(s, part, h0 + i) + lane * 4) =
             make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));

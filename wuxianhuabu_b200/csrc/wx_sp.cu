@@ -37,6 +37,12 @@ int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, con
                          const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
                          void* y_raw, void* wd, void* swiglu_tmp);
 bool qweight_ok(const wx_qweight* w);
+bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
+                      const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t);
+int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                          const wx_lora_pack* lora, void* y, int64_t ldy, const void* q_norm, const void* k_norm,
+                          const void* cos_t, const void* sin_t, int rot, float eps, void* wd, void* t,
+                          const QkvPeerOut* peers);
 size_t attention_scratch_bytes(int64_t S, int H, int hd, const wx_sparse_spec* spec);
 int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
                            int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os, void* scratch);
@@ -506,14 +512,25 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
     if ((st = launch_norm_modscale(ctx, h, rows, cfg->hidden, w->norm1, mods->shift_msa, mods->scale_msa, rowmap,
                                    cfg->eps, m)))
       return st;
-    tr.begin(WX_TRACE_QKV);
-    if ((st = qlinear_lora_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr, nullptr, nullptr, qkv,
-                                   3 * inner, nullptr, wd, lt, nullptr)))
-      return st;
     const float scale = 1.0f / sqrtf((float)hd);
     const P2PLayout PL = p2p_layout(S, rows, inner, Hl, hd);
     const int peer = p2p_ensure(ctx, PL.total, hd, cfg->rot, &st);
     if (st) return st;
+    // QK-norm + RoPE in the q|k|v GEMM's epilogue where the geometry allows
+    const bool fused = qkv_rope_fusable(&w->qkv, rows, w->lora[0] != nullptr, peer != 0, hd, cfg->rot, w->q_norm,
+                                        w->k_norm, cos_t, sin_t);
+    tr.begin(WX_TRACE_QKV);
+    if (!(peer && fused)) {
+      if (fused) {
+        if ((st = qkv_rope_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], qkv, 3 * inner, w->q_norm,
+                                        w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, wd, lt, nullptr)))
+          return st;
+      } else if ((st = qlinear_lora_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE,
+                                                 nullptr, nullptr, nullptr, qkv, 3 * inner, nullptr, wd, lt,
+                                                 nullptr))) {
+        return st;
+      }
+    }
     if (peer) {
       // exchange 1: QK-norm + RoPE (and v) of this rank's rows straight into the owners'
       // buffers; exchange 2: attention rows straight into the owners' out-proj operand
@@ -534,10 +551,23 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
       sig1.rank = rank;
       sig1.epoch = ep;
       uint8_t* mine = static_cast<uint8_t*>(ctx->p2p_buf);
-      tr.begin(WX_TRACE_ROPE);
-      if ((st = launch_qkv_to_peers(ctx, qkv, rows, (int64_t)rank * rows, cfg->heads, Hl, qkv_dst, P, w->q_norm,
-                                    w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, sig1)))
-        return st;
+      if (fused) {
+        // the GEMM's epilogue stores q|k|v rows straight into the owners' buffers
+        QkvPeerOut po1{};
+        for (int r = 0; r < P; ++r) po1.base[r] = qkv_dst[r];
+        po1.row0 = (int64_t)rank * rows;
+        po1.Hl = Hl;
+        po1.sig = sig1;
+        if ((st = qkv_rope_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], qkv, 3 * inner, w->q_norm,
+                                        w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, wd, lt, &po1)))
+          return st;
+        tr.begin(WX_TRACE_ROPE);
+      } else {
+        tr.begin(WX_TRACE_ROPE);
+        if ((st = launch_qkv_to_peers(ctx, qkv, rows, (int64_t)rank * rows, cfg->heads, Hl, qkv_dst, P, w->q_norm,
+                                      w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, sig1)))
+          return st;
+      }
       {
         ProfScope wprof(ctx, kProfPeerWait);
         sp_wait_flags_kernel<<<1, 32, 0, ctx->stream>>>(reinterpret_cast<const uint32_t*>(mine + PL.flags1), P, ep,
@@ -571,8 +601,8 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
     }
     if (!peer) {
       tr.begin(WX_TRACE_ROPE);
-      if ((st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, rows, cfg->heads, hd, w->q_norm,
-                                    w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
+      if (!fused && (st = launch_qk_norm_rope(ctx, qkv, 3 * inner, qkv, 3 * inner, inner, 2, rows, cfg->heads, hd,
+                                              w->q_norm, w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps)))
         return st;
       // q|k|v of this rank's rows, grouped by destination head block
       const int64_t pack_units = (int64_t)P * rows * 3 * Hl * hd / 8;
