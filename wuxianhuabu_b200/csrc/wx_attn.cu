@@ -47,8 +47,26 @@ __global__ void block_stats_kernel(const __nv_bfloat16* __restrict__ q, const __
   const int64_t r1 = min(r0 + block, S);
   const float len = (float)(r1 - r0);
   float aq = 0.f, ak = 0.f, av = 0.f;
-  for (int64_t s = r0; s < r1; ++s) {
-    const int64_t o = s * row_stride + (int64_t)h * hd + d;
+  const int64_t col = (int64_t)h * hd + d;
+  int64_t s = r0;
+  for (; s + 8 <= r1; s += 8) {  // 8 rows' loads in flight, then the sums in row order
+    float xq[8], xk[8], xv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t o = (s + u) * row_stride + col;
+      xq[u] = __bfloat162float(q[o]);
+      xk[u] = __bfloat162float(k[o]);
+      xv[u] = __bfloat162float(v[o]);
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      aq = __fadd_rn(aq, xq[u]);
+      ak = __fadd_rn(ak, xk[u]);
+      av = __fadd_rn(av, xv[u]);
+    }
+  }
+  for (; s < r1; ++s) {
+    const int64_t o = s * row_stride + col;
     aq = __fadd_rn(aq, __bfloat162float(q[o]));
     ak = __fadd_rn(ak, __bfloat162float(k[o]));
     av = __fadd_rn(av, __bfloat162float(v[o]));
@@ -64,11 +82,30 @@ __global__ void block_stats_kernel(const __nv_bfloat16* __restrict__ q, const __
 __global__ void kcenter_kernel(float* __restrict__ kc, int nb, int hd, float* __restrict__ kvar) {
   const int h = blockIdx.x, d = threadIdx.x;
   float* base = kc + (int64_t)h * nb * hd + d;
+  constexpr int U = 16;  // loads in flight per chain; the sums stay in block order
   float acc = 0.f;
-  for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, base[(int64_t)b * hd]);
+  int b = 0;
+  for (; b + U <= nb; b += U) {
+    float x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) x[u] = base[(int64_t)(b + u) * hd];
+#pragma unroll
+    for (int u = 0; u < U; ++u) acc = __fadd_rn(acc, x[u]);
+  }
+  for (; b < nb; ++b) acc = __fadd_rn(acc, base[(int64_t)b * hd]);
   const float mean = __fdiv_rn(acc, (float)nb);
   float vacc = 0.f;
-  for (int b = 0; b < nb; ++b) {
+  for (b = 0; b + U <= nb; b += U) {
+    float x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) x[u] = __fsub_rn(base[(int64_t)(b + u) * hd], mean);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      base[(int64_t)(b + u) * hd] = x[u];
+      vacc = __fadd_rn(vacc, __fmul_rn(x[u], x[u]));
+    }
+  }
+  for (; b < nb; ++b) {
     const float c = __fsub_rn(base[(int64_t)b * hd], mean);
     base[(int64_t)b * hd] = c;
     vacc = __fadd_rn(vacc, __fmul_rn(c, c));
@@ -258,29 +295,87 @@ __global__ void __launch_bounds__(256) topk_select_kernel(const float* __restric
 }
 
 // ------------------------------------------------------------- 3. tail pool
-// grid (nb, H), block hd: C = max over unselected bf16(cm); T = sum p*vsum; L = sum p*len
-__global__ void tail_kernel(const uint8_t* __restrict__ sel, const __nv_bfloat16* __restrict__ cm,
-                            const __nv_bfloat16* __restrict__ vsum, const float* __restrict__ lens, int nb, int hd,
-                            float* __restrict__ tT, float* __restrict__ tL, float* __restrict__ tC) {
-  const int qb = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
-  const int64_t rb = ((int64_t)h * nb + qb) * nb;
+// Of the unselected blocks j of row (h, qb), with p_j = exp(bf16(cm_j) - C):
+// C = max bf16(cm_j), T[d] = sum_j p_j * vsum[j][d], L = sum_j p_j * len_j, each sum in
+// ascending j with one fused multiply-add per term (an all-selected row gives C = -inf,
+// T = 0, L = 0). Selected blocks enter the products with p = 0, which leaves a sum's
+// bits unchanged, so T can run as a dense register-tiled product.
+
+// thread per (h, qb): C and L (sequential over j)
+__global__ void tail_rowstat_kernel(const uint8_t* __restrict__ sel, const __nv_bfloat16* __restrict__ cm,
+                                    const float* __restrict__ lens, int H, int nb, float* __restrict__ tL,
+                                    float* __restrict__ tC) {
+  const int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (row >= (int64_t)H * nb) return;
+  const uint8_t* sr = sel + row * nb;
+  const __nv_bfloat16* cr = cm + row * nb;
   float cmax = -INFINITY;
   for (int j = 0; j < nb; ++j)
-    if (!sel[rb + j]) cmax = fmaxf(cmax, __bfloat162float(cm[rb + j]));
-  float t = 0.f, l = 0.f;
-  if (cmax > -INFINITY) {
-    for (int j = 0; j < nb; ++j) {
-      if (sel[rb + j]) continue;
-      const float p = expf(__bfloat162float(cm[rb + j]) - cmax);
-      t += p * __bfloat162float(vsum[((int64_t)h * nb + j) * hd + d]);
-      l += p * lens[j];
+    if (!sr[j]) cmax = fmaxf(cmax, __bfloat162float(cr[j]));
+  float l = 0.f;
+  if (cmax > -INFINITY)
+    for (int j = 0; j < nb; ++j)
+      if (!sr[j]) l = __fmaf_rn(expf(__bfloat162float(cr[j]) - cmax), lens[j], l);
+  tL[row] = l;
+  tC[row] = cmax;
+}
+
+// grid (ceil(nb/64), H), block 256: T for 64 query blocks x HD columns, 4 x HD/16 per
+// thread; p (64 x 32) and vsum (32 x HD) staged through shared memory per chunk of 32 j
+template <int HD>
+__global__ void __launch_bounds__(256) tail_pool_kernel(const uint8_t* __restrict__ sel,
+                                                        const __nv_bfloat16* __restrict__ cm,
+                                                        const __nv_bfloat16* __restrict__ vsum,
+                                                        const float* __restrict__ tC, int nb,
+                                                        float* __restrict__ tT) {
+  constexpr int QB = 64, JC = 32, ND = HD / 16;
+  __shared__ float ps[QB][JC + 1];
+  __shared__ float vs[JC][HD];
+  const int h = blockIdx.y, qb0 = blockIdx.x * QB;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  float acc[4][ND];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int k = 0; k < ND; ++k) acc[i][k] = 0.f;
+  const int64_t hrow = (int64_t)h * nb;
+  for (int j0 = 0; j0 < nb; j0 += JC) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < QB * JC; e += 256) {
+      const int r = e / JC, jj = e % JC;
+      const int qb = qb0 + r, j = j0 + jj;
+      float pv = 0.f;
+      if (qb < nb && j < nb) {
+        const int64_t idx = (hrow + qb) * nb + j;
+        const float c = __ldg(tC + hrow + qb);
+        if (!sel[idx] && c > -INFINITY) pv = expf(__bfloat162float(cm[idx]) - c);
+      }
+      ps[r][jj] = pv;
+    }
+    for (int e = threadIdx.x; e < JC * HD; e += 256) {
+      const int jj = e / HD, d = e % HD, j = j0 + jj;
+      vs[jj][d] = j < nb ? __bfloat162float(vsum[(hrow + j) * HD + d]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int jj = 0; jj < JC; ++jj) {
+      float pq[4], vv[ND];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) pq[i] = ps[ty * 4 + i][jj];
+#pragma unroll
+      for (int k = 0; k < ND; ++k) vv[k] = vs[jj][tx + 16 * k];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int k = 0; k < ND; ++k) acc[i][k] = __fmaf_rn(pq[i], vv[k], acc[i][k]);
     }
   }
-  const int64_t o = (int64_t)h * nb + qb;
-  tT[o * hd + d] = t;
-  if (d == 0) {
-    tL[o] = l;
-    tC[o] = cmax;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int qb = qb0 + ty * 4 + i;
+    if (qb >= nb) continue;
+#pragma unroll
+    for (int k = 0; k < ND; ++k) tT[(hrow + qb) * HD + tx + 16 * k] = acc[i][k];
   }
 }
 
@@ -628,8 +723,14 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   ProfScope prof(ctx, kProfRoute);
   if (!a.dense) {
     if (tail) {
-      tail_kernel<<<dim3(a.nb, a.H), a.hd, 0, ctx->stream>>>(sel, cm, vsum, lens, a.nb, a.hd, tT, tL, tC);
-      if ((st = launch_status(ctx, "tail"))) return st;
+      tail_rowstat_kernel<<<(unsigned)((hnb + 127) / 128), 128, 0, ctx->stream>>>(sel, cm, lens, a.H, a.nb, tL,
+                                                                                  tC);
+      const dim3 tg((a.nb + 63) / 64, a.H);
+      if (a.hd == 64)
+        tail_pool_kernel<64><<<tg, 256, 0, ctx->stream>>>(sel, cm, vsum, tC, a.nb, tT);
+      else
+        tail_pool_kernel<128><<<tg, 256, 0, ctx->stream>>>(sel, cm, vsum, tC, a.nb, tT);
+      if ((st = launch_status(ctx, "tail", 2))) return st;
     }
     const int64_t warps = (int64_t)a.H * a.nvt;
     const unsigned blocks = (unsigned)((warps * 32 + 255) / 256);
