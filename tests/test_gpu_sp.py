@@ -1,8 +1,9 @@
-"""Ulysses sequence parallelism on 2 GPUs: wx_dit_block_forward_sp against the
-single-GPU block on the same inputs (dense, SOL and top-k attention; refresh,
-refresh, PAB reuse in sequence), with the exchange over NVLink peer memory
-(default) and over NCCL all-to-alls (WX_SP_P2P=0). Skipped on boxes with fewer
-than 2 GPUs."""
+"""Ulysses sequence parallelism on 2, 4 and 8 GPUs: wx_dit_block_forward_sp against the
+single-GPU block on the same inputs (dense, SOL and top-k attention; refresh, refresh, PAB
+reuse in sequence), with the exchange over NVLink peer memory (default: the q|k|v projection's
+epilogue stores into the owners' buffers) and over NCCL all-to-alls (WX_SP_P2P=0). S = 1000
+rows, so that rank boundaries fall inside 128-row query tiles; heads = max(4, P). Each world
+size is skipped on boxes with fewer GPUs."""
 import datetime
 import os
 import socket
@@ -44,8 +45,8 @@ def _worker(rank, world, port, sparse_name, p2p, out_q):
         from tests._util import cosine, f32, max_rel_err, to_np_bf16, to_torch_bf16
         from tests.test_gpu_block import gpu_block, make_block
         from wuxianhuabu_b200 import h3
-        hidden, heads, ffn, rot, eps, g = 256, 4, 512, 96, 1e-6, 40
-        S = 1000  # 500 rows per rank: the rank boundary falls inside a 128-row query tile
+        hidden, heads, ffn, rot, eps, g = 256, max(4, world), 512, 96, 1e-6, 40
+        S = 1000  # 1000 / P rows per rank: rank boundaries fall inside 128-row query tiles
         w, mods, h, cos, sin, rowmap = make_block(9, hidden, heads, ffn, 0, S, rot)
         sparse = {"dense": None, "sol": dict(tau=0.4), "topk": dict(block=128, topk_ratio=0.25, tail=False)}[sparse_name]
         spec = None if sparse is None else h3.H3SolAttnConfig(**sparse).spec(g)
@@ -88,15 +89,17 @@ def _worker(rank, world, port, sparse_name, p2p, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("p2p", ["1", "0"])
 @pytest.mark.parametrize("sparse_name", ["dense", "sol", "topk"])
-def test_ulysses_block_matches_single_gpu(sparse_name, p2p):
+def test_ulysses_block_matches_single_gpu(sparse_name, p2p, world):
+    if _gpus() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, sparse_name, p2p, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, sparse_name, p2p, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -104,11 +107,11 @@ def test_ulysses_block_matches_single_gpu(sparse_name, p2p):
     for p in procs:
         if p.is_alive():
             p.kill()
-    assert [p.exitcode for p in procs] == [0, 0]
+    assert [p.exitcode for p in procs] == [0] * world
     res = []
     while not q.empty():
         res.append(q.get())
-    assert len(res) == 2
+    assert len(res) == world
     for rank, path, *errs in res:
         # the exchange path asked for was taken (1 peer memory, 0 all-to-alls)
         assert path == int(p2p), (rank, path)

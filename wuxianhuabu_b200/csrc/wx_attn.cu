@@ -299,49 +299,51 @@ __global__ void __launch_bounds__(256) topk_select_kernel(const float* __restric
 // C = max bf16(cm_j), T[d] = sum_j p_j * vsum[j][d], L = sum_j p_j * len_j, each sum in
 // ascending j with one fused multiply-add per term (an all-selected row gives C = -inf,
 // T = 0, L = 0). Selected blocks enter the products with p = 0, which leaves a sum's
-// bits unchanged, so T can run as a dense register-tiled product.
+// bits unchanged, so T and L run as a dense register-tiled product.
 
-// thread per (h, qb): C and L (sequential over j)
-__global__ void tail_rowstat_kernel(const uint8_t* __restrict__ sel, const __nv_bfloat16* __restrict__ cm,
-                                    const float* __restrict__ lens, int H, int nb, float* __restrict__ tL,
-                                    float* __restrict__ tC) {
-  const int64_t row = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+// warp per (h, qb): C (a max, so any order)
+__global__ void tail_cmax_kernel(const uint8_t* __restrict__ sel, const __nv_bfloat16* __restrict__ cm, int H,
+                                 int nb, float* __restrict__ tC) {
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (row >= (int64_t)H * nb) return;
   const uint8_t* sr = sel + row * nb;
   const __nv_bfloat16* cr = cm + row * nb;
   float cmax = -INFINITY;
-  for (int j = 0; j < nb; ++j)
+  for (int j = lane; j < nb; j += 32)
     if (!sr[j]) cmax = fmaxf(cmax, __bfloat162float(cr[j]));
-  float l = 0.f;
-  if (cmax > -INFINITY)
-    for (int j = 0; j < nb; ++j)
-      if (!sr[j]) l = __fmaf_rn(expf(__bfloat162float(cr[j]) - cmax), lens[j], l);
-  tL[row] = l;
-  tC[row] = cmax;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, o));
+  if (lane == 0) tC[row] = cmax;
 }
 
-// grid (ceil(nb/64), H), block 256: T for 64 query blocks x HD columns, 4 x HD/16 per
-// thread; p (64 x 32) and vsum (32 x HD) staged through shared memory per chunk of 32 j
+// grid (ceil(nb/64), H), block 128: T for 64 query blocks x HD columns (8 x HD/16 per
+// thread) and L (threads tx == 0); p (64 x 32) and vsum (32 x HD) staged through shared
+// memory per chunk of 32 j
 template <int HD>
-__global__ void __launch_bounds__(256) tail_pool_kernel(const uint8_t* __restrict__ sel,
+__global__ void __launch_bounds__(128) tail_pool_kernel(const uint8_t* __restrict__ sel,
                                                         const __nv_bfloat16* __restrict__ cm,
                                                         const __nv_bfloat16* __restrict__ vsum,
+                                                        const float* __restrict__ lens,
                                                         const float* __restrict__ tC, int nb,
-                                                        float* __restrict__ tT) {
-  constexpr int QB = 64, JC = 32, ND = HD / 16;
+                                                        float* __restrict__ tT, float* __restrict__ tL) {
+  constexpr int QB = 64, JC = 32, ND = HD / 16, QT = 8;
   __shared__ float ps[QB][JC + 1];
   __shared__ float vs[JC][HD];
+  __shared__ float ls[JC];
   const int h = blockIdx.y, qb0 = blockIdx.x * QB;
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  float acc[4][ND];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 8 groups of 8 query blocks
+  float acc[QT][ND], accl[QT];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < QT; ++i) {
+    accl[i] = 0.f;
 #pragma unroll
     for (int k = 0; k < ND; ++k) acc[i][k] = 0.f;
+  }
   const int64_t hrow = (int64_t)h * nb;
   for (int j0 = 0; j0 < nb; j0 += JC) {
     __syncthreads();
-    for (int e = threadIdx.x; e < QB * JC; e += 256) {
+    for (int e = threadIdx.x; e < QB * JC; e += 128) {
       const int r = e / JC, jj = e % JC;
       const int qb = qb0 + r, j = j0 + jj;
       float pv = 0.f;
@@ -352,30 +354,37 @@ __global__ void __launch_bounds__(256) tail_pool_kernel(const uint8_t* __restric
       }
       ps[r][jj] = pv;
     }
-    for (int e = threadIdx.x; e < JC * HD; e += 256) {
+    for (int e = threadIdx.x; e < JC * HD; e += 128) {
       const int jj = e / HD, d = e % HD, j = j0 + jj;
       vs[jj][d] = j < nb ? __bfloat162float(vsum[(hrow + j) * HD + d]) : 0.f;
     }
+    if (threadIdx.x < JC) ls[threadIdx.x] = j0 + threadIdx.x < nb ? lens[j0 + threadIdx.x] : 0.f;
     __syncthreads();
-#pragma unroll 4
+#pragma unroll 2
     for (int jj = 0; jj < JC; ++jj) {
-      float pq[4], vv[ND];
+      float pq[QT], vv[ND];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pq[i] = ps[ty * 4 + i][jj];
+      for (int i = 0; i < QT; ++i) pq[i] = ps[ty * QT + i][jj];
 #pragma unroll
       for (int k = 0; k < ND; ++k) vv[k] = vs[jj][tx + 16 * k];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < QT; ++i)
 #pragma unroll
         for (int k = 0; k < ND; ++k) acc[i][k] = __fmaf_rn(pq[i], vv[k], acc[i][k]);
+      if (tx == 0) {
+        const float lj = ls[jj];
+#pragma unroll
+        for (int i = 0; i < QT; ++i) accl[i] = __fmaf_rn(pq[i], lj, accl[i]);
+      }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int qb = qb0 + ty * 4 + i;
+  for (int i = 0; i < QT; ++i) {
+    const int qb = qb0 + ty * QT + i;
     if (qb >= nb) continue;
 #pragma unroll
     for (int k = 0; k < ND; ++k) tT[(hrow + qb) * HD + tx + 16 * k] = acc[i][k];
+    if (tx == 0) tL[hrow + qb] = accl[i];
   }
 }
 
@@ -723,13 +732,12 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   ProfScope prof(ctx, kProfRoute);
   if (!a.dense) {
     if (tail) {
-      tail_rowstat_kernel<<<(unsigned)((hnb + 127) / 128), 128, 0, ctx->stream>>>(sel, cm, lens, a.H, a.nb, tL,
-                                                                                  tC);
+      tail_cmax_kernel<<<(unsigned)((hnb * 32 + 255) / 256), 256, 0, ctx->stream>>>(sel, cm, a.H, a.nb, tC);
       const dim3 tg((a.nb + 63) / 64, a.H);
       if (a.hd == 64)
-        tail_pool_kernel<64><<<tg, 256, 0, ctx->stream>>>(sel, cm, vsum, tC, a.nb, tT);
+        tail_pool_kernel<64><<<tg, 128, 0, ctx->stream>>>(sel, cm, vsum, lens, tC, a.nb, tT, tL);
       else
-        tail_pool_kernel<128><<<tg, 256, 0, ctx->stream>>>(sel, cm, vsum, tC, a.nb, tT);
+        tail_pool_kernel<128><<<tg, 128, 0, ctx->stream>>>(sel, cm, vsum, lens, tC, a.nb, tT, tL);
       if ((st = launch_status(ctx, "tail", 2))) return st;
     }
     const int64_t warps = (int64_t)a.H * a.nvt;
