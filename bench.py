@@ -599,6 +599,63 @@ def run_c1(args) -> dict:
                                   sample="the whole block (oracle, C, OpenMP), best of 3, same weights and inputs"))
 
 
+def _sm_clock_now(index: int = 0):
+    """The SM clock (MHz) at this moment, from NVML (None where NVML is unavailable): small
+    kernels are latency-bound and follow the clock, which the power cap lowers after heavy work."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(index)
+        return int(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+    except Exception:
+        return None
+
+
+def _qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g) -> dict:
+    """The same shape as a q|k|v projection (N = 3 * heads * 128) with QK-RMSNorm + RoPE
+    (rot 96): one GEMM with the norm/RoPE epilogue (wx_qkv_norm_rope) against the projection
+    followed by the separate row kernel, kernel CUDA-event time per call."""
+    import ctypes
+    import torch
+    from wuxianhuabu_b200 import h3
+    heads, hd, rot = N // 384, 128, 96
+    qn = (1 + 0.02 * torch.randn(hd, device=dev, generator=g)).to(torch.bfloat16)
+    kn = (1 + 0.02 * torch.randn(hd, device=dev, generator=g)).to(torch.bfloat16)
+    cos = torch.randn((M, rot // 2), device=dev, generator=g).to(torch.bfloat16)
+    sin = torch.randn((M, rot // 2), device=dev, generator=g).to(torch.bfloat16)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+    inner = N // 3
+    reps = max(1, args.steps)
+
+    def fused():
+        lin.qkv_norm_rope(x, heads, hd, qn, kn, cos, sin, rot, 1e-6, out=y)
+
+    def separate():
+        lin(x, out=y)
+        for part, w in ((0, qn), (1, kn)):
+            v = y[:, part * inner:(part + 1) * inner].view(M, heads, hd)
+            h3.H3FusedKernels.fused_rmsnorm_rope(v, w, cos, sin, rot, 1e-6, out=v)
+
+    out = {}
+    for name, fn in (("fused", fused), ("separate", separate)):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
+        torch.cuda._sleep(400_000 * reps)
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+        ms = (ctypes.c_double * 10)()
+        cnt = (ctypes.c_int64 * 10)()
+        ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
+        ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
+        t = sum(ms[i] for i in (0, 4, 6)) / reps / 1e3  # GEMM + weight expansion + norm/RoPE kernel
+        out[f"qkv_rope_{name}_ms"] = t * 1e3
+        out[f"qkv_rope_{name}_frac"] = fl / t / 1e12 / pk
+    return out
+
+
 def run_c2(args) -> dict:
     """the 6-bit quantized linear sweep."""
     import torch
@@ -630,11 +687,16 @@ def run_c2(args) -> dict:
             ctx = h3.context(0)
             ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
             reps = max(1, args.steps)
+            # hold the GPU in a spin while the host enqueues every call, so that the events
+            # around each launch (and around the loop) see device time only: a small-M call is
+            # shorter than its host-side launch path, and an idle GPU would count that path
+            torch.cuda._sleep(200_000 * reps)
+            e0.record()
             for _ in range(reps):
                 lin(x, out=y)
             e1.record()
+            sm_mhz = _sm_clock_now(0)  # while the last calls still run
             torch.cuda.synchronize()
             ms = (ctypes.c_double * 10)()
             cnt = (ctypes.c_int64 * 10)()
@@ -642,18 +704,22 @@ def run_c2(args) -> dict:
             ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
             t_call = e0.elapsed_time(e1) / reps / 1e3
             # the kernels' own time: CUDA events libwx records around each launch (the GEMM,
-            # plus the weight expansion of the two-pass path), free of host gaps between calls
+            # plus the weight expansion of the two-pass path)
             t = (ms[0] + ms[4]) / reps / 1e3
             fl = 2.0 * M * N * K
             byts = 2 * M * K + 0.75 * N * K + 4 * N * (K // 64) + 2 * M * N
-            res.append(dict(M=M, K=K, N=N, ms=t * 1e3, tflops=fl / t / 1e12, frac=fl / t / 1e12 / pk,
-                            gbs=byts / t / 1e9, gbs_frac=byts / t / 1e9 / hbm, ms_per_call=t_call * 1e3,
-                            path="fused" if (M <= 512 and N % 128 == 0 and args.lora == 0) else "two-pass",
-                            lora_rank=args.lora))
+            row = dict(M=M, K=K, N=N, ms=t * 1e3, tflops=fl / t / 1e12, frac=fl / t / 1e12 / pk,
+                       gbs=byts / t / 1e9, gbs_frac=byts / t / 1e9 / hbm, ms_per_call=t_call * 1e3,
+                       path="fused" if (M <= 512 and N % 128 == 0 and args.lora == 0) else "two-pass",
+                       lora_rank=args.lora, sm_mhz=sm_mhz)
+            if args.qkv_rope and N % 384 == 0:
+                row.update(_qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g))
+            res.append(row)
             del x, y
     return dict(metric="6-bit qGEMM sweep (c2)", unit="TFLOP/s", peak=pk, peak_kind=f"{kind} burst bf16", hbm_peak=hbm,
                 sweep=res, timing="ms = the kernels' CUDA-event time per call (libwx records events around each "
-                                  "launch); ms_per_call = events around the loop of calls (host gaps included)")
+                                  "launch); ms_per_call = events around the loop of calls; every call is enqueued "
+                                  "while the GPU spins, so neither includes host launch time")
 
 
 # ------------------------------------------------------------------ main
@@ -669,6 +735,9 @@ def main():
                     help="c3 / c3full / c5attn: top-k 25%% over 128-row blocks, or SOL tau 1.3 over 64-row blocks")
     ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
+    ap.add_argument("--qkv-rope", action="store_true",
+                    help="c2 only: also time N = 3*heads*128 shapes as q|k|v projections with QK-norm + RoPE, "
+                         "fused epilogue against the separate kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()

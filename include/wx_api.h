@@ -294,6 +294,15 @@ int wx_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, int64_t S, int
  * in one launch (the two fusedRmsnormRope calls of H3AttnW.forward, H3Transformer.swift:454-475) */
 int wx_qk_norm_rope_qkv(wx_ctx* ctx, void* qkv, int64_t S, int H, int head_dim, const void* q_w,
                         const void* k_w, const void* cos_t, const void* sin_t, int rot, float eps);
+/* The q|k|v projection of H3AttnW.forward together with its two fusedRmsnormRope calls
+ * (H3Transformer.swift:451-475): y = MfLinear(x) ([m, 3*H*head_dim] bf16, pitch ldy; with the
+ * LoRA delta when lora != NULL), then q and k normalised (q_w / k_w) and rotated per head.
+ * head_dim 128 with rot % 16 == 0 runs as ONE GEMM whose epilogue does the norm and the
+ * rotation, bit-identical to the two-pass wx_qlinear (M > 512) followed by
+ * wx_qk_norm_rope_qkv; other geometries run those two calls. */
+int wx_qkv_norm_rope(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                     const wx_lora_pack* lora, int H, int head_dim, const void* q_w, const void* k_w,
+                     const void* cos_t, const void* sin_t, int rot, float eps, void* y, int64_t ldy);
 /* H3FusedKernels.fusedNormModscale (fused:262-283); rowmap NULL = fusedNormModscaleRow (:295-315) */
 int wx_norm_modscale(wx_ctx* ctx, const void* x, int64_t S, int64_t hidden, const void* w,
                      const void* shift, const void* scale, const uint32_t* rowmap, float eps,

@@ -17,6 +17,8 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+from oracle import oracle as O
+
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parent.parent
 
@@ -73,3 +75,63 @@ def test_fused_qkv_rope_epilogue_is_bit_identical_to_the_separate_kernel():
         for k in a.files:
             diff = int(np.count_nonzero(a[k] != b[k]))
             assert diff == 0, f"{k}: {diff} of {a[k].size} elements differ"
+
+
+@pytest.mark.parametrize("m,heads,bias,lora", [(700, 3, True, False), (2048, 2, False, False), (1500, 2, True, True)])
+def test_wx_qkv_norm_rope_equals_projection_then_norm_rope(m, heads, bias, lora):
+    """The ABI call (one GEMM with the norm/RoPE epilogue) against the two calls it replaces:
+    the two-pass projection (M > 512; with the LoRA delta as a K extension) and the row kernel
+    on q and k, bit for bit."""
+    import torch
+    from tests._util import to_torch_bf16
+    from wuxianhuabu_b200 import h3
+    hidden, hd, rot, eps = 512, 128, 96, 1e-6
+    inner = heads * hd
+    wq, sc, bi = O.quantize(O.normal_f32((3 * inner, hidden), 71, m, std=0.02))
+    b = to_torch_bf16(O.normal_bf16((3 * inner,), 71, 1, std=0.5)) if bias else None
+    lin = h3.MfLinear(torch.from_numpy(wq.view(np.int32)).cuda(), to_torch_bf16(sc), to_torch_bf16(bi), hidden, b)
+    if lora:
+        a_ = to_torch_bf16(O.normal_bf16((hidden, 16), 71, 2, std=0.05))
+        b_ = to_torch_bf16(O.normal_bf16((16, 3 * inner), 71, 3, std=0.05))
+        lin.set_lora([h3.LoraRef(a_, b_, 0.5)])
+    x = to_torch_bf16(O.normal_bf16((m, hidden), 71, 4))
+    qn = to_torch_bf16(O.normal_bf16((hd,), 71, 5, mean=1.0, std=0.02))
+    kn = to_torch_bf16(O.normal_bf16((hd,), 71, 6, mean=1.0, std=0.02))
+    cos = to_torch_bf16(O.normal_bf16((m, rot // 2), 71, 7))
+    sin = to_torch_bf16(O.normal_bf16((m, rot // 2), 71, 8))
+    got = lin.qkv_norm_rope(x, heads, hd, qn, kn, cos, sin, rot, eps)
+    ref = lin(x)
+    for part, w in ((0, qn), (1, kn)):
+        view = ref[:, part * inner:(part + 1) * inner].view(m, heads, hd)
+        h3.H3FusedKernels.fused_rmsnorm_rope(view, w, cos, sin, rot, eps, out=view)
+    h3.context().check_device()
+    assert torch.equal(got, ref)
+
+
+def test_wx_qkv_norm_rope_small_m_and_head_dim_64_against_the_oracle():
+    """M <= 512 (the fused epilogue on the two-pass GEMM) and head_dim 64 (the two-call path)
+    against the oracle's projection + qk_norm_rope, at the GEMM's bound."""
+    import torch
+    from tests._util import assert_close, f32, to_np_bf16, to_torch_bf16
+    from wuxianhuabu_b200 import h3
+    for (m, heads, hd, rot) in [(300, 2, 128, 96), (257, 4, 64, 32)]:
+        hidden, eps = 256, 1e-6
+        inner = heads * hd
+        wq, sc, bi = O.quantize(O.normal_f32((3 * inner, hidden), 72, m, std=0.02))
+        bias = O.normal_bf16((3 * inner,), 72, 1, std=0.1)
+        lin = h3.MfLinear(torch.from_numpy(wq.view(np.int32)).cuda(), to_torch_bf16(sc), to_torch_bf16(bi), hidden,
+                          to_torch_bf16(bias))
+        x = O.normal_bf16((m, hidden), 72, 2)
+        qn = O.normal_bf16((hd,), 72, 3, mean=1.0, std=0.02)
+        kn = O.normal_bf16((hd,), 72, 4, mean=1.0, std=0.02)
+        cos = O.normal_bf16((m, rot // 2), 72, 5)
+        sin = O.normal_bf16((m, rot // 2), 72, 6)
+        got = to_np_bf16(lin.qkv_norm_rope(to_torch_bf16(x), heads, hd, to_torch_bf16(qn), to_torch_bf16(kn),
+                                           to_torch_bf16(cos), to_torch_bf16(sin), rot, eps))
+        h3.context().check_device()
+        y = O.qlinear(x, wq, sc, bi, bias=bias)
+        want = y.copy()
+        for part, w in ((0, qn), (1, kn)):
+            blk = np.ascontiguousarray(y[:, part * inner:(part + 1) * inner]).reshape(m, heads, hd)
+            want[:, part * inner:(part + 1) * inner] = O.qk_norm_rope(blk, w, cos, sin, rot, eps).reshape(m, inner)
+        assert_close(f32(got), f32(want), rel=1e-2, cos=0.9999, what=f"qkv_norm_rope m={m} hd={hd}")

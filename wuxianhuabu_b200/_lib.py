@@ -133,6 +133,8 @@ _SIGS = {
     "wx_lora_pack_build": (_i32, [_vp, _i64, _i64, C.POINTER(Lora), _i32, C.POINTER(LoraPack)]),
     "wx_qlinear_lora": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), C.POINTER(LoraPack), _i32, _vp, _vp, _vp,
                                _vp, _i64, _vp]),
+    "wx_qkv_norm_rope": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), C.POINTER(LoraPack), _i32, _i32, _vp, _vp,
+                                _vp, _vp, _i32, _f32, _vp, _i64]),
     "wx_qlinear_noalloc": (_i32, [_vp, _vp, _i64, _i64, C.POINTER(QWeight), _i32, _vp, _vp, _vp, _vp, _i64, _vp]),
     "wx_qlinear_noalloc_check": (_i32, [_vp]),
     "wx_qlinear_noalloc_last_error": (C.c_char_p, []),

@@ -677,6 +677,36 @@ extern "C" int wx_qlinear_lora(wx_ctx* ctx, const void* x, int64_t m, int64_t ld
                                    base + b_wd, base + b_wd + b_t);
 }
 
+namespace wx {
+int launch_qk_norm_rope(wx_ctx* ctx, const void* x, int64_t x_stride, void* out, int64_t out_stride,
+                        int64_t part_off, int nparts, int64_t S, int H, int hd, const void* w0, const void* w1,
+                        const void* cos_t, const void* sin_t, int rot, float eps);
+}
+
+extern "C" int wx_qkv_norm_rope(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                                const wx_lora_pack* lora, int H, int head_dim, const void* q_w, const void* k_w,
+                                const void* cos_t, const void* sin_t, int rot, float eps, void* y, int64_t ldy) {
+  WX_CHECK_ARG(ctx, ctx && x && y && qweight_ok(w) && m >= 0 && lda >= w->k && q_w && k_w);
+  WX_CHECK_ARG(ctx, H > 0 && (head_dim == 128 || head_dim == 64) && w->n == 3 * (int64_t)H * head_dim);
+  WX_CHECK_ARG(ctx, rot >= 0 && rot <= head_dim && rot % 2 == 0 && (rot == 0 || (cos_t && sin_t)));
+  WX_CHECK_ARG(ctx, ldy >= w->n && (!lora || lora_pack_ok(lora, w)));
+  if (m == 0) return WX_OK;
+  auto al = [](size_t b) { return (b + 255) & ~size_t(255); };
+  const size_t b_wd = al((size_t)w->n * w->k * 2), b_t = lora ? al((size_t)m * lora->R * 2) : 0;
+  int st = WX_OK;
+  void* ws = workspace(ctx, b_wd + b_t, &st);
+  if (!ws) return st;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  if (head_dim == 128 && qkv_rope_fusable(w, m, lora != nullptr, true, head_dim, rot, q_w, k_w, cos_t, sin_t))
+    return qkv_rope_with_scratch(ctx, x, m, lda, w, lora, y, ldy, q_w, k_w, cos_t, sin_t, rot, eps, base,
+                                 base + b_wd, nullptr);
+  if ((st = qlinear_lora_with_scratch(ctx, x, m, lda, w, lora, WX_EPI_NONE, nullptr, nullptr, nullptr, y, ldy,
+                                      nullptr, base, base + b_wd, nullptr)))
+    return st;
+  const int64_t inner = (int64_t)H * head_dim;
+  return launch_qk_norm_rope(ctx, y, ldy, y, ldy, inner, 2, m, H, head_dim, q_w, k_w, cos_t, sin_t, rot, eps);
+}
+
 extern "C" int wx_qlinear(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w, int epilogue,
                           const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
                           void* y_raw) {

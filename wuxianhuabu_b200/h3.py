@@ -239,6 +239,25 @@ class MfLinear:
 
     __call__ = forward
 
+    def qkv_norm_rope(self, x: torch.Tensor, heads: int, head_dim: int, q_norm: torch.Tensor,
+                      k_norm: torch.Tensor, cos: Optional[torch.Tensor], sin: Optional[torch.Tensor], rot: int,
+                      eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The q|k|v projection of H3AttnW.forward with its two fusedRmsnormRope calls
+        (H3Transformer.swift:451-475) as one call (wx_qkv_norm_rope): x [m, in] -> [m, 3*heads*head_dim]
+        with q and k normalised and rotated (in the GEMM's epilogue where the geometry allows)."""
+        _need_bf16_cuda(x, q_norm, k_norm, cos, sin)
+        x2 = x.reshape(-1, self.in_dim)
+        if x2.stride(1) != 1:
+            x2 = x2.contiguous()
+        m = x2.shape[0]
+        y = out if out is not None else torch.empty((m, self.out_dim), dtype=torch.bfloat16, device=x.device)
+        qw = self.qweight()
+        pack = self.lora_pack()
+        context(x.device.index).call("wx_qkv_norm_rope", _p(x2), m, x2.stride(0), C.byref(qw),
+                                     C.byref(pack) if pack is not None else None, heads, head_dim, _p(q_norm),
+                                     _p(k_norm), _p(cos), _p(sin), rot, float(eps), _p(y), y.stride(0))
+        return y
+
 
 # ------------------------------------------------------------------- fused row kernels
 class H3FusedKernels:
