@@ -599,6 +599,73 @@ def run_c1(args) -> dict:
                                   sample="the whole block (oracle, C, OpenMP), best of 3, same weights and inputs"))
 
 
+def run_rowops(args) -> dict:
+    """The HBM-bound row kernels standalone at the config-1 / config-4 / config-5 shapes:
+    QK-RMSNorm + RoPE of q and k of a packed q|k|v buffer in place (K3, the separate path;
+    in the step it runs in the q|k|v GEMM's epilogue where the geometry allows), RMSNorm +
+    modulation (K4) and the gated residual (K5, the PAB reuse path; the step fuses it into
+    GEMM epilogues otherwise). Kernel time = the CUDA events libwx records around each launch;
+    a 256 MB buffer is written between launches to flush L2 (outside the events).
+    Bytes: K3 2 x (read + write of S x H x hd bf16) + cos/sin rows; K4 read + write of S x hidden
+    bf16 + the u32 row map; K5 two reads + one write of S x hidden bf16 + the row map."""
+    import ctypes
+    import torch
+    from wuxianhuabu_b200 import h3
+    dev = torch.device("cuda", 0)
+    gen = torch.Generator(device=dev).manual_seed(1234 + 7)
+    peaks, kind = load_peaks()
+    hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
+    ctx = h3.context(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    shapes = [("c1", 4096, 16, 64, 64, 1024), ("c4", 29032, 24, 128, 96, 3072), ("c5", 126512, 24, 128, 96, 3072)]
+    reps = max(1, args.steps)
+    res = []
+    for name, S, H, hd, rot, hidden in shapes:
+        inner = H * hd
+        qkv = torch.randn((S, 3 * inner), device=dev, generator=gen).to(torch.bfloat16)
+        wq = (1 + 0.02 * torch.randn(hd, device=dev, generator=gen)).to(torch.bfloat16)
+        wk = (1 + 0.02 * torch.randn(hd, device=dev, generator=gen)).to(torch.bfloat16)
+        cos = torch.randn((S, rot // 2), device=dev, generator=gen).to(torch.bfloat16)
+        sin = torch.randn((S, rot // 2), device=dev, generator=gen).to(torch.bfloat16)
+        x = torch.randn((S, hidden), device=dev, generator=gen).to(torch.bfloat16)
+        other = torch.randn((S, hidden), device=dev, generator=gen).to(torch.bfloat16)
+        out = torch.empty_like(x)
+        wn = (1 + 0.02 * torch.randn(hidden, device=dev, generator=gen)).to(torch.bfloat16)
+        tabs = [(0.02 * torch.randn((6, hidden), device=dev, generator=gen)).to(torch.bfloat16) for _ in range(3)]
+        rm = torch.from_numpy((np.arange(S) % 6).astype(np.int32)).to(dev)
+        P = h3._p
+        kernels = [
+            ("qk_norm_rope", 6, 2 * (2 * S * inner * 2) + 2 * S * (rot // 2) * 2,
+             lambda: ctx.call("wx_qk_norm_rope_qkv", P(qkv), S, H, hd, P(wq), P(wk), P(cos), P(sin), rot, 1e-6)),
+            ("norm_modscale", 7, 2 * S * hidden * 2 + S * 4,
+             lambda: ctx.call("wx_norm_modscale", P(x), S, hidden, P(wn), P(tabs[0]), P(tabs[1]), P(rm), 1e-6,
+                              P(out))),
+            ("mod_gate", 3, 3 * S * hidden * 2 + S * 4,
+             lambda: ctx.call("wx_mod_gate", P(x), P(other), P(tabs[2]), P(rm), S, hidden, P(out))),
+        ]
+        for kname, kind_idx, nbytes, fn in kernels:
+            for _ in range(max(1, args.warmup)):
+                fn()
+            torch.cuda.synchronize()
+            ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
+            for _ in range(reps):
+                flush.fill_(1)
+                fn()
+            torch.cuda.synchronize()
+            ms = (ctypes.c_double * 10)()
+            cnt = (ctypes.c_int64 * 10)()
+            ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
+            ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
+            t = ms[kind_idx] / max(1, cnt[kind_idx]) / 1e3
+            res.append(dict(config=name, kernel=kname, S=S, ms=t * 1e3, bytes=nbytes, gbs=nbytes / t / 1e9,
+                            frac=nbytes / t / 1e9 / hbm, launches=int(cnt[kind_idx]), sm_mhz=_sm_clock_now(0)))
+        ctx.check_device()
+        del qkv, x, other, out
+    return dict(metric="HBM-bound row kernels (K3 QK-norm+RoPE, K4 norm+modulation, K5 gated residual)",
+                unit="GB/s", hbm_peak=hbm, peak_kind=f"{kind} HBM GB/s (copy)", kernels=res,
+                l2="256 MB written between launches (outside the events)")
+
+
 def _sm_clock_now(index: int = 0):
     """The SM clock (MHz) at this moment, from NVML (None where NVML is unavailable): small
     kernels are latency-bound and follow the clock, which the power cap lowers after heavy work."""
@@ -673,7 +740,8 @@ def run_c2(args) -> dict:
         M0, K0, N0 = (int(v) for v in args.shape.split(","))
         shapes, ms_list = [(K0, N0)], (M0,)
     for (K, N) in shapes:
-        lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02)
+        bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16) if args.bias else None
+        lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02, bias=bias)
         if args.lora > 0:  # one adapter of rank args.lora (the LoRA row: a K extension of the GEMM)
             a = (torch.randn((K, args.lora), device=dev, generator=g) * 0.02).to(torch.bfloat16)
             b = (torch.randn((args.lora, N), device=dev, generator=g) * 0.02).to(torch.bfloat16)
@@ -711,7 +779,7 @@ def run_c2(args) -> dict:
             row = dict(M=M, K=K, N=N, ms=t * 1e3, tflops=fl / t / 1e12, frac=fl / t / 1e12 / pk,
                        gbs=byts / t / 1e9, gbs_frac=byts / t / 1e9 / hbm, ms_per_call=t_call * 1e3,
                        path="fused" if (M <= 512 and N % 128 == 0 and args.lora == 0) else "two-pass",
-                       lora_rank=args.lora, sm_mhz=sm_mhz)
+                       lora_rank=args.lora, bias=bool(args.bias), sm_mhz=sm_mhz)
             if args.qkv_rope and N % 384 == 0:
                 row.update(_qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g))
             res.append(row)
@@ -730,22 +798,26 @@ def main():
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", default="wx", choices=["wx", "reference"])
     ap.add_argument("--config", default="c5",
-                    choices=list(CONFIGS) + ["c1", "c3", "c3full", "c3dense", "c2", "c5attn", "c5attn_dense"])
+                    choices=list(CONFIGS) + ["c1", "c3", "c3full", "c3dense", "c2", "c5attn", "c5attn_dense",
+                                             "rowops"])
     ap.add_argument("--router", default="topk", choices=["topk", "sol"],
                     help="c3 / c3full / c5attn: top-k 25%% over 128-row blocks, or SOL tau 1.3 over 64-row blocks")
     ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
+    ap.add_argument("--bias", action="store_true", help="c2 only: the linears carry a bias (added in the epilogue)")
     ap.add_argument("--qkv-rope", action="store_true",
                     help="c2 only: also time N = 3*heads*128 shapes as q|k|v projections with QK-norm + RoPE, "
                          "fused epilogue against the separate kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
-    if args.config in ("c1", "c3", "c3full", "c3dense", "c2", "c5attn", "c5attn_dense"):
+    if args.config in ("c1", "c3", "c3full", "c3dense", "c2", "c5attn", "c5attn_dense", "rowops"):
         import torch
         torch.cuda.set_device(0)
         if args.config == "c1":
             r = run_c1(args)
+        elif args.config == "rowops":
+            r = run_rowops(args)
         elif args.config == "c2":
             r = run_c2(args)
         elif args.config.startswith("c5attn"):  # the config-5 step's attention call, standalone

@@ -5,8 +5,8 @@ so that every projection runs the same GEMM).
 
 The two paths round at the same points and form the sum of squares in the same order, so whole
 DiT blocks (dense, top-k and SOL attention, ragged last row tile, 2 and 3 heads so that both the
-256- and the 128-column tiles run, with and without a bias on the projection, a PAB slot) must
-come out bit-identical. The oracle comparison of the fused path is in test_gpu_block /
+256- and the 128-column tiles run, head_dim 128 and 64 (the config-1 geometry: 16 x 64, rot 64),
+with and without a bias on the projection, a PAB slot) must come out bit-identical. The oracle comparison of the fused path is in test_gpu_block /
 test_gpu_parity_full (they run the default path)."""
 import os
 import subprocess
@@ -32,13 +32,15 @@ from tests._util import to_np_bf16, to_torch_bf16
 from tests.test_gpu_block import gpu_block, make_block
 from wuxianhuabu_b200 import h3
 outs = {}
-for (S, heads, bias, mode, g) in [(300, 2, False, "dense", 0), (1000, 3, True, "topk", 200),
-                                  (1000, 2, False, "sol", 130), (2048, 2, True, "dense", 0)]:
-    hidden, ffn, rot, eps = 256, 512, 96, 1e-6
-    w, mods, h, cos, sin, rowmap = make_block(50 + S + heads, hidden, heads, ffn, 0, S, rot)
+for (S, heads, hd, bias, mode, g) in [(300, 2, 128, False, "dense", 0), (1000, 3, 128, True, "topk", 200),
+                                      (1000, 2, 128, False, "sol", 130), (2048, 2, 128, True, "dense", 0),
+                                      (4096, 16, 64, True, "dense", 0), (777, 4, 64, False, "dense", 0)]:
+    hidden, ffn, eps = 256, 512, 1e-6
+    rot = 96 if hd == 128 else 64
+    w, mods, h, cos, sin, rowmap = make_block(50 + S + heads, hidden, heads, ffn, 0, S, rot, hd=hd)
     wq, sc, bi, b = w["qkv"]
-    w["qkv"] = (wq, sc, bi, O.normal_bf16((3 * heads * 128,), 9, S, std=0.5) if bias else None)
-    blk = gpu_block(w, hidden, heads, ffn, 0, rot, eps)
+    w["qkv"] = (wq, sc, bi, O.normal_bf16((3 * heads * hd,), 9, S, std=0.5) if bias else None)
+    blk = gpu_block(w, hidden, heads, ffn, 0, rot, eps, hd=hd)
     spec = None
     if mode == "topk":
         spec = h3.H3SolAttnConfig(block=128, topk_ratio=0.25, tail=False).spec(g)
@@ -49,7 +51,7 @@ for (S, heads, bias, mode, g) in [(300, 2, False, "dense", 0), (1000, 3, True, "
     blk.block_forward(0, x, [to_torch_bf16(m) for m in mods], torch.from_numpy(rowmap.view(np.int32)).cuda(),
                       to_torch_bf16(cos), to_torch_bf16(sin), spec, pab_slot=slot, refresh=True)
     h3.context().check_device()
-    key = f"{S}_{heads}_{int(bias)}_{mode}"
+    key = f"{S}_{heads}_{hd}_{int(bias)}_{mode}"
     outs[key + "_h"] = to_np_bf16(x).view(np.uint16)
     outs[key + "_at"] = to_np_bf16(slot).view(np.uint16)
 np.savez(sys.argv[2], **outs)
@@ -77,15 +79,18 @@ def test_fused_qkv_rope_epilogue_is_bit_identical_to_the_separate_kernel():
             assert diff == 0, f"{k}: {diff} of {a[k].size} elements differ"
 
 
-@pytest.mark.parametrize("m,heads,bias,lora", [(700, 3, True, False), (2048, 2, False, False), (1500, 2, True, True)])
-def test_wx_qkv_norm_rope_equals_projection_then_norm_rope(m, heads, bias, lora):
+@pytest.mark.parametrize("m,heads,hd,bias,lora", [(700, 3, 128, True, False), (2048, 2, 128, False, False),
+                                                  (1500, 2, 128, True, True), (1024, 4, 64, True, False),
+                                                  (4096, 16, 64, False, False)])
+def test_wx_qkv_norm_rope_equals_projection_then_norm_rope(m, heads, hd, bias, lora):
     """The ABI call (one GEMM with the norm/RoPE epilogue) against the two calls it replaces:
     the two-pass projection (M > 512; with the LoRA delta as a K extension) and the row kernel
     on q and k, bit for bit."""
     import torch
     from tests._util import to_torch_bf16
     from wuxianhuabu_b200 import h3
-    hidden, hd, rot, eps = 512, 128, 96, 1e-6
+    hidden, eps = 512, 1e-6
+    rot = 96 if hd == 128 else 64
     inner = heads * hd
     wq, sc, bi = O.quantize(O.normal_f32((3 * inner, hidden), 71, m, std=0.02))
     b = to_torch_bf16(O.normal_bf16((3 * inner,), 71, 1, std=0.5)) if bias else None

@@ -29,9 +29,9 @@ struct QkvPeerOut;
 bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
                       const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t);
 int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
-                          const wx_lora_pack* lora, void* y, int64_t ldy, const void* q_norm, const void* k_norm,
-                          const void* cos_t, const void* sin_t, int rot, float eps, void* wd, void* t,
-                          const QkvPeerOut* peers);
+                          const wx_lora_pack* lora, int head_dim, void* y, int64_t ldy, const void* q_norm,
+                          const void* k_norm, const void* cos_t, const void* sin_t, int rot, float eps, void* wd,
+                          void* t, const QkvPeerOut* peers);
 size_t attention_scratch_bytes(int64_t S, int H, int hd, const wx_sparse_spec* spec);
 int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
                            int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os, void* scratch);
@@ -138,8 +138,8 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
     tr.begin(WX_TRACE_QKV);
     if (qkv_rope_fusable(&w->qkv, S, w->lora[0] != nullptr, false, cfg->head_dim, cfg->rot, w->q_norm, w->k_norm,
                          cos_t, sin_t)) {
-      if ((st = qkv_rope_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], qkv, 3 * inner, w->q_norm,
-                                      w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, wd, lt, nullptr)))
+      if ((st = qkv_rope_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], cfg->head_dim, qkv, 3 * inner,
+                                      w->q_norm, w->k_norm, cos_t, sin_t, cfg->rot, cfg->eps, wd, lt, nullptr)))
         return st;
     } else {
       if ((st = qlinear_lora_with_scratch(ctx, m, S, cfg->hidden, &w->qkv, w->lora[0], WX_EPI_NONE, nullptr,

@@ -57,6 +57,7 @@ struct QkRopeEpi {
   int rot;
   float eps;
   int inner;
+  int hd;  // head_dim: 128 or 64
   __nv_bfloat16* base[kMaxPeers];
   int64_t row0;
   int Hl;
@@ -172,29 +173,35 @@ __device__ __forceinline__ void gemm_epilogue32(const GemmParams& p, float (&v)[
   }
 }
 
-// 16-byte chunk c (of 16) of staging row r: XOR-swizzled so that the row-per-thread
-// writes and the row-pair reads of the copy-out are both free of bank conflicts
+// 16-byte chunk c of staging row r (HD / 8 chunks of a head row): XOR-swizzled so that
+// the row-per-thread writes and the multi-row reads of the copy-out are both free of
+// bank conflicts
+template <int HD>
 __device__ __forceinline__ uint4* stage_chunk(uint8_t* buf, int r, int c) {
-  return reinterpret_cast<uint4*>(buf + r * 256 + ((c ^ (r & 15)) << 4));
+  constexpr int NC = HD / 8;
+  return reinterpret_cast<uint4*>(buf + r * (HD * 2) + ((c ^ (r & (NC - 1))) << 4));
 }
 
-// One 128-column head of output row m for the q|k|v projection (one thread per row,
-// v = the fp32 accumulators): the GEMM's bf16 result (+ bias, rounded again); for q and
-// k heads then nv = bf16(x * rstd * w) and the split-half rotation of pairs (j, j + rot/2)
-// of h3_fused_rmsnorm_rope (网络算子-融合-RMSNormRoPE-通用.swift:41-94); v heads pass
-// through. The result goes as bf16 into the thread's staging row `lane`. The sum of
-// squares is formed in the order of qk_norm_rope_vec_kernel (partials over 4 consecutive
-// elements, combined as its xor butterfly combines lanes) and the rotation with the same
-// explicit roundings, so the fused and the separate path give identical bits.
-__device__ __forceinline__ void qk_rope_head(const GemmParams& p, float (&v)[4][32], int64_t m, int64_t n0,
+// One HD-column head (HD = 128 or 64) of output row m for the q|k|v projection (one
+// thread per row, v = the fp32 accumulators): the GEMM's bf16 result (+ bias, rounded
+// again); for q and k heads then nv = bf16(x * rstd * w) and the split-half rotation of
+// pairs (j, j + rot/2) of h3_fused_rmsnorm_rope (网络算子-融合-RMSNormRoPE-通用.swift:41-94);
+// v heads pass through. The result goes as bf16 into the thread's staging row `lane`. The
+// sum of squares is formed in the order of the warp-per-row kernels (qk_norm_rope_vec_kernel,
+// qk_norm_rope_kernel<64>: partials over HD / 32 consecutive elements, combined as their
+// xor butterfly combines lanes) and the rotation with the same explicit roundings, so the
+// fused and the separate path give identical bits.
+template <int HD>
+__device__ __forceinline__ void qk_rope_head(const GemmParams& p, float (&v)[HD / 32][32], int64_t m, int64_t n0,
                                              int part, uint8_t* buf, int lane) {
+  constexpr int NCH = HD / 32, E = HD / 32;
 #pragma unroll
-  for (int c = 0; c < 4; ++c)
+  for (int c = 0; c < NCH; ++c)
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[c][i] = round_bf16(v[c][i]);
   if (p.bias) {
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int c = 0; c < NCH; ++c)
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
         const uint4 bv = __ldg(reinterpret_cast<const uint4*>(p.bias + n0 + c * 32 + i));
@@ -210,20 +217,20 @@ __device__ __forceinline__ void qk_rope_head(const GemmParams& p, float (&v)[4][
     float t[32];
 #pragma unroll
     for (int l = 0; l < 32; ++l) {
-      const int c = l >> 3, i = (l & 7) * 4;
-      float a = __fmaf_rn(v[c][i], v[c][i], 0.f);
-      a = __fmaf_rn(v[c][i + 1], v[c][i + 1], a);
-      a = __fmaf_rn(v[c][i + 2], v[c][i + 2], a);
-      t[l] = __fmaf_rn(v[c][i + 3], v[c][i + 3], a);
+      const int c = (l * E) >> 5, i = (l * E) & 31;
+      float a = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) a = __fmaf_rn(v[c][i + e], v[c][i + e], a);
+      t[l] = a;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
       for (int l = 0; l < o; ++l) t[l] = __fadd_rn(t[l], t[l + o]);
-    const float rstd = rsqrtf(t[0] / 128.f + p.qk.eps);
+    const float rstd = rsqrtf(t[0] / (float)HD + p.qk.eps);
     const __nv_bfloat16* w = part == 0 ? p.qk.w0 : p.qk.w1;
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int c = 0; c < NCH; ++c)
 #pragma unroll
       for (int i = 0; i < 32; i += 8) {
         const uint4 wv = __ldg(reinterpret_cast<const uint4*>(w + c * 32 + i));
@@ -236,10 +243,10 @@ __device__ __forceinline__ void qk_rope_head(const GemmParams& p, float (&v)[4][
       }
   }
 #pragma unroll
-  for (int c = 0; c < 4; ++c)
+  for (int c = 0; c < NCH; ++c)
 #pragma unroll
     for (int i = 0; i < 32; i += 8)
-      *stage_chunk(buf, lane, c * 4 + i / 8) =
+      *stage_chunk<HD>(buf, lane, c * 4 + i / 8) =
           make_uint4(pack_bf16x2(v[c][i], v[c][i + 1]), pack_bf16x2(v[c][i + 2], v[c][i + 3]),
                      pack_bf16x2(v[c][i + 4], v[c][i + 5]), pack_bf16x2(v[c][i + 6], v[c][i + 7]));
   if (part < 2 && p.qk.rot > 0) {
@@ -249,8 +256,8 @@ __device__ __forceinline__ void qk_rope_head(const GemmParams& p, float (&v)[4][
     const __nv_bfloat16* sr = p.qk.sin_t + m * rh;
 #pragma unroll 1
     for (int ch = 0; ch < rc; ++ch) {
-      uint4* pa = stage_chunk(buf, lane, ch);
-      uint4* pb = stage_chunk(buf, lane, ch + rc);
+      uint4* pa = stage_chunk<HD>(buf, lane, ch);
+      uint4* pb = stage_chunk<HD>(buf, lane, ch + rc);
       const uint4 av = *pa, bv = *pb;
       const uint4 cv = __ldg(reinterpret_cast<const uint4*>(cr + ch * 8));
       const uint4 sv = __ldg(reinterpret_cast<const uint4*>(sr + ch * 8));
@@ -272,12 +279,14 @@ __device__ __forceinline__ void qk_rope_head(const GemmParams& p, float (&v)[4][
   }
 }
 
-template <int BN, bool QKR>
+// QKR: 0 = the plain epilogues; 128 / 64 = the q|k|v projection with QK-RMSNorm + RoPE
+// of heads of that many columns
+template <int BN, int QKR>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                         GemmParams p) {
-  using L = GemmSmem<BN, QKR>;
+  using L = GemmSmem<BN, (QKR > 0)>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
@@ -388,9 +397,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) umma_commit(accf_bar(acc));
       }
     }
-  } else if constexpr (QKR) {
+  } else if constexpr (QKR > 0) {
     // epilogue of the q|k|v projection: QK-RMSNorm + RoPE per head, rows staged in
     // shared memory and stored in 512-byte pieces (in place, or into the owners' buffers)
+    constexpr int HD = QKR, RPI = 512 / (HD * 2), NC = HD / 8;  // rows per store instruction
     const int quarter = warp & 3;
     uint8_t* buf = smem + L::kOutOffset + quarter * 32 * 256;
     int local = 0;
@@ -404,16 +414,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int64_t row_base = (int64_t)mb * kGemmBM + quarter * 32;
       const int64_t m = row_base + lane;
 #pragma unroll 1
-      for (int hh = 0; hh < BN / 128; ++hh) {
-        float v[4][32];
+      for (int hh = 0; hh < BN / HD; ++hh) {
+        float v[HD / 32][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-          tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + hh * 128 + c * 32, v[c]);
+        for (int c = 0; c < HD / 32; ++c)
+          tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + hh * HD + c * 32, v[c]);
         tmem_wait_ld();
-        const int64_t n0 = (int64_t)nb * BN + hh * 128;
+        const int64_t n0 = (int64_t)nb * BN + hh * HD;
         const int part = (int)(n0 / p.qk.inner);
-        const int head = (int)((n0 - (int64_t)part * p.qk.inner) >> 7);
-        if (m < p.M) qk_rope_head(p, v, m, n0, part, buf, lane);
+        const int head = (int)((n0 - (int64_t)part * p.qk.inner) / HD);
+        if (m < p.M) qk_rope_head<HD>(p, v, m, n0, part, buf, lane);
         __syncwarp();
         __nv_bfloat16* dst;
         int64_t dst_stride;
@@ -426,14 +436,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int r = 1; r < kMaxPeers; ++r)
             if (owner == r) b = p.qk.base[r];
-          dst_stride = 3 * (int64_t)p.qk.Hl * 128;
-          dst = b + (p.qk.row0 + row_base) * dst_stride + (int64_t)part * p.qk.Hl * 128 +
-                (int64_t)(head - owner * p.qk.Hl) * 128;
+          dst_stride = 3 * (int64_t)p.qk.Hl * HD;
+          dst = b + (p.qk.row0 + row_base) * dst_stride + (int64_t)part * p.qk.Hl * HD +
+                (int64_t)(head - owner * p.qk.Hl) * HD;
         }
 #pragma unroll 4
-        for (int i = 0; i < 16; ++i) {
-          const int r = 2 * i + (lane >> 4), ch = lane & 15;
-          const uint4 val = *stage_chunk(buf, r, ch);
+        for (int i = 0; i < 32 / RPI; ++i) {
+          const int r = RPI * i + lane / NC, ch = lane % NC;
+          const uint4 val = *stage_chunk<HD>(buf, r, ch);
           if (row_base + r < p.M) *reinterpret_cast<uint4*>(dst + r * dst_stride + ch * 8) = val;
         }
         __syncwarp();
@@ -475,15 +485,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }
-  if constexpr (QKR) {
+  if constexpr (QKR > 0) {
     if (p.qk.sig.counter) peer_signal_cta_done(p.qk.sig);  // after every store of this CTA
   }
 }
 
-template <int BN, bool QKR = false>
+template <int BN, int QKR = 0>
 static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
                           const CUtensorMap& tb2, GemmParams& p) {
-  using L = GemmSmem<BN, QKR>;
+  using L = GemmSmem<BN, (QKR > 0)>;
   int st = ensure_smem_attr(ctx, (const void*)gemm_bf16_tc_kernel<BN, QKR>, L::kBytes,
                             QKR ? "gemm_bf16_tc (qk-norm/rope epilogue)" : "gemm_bf16_tc");
   if (st) return st;
@@ -491,7 +501,7 @@ static int launch_gemm_bn(wx_ctx* ctx, const CUtensorMap& ta, const CUtensorMap&
   p.tiles_n = p.N / BN;
   p.num_tiles = p.tiles_m * p.tiles_n;
   const int grid = std::min(p.num_tiles, ctx->num_sms);
-  if (QKR) p.qk.sig.total = grid;  // every CTA of the launch counts once
+  if (QKR > 0) p.qk.sig.total = grid;  // every CTA of the launch counts once
   ProfScope prof(ctx, kProfGemm);
   gemm_bf16_tc_kernel<BN, QKR><<<grid, kGemmThreads, L::kBytes, ctx->stream>>>(ta, tb, ta2, tb2, p);
   return launch_status(ctx, "gemm_bf16_tc");
@@ -539,11 +549,13 @@ int gemm_bf16_ext(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const void
   p.y_raw = static_cast<__nv_bfloat16*>(y_raw);
   p.err = ctx->dev_err;
   if (qk) {
-    if (epi != WX_EPI_NONE || BN < 128 || qk->inner % 128 != 0 || N != 3 * (int64_t)qk->inner)
-      return set_error(ctx, WX_ERR_UNSUPPORTED, "qk-norm/rope epilogue: q|k|v of 128-wide heads, N %% 128 == 0");
+    if (epi != WX_EPI_NONE || BN < 128 || (qk->hd != 128 && qk->hd != 64) || qk->inner % qk->hd != 0 ||
+        N != 3 * (int64_t)qk->inner)
+      return set_error(ctx, WX_ERR_UNSUPPORTED, "qk-norm/rope epilogue: q|k|v of 128- or 64-wide heads, N %% 128 == 0");
     p.qk = *qk;
-    if (BN == 256) return launch_gemm_bn<256, true>(ctx, ta, tb, ta2, tb2, p);
-    return launch_gemm_bn<128, true>(ctx, ta, tb, ta2, tb2, p);
+    if (qk->hd == 64)
+      return BN == 256 ? launch_gemm_bn<256, 64>(ctx, ta, tb, ta2, tb2, p) : launch_gemm_bn<128, 64>(ctx, ta, tb, ta2, tb2, p);
+    return BN == 256 ? launch_gemm_bn<256, 128>(ctx, ta, tb, ta2, tb2, p) : launch_gemm_bn<128, 128>(ctx, ta, tb, ta2, tb2, p);
   }
   if (BN == 256) return launch_gemm_bn<256>(ctx, ta, tb, ta2, tb2, p);
   if (BN == 128) return launch_gemm_bn<128>(ctx, ta, tb, ta2, tb2, p);
@@ -596,8 +608,9 @@ int qlinear_lora_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda
 // exchange (peer = true), which the fused epilogue replaces whatever M is.
 bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
                       const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t) {
-  if (!qkv_rope_fused_enabled() || head_dim != 128 || rot < 0 || rot > 128 || rot % 16 != 0 || !aligned16(q_norm) ||
-      !aligned16(k_norm) || (rot != 0 && (!aligned16(cos_t) || !aligned16(sin_t))))
+  if (!qkv_rope_fused_enabled() || (head_dim != 128 && head_dim != 64) || (peer && head_dim != 128) || rot < 0 ||
+      rot > head_dim || rot % 16 != 0 || !aligned16(q_norm) || !aligned16(k_norm) ||
+      (rot != 0 && (!aligned16(cos_t) || !aligned16(sin_t))) || w->n % (3 * head_dim) != 0 || w->n % 128 != 0)
     return false;
   const bool small_m = !has_lora && fused_eligible(w, m, WX_EPI_NONE) && !force_two_pass();
   return peer || !small_m;
@@ -608,12 +621,13 @@ bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, 
 // head. peers == nullptr: the result goes in place into y (pitch ldy); otherwise into
 // the owners' exchange buffers, and the launch's last CTA raises peers->sig.
 int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
-                          const wx_lora_pack* lora, void* y, int64_t ldy, const void* q_norm, const void* k_norm,
-                          const void* cos_t, const void* sin_t, int rot, float eps, void* wd, void* t,
-                          const QkvPeerOut* peers) {
-  if (w->n % 3 != 0 || (w->n / 3) % 128 != 0 || m <= 0 ||
-      !qkv_rope_fusable(w, m, lora != nullptr, true, 128, rot, q_norm, k_norm, cos_t, sin_t))
-    return set_error(ctx, WX_ERR_UNSUPPORTED, "qkv rope epilogue: n = 3 * heads * 128, rot %% 16 == 0");
+                          const wx_lora_pack* lora, int head_dim, void* y, int64_t ldy, const void* q_norm,
+                          const void* k_norm, const void* cos_t, const void* sin_t, int rot, float eps, void* wd,
+                          void* t, const QkvPeerOut* peers) {
+  if (m <= 0 || !qkv_rope_fusable(w, m, lora != nullptr, true, head_dim, rot, q_norm, k_norm, cos_t, sin_t) ||
+      (peers && head_dim != 128))
+    return set_error(ctx, WX_ERR_UNSUPPORTED,
+                     "qkv rope epilogue: n = 3 * heads * head_dim (128 or 64, 128 with peers), rot %% 16 == 0");
   int st = launch_dequant(ctx, w, wd);
   if (st) return st;
   const int64_t R = lora ? lora->R : 0;
@@ -628,6 +642,7 @@ int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, co
   e.rot = rot;
   e.eps = eps;
   e.inner = (int)(w->n / 3);
+  e.hd = head_dim;
   if (peers) {
     for (int r = 0; r < kMaxPeers; ++r) e.base[r] = static_cast<__nv_bfloat16*>(peers->base[r]);
     e.row0 = peers->row0;
@@ -697,8 +712,8 @@ extern "C" int wx_qkv_norm_rope(wx_ctx* ctx, const void* x, int64_t m, int64_t l
   void* ws = workspace(ctx, b_wd + b_t, &st);
   if (!ws) return st;
   uint8_t* base = static_cast<uint8_t*>(ws);
-  if (head_dim == 128 && qkv_rope_fusable(w, m, lora != nullptr, true, head_dim, rot, q_w, k_w, cos_t, sin_t))
-    return qkv_rope_with_scratch(ctx, x, m, lda, w, lora, y, ldy, q_w, k_w, cos_t, sin_t, rot, eps, base,
+  if (qkv_rope_fusable(w, m, lora != nullptr, true, head_dim, rot, q_w, k_w, cos_t, sin_t))
+    return qkv_rope_with_scratch(ctx, x, m, lda, w, lora, head_dim, y, ldy, q_w, k_w, cos_t, sin_t, rot, eps, base,
                                  base + b_wd, nullptr);
   if ((st = qlinear_lora_with_scratch(ctx, x, m, lda, w, lora, WX_EPI_NONE, nullptr, nullptr, nullptr, y, ldy,
                                       nullptr, base, base + b_wd, nullptr)))
