@@ -606,11 +606,18 @@ int qlinear_lora_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda
 // The fused epilogue runs on the two-pass GEMM; where the small-M kernel would serve the
 // projection (M <= 512, no LoRA) the separate path is kept, except for the peer-memory
 // exchange (peer = true), which the fused epilogue replaces whatever M is.
+// geometry the epilogue takes: heads of 128 or 64 columns, rot/2 a multiple of 8, N % 128 == 0
+static bool qkv_rope_geometry_ok(const wx_qweight* w, int head_dim, int rot, const void* q_norm, const void* k_norm,
+                                 const void* cos_t, const void* sin_t) {
+  return (head_dim == 128 || head_dim == 64) && rot >= 0 && rot <= head_dim && rot % 16 == 0 && aligned16(q_norm) &&
+         aligned16(k_norm) && (rot == 0 || (aligned16(cos_t) && aligned16(sin_t))) &&
+         w->n % (3 * head_dim) == 0 && w->n % 128 == 0;
+}
+
 bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
                       const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t) {
-  if (!qkv_rope_fused_enabled() || (head_dim != 128 && head_dim != 64) || (peer && head_dim != 128) || rot < 0 ||
-      rot > head_dim || rot % 16 != 0 || !aligned16(q_norm) || !aligned16(k_norm) ||
-      (rot != 0 && (!aligned16(cos_t) || !aligned16(sin_t))) || w->n % (3 * head_dim) != 0 || w->n % 128 != 0)
+  if (!qkv_rope_fused_enabled() || (peer && head_dim != 128) ||
+      !qkv_rope_geometry_ok(w, head_dim, rot, q_norm, k_norm, cos_t, sin_t))
     return false;
   const bool small_m = !has_lora && fused_eligible(w, m, WX_EPI_NONE) && !force_two_pass();
   return peer || !small_m;
@@ -624,8 +631,7 @@ int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, co
                           const wx_lora_pack* lora, int head_dim, void* y, int64_t ldy, const void* q_norm,
                           const void* k_norm, const void* cos_t, const void* sin_t, int rot, float eps, void* wd,
                           void* t, const QkvPeerOut* peers) {
-  if (m <= 0 || !qkv_rope_fusable(w, m, lora != nullptr, true, head_dim, rot, q_norm, k_norm, cos_t, sin_t) ||
-      (peers && head_dim != 128))
+  if (m <= 0 || !qkv_rope_geometry_ok(w, head_dim, rot, q_norm, k_norm, cos_t, sin_t) || (peers && head_dim != 128))
     return set_error(ctx, WX_ERR_UNSUPPORTED,
                      "qkv rope epilogue: n = 3 * heads * head_dim (128 or 64, 128 with peers), rot %% 16 == 0");
   int st = launch_dequant(ctx, w, wd);
@@ -712,7 +718,7 @@ extern "C" int wx_qkv_norm_rope(wx_ctx* ctx, const void* x, int64_t m, int64_t l
   void* ws = workspace(ctx, b_wd + b_t, &st);
   if (!ws) return st;
   uint8_t* base = static_cast<uint8_t*>(ws);
-  if (qkv_rope_fusable(w, m, lora != nullptr, true, head_dim, rot, q_w, k_w, cos_t, sin_t))
+  if (qkv_rope_fused_enabled() && qkv_rope_geometry_ok(w, head_dim, rot, q_w, k_w, cos_t, sin_t))
     return qkv_rope_with_scratch(ctx, x, m, lda, w, lora, head_dim, y, ldy, q_w, k_w, cos_t, sin_t, rot, eps, base,
                                  base + b_wd, nullptr);
   if ((st = qlinear_lora_with_scratch(ctx, x, m, lda, w, lora, WX_EPI_NONE, nullptr, nullptr, nullptr, y, ldy,
