@@ -25,13 +25,6 @@ int qlinear_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, con
                          const void* gate, const void* resid, const uint32_t* rowmap, void* y, int64_t ldy,
                          void* y_raw, void* wd, void* swiglu_tmp);
 bool qweight_ok(const wx_qweight* w);
-struct QkvPeerOut;
-bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
-                      const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t);
-int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
-                          const wx_lora_pack* lora, int head_dim, void* y, int64_t ldy, const void* q_norm,
-                          const void* k_norm, const void* cos_t, const void* sin_t, int rot, float eps, void* wd,
-                          void* t, const QkvPeerOut* peers);
 size_t attention_scratch_bytes(int64_t S, int H, int hd, const wx_sparse_spec* spec);
 int attention_with_scratch(wx_ctx* ctx, const void* q, const void* k, const void* v, int64_t rs, int64_t S, int H,
                            int hd, const wx_sparse_spec* spec, float scale, void* out, int64_t os, void* scratch);

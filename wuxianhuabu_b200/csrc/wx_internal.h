@@ -154,6 +154,20 @@ int qlinear_lora_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda
                               void* swiglu_tmp);
 bool lora_pack_ok(const wx_lora_pack* l, const wx_qweight* w);
 
+// The q|k|v projection with QK-RMSNorm + RoPE in its GEMM epilogue (wx_gemm.cu).
+// qkv_rope_fusable: whether a block takes that path (the geometry the epilogue
+// supports; not where the small-M kernel serves the projection, unless `peer`: the
+// sequence-parallel exchange, head_dim 128). qkv_rope_with_scratch: dequant into `wd`,
+// the LoRA product into `t`, then the GEMM; peers == nullptr writes y in place,
+// otherwise the owners' exchange buffers (QkvPeerOut, wx_ptx.cuh) and their signal.
+struct QkvPeerOut;
+bool qkv_rope_fusable(const wx_qweight* w, int64_t m, bool has_lora, bool peer, int head_dim, int rot,
+                      const void* q_norm, const void* k_norm, const void* cos_t, const void* sin_t);
+int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, const wx_qweight* w,
+                          const wx_lora_pack* lora, int head_dim, void* y, int64_t ldy, const void* q_norm,
+                          const void* k_norm, const void* cos_t, const void* sin_t, int rot, float eps, void* wd,
+                          void* t, const QkvPeerOut* peers);
+
 // Attention output delivered straight into other ranks' memory (sequence
 // parallelism): query row s goes to rank s / rows at out_peer[r] + (s % rows) *
 // out_stride + col + head*128, and the last CTA stores `epoch` into flags[r][rank]
