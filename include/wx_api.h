@@ -157,6 +157,17 @@ size_t wx_ctx_workspace_bytes(wx_ctx* ctx);
 /* number of kernels this context has launched so far */
 int64_t wx_ctx_launch_count(wx_ctx* ctx);
 int wx_version(void);
+
+/* Device memory for hosts that do not link the CUDA runtime themselves (the Swift
+ * wrapper; MLXArray's role in the reference): buffers on the context's device, 256-byte
+ * aligned, and host <-> device copies ordered on the context stream (host memory pinned
+ * or pageable; a copy from pageable memory returns once the source may be reused).
+ * wx_ctx_synchronize waits for everything queued on the context stream. */
+int wx_alloc(wx_ctx* ctx, size_t bytes, void** out);
+int wx_free(wx_ctx* ctx, void* p);
+int wx_upload(wx_ctx* ctx, void* dst, const void* src_host, size_t bytes);
+int wx_download(wx_ctx* ctx, void* dst_host, const void* src, size_t bytes);
+int wx_ctx_synchronize(wx_ctx* ctx);
 /* Device timing by kernel class (0 qGEMM, 1 flash attention, 2 routing + list
  * build, 3 other row kernels (gated residual, RMSNorm, conversions), 4 weight
  * dequant, 5 other (NCCL all-to-alls, pack/unpack), 6 QK-RMSNorm + RoPE,

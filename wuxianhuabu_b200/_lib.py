@@ -121,6 +121,11 @@ _SIGS = {
     "wx_ctx_check_device": (_i32, [_vp]),
     "wx_ctx_workspace_bytes": (C.c_size_t, [_vp]),
     "wx_ctx_launch_count": (_i64, [_vp]),
+    "wx_alloc": (_i32, [_vp, C.c_size_t, C.POINTER(_vp)]),
+    "wx_free": (_i32, [_vp, _vp]),
+    "wx_upload": (_i32, [_vp, _vp, _vp, C.c_size_t]),
+    "wx_download": (_i32, [_vp, _vp, _vp, C.c_size_t]),
+    "wx_ctx_synchronize": (_i32, [_vp]),
     "wx_ctx_profile_enable": (_i32, [_vp, _i32]),
     "wx_ctx_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "wx_ctx_trace_enable": (_i32, [_vp, _i32]),

@@ -323,6 +323,49 @@ int wx_ctx_set_stream(wx_ctx* ctx, void* stream) {
 
 const char* wx_last_error(wx_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
 
+int wx_alloc(wx_ctx* ctx, size_t bytes, void** out) {
+  WX_CHECK_ARG(ctx, ctx && out);
+  *out = nullptr;
+  if (bytes == 0) return WX_OK;
+  WX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  void* p = nullptr;
+  const cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess)
+    return set_error(ctx, WX_ERR_NOMEM, "wx_alloc of %zu bytes on device %d: %s", bytes, ctx->device,
+                     cudaGetErrorString(e));
+  *out = p;
+  return WX_OK;
+}
+
+int wx_free(wx_ctx* ctx, void* p) {
+  WX_CHECK_ARG(ctx, ctx);
+  if (!p) return WX_OK;
+  WX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  WX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));  // no queued work may still use it
+  WX_CUDA_TRY(ctx, cudaFree(p));
+  return WX_OK;
+}
+
+int wx_upload(wx_ctx* ctx, void* dst, const void* src_host, size_t bytes) {
+  WX_CHECK_ARG(ctx, ctx && (bytes == 0 || (dst && src_host)));
+  if (bytes == 0) return WX_OK;
+  WX_CUDA_TRY(ctx, cudaMemcpyAsync(dst, src_host, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  return WX_OK;
+}
+
+int wx_download(wx_ctx* ctx, void* dst_host, const void* src, size_t bytes) {
+  WX_CHECK_ARG(ctx, ctx && (bytes == 0 || (dst_host && src)));
+  if (bytes == 0) return WX_OK;
+  WX_CUDA_TRY(ctx, cudaMemcpyAsync(dst_host, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  return WX_OK;
+}
+
+int wx_ctx_synchronize(wx_ctx* ctx) {
+  if (!ctx) return WX_ERR_INVALID;
+  WX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  return WX_OK;
+}
+
 size_t wx_ctx_workspace_bytes(wx_ctx* ctx) { return ctx ? ctx->ws_bytes : 0; }
 
 int64_t wx_ctx_launch_count(wx_ctx* ctx) { return ctx ? ctx->launches : -1; }
