@@ -24,6 +24,17 @@ def test_every_declared_symbol_is_exported():
     assert not missing, missing
 
 
+def test_checked_build_exports_the_same_symbols():
+    """The bounds-checked build (libwx_checked.so, -DWX_BOUNDS_CHECK=1) is the same ABI."""
+    import pytest
+    path = _lib.LIB_PATH.parent / "libwx_checked.so"
+    if not path.exists():
+        pytest.skip("libwx_checked.so not built")
+    lib = C.CDLL(str(path))
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
 def test_binding_covers_header():
     assert set(declared_symbols()) == set(_lib.exported_symbols())
 

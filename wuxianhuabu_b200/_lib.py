@@ -11,7 +11,8 @@ import os
 from pathlib import Path
 
 _PKG = Path(__file__).resolve().parent
-LIB_PATH = _PKG / "libwx.so"
+# WX_LIB_VARIANT=checked loads the bounds-checked build of the same sources
+LIB_PATH = _PKG / ("libwx_checked.so" if os.environ.get("WX_LIB_VARIANT") == "checked" else "libwx.so")
 
 WX_OK = 0
 WX_ERR_INVALID = -1

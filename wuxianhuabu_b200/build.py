@@ -2,6 +2,9 @@
 
 * ``wuxianhuabu_b200/libwx.so`` — the CUDA product (sm_100a kernels + C ABI of
   ``include/wx_api.h``), compiled with nvcc for ``compute_100a``/``sm_100a``.
+* ``wuxianhuabu_b200/libwx_checked.so`` — the same sources with ``-DWX_BOUNDS_CHECK=1``:
+  the guarded global accesses test their indices and record an error instead of
+  touching memory outside their buffers (loaded when ``WX_LIB_VARIANT=checked``).
 * ``oracle/_build/libwxoracle.so`` — the CPU restatement used only as the
   parity checker by the tests and the CPU baseline of ``bench.py``.
 
@@ -22,6 +25,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libwx.so"
+BUILD_CHECKED = PKG / "_build_checked"
+LIB_CHECKED = PKG / "libwx_checked.so"
 ORACLE_DIR = ROOT / "oracle"
 ORACLE_LIB = ORACLE_DIR / "_build" / "libwxoracle.so"
 
@@ -51,16 +56,17 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build_cuda(force: bool = False, verbose_ptxas: bool = False) -> Path:
-    BUILD.mkdir(exist_ok=True)
+def build_cuda(force: bool = False, verbose_ptxas: bool = False, checked: bool = False) -> Path:
+    build_dir, lib = (BUILD_CHECKED, LIB_CHECKED) if checked else (BUILD, LIB)
+    build_dir.mkdir(exist_ok=True)
     headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [ROOT / "include" / "wx_api.h"]
     objs = []
     jobs = []
     for src in _sources():
-        obj = BUILD / (src.stem + ".o")
+        obj = build_dir / (src.stem + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + headers):
-            flags = NVCC_FLAGS + (["-Xptxas", "-v"] if verbose_ptxas else [])
+            flags = NVCC_FLAGS + (["-Xptxas", "-v"] if verbose_ptxas else []) + (["-DWX_BOUNDS_CHECK=1"] if checked else [])
             jobs.append([NVCC] + flags + ["-c", str(src), "-o", str(obj)])
     if jobs:
         with cf.ThreadPoolExecutor(max_workers=min(8, len(jobs))) as ex:
@@ -68,9 +74,9 @@ def build_cuda(force: bool = False, verbose_ptxas: bool = False) -> Path:
         if verbose_ptxas:
             for o in outs:
                 sys.stdout.write(o)
-    if force or jobs or _stale(LIB, objs):
-        _run([NVCC] + ARCH + ["-shared", "-o", str(LIB)] + [str(o) for o in objs])
-    return LIB
+    if force or jobs or _stale(lib, objs):
+        _run([NVCC] + ARCH + ["-shared", "-o", str(lib)] + [str(o) for o in objs])
+    return lib
 
 
 def build_oracle(force: bool = False) -> Path:
@@ -86,8 +92,9 @@ def build_oracle(force: bool = False) -> Path:
 def build_all(force: bool = False, verbose_ptxas: bool = False) -> None:
     build_oracle(force)
     build_cuda(force, verbose_ptxas)
+    build_cuda(force, False, checked=True)
 
 
 if __name__ == "__main__":
     build_all(force="--force" in sys.argv, verbose_ptxas="-v" in sys.argv)
-    print("built", LIB, ORACLE_LIB)
+    print("built", LIB, LIB_CHECKED, ORACLE_LIB)

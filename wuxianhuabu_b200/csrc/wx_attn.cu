@@ -718,8 +718,8 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   float* tC = reinterpret_cast<float*>(base + c.take(hnb * 4));
   int* counts = reinterpret_cast<int*>(base + c.take((size_t)a.H * a.nvt * 4));
   int* offsets = reinterpret_cast<int*>(base + c.take(((size_t)a.H * a.nvt + 1) * 4));
-  int4* entries = reinterpret_cast<int4*>(
-      base + c.take((size_t)a.H * a.nvt * (size_t)((a.nb + a.qpb - 1) / a.qpb + 1) * 16));
+  const size_t n_entries = (size_t)a.H * a.nvt * (size_t)((a.nb + a.qpb - 1) / a.qpb + 1);
+  int4* entries = reinterpret_cast<int4*>(base + c.take(n_entries * 16));
   WorkItem* items =
       reinterpret_cast<WorkItem*>(base + c.take(((size_t)a.H * (a.nst + a.nvt) + 1) * sizeof(WorkItem)));
   const bool tail = !a.dense && spec->tail && cm && vsum && lens;
@@ -784,6 +784,9 @@ static int run_flash(wx_ctx* ctx, const void* q, const void* k, const void* v, i
   p.out = static_cast<__nv_bfloat16*>(out);
   p.out_stride = os;
   p.err = ctx->dev_err;
+  p.S = a.S;
+  p.n_entries = (int64_t)n_entries;
+  p.P = po ? po->P : 0;
   if (po) {
     static_assert(kSpMaxPeers == kMaxPeers, "peer table sizes");
     if (!attn_peer_path_ok() || po->P < 1 || po->P > kMaxPeers || po->rows <= 0)

@@ -30,7 +30,20 @@ struct AttnParams {
   int64_t peer_rows;
   int peer_col;
   PeerSignal sig;
+  // extents the bounds-checked build tests against: query rows of the sequence, list
+  // entries, ranks receiving rows (0 = local output)
+  int64_t S;
+  int64_t n_entries;
+  int P;
 };
+
+// (bounds-checked build) output row `row` has a destination
+__device__ __forceinline__ bool attn_row_ok(const AttnParams& p, int64_t row) {
+  if (row < 0 || row >= p.S) return false;
+  if (p.out_peer[0] == nullptr) return true;
+  const int64_t owner = row / p.peer_rows;
+  return owner < p.P && owner < kMaxPeers && p.out_peer[owner] != nullptr;
+}
 
 // destination of output row `row` (query row of the sequence) of head `head`
 template <int HD>
@@ -58,13 +71,15 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 }
 
 // key tile j of a work item: two 64-row halves (start row, valid length | q-half mask << 8)
-__device__ __forceinline__ int4 kv_entry(const WorkItem& it, const int4* entries, int j) {
+__device__ __forceinline__ int4 kv_entry(const WorkItem& it, const AttnParams& p, int j) {
   if (j < it.n_implicit) {
     const int s0 = j * 128;
     return make_int4(s0, s0 + 64, max(0, min(64, it.implicit_end - s0)) | (3 << 8),
                      max(0, min(64, it.implicit_end - s0 - 64)) | (3 << 8));
   }
-  return __ldg(entries + it.list_begin + (j - it.n_implicit));
+  const int64_t idx = (int64_t)it.list_begin + (j - it.n_implicit);
+  if (!WX_IN_BOUNDS(p.err, idx >= 0 && idx < p.n_entries)) return make_int4(0, 0, 0, 0);  // (empty halves)
+  return __ldg(p.entries + idx);
 }
 
 __device__ __forceinline__ int item_tiles(const WorkItem& it) { return it.n_implicit + it.list_len; }

@@ -76,10 +76,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       for (int ch = 0; ch < 2; ++ch)
         for (int rh = 0; rh < 2; ++rh)
           tma_load_2d(sQ + ch * kChunkBytes + rh * kHalfBytes, &tmQ, q_full, hcol + ch * 64, it.q_start + rh * 64);
-      int4 e = kv_entry(it, p.entries, 0);
+      int4 e = kv_entry(it, p, 0);
       for (int j = 0; j < n_kv; ++j) {
         const int4 cur = e;
-        if (j + 1 < n_kv) e = kv_entry(it, p.entries, j + 1);
+        if (j + 1 < n_kv) e = kv_entry(it, p, j + 1);
         if (!mbar_wait(k_empty, (j & 1) ^ 1u, p.err, kDevTimeoutEmpty, abort_flag)) break;
         mbar_arrive_expect_tx(k_full, kTileBytes);
         for (int ch = 0; ch < 2; ++ch) {
@@ -129,10 +129,10 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    int4 e = n_kv > 0 ? kv_entry(it, p.entries, 0) : make_int4(0, 0, 0, 0);
+    int4 e = n_kv > 0 ? kv_entry(it, p, 0) : make_int4(0, 0, 0, 0);
     for (int j = 0; j < n_kv && ok; ++j) {
       const int4 cur = e;
-      if (j + 1 < n_kv) e = kv_entry(it, p.entries, j + 1);
+      if (j + 1 < n_kv) e = kv_entry(it, p, j + 1);
       if (!mbar_wait(s_full, j & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
         ok = false;
         break;
@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       }
     }
     const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-    const bool row_ok = ok && r < it.q_rows;
+    const bool row_ok = ok && r < it.q_rows && WX_IN_BOUNDS(p.err, attn_row_ok(p, (int64_t)it.q_start + r));
     __nv_bfloat16* orow = p.out + (int64_t)(it.q_start + r) * p.out_stride + hcol;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {

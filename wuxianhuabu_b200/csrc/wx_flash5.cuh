@@ -158,7 +158,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
           if (!mbar_wait(bar((is_k ? kB5KEmpty : kB5VEmpty) + s), par, p.err, kDevTimeoutEmpty, abort_flag))
             return false;
           tile_load(is_k ? &tmK : &tmV, is_k ? sK(s) : sV(s), bar((is_k ? kB5KFull : kB5VFull) + s), hcol,
-                    kv_entry(itA, p.entries, j));
+                    kv_entry(itA, p, j));
           if (is_k) ++nk; else ++nv;
           return true;
         };
@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
               ok = false;
               break;
             }
-            tile_load(&tmK, sK(2 * X), bar(kB5KFull + X), w.head * HD, kv_entry(w, p.entries, t));
+            tile_load(&tmK, sK(2 * X), bar(kB5KFull + X), w.head * HD, kv_entry(w, p, t));
             (X == 0 ? nk : nk_b) = (uint32_t)t + 1;
           }
         }
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kA5Threads, 1)
             ok = false;
             break;
           }
-          const int4 e = kv_entry(w, p.entries, t);
+          const int4 e = kv_entry(w, p, t);
           const uint32_t full = bar(kB5VFull + X), dst = sV(2 * X);
           mbar_arrive_expect_tx(full, kTile);
           for (int ch = 0; ch < G::kChunks; ++ch) {
@@ -346,10 +346,10 @@ __global__ void __launch_bounds__(kA5Threads, 1)
     float m = -INFINITY;
     float l = 0.f;
     bool ok = true;
-    int4 e = nX > 0 ? kv_entry(it, p.entries, 0) : make_int4(0, 0, 0, 0);
+    int4 e = nX > 0 ? kv_entry(it, p, 0) : make_int4(0, 0, 0, 0);
     for (int t = 0; t < nX; ++t) {
       const int4 cur = e;
-      if (t + 1 < nX) e = kv_entry(it, p.entries, t + 1);
+      if (t + 1 < nX) e = kv_entry(it, p, t + 1);
       if (!mbar_wait(bar(kB5SFull + X), (uint32_t)t & 1, p.err, kDevTimeoutSoftmax, abort_flag)) {
         ok = false;
         break;
@@ -501,7 +501,8 @@ __global__ void __launch_bounds__(kA5Threads, 1)
       }
     }
     const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-    const bool row_ok = ok && present && r < it.q_rows;
+    const bool row_ok = ok && present && r < it.q_rows &&
+                        WX_IN_BOUNDS(p.err, attn_row_ok(p, (int64_t)it.q_start + r));
     __nv_bfloat16* orow = attn_out_row<HD>(p, (int64_t)(it.q_start + r), it.head);
 #pragma unroll 1
     for (int c = 0; c < HD / 32 && present; ++c) {

@@ -60,6 +60,7 @@ struct QkRopeEpi {
   int hd;  // head_dim: 128 or 64
   __nv_bfloat16* base[kMaxPeers];
   int64_t row0;
+  int64_t rows_total;  // rows of each destination buffer (peer mode)
   int Hl;
   PeerSignal sig;
 };
@@ -122,6 +123,7 @@ __device__ __forceinline__ float gelu_tanh_f(float x) {
 // nothing; bf16 stores (and the raw pre-gate values when y_raw is set).
 __device__ __forceinline__ void gemm_epilogue32(const GemmParams& p, float (&v)[32], int64_t m, int64_t mr,
                                                 int64_t n0) {
+  if (!WX_IN_BOUNDS(p.err, m >= 0 && m < p.M && n0 >= 0 && n0 + 32 <= p.N)) return;
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = round_bf16(v[i]);
   if (p.bias) {
@@ -427,11 +429,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
         __nv_bfloat16* dst;
         int64_t dst_stride;
+        bool dst_ok = true;  // (bounds-checked build) the destination rows and owner exist
         if (p.qk.base[0] == nullptr) {
           dst = p.y + row_base * p.ldy + n0;
           dst_stride = p.ldy;
+          dst_ok = WX_IN_BOUNDS(p.err, n0 + HD <= p.N);
         } else {
           const int owner = head / p.qk.Hl;
+          dst_ok = WX_IN_BOUNDS(p.err, owner < kMaxPeers && p.qk.base[owner < kMaxPeers ? owner : 0] != nullptr);
           __nv_bfloat16* b = p.qk.base[0];
 #pragma unroll
           for (int r = 1; r < kMaxPeers; ++r)
@@ -444,7 +449,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int i = 0; i < 32 / RPI; ++i) {
           const int r = RPI * i + lane / NC, ch = lane % NC;
           const uint4 val = *stage_chunk<HD>(buf, r, ch);
-          if (row_base + r < p.M) *reinterpret_cast<uint4*>(dst + r * dst_stride + ch * 8) = val;
+          if (row_base + r < p.M && dst_ok &&
+              WX_IN_BOUNDS(p.err, p.qk.base[0] == nullptr || p.qk.row0 + row_base + r < p.qk.rows_total))
+            *reinterpret_cast<uint4*>(dst + r * dst_stride + ch * 8) = val;
         }
         __syncwarp();
       }
@@ -652,6 +659,7 @@ int qkv_rope_with_scratch(wx_ctx* ctx, const void* x, int64_t m, int64_t lda, co
   if (peers) {
     for (int r = 0; r < kMaxPeers; ++r) e.base[r] = static_cast<__nv_bfloat16*>(peers->base[r]);
     e.row0 = peers->row0;
+    e.rows_total = peers->rows_total;
     e.Hl = peers->Hl;
     e.sig = peers->sig;
   }

@@ -291,6 +291,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     for (int c = c_lo + cg; c < c_hi; c += 2) {
       const int64_t m = m0 + c;
       if (m >= p.M) break;
+      if (!WX_IN_BOUNDS(p.err, n < p.N)) break;
       const uint32_t off = (uint32_t)c * kQRows * 4;
       float acc = ld_shared_cluster_f32(peer[0] + off);
 #pragma unroll

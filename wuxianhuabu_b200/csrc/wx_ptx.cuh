@@ -22,7 +22,23 @@ enum DevErr : int {
   kDevTimeoutOther = 5,
   kDevBadArgs = 6,
   kDevTimeoutPeer = 7,  // another rank's signal did not arrive (sequence parallelism)
+  kDevBounds = 8,       // (bounds-checked build) a guarded global access fell outside its buffer
 };
+
+// Bounds-checked build (-DWX_BOUNDS_CHECK=1; build.py --checked makes libwx_checked.so): each
+// guarded global access tests its index against the extent of its buffer first; one outside
+// records kDevBounds in the error word and the access is skipped. In the normal build the
+// guard is `true` and its condition is not evaluated. Guarded: the GEMM epilogues' stores
+// (plain, q|k|v norm/RoPE with its peer rows, small-M), the attention output rows (local and
+// peer) and the reads of the kept-block lists.
+#ifndef WX_BOUNDS_CHECK
+#define WX_BOUNDS_CHECK 0
+#endif
+#if WX_BOUNDS_CHECK
+#define WX_IN_BOUNDS(err, cond) ((cond) ? true : (::wx::set_dev_error((err), ::wx::kDevBounds), false))
+#else
+#define WX_IN_BOUNDS(err, cond) true
+#endif
 
 static constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
@@ -323,6 +339,7 @@ struct PeerSignal {
 struct QkvPeerOut {
   void* base[kMaxPeers];
   int64_t row0;
+  int64_t rows_total;  // rows of each destination buffer (the whole sequence)
   int Hl;
   PeerSignal sig;
 };

@@ -550,6 +550,7 @@ int wx_dit_block_forward_sp(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bloc
         QkvPeerOut po1{};
         for (int r = 0; r < P; ++r) po1.base[r] = qkv_dst[r];
         po1.row0 = (int64_t)rank * rows;
+        po1.rows_total = S;
         po1.Hl = Hl;
         po1.sig = sig1;
         if ((st = qkv_rope_with_scratch(ctx, m, rows, cfg->hidden, &w->qkv, w->lora[0], hd, qkv, 3 * inner,
