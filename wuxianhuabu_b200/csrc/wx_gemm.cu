@@ -44,7 +44,7 @@ constexpr int kGemmStages = 4;
 constexpr int kGemmThreads = 192;
 constexpr int kGroupM = 16;
 
-// q|k|v projection epilogue with QK-RMSNorm + RoPE fused (gemm_bf16_tc_kernel<BN, true>):
+// q|k|v projection epilogue with QK-RMSNorm + RoPE fused (gemm_bf16_tc_kernel<BN, HD>):
 // columns [0, inner) are q heads, [inner, 2 inner) k heads, [2 inner, 3 inner) v heads,
 // head_dim 128. base[0] == nullptr: the result goes in place into y; otherwise head h of
 // row m goes to the exchange buffer of rank h / Hl (layout [S][3][Hl][128], row row0 + m)
