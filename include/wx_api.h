@@ -162,7 +162,8 @@ int wx_version(void);
  * wrapper; MLXArray's role in the reference): buffers on the context's device, 256-byte
  * aligned, and host <-> device copies ordered on the context stream (host memory pinned
  * or pageable; a copy from pageable memory returns once the source may be reused).
- * wx_ctx_synchronize waits for everything queued on the context stream. */
+ * The caller's current CUDA device is left as it was. wx_ctx_synchronize waits for
+ * everything queued on the context stream. */
 int wx_alloc(wx_ctx* ctx, size_t bytes, void** out);
 int wx_free(wx_ctx* ctx, void* p);
 int wx_upload(wx_ctx* ctx, void* dst, const void* src_host, size_t bytes);

@@ -323,27 +323,40 @@ int wx_ctx_set_stream(wx_ctx* ctx, void* stream) {
 
 const char* wx_last_error(wx_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
 
+// runs `fn` with the context's device current, then restores the caller's current device
+template <class F>
+static int on_ctx_device(wx_ctx* ctx, F fn) {
+  int prev = 0;
+  WX_CUDA_TRY(ctx, cudaGetDevice(&prev));
+  if (prev != ctx->device) WX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  const int st = fn();
+  if (prev != ctx->device) cudaSetDevice(prev);
+  return st;
+}
+
 int wx_alloc(wx_ctx* ctx, size_t bytes, void** out) {
   WX_CHECK_ARG(ctx, ctx && out);
   *out = nullptr;
   if (bytes == 0) return WX_OK;
-  WX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-  void* p = nullptr;
-  const cudaError_t e = cudaMalloc(&p, bytes);
-  if (e != cudaSuccess)
-    return set_error(ctx, WX_ERR_NOMEM, "wx_alloc of %zu bytes on device %d: %s", bytes, ctx->device,
-                     cudaGetErrorString(e));
-  *out = p;
-  return WX_OK;
+  return on_ctx_device(ctx, [&]() -> int {
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess)
+      return set_error(ctx, WX_ERR_NOMEM, "wx_alloc of %zu bytes on device %d: %s", bytes, ctx->device,
+                       cudaGetErrorString(e));
+    *out = p;
+    return WX_OK;
+  });
 }
 
 int wx_free(wx_ctx* ctx, void* p) {
   WX_CHECK_ARG(ctx, ctx);
   if (!p) return WX_OK;
-  WX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-  WX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));  // no queued work may still use it
-  WX_CUDA_TRY(ctx, cudaFree(p));
-  return WX_OK;
+  return on_ctx_device(ctx, [&]() -> int {
+    WX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));  // no queued work may still use it
+    WX_CUDA_TRY(ctx, cudaFree(p));
+    return WX_OK;
+  });
 }
 
 int wx_upload(wx_ctx* ctx, void* dst, const void* src_host, size_t bytes) {
