@@ -264,6 +264,17 @@ __global__ void euler_kernel(float* __restrict__ x, const float* __restrict__ v,
     x[i] = x[i] + (-v[i]) * dsigma;
 }
 
+// runs `fn` with the context's device current, then restores the caller's current device
+template <class F>
+static int on_ctx_device(wx_ctx* ctx, F fn) {
+  int prev = 0;
+  WX_CUDA_TRY(ctx, cudaGetDevice(&prev));
+  if (prev != ctx->device) WX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  const int st = fn();
+  if (prev != ctx->device) cudaSetDevice(prev);
+  return st;
+}
+
 }  // namespace wx
 
 using namespace wx;
@@ -322,17 +333,6 @@ int wx_ctx_set_stream(wx_ctx* ctx, void* stream) {
 }
 
 const char* wx_last_error(wx_ctx* ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
-
-// runs `fn` with the context's device current, then restores the caller's current device
-template <class F>
-static int on_ctx_device(wx_ctx* ctx, F fn) {
-  int prev = 0;
-  WX_CUDA_TRY(ctx, cudaGetDevice(&prev));
-  if (prev != ctx->device) WX_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
-  const int st = fn();
-  if (prev != ctx->device) cudaSetDevice(prev);
-  return st;
-}
 
 int wx_alloc(wx_ctx* ctx, size_t bytes, void** out) {
   WX_CHECK_ARG(ctx, ctx && out);
