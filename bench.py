@@ -480,7 +480,10 @@ def run_c1(args) -> dict:
     pairs, dense attention, 6-bit group-64 weights ~ N(0, 0.02), activations ~ N(0, 1)) on one
     GPU, beside the oracle's whole block on every host thread (timed whole, not extrapolated).
     The same quantized weights and inputs go to both sides; the line also carries the GPU
-    block's max rel err and cosine against the oracle's output."""
+    block's max rel err and cosine against the oracle's output. `value` is the block replayed
+    as one CUDA graph (wx_graph_launch: the same kernels, the launch gaps gone; its output is
+    checked equal to the direct call's); `direct` is the plain wx_dit_block_forward call, and
+    `e2e` the graph with the pinned H2D / D2H of h around it."""
     import ctypes
     import torch
     from oracle import oracle as O
@@ -528,37 +531,64 @@ def run_c1(args) -> dict:
     stream = torch.cuda.current_stream()
     clocks = ClockSampler(0)
     clocks.start()
-    ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
-    n0 = ctx.lib.wx_ctx_launch_count(ctx.h)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     steps = max(1, args.steps)
-    e0.record(stream)
-    for _ in range(steps):
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # written between steps: L2 is 126 MB
+
+    def timed(body) -> float:
+        """mean ms of body() over `steps`, each step after an L2 flush that the events exclude"""
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a_, b_ in evs:
+            flush.fill_(1)
+            a_.record(stream)
+            body()
+            b_.record(stream)
+        torch.cuda.synchronize()
+        return sum(a_.elapsed_time(b_) for a_, b_ in evs) / steps
+
+    def direct():
         h.copy_(h_init)  # every step starts from the same input (an 8 MB device copy)
         blk.block_forward(0, h, md, rm, ct, st, None)
-    e1.record(stream)
-    torch.cuda.synchronize()
+
+    ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
+    n0 = ctx.lib.wx_ctx_launch_count(ctx.h)
+    ms_block = timed(direct)
     n1 = ctx.lib.wx_ctx_launch_count(ctx.h)
-    clk = clocks.stop()
     ms = (ctypes.c_double * 10)()
     cnt = (ctypes.c_int64 * 10)()
     ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
     ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
     ctx.check_device()
-    ms_block = e0.elapsed_time(e1) / steps
-    # end to end through the public API with host buffers: pinned H2D of h, the block, D2H of h
+    # the same block replayed as one CUDA graph (wx_dit_block_graph_create / wx_graph_launch)
+    graph = blk.block_graph(0, h, md, rm, ct, st, None)
+    for _ in range(max(3, args.warmup)):
+        h.copy_(h_init)
+        graph.launch()
+    torch.cuda.synchronize()
+    ng0 = ctx.lib.wx_ctx_launch_count(ctx.h)
+
+    def replay():
+        h.copy_(h_init)
+        graph.launch()
+
+    graph_ms = timed(replay)
+    graph_launches = ctx.lib.wx_ctx_launch_count(ctx.h) - ng0
+    clk = clocks.stop()  # sampled over the direct and the graph loops
+    graph_kernels = graph.kernels()
+    graph_ok = bool(torch.equal(h.cpu().view(torch.int16), torch.from_numpy(got.view(np.int16))))
+    # end to end through the public API with host buffers: pinned H2D of h, the block's
+    # graph, D2H of h
     host_in = torch.from_numpy(h0.view(np.int16).copy()).view(torch.bfloat16).pin_memory()
     host_out = torch.empty_like(host_in).pin_memory()
     torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(steps):
+
+    def end_to_end():
         h.copy_(host_in, non_blocking=True)
-        blk.block_forward(0, h, md, rm, ct, st, None)
+        graph.launch()
         host_out.copy_(h, non_blocking=True)
-    f1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = f0.elapsed_time(f1) / steps
+
+    e2e_ms = timed(end_to_end)
+    graph.close()
+    ctx.check_device()
     gemm_fl = 2.0 * S * (hdn * 3 * inner + inner * hdn + hdn * ffn + ffn * hdn)
     attn_fl = 4.0 * S * S * hd * H
     peaks, kind = load_peaks()
@@ -579,21 +609,28 @@ def run_c1(args) -> dict:
     gf, rf = O.bf16_to_f32(got).astype(np.float64), O.bf16_to_f32(ref).astype(np.float64)
     rel = float(np.abs(gf - rf).max() / np.abs(rf).max())
     cosv = float((gf.ravel() @ rf.ravel()) / (np.linalg.norm(gf) * np.linalg.norm(rf)))
-    return dict(metric="DiT block ms/block (c1)", value=ms_block, unit="ms/block", n_gpus=1, steps=steps,
-                warmup=max(3, args.warmup), ms_per_step=ms_block, higher_is_better=False, scaling="weak",
+    if not graph_ok:
+        raise RuntimeError("the block's CUDA graph gave a different output from the direct call")
+    return dict(metric="DiT block ms/block (c1)", value=graph_ms, unit="ms/block", n_gpus=1, steps=steps,
+                warmup=max(3, args.warmup), ms_per_step=graph_ms, higher_is_better=False, scaling="weak",
                 vs_baseline=None, dtype="bf16", data="synthetic",
                 config=dict(workload="c1: one DiT block, S=4096 (16x16x16), hidden 1024, 16x64 heads, FFN 4096 GELU, "
                                      "dense attention, 6-bit g64", S=S, hidden=hdn, heads=H, head_dim=hd, ffn=ffn,
-                            l2="inputs smaller than L2; each step restarts from the same h (device copy inside the "
-                               "timed region)"),
+                            l2="inputs smaller than L2: a 256 MB buffer is written before each step, outside its "
+                               "events; each step restarts from the same h (an 8 MB device copy inside them)"),
                 roofline=roof,
                 qgemm=dict(tflops=gemm_fl / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0, ms=gemm_ms,
                            flops=gemm_fl),
-                kernel_ms={k: dict(ms=float(ms[i]) / steps, launches=int(cnt[i]) // steps) for i, k in
+                kernel_ms_direct={k: dict(ms=float(ms[i]) / steps, launches=int(cnt[i]) // steps) for i, k in
                            enumerate(["qgemm", "attention", "routing", "row_kernels", "dequant", "other",
                                       "qk_norm_rope", "norm_modscale"])},
-                gpu_launches=int(n1 - n0), clocks=clk,
+                gpu_launches=int(graph_launches), clocks=clk,
                 e2e=dict(value=e2e_ms, unit="ms/block", h2d_bytes_per_step=S * hdn * 2, d2h_bytes_per_step=S * hdn * 2),
+                graph=dict(kernels_per_replay=graph_kernels, same_output_as_direct=graph_ok,
+                           what="value: the block replayed as one CUDA graph (wx_graph_launch), the same 8 MB "
+                                "input copy per step"),
+                direct=dict(ms_per_block=ms_block, graph_speedup=ms_block / graph_ms,
+                            what="the plain wx_dit_block_forward call per step"),
                 parity=dict(max_rel_err=rel, cosine=cosv, bound="max rel err <= 2e-2, cosine >= 0.999"),
                 cpu_baseline=dict(value=min(cpu_t) * 1e3, unit="ms/block", cores=threads, kind="port",
                                   sample="the whole block (oracle, C, OpenMP), best of 3, same weights and inputs"))
@@ -678,7 +715,7 @@ def _sm_clock_now(index: int = 0):
         return None
 
 
-def _qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g) -> dict:
+def _qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g, flush) -> dict:
     """The same shape as a q|k|v projection (N = 3 * heads * 128) with QK-RMSNorm + RoPE
     (rot 96): one GEMM with the norm/RoPE epilogue (wx_qkv_norm_rope) against the projection
     followed by the separate row kernel, kernel CUDA-event time per call."""
@@ -709,8 +746,8 @@ def _qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g) -> dict:
             fn()
         torch.cuda.synchronize()
         ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
-        torch.cuda._sleep(400_000 * reps)
         for _ in range(reps):
+            flush.fill_(1)  # evicts L2 (outside the kernels' events)
             fn()
         torch.cuda.synchronize()
         ms = (ctypes.c_double * 10)()
@@ -734,6 +771,7 @@ def run_c2(args) -> dict:
     pk = peaks.get("bf16_tflops", PEAKS_FALLBACK["bf16_tflops"])
     hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
     res = []
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     shapes = [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]
     ms_list = (256, 4096, 28520, 111600)
     if args.shape:  # one point "M,K,N" of the sweep (profiling runs)
@@ -754,23 +792,24 @@ def run_c2(args) -> dict:
             torch.cuda.synchronize()
             ctx = h3.context(0)
             ctx.lib.wx_ctx_profile_enable(ctx.h, 1)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             reps = max(1, args.steps)
-            # hold the GPU in a spin while the host enqueues every call, so that the events
-            # around each launch (and around the loop) see device time only: a small-M call is
-            # shorter than its host-side launch path, and an idle GPU would count that path
-            torch.cuda._sleep(200_000 * reps)
-            e0.record()
-            for _ in range(reps):
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            # each call after a 256 MB write that evicts L2 (the weights and activations of the
+            # small points would stay L2-resident otherwise); the kernels' own events exclude it
+            # and so do the events around each call. The write also gives the host time to
+            # enqueue the next call, so no host launch time lands inside the events.
+            for a_, b_ in evs:
+                flush.fill_(1)
+                a_.record()
                 lin(x, out=y)
-            e1.record()
+                b_.record()
             sm_mhz = _sm_clock_now(0)  # while the last calls still run
             torch.cuda.synchronize()
             ms = (ctypes.c_double * 10)()
             cnt = (ctypes.c_int64 * 10)()
             ctx.lib.wx_ctx_profile_read(ctx.h, ms, cnt, 10)
             ctx.lib.wx_ctx_profile_enable(ctx.h, 0)
-            t_call = e0.elapsed_time(e1) / reps / 1e3
+            t_call = sum(a_.elapsed_time(b_) for a_, b_ in evs) / reps / 1e3
             # the kernels' own time: CUDA events libwx records around each launch (the GEMM,
             # plus the weight expansion of the two-pass path)
             t = (ms[0] + ms[4]) / reps / 1e3
@@ -781,13 +820,13 @@ def run_c2(args) -> dict:
                        path="fused" if (M <= 512 and N % 128 == 0 and args.lora == 0) else "two-pass",
                        lora_rank=args.lora, bias=bool(args.bias), sm_mhz=sm_mhz)
             if args.qkv_rope and N % 384 == 0:
-                row.update(_qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g))
+                row.update(_qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g, flush))
             res.append(row)
             del x, y
     return dict(metric="6-bit qGEMM sweep (c2)", unit="TFLOP/s", peak=pk, peak_kind=f"{kind} burst bf16", hbm_peak=hbm,
                 sweep=res, timing="ms = the kernels' CUDA-event time per call (libwx records events around each "
-                                  "launch); ms_per_call = events around the loop of calls; every call is enqueued "
-                                  "while the GPU spins, so neither includes host launch time")
+                                  "launch); ms_per_call = events around each call; L2 is evicted by a 256 MB write "
+                                  "before every call, outside both")
 
 
 # ------------------------------------------------------------------ main

@@ -377,6 +377,21 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
                          const void* cos_t, const void* sin_t, const wx_sparse_spec* spec,
                          void* pab_slot, int refresh, void* scratch);
 
+/* The same block forward as a CUDA graph: captured once (on a private stream, nothing
+ * runs), replayed on the context stream by wx_graph_launch. Every pointer and scalar of
+ * the call is baked in; the caller refreshes the buffers' contents between replays
+ * (h is updated in place by each replay, as by wx_dit_block_forward). Cuts the gaps
+ * between the block's ~12-20 dependent launches where they matter (small S). */
+typedef struct wx_graph wx_graph;
+int wx_dit_block_graph_create(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_weights* w,
+                              const wx_block_mods* mods, const uint32_t* rowmap, void* h, int64_t S,
+                              const void* cos_t, const void* sin_t, const wx_sparse_spec* spec, void* pab_slot,
+                              int refresh, void* scratch, wx_graph** out);
+int wx_graph_launch(wx_ctx* ctx, wx_graph* g);
+/* libwx kernels one replay launches */
+int64_t wx_graph_kernels(const wx_graph* g);
+int wx_graph_destroy(wx_graph* g);
+
 /* ------------------------------------------- Ulysses sequence parallelism */
 /* No counterpart in the reference (it runs on a single device, with no
  * DP/TP/SP). Rank `rank` of P owns rows [row0, row0 + rows) of the packed

@@ -127,6 +127,11 @@ _SIGS = {
     "wx_upload": (_i32, [_vp, _vp, _vp, C.c_size_t]),
     "wx_download": (_i32, [_vp, _vp, _vp, C.c_size_t]),
     "wx_ctx_synchronize": (_i32, [_vp]),
+    "wx_dit_block_graph_create": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _i32, _vp,
+                                          C.POINTER(_vp)]),
+    "wx_graph_launch": (_i32, [_vp, _vp]),
+    "wx_graph_kernels": (_i64, [_vp]),
+    "wx_graph_destroy": (_i32, [_vp]),
     "wx_ctx_profile_enable": (_i32, [_vp, _i32]),
     "wx_ctx_profile_read": (_i32, [_vp, _vp, _vp, _i32]),
     "wx_ctx_trace_enable": (_i32, [_vp, _i32]),

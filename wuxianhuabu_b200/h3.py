@@ -565,6 +565,13 @@ class H3DiTBlocks:
                      _p(h), S, _p(cos), _p(sin), C.byref(sp), _p(pab_slot), int(refresh), _p(scr))
         return h
 
+    def block_graph(self, bi: int, h: torch.Tensor, mods: Sequence[torch.Tensor], rowmap: torch.Tensor,
+                    cos: torch.Tensor, sin: torch.Tensor, spec: Optional[SparseSpec],
+                    pab_slot: Optional[torch.Tensor] = None, refresh: bool = True) -> "BlockGraph":
+        """block_forward of block bi on exactly these buffers, captured as a CUDA graph
+        (wx_dit_block_graph_create); BlockGraph.launch() replays it (single GPU)."""
+        return BlockGraph(self, bi, h, mods, rowmap, cos, sin, spec, pab_slot, refresh)
+
     def forward(self, h: torch.Tensor, mods: Sequence[Sequence[torch.Tensor]], rowmap: torch.Tensor,
                 cos: torch.Tensor, sin: torch.Tensor, sparse_cfg: Optional[H3SolAttnConfig], g: int,
                 policy: int = SparsePolicy.MIX, attn_bcast: Optional[H3AttnBroadcast] = None,
@@ -585,6 +592,51 @@ class H3DiTBlocks:
         if attn_bcast is not None and attn_refresh and sigma is not None:
             attn_bcast.cached_sigma = sigma
         return h
+
+
+class BlockGraph:
+    """One block forward captured as a CUDA graph (wx_dit_block_graph_create) and replayed
+    by launch() (wx_graph_launch) on the current stream. The graph holds the buffers'
+    addresses: this object keeps the tensors alive, owns its own scratch, and the caller
+    refreshes the contents (h is updated in place by each replay)."""
+
+    def __init__(self, blocks: "H3DiTBlocks", bi: int, h: torch.Tensor, mods: Sequence[torch.Tensor],
+                 rowmap: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, spec: Optional[SparseSpec],
+                 pab_slot: Optional[torch.Tensor], refresh: bool):
+        _need_bf16_cuda(h, cos, sin, *mods)
+        ctx = context(h.device.index)
+        if getattr(ctx, "sp_size", 1) != 1:
+            raise WxError(_lib.WX_ERR_UNSUPPORTED, "block graphs are single-GPU")
+        S = h.shape[0]
+        need = int(ctx.lib.wx_dit_block_scratch_bytes(C.byref(blocks._c), S))
+        self._scratch = torch.empty(max(need, 1), dtype=torch.uint8, device=h.device)
+        self._keep = (blocks, h, list(mods), rowmap, cos, sin, pab_slot)
+        bm = BlockMods(*[_p(m) for m in mods])
+        sp = spec if spec is not None else dense_spec()
+        self._ctx = ctx
+        self._g = C.c_void_p()
+        ctx.call("wx_dit_block_graph_create", C.byref(blocks._c), C.byref(blocks._wc[bi]), C.byref(bm), _p(rowmap),
+                 _p(h), S, _p(cos), _p(sin), C.byref(sp), _p(pab_slot), int(refresh), _p(self._scratch),
+                 C.byref(self._g))
+
+    def launch(self) -> None:
+        self._ctx.call("wx_graph_launch", self._g)
+
+    def kernels(self) -> int:
+        return int(self._ctx.lib.wx_graph_kernels(self._g))
+
+    def close(self) -> None:
+        if self._g is not None and self._g.value:
+            self._ctx.sync_stream()
+            torch.cuda.current_stream(self._scratch.device).synchronize()
+            self._ctx.lib.wx_graph_destroy(self._g)
+        self._g = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 @dataclass
