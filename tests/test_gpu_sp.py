@@ -1,9 +1,10 @@
 """Ulysses sequence parallelism on 2, 4 and 8 GPUs: wx_dit_block_forward_sp against the
-single-GPU block on the same inputs (dense, SOL and top-k attention; refresh, refresh, PAB
-reuse in sequence), with the exchange over NVLink peer memory (default: the q|k|v projection's
-epilogue stores into the owners' buffers) and over NCCL all-to-alls (WX_SP_P2P=0). S = 1000
-rows, so that rank boundaries fall inside 128-row query tiles; heads = max(4, P). Each world
-size is skipped on boxes with fewer GPUs."""
+single-GPU block on the same inputs (dense, SOL and top-k attention, and a dense block with
+LoRA adapters on its four linears; refresh, refresh, PAB reuse in sequence), with the exchange
+over NVLink peer memory (default: the q|k|v projection's epilogue stores into the owners'
+buffers) and over NCCL all-to-alls (WX_SP_P2P=0). S = 1000 rows, so that rank boundaries fall
+inside 128-row query tiles; heads = max(4, P). Each world size is skipped on boxes with fewer
+GPUs."""
 import datetime
 import os
 import socket
@@ -30,6 +31,19 @@ def _free_port() -> int:
     return p
 
 
+def _maybe_lora(blk, sparse_name, hidden, heads, ffn):
+    """("lora" case) one adapter on each of the four linears, the same on every rank"""
+    if sparse_name != "lora":
+        return blk
+    from tests.test_gpu_lora import _adapters, _refs
+    from wuxianhuabu_b200 import h3
+    inner = heads * 128
+    dims = [(hidden, 3 * inner), (inner, hidden), (hidden, ffn), (ffn, hidden)]
+    for i, (lin, (k, n)) in enumerate(zip(blk.blocks[0].linears(), dims)):
+        lin.set_lora(_refs(_adapters(60 + i, k, n, [16], [0.9])))
+    return h3.H3DiTBlocks(blk.cfg, blk.blocks)
+
+
 def _worker(rank, world, port, sparse_name, p2p, out_q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -48,9 +62,10 @@ def _worker(rank, world, port, sparse_name, p2p, out_q):
         hidden, heads, ffn, rot, eps, g = 256, max(4, world), 512, 96, 1e-6, 40
         S = 1000  # 1000 / P rows per rank: rank boundaries fall inside 128-row query tiles
         w, mods, h, cos, sin, rowmap = make_block(9, hidden, heads, ffn, 0, S, rot)
-        sparse = {"dense": None, "sol": dict(tau=0.4), "topk": dict(block=128, topk_ratio=0.25, tail=False)}[sparse_name]
+        sparse = {"dense": None, "lora": None, "sol": dict(tau=0.4),
+                  "topk": dict(block=128, topk_ratio=0.25, tail=False)}[sparse_name]
         spec = None if sparse is None else h3.H3SolAttnConfig(**sparse).spec(g)
-        blk = gpu_block(w, hidden, heads, ffn, 0, rot, eps)
+        blk = _maybe_lora(gpu_block(w, hidden, heads, ffn, 0, rot, eps), sparse_name, hidden, heads, ffn)
         md = [to_torch_bf16(m, dev) for m in mods]
         rm = torch.from_numpy(rowmap.view(np.int32)).to(dev)
         c, s = to_torch_bf16(cos, dev), to_torch_bf16(sin, dev)
@@ -73,7 +88,7 @@ def _worker(rank, world, port, sparse_name, p2p, out_q):
         r0 = rank * rows
         hl = to_torch_bf16(h, dev)[r0:r0 + rows].contiguous()
         slot = torch.empty((rows, hidden), dtype=torch.bfloat16, device=dev)
-        blk2 = gpu_block(w, hidden, heads, ffn, 0, rot, eps)
+        blk2 = _maybe_lora(gpu_block(w, hidden, heads, ffn, 0, rot, eps), sparse_name, hidden, heads, ffn)
         res = []
         for refresh, want in zip(schedule, refs):
             blk2.block_forward(0, hl, md, rm[r0:r0 + rows].contiguous(), c[r0:r0 + rows].contiguous(),
@@ -91,7 +106,7 @@ def _worker(rank, world, port, sparse_name, p2p, out_q):
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("p2p", ["1", "0"])
-@pytest.mark.parametrize("sparse_name", ["dense", "sol", "topk"])
+@pytest.mark.parametrize("sparse_name", ["dense", "sol", "topk", "lora"])
 def test_ulysses_block_matches_single_gpu(sparse_name, p2p, world):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
