@@ -381,7 +381,8 @@ int wx_dit_block_forward(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_w
  * runs), replayed on the context stream by wx_graph_launch. Every pointer and scalar of
  * the call is baked in; the caller refreshes the buffers' contents between replays
  * (h is updated in place by each replay, as by wx_dit_block_forward). Cuts the gaps
- * between the block's ~12-20 dependent launches where they matter (small S). */
+ * between the block's ~12-20 dependent launches where they matter (small S).
+ * Single-GPU contexts only (WX_ERR_UNSUPPORTED after wx_ctx_init_comm with > 1 rank). */
 typedef struct wx_graph wx_graph;
 int wx_dit_block_graph_create(wx_ctx* ctx, const wx_dit_config* cfg, const wx_block_weights* w,
                               const wx_block_mods* mods, const uint32_t* rowmap, void* h, int64_t S,

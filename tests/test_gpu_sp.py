@@ -44,11 +44,12 @@ def _maybe_lora(blk, sparse_name, hidden, heads, ffn):
     return h3.H3DiTBlocks(blk.cfg, blk.blocks)
 
 
-def _worker(rank, world, port, sparse_name, p2p, out_q):
+def _worker(rank, world, port, sparse_name, p2p, out_q, fused="1"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     os.environ["WX_SP_P2P"] = p2p
+    os.environ["WX_QKV_ROPE_FUSED"] = fused
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(rank)
@@ -108,13 +109,24 @@ def _worker(rank, world, port, sparse_name, p2p, out_q):
 @pytest.mark.parametrize("p2p", ["1", "0"])
 @pytest.mark.parametrize("sparse_name", ["dense", "sol", "topk", "lora"])
 def test_ulysses_block_matches_single_gpu(sparse_name, p2p, world):
+    _run_group(sparse_name, p2p, world, "1")
+
+
+@pytest.mark.parametrize("sparse_name", ["dense", "sol"])
+def test_ulysses_peer_exchange_with_the_separate_norm_rope_kernel(sparse_name):
+    """WX_QKV_ROPE_FUSED=0: the q|k|v stores into the owners' buffers come from
+    qk_norm_rope_vec_kernel<RopePeerDst> after the projection instead of its epilogue."""
+    _run_group(sparse_name, "1", 2, "0")
+
+
+def _run_group(sparse_name, p2p, world, fused):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, sparse_name, p2p, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, sparse_name, p2p, q, fused)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:

@@ -28,6 +28,9 @@ int wx_dit_block_graph_create(wx_ctx* ctx, const wx_dit_config* cfg, const wx_bl
                               int refresh, void* scratch, wx_graph** out) {
   WX_CHECK_ARG(ctx, ctx && out);
   *out = nullptr;
+  if (ctx->sp_size != 1)  // the sequence-parallel block waits on other ranks: not a replayable graph
+    return set_error(ctx, WX_ERR_UNSUPPORTED, "block graphs are single-GPU (this context has %d ranks)",
+                     ctx->sp_size);
   WX_CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));  // nothing of the caller's is in flight
   cudaStream_t cap = nullptr;
   WX_CUDA_TRY(ctx, cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking));
