@@ -1066,6 +1066,21 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
                 kernel_ms=prof, gpu_launches=int(_sum_over_ranks(n1 - n0, dist)), clocks=clk)
     line.update(memory_bound_kernels(c, prof, world, peaks, peaks_kind))
     line["phases"] = phase_summary(trace, args.steps)
+    if world > 1 and "exchange" in line:
+        # NVLink stores inside the compute kernels (the q|k|v projection's epilogue, the attention
+        # epilogue): bytes this rank sends per step over the time of the phase that sends them,
+        # a lower bound on the store bandwidth (the phases also compute)
+        ex = line["exchange"]
+        blocks_refreshed = sum(1 for r in trace if r["mode"] != "reuse")
+        rows = c["S"] // world
+        qkv_b = rows * 3 * c["inner"] * 2 * (world - 1) / world * blocks_refreshed / args.steps
+        att_b = ex["attention_out_peer_bytes_per_launch"] * blocks_refreshed / args.steps
+        ph = line["phases"]["ms_per_step"]
+        ex["peer_bytes_per_step"] = dict(qkv_from_projection_epilogue=qkv_b, attention_rows=att_b)
+        ex["peer_gbs_lower_bound"] = dict(
+            qkv_phase=qkv_b / (ph["qkv"] / 1e3) / 1e9 if ph["qkv"] > 0 else None,
+            attn_phase=att_b / (ph["attn"] / 1e3) / 1e9 if ph["attn"] > 0 else None,
+            what="bytes sent to the other ranks per step / the phase's time per step (the phase also computes)")
     # e2e through the public API with host buffers (pinned H2D of each rank's latent rows,
     # D2H of the updated rows)
     if not args.no_e2e:
