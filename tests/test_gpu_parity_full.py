@@ -11,7 +11,9 @@
 * one DiT block at the configs' width (hidden 3072, 24 x 128 heads, FFN 12288 GELU, rot 96) with
   top-k and SOL attention, the oracle taking the GPU block's own block selection;
 * the sampler step under the mix policy (dense anchor layers + sparse layers) against the
-  oracle composition, again with the GPU's selections per sparse layer.
+  oracle composition, again with the GPU's selections per sparse layer;
+* the SOL self-test's production geometry (Case R: 56 heads, g = 934, L = 9324) with the
+  production router: tables bit-exact, attention of four heads over every row.
 
 Tolerances: routing tables bit-exact; attention and block outputs max rel err <= 2e-2 and
 cosine >= 0.999; the step's velocity the same.
@@ -223,3 +225,30 @@ def test_step_mix_policy_vs_oracle(name, sparse):
     assert np.array_equal(got[:video_start - text], lat[:video_start - text])
     v_got = (got[video_start - text:] - lat[video_start - text:]) / -dsigma
     assert_close(v_got, ref_v, rel=2e-2, cos=0.999, what=f"mix-policy step velocity ({name})")
+
+
+def test_sol_case_r_production_geometry():
+    """The SOL self-test's production geometry (Case R, SOL:874-886: 56 heads, g = 934 strip rows,
+    L = 9324 video rows, head_dim 128; neither g nor L a multiple of 64) with the production router
+    (tau 1.3, 64-row blocks, tail): routing tables bit-exact over all 56 heads, and the attention
+    of four heads over every row against the oracle."""
+    import json
+    from pathlib import Path
+    from wuxianhuabu_b200 import h3
+    gd = json.load(open(Path(__file__).resolve().parent / "golden" / "sol_selftest.json"))["caseR"]
+    H, g, L = gd["h"], gd["g"], gd["L"]
+    S = g + L
+    q, k, v = _qkv_device(S, H, 4000)
+    cfg = h3.H3SolAttnConfig(tau=1.3, tail=True)
+    got = h3.H3SolAttn.route(q, k, v, g, SCALE, cfg)
+    qh, kh, vh = _host(q), _host(k), _host(v)
+    ref = O.sol_route(qh, kh, vh, g, SCALE, 1.3)
+    _check_tables(got, ref, "thr")
+    out = h3.H3SolAttn.forward(q, k, v, g, SCALE, cfg)
+    h3.context().check_device()
+    heads = [0, 17, 38, 55]
+    qs, ks, vs = (np.ascontiguousarray(a[:, heads, :]) for a in (qh, kh, vh))
+    route = O.sol_route(qs, ks, vs, g, SCALE, 1.3)
+    route.update(g=g, block=64)
+    want = O.sparse_attention(qs, ks, vs, g, SCALE, route=route, tail=True)
+    assert_close(f32(_host(out[:, heads, :])), f32(want), rel=2e-2, cos=0.999, what="case R attention")
