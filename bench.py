@@ -78,6 +78,24 @@ def phase_summary(trace: list, steps: int) -> dict:
     return out
 
 
+def peer_store_summary(trace: list, phases: dict, c: dict, world: int, steps: int, att_bytes_per_launch: float) -> dict:
+    """NVLink stores inside the compute kernels (the q|k|v projection's epilogue, the attention
+    epilogue) under sequence parallelism: bytes this rank sends per step, and those bytes over
+    the time of the phase that sends them, a lower bound on the store bandwidth (the phases
+    also compute)."""
+    blocks_refreshed = sum(1 for r in trace if r["mode"] != "reuse")
+    rows = c["S"] // world
+    qkv_b = rows * 3 * c["inner"] * 2 * (world - 1) / world * blocks_refreshed / steps
+    att_b = att_bytes_per_launch * blocks_refreshed / steps
+    ph = phases["ms_per_step"]
+    return dict(peer_bytes_per_step=dict(qkv_from_projection_epilogue=qkv_b, attention_rows=att_b),
+                peer_gbs_lower_bound=dict(
+                    qkv_phase=qkv_b / (ph["qkv"] / 1e3) / 1e9 if ph["qkv"] > 0 else None,
+                    attn_phase=att_b / (ph["attn"] / 1e3) / 1e9 if ph["attn"] > 0 else None,
+                    what="bytes sent to the other ranks per step / the phase's time per step (the phase "
+                         "also computes)"))
+
+
 def geometry(name: str) -> dict:
     c = dict(CONFIGS[name])
     t, hh, ww = c["grid"]
@@ -1067,20 +1085,8 @@ def run_step_bench(args, c, base_cfg, dev, world, rank, local, dist) -> dict:
     line.update(memory_bound_kernels(c, prof, world, peaks, peaks_kind))
     line["phases"] = phase_summary(trace, args.steps)
     if world > 1 and "exchange" in line:
-        # NVLink stores inside the compute kernels (the q|k|v projection's epilogue, the attention
-        # epilogue): bytes this rank sends per step over the time of the phase that sends them,
-        # a lower bound on the store bandwidth (the phases also compute)
-        ex = line["exchange"]
-        blocks_refreshed = sum(1 for r in trace if r["mode"] != "reuse")
-        rows = c["S"] // world
-        qkv_b = rows * 3 * c["inner"] * 2 * (world - 1) / world * blocks_refreshed / args.steps
-        att_b = ex["attention_out_peer_bytes_per_launch"] * blocks_refreshed / args.steps
-        ph = line["phases"]["ms_per_step"]
-        ex["peer_bytes_per_step"] = dict(qkv_from_projection_epilogue=qkv_b, attention_rows=att_b)
-        ex["peer_gbs_lower_bound"] = dict(
-            qkv_phase=qkv_b / (ph["qkv"] / 1e3) / 1e9 if ph["qkv"] > 0 else None,
-            attn_phase=att_b / (ph["attn"] / 1e3) / 1e9 if ph["attn"] > 0 else None,
-            what="bytes sent to the other ranks per step / the phase's time per step (the phase also computes)")
+        line["exchange"].update(peer_store_summary(trace, line["phases"], c, world, args.steps,
+                                                   line["exchange"]["attention_out_peer_bytes_per_launch"]))
     # e2e through the public API with host buffers (pinned H2D of each rank's latent rows,
     # D2H of the updated rows)
     if not args.no_e2e:
