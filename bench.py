@@ -790,19 +790,29 @@ def run_c2(args) -> dict:
     hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
     res = []
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    shapes = [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]
-    ms_list = (256, 4096, 28520, 111600)
-    if args.shape:  # one point "M,K,N" of the sweep (profiling runs)
-        M0, K0, N0 = (int(v) for v in args.shape.split(","))
-        shapes, ms_list = [(K0, N0)], (M0,)
-    for (K, N) in shapes:
+    ms_all = (256, 4096, 28520, 111600)
+    plan = [((K, N), ms_all) for K, N in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]]
+    if args.shape:  # points "M,K,N[;M,K,N...]" instead of the sweep (profiling runs)
+        plan = []
+        for pt in args.shape.split(";"):
+            M0, K0, N0 = (int(v) for v in pt.split(","))
+            if plan and plan[-1][0] == (K0, N0):
+                plan[-1] = (plan[-1][0], plan[-1][1] + (M0,))
+            else:
+                plan.append(((K0, N0), (M0,)))
+    # small-M CTA shapes to time (WX_QGEMM_ROWS: 128 or 256 weight rows per CTA, 0 = chosen per
+    # call); by default the library's own choice, with the environment left as it is
+    rows_list = [int(v) for v in args.rows.split(",")] if args.rows else [None]
+    for (K, N), ms_list in plan:
         bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16) if args.bias else None
         lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02, bias=bias)
         if args.lora > 0:  # one adapter of rank args.lora (the LoRA row: a K extension of the GEMM)
             a = (torch.randn((K, args.lora), device=dev, generator=g) * 0.02).to(torch.bfloat16)
             b = (torch.randn((args.lora, N), device=dev, generator=g) * 0.02).to(torch.bfloat16)
             lin.set_lora([h3.LoraRef(a, b, 1.0)])
-        for M in ms_list:
+        for M, rows in [(M, r) for M in ms_list for r in rows_list]:
+            if rows is not None:
+                os.environ["WX_QGEMM_ROWS"] = str(rows)
             x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
             y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
             for _ in range(max(1, args.warmup)):
@@ -837,6 +847,8 @@ def run_c2(args) -> dict:
                        gbs=byts / t / 1e9, gbs_frac=byts / t / 1e9 / hbm, ms_per_call=t_call * 1e3,
                        path="fused" if (M <= 512 and N % 128 == 0 and args.lora == 0) else "two-pass",
                        lora_rank=args.lora, bias=bool(args.bias), sm_mhz=sm_mhz)
+            if rows is not None:
+                row["cta_rows"] = rows
             if args.qkv_rope and N % 384 == 0:
                 row.update(_qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g, flush))
             res.append(row)
@@ -859,7 +871,10 @@ def main():
                                              "rowops"])
     ap.add_argument("--router", default="topk", choices=["topk", "sol"],
                     help="c3 / c3full / c5attn: top-k 25%% over 128-row blocks, or SOL tau 1.3 over 64-row blocks")
-    ap.add_argument("--shape", default="", help="c2 only: a single M,K,N point")
+    ap.add_argument("--shape", default="", help="c2 only: points M,K,N[;M,K,N...] instead of the sweep")
+    ap.add_argument("--rows", default="",
+                    help="c2 only: small-M CTA shapes to time at each point, e.g. 128,256,0 (weight rows per CTA; "
+                         "0 = the library's choice)")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
     ap.add_argument("--bias", action="store_true", help="c2 only: the linears carry a bias (added in the epilogue)")
     ap.add_argument("--qkv-rope", action="store_true",

@@ -86,6 +86,54 @@ def test_qlinear_fused_is_deterministic(torch_mod, m, k, n):
         assert torch_mod.equal(a, lin(x))
 
 
+ROWS_SHAPES = [(1, 256, 256), (8, 3072, 9216), (100, 704, 768), (256, 3072, 3072), (257, 1024, 1024),
+               (512, 1024, 3072), (33, 12288, 3072), (256, 12288, 3072)]
+
+
+@pytest.mark.parametrize("rows", [128, 256])
+@pytest.mark.parametrize("m,k,n", ROWS_SHAPES)
+def test_qlinear_small_m_rows_per_cta(torch_mod, monkeypatch, rows, m, k, n):
+    """Both CTA shapes of the small-M kernel, forced by WX_QGEMM_ROWS: 128 weight rows
+    (one TMEM accumulator) or 256 (two accumulators sharing each activation tile, the split-K
+    reduction run once per accumulator), with bias, against the oracle, and deterministic."""
+    monkeypatch.setenv("WX_QGEMM_ROWS", str(rows))
+    x = O.normal_bf16((m, k), 36, 1)
+    wq, sc, bi = O.quantize(O.normal_f32((n, k), 36, 2, std=0.02))
+    bias = O.normal_bf16((n,), 36, 3, std=0.1)
+    lin = _mf(torch_mod, wq, sc, bi, k, bias)
+    xt = to_torch_bf16(x)
+    got = lin(xt).clone()
+    assert_close(f32(to_np_bf16(got)), f32(O.qlinear(x, wq, sc, bi, bias=bias)), rel=1e-2, cos=0.9999,
+                 what=f"qlinear {m}x{k}x{n}, {rows} rows per CTA")
+    assert torch_mod.equal(got, lin(xt))
+
+
+@pytest.mark.parametrize("rows", [128, 256])
+def test_qlinear_small_m_epilogues_rows_per_cta(torch_mod, monkeypatch, rows):
+    """GELU and gate + residual (with y_raw and a row map) through both CTA shapes."""
+    from wuxianhuabu_b200 import h3
+    torch = torch_mod
+    monkeypatch.setenv("WX_QGEMM_ROWS", str(rows))
+    m, k, n = 200, 1024, 768
+    x = O.normal_bf16((m, k), 37, 1)
+    wq, sc, bi = O.quantize(O.normal_f32((n, k), 37, 2, std=0.05))
+    bias = O.normal_bf16((n,), 37, 3, std=0.1)
+    lin = _mf(torch, wq, sc, bi, k, bias)
+    got = to_np_bf16(lin(to_torch_bf16(x), epilogue=h3.EPI_GELU))
+    assert_close(f32(got), f32(O.qlinear(x, wq, sc, bi, bias=bias, epilogue=O.EPI_GELU)), rel=1e-2, cos=0.9999,
+                 what=f"gelu, {rows} rows per CTA")
+    gate, resid = O.normal_bf16((3, n), 37, 4), O.normal_bf16((m, n), 37, 5)
+    rowmap = (np.arange(m) % 3).astype(np.uint32)
+    raw = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    got = to_np_bf16(lin(to_torch_bf16(x), epilogue=h3.EPI_GATE_RESID, gate=to_torch_bf16(gate),
+                         resid=to_torch_bf16(resid), rowmap=torch.from_numpy(rowmap.view(np.int32)).cuda(),
+                         y_raw=raw))
+    want, want_raw = O.qlinear(x, wq, sc, bi, bias=bias, epilogue=O.EPI_GATE_RESID, gate=gate, resid=resid,
+                               rowmap=rowmap, want_raw=True)
+    assert_close(f32(got), f32(want), rel=1e-2, cos=0.9999, what=f"gate+resid, {rows} rows per CTA")
+    assert_close(f32(to_np_bf16(raw)), f32(want_raw), rel=1e-2, cos=0.9999, what=f"raw, {rows} rows per CTA")
+
+
 def test_qlinear_gelu(torch_mod):
     m, k, n = 200, 512, 768
     x = O.normal_bf16((m, k), 32, 1)
