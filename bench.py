@@ -802,7 +802,7 @@ def run_c2(args) -> dict:
                 plan.append(((K0, N0), (M0,)))
     # small-M CTA shapes to time (WX_QGEMM_ROWS: 128 or 256 weight rows per CTA, 0 = chosen per
     # call); by default the library's own choice, with the environment left as it is
-    rows_list = [int(v) for v in args.rows.split(",")] if args.rows else [None]
+    rows_list = args.rows.split(",") if args.rows else [None]
     for (K, N), ms_list in plan:
         bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16) if args.bias else None
         lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02, bias=bias)
@@ -811,8 +811,9 @@ def run_c2(args) -> dict:
             b = (torch.randn((args.lora, N), device=dev, generator=g) * 0.02).to(torch.bfloat16)
             lin.set_lora([h3.LoraRef(a, b, 1.0)])
         for M, rows in [(M, r) for M in ms_list for r in rows_list]:
-            if rows is not None:
-                os.environ["WX_QGEMM_ROWS"] = str(rows)
+            if rows is not None:  # "R" or "R/T": weight rows per CTA, expansion threads per row
+                os.environ["WX_QGEMM_ROWS"] = rows.split("/")[0]
+                os.environ["WX_QGEMM_TPR"] = rows.split("/")[1] if "/" in rows else "0"
             x = torch.randn((M, K), device=dev, generator=g).to(torch.bfloat16)
             y = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
             for _ in range(max(1, args.warmup)):
@@ -873,8 +874,8 @@ def main():
                     help="c3 / c3full / c5attn: top-k 25%% over 128-row blocks, or SOL tau 1.3 over 64-row blocks")
     ap.add_argument("--shape", default="", help="c2 only: points M,K,N[;M,K,N...] instead of the sweep")
     ap.add_argument("--rows", default="",
-                    help="c2 only: small-M CTA shapes to time at each point, e.g. 128,256,0 (weight rows per CTA; "
-                         "0 = the library's choice)")
+                    help="c2 only: small-M CTA shapes to time at each point, e.g. 128/2,128/4,256,0 (weight rows "
+                         "per CTA [/ expansion threads per row]; 0 = the library's choice)")
     ap.add_argument("--lora", type=int, default=0, help="c2 only: attach one LoRA adapter of this rank")
     ap.add_argument("--bias", action="store_true", help="c2 only: the linears carry a bias (added in the epilogue)")
     ap.add_argument("--qkv-rope", action="store_true",

@@ -90,13 +90,15 @@ ROWS_SHAPES = [(1, 256, 256), (8, 3072, 9216), (100, 704, 768), (256, 3072, 3072
                (512, 1024, 3072), (33, 12288, 3072), (256, 12288, 3072)]
 
 
-@pytest.mark.parametrize("rows", [128, 256])
+@pytest.mark.parametrize("rows,tpr", [(128, 2), (128, 4), (256, 2)])
 @pytest.mark.parametrize("m,k,n", ROWS_SHAPES)
-def test_qlinear_small_m_rows_per_cta(torch_mod, monkeypatch, rows, m, k, n):
-    """Both CTA shapes of the small-M kernel, forced by WX_QGEMM_ROWS: 128 weight rows
-    (one TMEM accumulator) or 256 (two accumulators sharing each activation tile, the split-K
-    reduction run once per accumulator), with bias, against the oracle, and deterministic."""
+def test_qlinear_small_m_rows_per_cta(torch_mod, monkeypatch, rows, tpr, m, k, n):
+    """Every CTA shape of the small-M kernel, forced by WX_QGEMM_ROWS / WX_QGEMM_TPR: 128 weight
+    rows (one TMEM accumulator) expanded by 2 or 4 threads per row, or 256 (two accumulators
+    sharing each activation tile, the split-K reduction run once per accumulator), with bias,
+    against the oracle, and deterministic."""
     monkeypatch.setenv("WX_QGEMM_ROWS", str(rows))
+    monkeypatch.setenv("WX_QGEMM_TPR", str(tpr))
     x = O.normal_bf16((m, k), 36, 1)
     wq, sc, bi = O.quantize(O.normal_f32((n, k), 36, 2, std=0.02))
     bias = O.normal_bf16((n,), 36, 3, std=0.1)
@@ -108,12 +110,28 @@ def test_qlinear_small_m_rows_per_cta(torch_mod, monkeypatch, rows, m, k, n):
     assert torch_mod.equal(got, lin(xt))
 
 
-@pytest.mark.parametrize("rows", [128, 256])
-def test_qlinear_small_m_epilogues_rows_per_cta(torch_mod, monkeypatch, rows):
-    """GELU and gate + residual (with y_raw and a row map) through both CTA shapes."""
+@pytest.mark.parametrize("m,k,n", [(256, 3072, 3072), (33, 12288, 3072), (512, 1024, 3072)])
+def test_qlinear_small_m_threads_per_row_bit_identical(torch_mod, monkeypatch, m, k, n):
+    """Two or four expansion threads per weight row write the same expanded tiles and keep the
+    same split plan: bit-identical outputs."""
+    x = to_torch_bf16(O.normal_bf16((m, k), 38, 1))
+    wq, sc, bi = O.quantize(O.normal_f32((n, k), 38, 2, std=0.02))
+    lin = _mf(torch_mod, wq, sc, bi, k)
+    monkeypatch.setenv("WX_QGEMM_ROWS", "128")
+    outs = []
+    for tpr in ("2", "4"):
+        monkeypatch.setenv("WX_QGEMM_TPR", tpr)
+        outs.append(lin(x).clone())
+    assert torch_mod.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("rows,tpr", [(128, 2), (128, 4), (256, 2)])
+def test_qlinear_small_m_epilogues_rows_per_cta(torch_mod, monkeypatch, rows, tpr):
+    """GELU and gate + residual (with y_raw and a row map) through every CTA shape."""
     from wuxianhuabu_b200 import h3
     torch = torch_mod
     monkeypatch.setenv("WX_QGEMM_ROWS", str(rows))
+    monkeypatch.setenv("WX_QGEMM_TPR", str(tpr))
     m, k, n = 200, 1024, 768
     x = O.normal_bf16((m, k), 37, 1)
     wq, sc, bi = O.quantize(O.normal_f32((n, k), 37, 2, std=0.05))

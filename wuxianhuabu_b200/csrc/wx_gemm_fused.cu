@@ -9,7 +9,7 @@
 // K block (one quantization group):
 //   warp 0      TMA: the activation tile X [Mt x 64] bf16 (SW128) and the packed
 //               weight words [A*128 rows x 12 u32] of the block
-//   warps 2..   two threads per weight row (row n0 + t/2, half t%2): 32 six-bit
+//   warps 2..   T = 2 or 4 threads per weight row (row n0 + t/T, part t%T): 64/T six-bit
 //               values each -> fp32 q*scale+bias (one rounding, as the reference's
 //               dequant) -> bf16, stored in the SW128 K-major layout the MMA reads;
 //               scales and biases come from a 4-deep register ring of plain loads
@@ -50,18 +50,18 @@ constexpr int kQMaxMt = 256;         // tokens per CTA (the MMA's N)
 constexpr int kQMaxSplits = 8;       // K splits = cluster size (portable limit)
 
 // Shared-memory plan of the kernel with A accumulators (A * 128 weight rows per CTA, all
-// sharing one activation tile per K block). Ring 1 holds what TMA brings per K block (the
+// sharing one activation tile per K block) and T expansion threads per weight row. Ring 1 holds what TMA brings per K block (the
 // activation tile and the packed words of the CTA's rows), ring 2 the expanded weight tiles;
 // the fp32 partial tile of one accumulator ([Mt][128]) reuses ring 1 after the last MMA.
 //   A = 1: 4 x (32 + 6) KB + 4 x 16 KB  (216 KB)
 //   A = 2: 3 x (32 + 12) KB + 2 x 32 KB (196 KB): the activation tile is read from L2 once
 //          per 256 weight rows instead of once per 128
-template <int A>
+template <int A, int T>
 struct Q6Cfg {
   static constexpr int kStages = A == 1 ? 4 : 3;     // ring 1 (TMA)
   static constexpr int kWStages = A == 1 ? 4 : 2;    // ring 2 (expanded weights)
   static constexpr int kRows = kQRows * A;           // weight rows per CTA
-  static constexpr int kDequantWarps = 8 * A;        // two threads per weight row
+  static constexpr int kDequantWarps = 4 * A * T;    // T threads per weight row
   static constexpr int kThreads = 64 + 32 * kDequantWarps;  // warp 0 TMA, warp 1 MMA
   static constexpr int kXBytes = kQMaxMt * kQBK * 2;        // activation tile (32 KB)
   static constexpr int kPBytes = kRows * kQWords * 4;       // packed weight words
@@ -125,11 +125,11 @@ __device__ __forceinline__ float gelu_tanh_q(float x) {
   return 0.5f * x * (1.0f + tanhf(c * (x + 0.044715f * x * x * x)));
 }
 
-template <int A>
-__global__ void __launch_bounds__(Q6Cfg<A>::kThreads, 1)
+template <int A, int T>
+__global__ void __launch_bounds__(Q6Cfg<A, T>::kThreads, 1)
     gemm_q6_fused_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
                          Q6Params p) {
-  using L = Q6Cfg<A>;
+  using L = Q6Cfg<A, T>;
   constexpr int S1 = L::kStages, S2 = L::kWStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -220,8 +220,10 @@ __global__ void __launch_bounds__(Q6Cfg<A>::kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- dequant
-    const int t = threadIdx.x - 64;  // 0 .. 256 A - 1
-    const int row = t >> 1, hf = t & 1;  // weight row n0 + row, values [32 hf, 32 hf + 32) of the block
+    constexpr int V = kQBK / T;        // values of the K block per thread (32 or 16)
+    constexpr int NW = 3 * (V / 16);   // their packed words (3 per 16 values)
+    const int t = threadIdx.x - 64;    // 0 .. 128 A T - 1
+    const int row = t / T, sub = t % T;  // weight row n0 + row, values [V sub, V sub + V) of the block
     const int64_t n = n0 + row;
     const __nv_bfloat16* srow = p.scales + n * p.groups;
     const __nv_bfloat16* brow = p.biases + n * p.groups;
@@ -245,11 +247,16 @@ __global__ void __launch_bounds__(Q6Cfg<A>::kThreads, 1)
           ok = false;
           break;
         }
-        uint32_t wd[6];  // two 3-word bundles = 32 values
-        const uint32_t pa = sP(s) + row * (kQWords * 4) + hf * 24;
+        uint32_t wd[NW];  // 3-word bundles of 16 values
+        const uint32_t pa = sP(s) + row * (kQWords * 4) + sub * (NW * 4);
+        if constexpr (NW % 2 == 0) {
 #pragma unroll
-        for (int q = 0; q < 3; ++q)
-          asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(wd[2 * q]), "=r"(wd[2 * q + 1]) : "r"(pa + q * 8));
+          for (int q = 0; q < NW / 2; ++q)
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(wd[2 * q]), "=r"(wd[2 * q + 1]) : "r"(pa + q * 8));
+        } else {
+#pragma unroll
+          for (int q = 0; q < NW; ++q) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(wd[q]) : "r"(pa + q * 4));
+        }
         const float sv = __uint_as_float((uint32_t)rs[d] << 16), bvv = __uint_as_float((uint32_t)rb[d] << 16);
         const float2 s2 = make_float2(sv, sv), b2 = make_float2(bvv, bvv);
         if (i + kDepth < nkb) {
@@ -259,8 +266,8 @@ __global__ void __launch_bounds__(Q6Cfg<A>::kThreads, 1)
         const uint32_t rowaddr = sW(w) + row * 128;  // rows >= 128 land in the second 16 KB tile
         const float2 magic = make_float2(-8388608.0f, -8388608.0f);
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {  // 8 values per 16-byte chunk; 16 values per 3 words
-          const int ch = hf * 4 + c4;
+        for (int c4 = 0; c4 < V / 8; ++c4) {  // 8 values per 16-byte chunk; 16 values per 3 words
+          const int ch = sub * (V / 8) + c4;
           const int bundle = c4 >> 1, half = c4 & 1;
           const uint32_t w0 = wd[bundle * 3], w1 = wd[bundle * 3 + 1], w2 = wd[bundle * 3 + 2];
           uint32_t packed[4];
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(Q6Cfg<A>::kThreads, 1)
     acc_ok = ok && nkb > 0 && mbar_wait(done_bar, 0, p.err, kDevTimeoutAcc, abort_flag);
     tc_fence_after();
   }
-  constexpr int G = 2 * A;  // column groups of the epilogue warps
+  constexpr int G = L::kDequantWarps / 4;  // column groups of the epilogue warps
   constexpr int U = 4;      // columns reduced per iteration (all their loads in flight at once)
   float* part = reinterpret_cast<float*>(smem);
   const int q4 = warp & 3;                // TMEM lane quarter of this warp
@@ -381,11 +388,11 @@ bool fused_eligible(const wx_qweight* w, int64_t M, int epilogue) {
          epilogue != WX_EPI_SWIGLU && w->n <= INT32_MAX && w->k <= INT32_MAX;
 }
 
-// clusters of `size` CTAs of gemm_q6_fused_kernel<A> the current device holds at once
+// clusters of `size` CTAs of gemm_q6_fused_kernel<A, T> the current device holds at once
 // (cached per device)
-template <int A>
+template <int A, int T>
 static int max_active_clusters(int size) {
-  using L = Q6Cfg<A>;
+  using L = Q6Cfg<A, T>;
   static std::mutex mu;
   static std::map<std::pair<int, int>, int> cache;
   int dev = 0;
@@ -405,7 +412,7 @@ static int max_active_clusters(int size) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_q6_fused_kernel<A>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_q6_fused_kernel<A, T>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = 0;
   }
@@ -419,9 +426,16 @@ static int forced_rows() {
   const char* e = getenv("WX_QGEMM_ROWS");
   return e ? atoi(e) : 0;
 }
+// WX_QGEMM_TPR=2 or 4 forces the expansion threads per weight row of the 128-row CTA (A/B
+// measurements and tests); unset or 0: chosen per call
+static int forced_tpr() {
+  const char* e = getenv("WX_QGEMM_TPR");
+  const int v = e ? atoi(e) : 0;
+  return v == 2 || v == 4 ? v : 0;
+}
 
 struct Q6Plan {
-  int A = 1, splits = 1;
+  int A = 1, T = 2, splits = 1;
   double cost = 1e30;
 };
 
@@ -436,29 +450,31 @@ constexpr double kQBlockCost = A == 1 ? 1.0 : 1.45;
 // K splits (= cluster size, <= 8) for CTAs of A * 128 weight rows: the fewest waves of
 // clusters (at most the number of clusters of that size the device holds at once) times
 // the K blocks per CTA, plus a fixed cost per reduction pass and a small one per split
-template <int A>
+template <int A, int T>
 static int plan_q6(wx_ctx* ctx, int64_t N, int zt, int kbs, Q6Plan* best) {
-  const int st = ensure_smem_attr(ctx, (const void*)gemm_q6_fused_kernel<A>, Q6Cfg<A>::kSmem, "gemm_q6_fused");
+  const int st =
+      ensure_smem_attr(ctx, (const void*)gemm_q6_fused_kernel<A, T>, Q6Cfg<A, T>::kSmem, "gemm_q6_fused");
   if (st) return st;
-  const int64_t clusters = N / Q6Cfg<A>::kRows * zt;
+  const int64_t clusters = N / Q6Cfg<A, T>::kRows * zt;
   for (int s = 1; s <= kQMaxSplits && s <= kbs; ++s) {
-    const int active = max_active_clusters<A>(s);
+    const int active = max_active_clusters<A, T>(s);
     if (active <= 0) continue;
     const double waves = (double)((clusters + active - 1) / active);
     const double cost = waves * (((kbs + s - 1) / s) * kQBlockCost<A> + 3.0 * A) + 0.25 * s * A;
     if (cost < best->cost - 1e-9) {
       best->cost = cost;
       best->A = A;
+      best->T = T;
       best->splits = s;
     }
   }
   return WX_OK;
 }
 
-template <int A>
+template <int A, int T>
 static int launch_q6(wx_ctx* ctx, const CUtensorMap& tx, const CUtensorMap& tw, const Q6Params& p, int64_t N,
                      int zt) {
-  using L = Q6Cfg<A>;
+  using L = Q6Cfg<A, T>;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(N / L::kRows), (unsigned)p.splits, (unsigned)zt);
   cfg.blockDim = dim3(L::kThreads, 1, 1);
@@ -472,7 +488,7 @@ static int launch_q6(wx_ctx* ctx, const CUtensorMap& tx, const CUtensorMap& tw, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   ProfScope prof(ctx, kProfGemm);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_q6_fused_kernel<A>, tx, tw, p);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_q6_fused_kernel<A, T>, tx, tw, p);
   if (e != cudaSuccess) {
     cudaGetLastError();
     return set_error(ctx, WX_ERR_CUDA, "gemm_q6_fused<%d> launch (cluster of %d): %s", A, p.splits,
@@ -491,13 +507,24 @@ int qlinear_fused(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const wx_q
   const int Mt = (int)((((M + zt - 1) / zt) + 15) / 16 * 16);
   const int kbs = (int)(w->k / kQBK);
   const int forced = forced_rows();
-  const bool two_ok = w->n % Q6Cfg<2>::kRows == 0;
+  const bool two_ok = w->n % (2 * kQRows) == 0;
   Q6Plan plan;
   int st;
-  if ((forced != 256 || !two_ok) && (st = plan_q6<1>(ctx, w->n, zt, kbs, &plan))) return st;
-  if (forced != 128 && two_ok && (st = plan_q6<2>(ctx, w->n, zt, kbs, &plan))) return st;
+  // (both thread counts of the 128-row CTA hold one CTA per SM: the same cluster occupancy)
+  if ((forced != 256 || !two_ok) && (st = plan_q6<1, 2>(ctx, w->n, zt, kbs, &plan))) return st;
+  if (forced != 128 && two_ok && (st = plan_q6<2, 2>(ctx, w->n, zt, kbs, &plan))) return st;
   if (plan.cost >= 1e30) return set_error(ctx, WX_ERR_CUDA, "gemm_q6_fused: no cluster size fits the device");
   const int kb_per = (kbs + plan.splits - 1) / plan.splits;
+  if (plan.A == 1) {
+    // four expansion threads per weight row (16 warps, 16 values each) shorten the expansion
+    // of a K block; measured faster with full 256-token tiles and short K ranges per CTA
+    // (the pipeline start dominates), slower with small token tiles or long K ranges
+    const int tpr = forced_tpr();
+    plan.T = tpr ? tpr : (Mt == kQMaxMt && kb_per <= 32 ? 4 : 2);
+    if (plan.T == 4 &&
+        (st = ensure_smem_attr(ctx, (const void*)gemm_q6_fused_kernel<1, 4>, Q6Cfg<1, 4>::kSmem, "gemm_q6_fused")))
+      return st;
+  }
   CUtensorMap tx, tw;
   if ((st = make_tmap_bf16_2d(ctx, &tx, x, (uint64_t)M, (uint64_t)w->k, (uint64_t)lda, kQBK, (uint32_t)Mt))) return st;
   const int64_t words = w->k * 6 / 32;
@@ -523,7 +550,8 @@ int qlinear_fused(wx_ctx* ctx, const void* x, int64_t M, int64_t lda, const wx_q
   p.ldy = ldy;
   p.y_raw = static_cast<__nv_bfloat16*>(y_raw);
   p.err = ctx->dev_err;
-  return plan.A == 2 ? launch_q6<2>(ctx, tx, tw, p, w->n, zt) : launch_q6<1>(ctx, tx, tw, p, w->n, zt);
+  if (plan.A == 2) return launch_q6<2, 2>(ctx, tx, tw, p, w->n, zt);
+  return plan.T == 4 ? launch_q6<1, 4>(ctx, tx, tw, p, w->n, zt) : launch_q6<1, 2>(ctx, tx, tw, p, w->n, zt);
 }
 
 }  // namespace wx
