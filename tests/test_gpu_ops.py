@@ -47,6 +47,15 @@ def test_dequant_bit_exact(torch_mod, bits):
     assert np.array_equal(got, ref)
 
 
+@pytest.mark.parametrize("n,k", [(1000, 3072), (9216, 3072), (130, 704)])
+def test_dequant_6bit_bundles_bit_exact(torch_mod, n, k):
+    """The 6-bit expansion (one thread per 16-value bundle) at projection sizes: 9216 x 3072
+    has more bundles than the grid's threads (the grid-stride loop), 704 = 11 groups per row."""
+    wq, sc, bi = O.quantize(O.normal_f32((n, k), 23, 6, std=0.02))
+    got = to_np_bf16(_mf(torch_mod, wq, sc, bi, k).dequantized_weight())
+    assert np.array_equal(got, O.dequantize(wq, sc, bi, k))
+
+
 def test_dequant_reference_4bit_fixture(torch_mod):
     d = np.load(GOLD / "dequant4.npz")
     m = _mf(torch_mod, d["words"], d["scales"], d["biases"], int(d["in_dim"]))

@@ -396,6 +396,44 @@ __global__ void dequant_kernel(const uint32_t* __restrict__ wq, const __nv_bfloa
   }
 }
 
+// 6-bit value j (0..15) of a 16-value bundle of three packed words (value j at bit 6j of the
+// 96-bit little-endian bundle, as dequant_kernel reads it)
+__device__ __forceinline__ uint32_t q6_at(uint32_t w0, uint32_t w1, uint32_t w2, int j) {
+  const int bit = 6 * j, wi = bit >> 5, off = bit & 31;
+  const uint32_t lo = wi == 0 ? w0 : (wi == 1 ? w1 : w2);
+  const uint32_t hi = wi == 0 ? w1 : w2;
+  return (off + 6 > 32 ? __funnelshift_r(lo, hi, off) : (lo >> off)) & 63u;
+}
+
+// The 6-bit weight expansion (group a multiple of 16): one thread per 16-value bundle, i.e.
+// three packed words (a warp reads 384 contiguous bytes) and two 16-byte stores, instead of
+// dequant_kernel's per-value word loads. Same arithmetic (q*s exact, one rounding of q*s + b),
+// so the output is bit-identical to dequant_kernel's. Bundle i of the matrix starts at word
+// 3i and its values land at element 16i (rows are 3k/16 words and k elements).
+__global__ void dequant6_kernel(const uint32_t* __restrict__ wq, const __nv_bfloat16* __restrict__ scales,
+                                const __nv_bfloat16* __restrict__ biases, int64_t n, int64_t k, int group,
+                                __nv_bfloat16* __restrict__ out) {
+  const int64_t per_row = k / 16;
+  const int64_t total = n * per_row;
+  const int64_t groups = k / group;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / per_row, c = i % per_row;
+    const uint32_t w0 = __ldg(wq + 3 * i), w1 = __ldg(wq + 3 * i + 1), w2 = __ldg(wq + 3 * i + 2);
+    const int64_t gidx = r * groups + (c * 16) / group;
+    const float s = __bfloat162float(scales[gidx]);
+    const float b = __bfloat162float(biases[gidx]);
+    uint32_t pk[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      pk[e] = pack_bf16x2(__fmaf_rn((float)q6_at(w0, w1, w2, 2 * e), s, b),
+                          __fmaf_rn((float)q6_at(w0, w1, w2, 2 * e + 1), s, b));
+    uint4* dst = reinterpret_cast<uint4*>(out + 16 * i);
+    dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+  }
+}
+
 static unsigned grid_for(int64_t total, int threads, int num_sms) {
   int64_t b = (total + threads - 1) / threads;
   int64_t cap = (int64_t)num_sms * 32;
@@ -410,6 +448,12 @@ int launch_swiglu(wx_ctx* ctx, const void* t, int64_t m, int64_t F, int64_t ldt,
 
 int launch_dequant(wx_ctx* ctx, const wx_qweight* w, void* out) {
   ProfScope prof(ctx, kProfDequant);
+  if (w->bits == 6 && w->group % 16 == 0 && aligned16(out)) {
+    dequant6_kernel<<<grid_for(w->n * (w->k / 16), 256, ctx->num_sms), 256, 0, ctx->stream>>>(
+        w->wq, static_cast<const __nv_bfloat16*>(w->scales), static_cast<const __nv_bfloat16*>(w->biases), w->n,
+        w->k, w->group, static_cast<__nv_bfloat16*>(out));
+    return launch_status(ctx, "dequant6");
+  }
   dequant_kernel<<<grid_for(w->n * (w->k / 8), 256, ctx->num_sms), 256, 0, ctx->stream>>>(
       w->wq, static_cast<const __nv_bfloat16*>(w->scales), static_cast<const __nv_bfloat16*>(w->biases),
       w->n, w->k, w->group, w->bits, static_cast<__nv_bfloat16*>(out));
