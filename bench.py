@@ -778,6 +778,33 @@ def _qkv_rope_point(args, lin, x, M, K, N, fl, pk, ctx, dev, g, flush) -> dict:
     return out
 
 
+def c2_plan(shape: str, rows: str):
+    """The config-2 points to time and the small-M CTA shapes to force at each.
+
+    Points: the sweep (M 256 / 4096 / 28520 / 111600 at four K, N), or `shape` =
+    "M,K,N[;M,K,N...]", consecutive points of one K, N sharing one weight. CTA shapes: `rows` =
+    "R[/T],..." (WX_QGEMM_ROWS = R weight rows per CTA, WX_QGEMM_TPR = T expansion threads per
+    row; 0 = the library's choice), or [None]: the environment left as it is."""
+    ms_all = (256, 4096, 28520, 111600)
+    plan = [((K, N), ms_all) for K, N in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]]
+    if shape:
+        plan = []
+        for pt in shape.split(";"):
+            M0, K0, N0 = (int(v) for v in pt.split(","))
+            if plan and plan[-1][0] == (K0, N0):
+                plan[-1] = (plan[-1][0], plan[-1][1] + (M0,))
+            else:
+                plan.append(((K0, N0), (M0,)))
+    rows_list = []
+    for r in rows.split(",") if rows else []:
+        parts = r.split("/")
+        if len(parts) > 2 or not all(p.isdigit() for p in parts) or int(parts[0]) not in (0, 128, 256) or \
+                (len(parts) == 2 and int(parts[1]) not in (0, 2, 4)):
+            raise ValueError(f"--rows: {r!r} is not R or R/T with R in 0/128/256 and T in 0/2/4")
+        rows_list.append(r)
+    return plan, rows_list or [None]
+
+
 def run_c2(args) -> dict:
     """the 6-bit quantized linear sweep."""
     import torch
@@ -790,19 +817,7 @@ def run_c2(args) -> dict:
     hbm = peaks.get("hbm_gbs", PEAKS_FALLBACK["hbm_gbs"])
     res = []
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    ms_all = (256, 4096, 28520, 111600)
-    plan = [((K, N), ms_all) for K, N in [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]]
-    if args.shape:  # points "M,K,N[;M,K,N...]" instead of the sweep (profiling runs)
-        plan = []
-        for pt in args.shape.split(";"):
-            M0, K0, N0 = (int(v) for v in pt.split(","))
-            if plan and plan[-1][0] == (K0, N0):
-                plan[-1] = (plan[-1][0], plan[-1][1] + (M0,))
-            else:
-                plan.append(((K0, N0), (M0,)))
-    # small-M CTA shapes to time (WX_QGEMM_ROWS: 128 or 256 weight rows per CTA, 0 = chosen per
-    # call); by default the library's own choice, with the environment left as it is
-    rows_list = args.rows.split(",") if args.rows else [None]
+    plan, rows_list = c2_plan(args.shape, args.rows)
     for (K, N), ms_list in plan:
         bias = (torch.randn(N, device=dev, generator=g) * 0.02).to(torch.bfloat16) if args.bias else None
         lin = h3.MfLinear.quantize(torch.randn((N, K), device=dev, generator=g) * 0.02, bias=bias)

@@ -1,7 +1,8 @@
 """CPU tests of bench.py's host-side arithmetic (no GPU): the config-5 geometry and PAB window,
 the algorithmic FLOP counts the roofline divides by (GEMM 1.375 PFLOP per refresh step; the
 attention of the mix policy), the phase summary of a trace, the memory-bound and peer-store
-summaries, so that a refactor cannot break a GPU run's final JSON line unnoticed."""
+summaries, and the config-2 point and CTA-shape parsing, so that a refactor cannot break a GPU
+run's final JSON line unnoticed."""
 import importlib.util
 from pathlib import Path
 
@@ -70,3 +71,15 @@ def test_memory_and_peer_summaries(bench):
     qkv_b = rows * 3 * c["inner"] * 2 / 2 * 2
     assert ps["peer_bytes_per_step"]["qkv_from_projection_epilogue"] == qkv_b
     assert abs(ps["peer_gbs_lower_bound"]["qkv_phase"] - qkv_b / 0.1 / 1e9) < 1e-6
+
+
+def test_c2_plan_points_and_cta_shapes(bench):
+    plan, rows = bench.c2_plan("", "")
+    assert [kn for kn, _ in plan] == [(3072, 3072), (3072, 9216), (3072, 12288), (12288, 3072)]
+    assert all(ms == (256, 4096, 28520, 111600) for _, ms in plan) and rows == [None]
+    plan, rows = bench.c2_plan("256,3072,3072;512,3072,3072;8,3072,9216;256,3072,3072", "128/2,128/4,256,0")
+    assert plan == [((3072, 3072), (256, 512)), ((3072, 9216), (8,)), ((3072, 3072), (256,))]
+    assert rows == ["128/2", "128/4", "256", "0"]
+    for bad in ("64", "128/3", "128/2/4", "x"):
+        with pytest.raises(ValueError):
+            bench.c2_plan("", bad)
